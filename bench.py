@@ -1,0 +1,346 @@
+#!/usr/bin/env python
+"""Benchmark of the reference's headline metric on B200:
+
+    prefill+decode tok/s at B32/L1024 (27B hybrid, bf16); sum of call medians
+    = (32*1024 + 32) tokens / (median prefill-call time + median decode-call time)
+
+One step = one ``forward_step`` prefill of 32 requests x 1024 tokens into a fresh cache
+(``new_cache(32, initial_capacity=64)``, so cache growth is inside the call, as in the
+reference benchmark) followed by one decode ``forward_step`` of 32 tokens at 1024 prior
+context. Weights: seeded N(0, 0.02) random init of the 27B geometry (54 GB, larger than
+L2, streamed by every call). Token ids: the reference case ``batch_32_length_1024``
+(uniform ids, seeds 26/27).
+
+``value`` is device time (CUDA events around each call on the launching stream);
+``e2e`` is wall time of the same public calls with the host token lists as input and the
+logits read back to host memory. With N GPUs (torchrun) every rank runs its own B32/L1024
+requests on its own replica (weak scaling, no collective on the data path); times are the
+max over ranks. ``--impl reference`` times the CPU restatement of the reference
+(oracle/) on a bounded sample of the same workload and extrapolates.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "prefill+decode tok/s at B32/L1024 (27B hybrid, bf16); sum of call medians"
+UNIT = "tok/s"
+
+
+def _peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return p["hbm_gbs"], p["bf16_tflops"], p["bf16_tflops_sustained"], "measured"
+    except Exception:
+        return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms during the timed region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.f,
+                                         stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        self.f.flush()
+        rows = []
+        with open(self.f.name) as fh:
+            for line in fh:
+                parts = [x.strip() for x in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+        os.unlink(self.f.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def make_inputs(V, B, L, rank):
+    import torch
+    g = torch.Generator().manual_seed(26 + 1000 * rank)
+    ids = torch.randint(V, (B * L,), generator=g)
+    prefill = [r.tolist() for r in ids.split([L] * B)]
+    g = torch.Generator().manual_seed(27 + 1000 * rank)
+    decode = [[t] for t in torch.randint(V, (B,), generator=g).tolist()]
+    return prefill, decode
+
+
+# ------------------------------------------------------------------------- CPU baseline
+def cpu_baseline(B=32, L=1024, sample_tokens=512, decode_ctx=128):
+    """CPU restatement (oracle/) of the 27B step on a bounded sample: one GDN layer, one
+    attention layer and one MLP at full 27B width for a prefill of 2 requests of
+    sample_tokens/2 tokens and a decode of B requests at decode_ctx context, plus the
+    lm_head; extrapolated by layer counts and (prefill) linearly in tokens."""
+    import torch
+
+    from oracle import ops as O
+    from qwen38_inference_b200.config import qwen38_27b
+    threads = len(os.sched_getaffinity(0))
+    torch.set_num_threads(threads)
+    c = qwen38_27b()
+    g = torch.Generator().manual_seed(0)
+
+    def W(*shape):
+        return (torch.randn(*shape, generator=g) * 0.02).to(torch.bfloat16).float()
+
+    H = c.hidden_size
+    gdn = dict(qkvz=W(c.qkvz_dim, H), ba=W(c.ba_dim, H), conv=W(c.conv_dim, 4), A_log=torch.zeros(48),
+               dt_bias=W(48), norm=W(128) + 1, out=W(H, c.gdn_v_dim))
+    att = dict(qkv=W(c.qkv_dim, H), out=W(H, c.attn_out_dim), q_norm=W(256), k_norm=W(256))
+    mlp = dict(gate_up=W(2 * c.intermediate_size, H), down=W(H, c.intermediate_size))
+    lm = W(c.vocab_size, H)
+    rope = torch.randn(8192, 64)
+    rnd = O.bf16
+
+    def gdn_layer(x, n_req, decode):
+        T = x.shape[0]
+        qkvz = O.linear(x, gdn["qkvz"], rnd)
+        ba = O.linear(x, gdn["ba"], rnd)
+        st = torch.zeros(n_req, c.conv_dim, 3, dtype=torch.bfloat16)
+        rec = torch.zeros(n_req, 48, 128, 128)
+        gg, beta = O.gdn_gating(gdn["A_log"], ba[:, 48:], ba[:, :48], gdn["dt_bias"], rnd)
+        if decode:
+            mixed = O.conv_decode(qkvz[:, :c.conv_dim], gdn["conv"], st, list(range(n_req)), rnd)
+        else:
+            per = T // n_req
+            mixed = O.conv_prefill(qkvz[:, :c.conv_dim], gdn["conv"], st, [i * per for i in range(n_req + 1)],
+                                   list(range(n_req)), [False] * n_req, rnd)
+        q = O.l2norm(mixed[:, :2048].reshape(T, 16, 128))
+        k = O.l2norm(mixed[:, 2048:4096].reshape(T, 16, 128))
+        v = mixed[:, 4096:].reshape(T, 48, 128)
+        per = T // n_req
+        o = torch.empty(T, 48, 128)
+        for i in range(n_req):
+            s = slice(i * per, (i + 1) * per)
+            o[s], rec[i] = O.gdn_recurrence(q[s], k[s], v[s], gg[s], beta[s], rec[i], 128 ** -0.5, 3)
+        y = O.gated_rmsnorm(rnd(o).reshape(-1, 128), gdn["norm"], qkvz[:, c.conv_dim:].reshape(-1, 128), 1e-6, rnd)
+        return O.linear(y.reshape(T, -1), gdn["out"], rnd)
+
+    def attn_layer(x, n_req, ctx):
+        T = x.shape[0]
+        proj = O.linear(x, att["qkv"], rnd)
+        qg, k, v = proj.split([c.q_gate_dim, c.kv_dim, c.kv_dim], dim=-1)
+        pos = torch.arange(T) % 4096
+        q, k, gate = O.qk_norm_rope_gate(qg, k, att["q_norm"], att["k_norm"], rope, pos, 1e-6, 24, 4, 256, 64, rnd)
+        per = T // n_req
+        rows = n_req * (ctx + per) + 64
+        kc = torch.zeros(rows, 4, 256, dtype=torch.bfloat16)
+        vc = torch.zeros(rows, 4, 256, dtype=torch.bfloat16)
+        starts = [64 + i * (ctx + per) for i in range(n_req)]
+        loc = torch.tensor([starts[i] + ctx + j for i in range(n_req) for j in range(per)])
+        kc[loc] = k.to(torch.bfloat16)
+        vc[loc] = v.reshape(-1, 4, 256).to(torch.bfloat16)
+        a = O.paged_attention(q, kc, vc, starts, [ctx] * n_req, [per] * n_req, 256 ** -0.5, rnd)
+        out = O.sigmoid_mul(a.reshape(T, -1), gate.reshape(T, -1), rnd)
+        return O.linear(out, att["out"], rnd)
+
+    def mlp_layer(x):
+        return O.linear(O.silu_mul(O.linear(x, mlp["gate_up"], rnd), rnd), mlp["down"], rnd)
+
+    def timed(fn):
+        t = time.perf_counter()
+        fn()
+        return time.perf_counter() - t
+
+    x = torch.randn(sample_tokens, H).to(torch.bfloat16).float()
+    tp = {"gdn": timed(lambda: gdn_layer(x, 2, False)), "attn": timed(lambda: attn_layer(x, 2, 0)),
+          "mlp": timed(lambda: mlp_layer(x)), "lm": timed(lambda: O.linear(x[:2], lm, rnd))}
+    xd = torch.randn(B, H).to(torch.bfloat16).float()
+    td = {"gdn": timed(lambda: gdn_layer(xd, B, True)), "attn": timed(lambda: attn_layer(xd, B, decode_ctx)),
+          "mlp": timed(lambda: mlp_layer(xd)), "lm": timed(lambda: O.linear(xd, lm, rnd))}
+    scale = B * L / sample_tokens
+    prefill_s = scale * (48 * tp["gdn"] + 16 * tp["attn"] + 64 * tp["mlp"]) + (B / 2) * tp["lm"]
+    decode_s = 48 * td["gdn"] + 16 * td["attn"] + 64 * td["mlp"] + td["lm"]
+    value = (B * L + B) / (prefill_s + decode_s)
+    sample = (f"CPU restatement (oracle/, fp32 math with bf16 rounding points), extrapolated: one GDN, one "
+              f"attention and one MLP layer at 27B width on a {sample_tokens}-token prefill (2 requests) and a "
+              f"B{B} decode at {decode_ctx} context, plus lm_head; scaled by layer counts (48/16/64) and linearly "
+              f"to {B}x{L} tokens; est. prefill {prefill_s:.1f} s + decode {decode_s:.2f} s")
+    return {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample,
+            "sample_seconds": sum(tp.values()) + sum(td.values())}
+
+
+# ------------------------------------------------------------------------- GPU arm
+def run_gpu(args):
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=torch.device("cuda", local))
+    from qwen38_inference_b200 import Qwen38, ops
+    from qwen38_inference_b200.config import qwen38_27b
+
+    cfg = qwen38_27b()
+    B, L = args.batch, args.length
+    model = Qwen38(config=cfg, seed=0, device=f"cuda:{local}", max_context=max(8192, 2 * L))
+    prefill, decode = make_inputs(cfg.vocab_size, B, L, rank)
+    stream = torch.cuda.current_stream()
+
+    def barrier():
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def one_step(record):
+        cache = model.new_cache(B, initial_capacity=64)
+        torch.cuda.synchronize()
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+        t0 = time.perf_counter()
+        ev[0].record(stream)
+        lg = model.forward_step(prefill, cache)
+        ev[1].record(stream)
+        h2d = model._engine.last_h2d_bytes
+        host_p = lg.cpu()
+        t1 = time.perf_counter()
+        ev[2].record(stream)
+        lg = model.forward_step(decode, cache)
+        ev[3].record(stream)
+        h2d += model._engine.last_h2d_bytes
+        host_d = lg.cpu()
+        t2 = time.perf_counter()
+        torch.cuda.synchronize()
+        if record is not None:
+            record["p"].append(ev[0].elapsed_time(ev[1]))
+            record["d"].append(ev[2].elapsed_time(ev[3]))
+            record["p_wall"].append((t1 - t0) * 1e3)
+            record["d_wall"].append((t2 - t1) * 1e3)
+        return h2d, host_p.numel() * 4 + host_d.numel() * 4
+    for _ in range(args.warmup):
+        one_step(None)
+    rec = {"p": [], "d": [], "p_wall": [], "d_wall": []}
+    ops.LAUNCHES[0] = 0
+    barrier()
+    with ClockSampler(local) as clk:
+        for _ in range(args.steps):
+            h2d, d2h = one_step(rec)
+        barrier()
+    launches = ops.LAUNCHES[0] // max(1, args.steps)
+    clocks = clk.summary()
+    med_p, med_d = statistics.median(rec["p"]), statistics.median(rec["d"])
+    med_pw, med_dw = statistics.median(rec["p_wall"]), statistics.median(rec["d_wall"])
+    t = torch.tensor([med_p + med_d, med_pw + med_dw, med_p, med_d], dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    step_ms, e2e_ms, mp, md = t.tolist()
+    tokens = world * (B * L + B)
+
+    # ---- roofline of the dominant kernel (the tcgen05 GEMM): one instrumented prefill
+    prof = []
+    ops.PROFILE = prof
+    cache = model.new_cache(B, initial_capacity=64)
+    model.forward_step(prefill, cache)
+    torch.cuda.synchronize()
+    ops.PROFILE = None
+    flops = sum(f for f, _, _ in prof)
+    ms = sum(a.elapsed_time(b) for _, a, b in prof)
+    hbm, tf_burst, tf_sust, src = _peaks()
+    achieved = flops / (ms * 1e-3) / 1e12 if ms > 0 else None
+    roof = {"bound": "tensor", "kernel": "gemm_tcgen05_kernel (all prefill projections)",
+            "achieved": round(achieved, 1) if achieved else None, "peak": tf_sust, "unit": "TFLOP/s",
+            "frac": round(achieved / tf_sust, 4) if achieved else None,
+            "peak_source": f"{src} bf16_tflops_sustained (kernel timed inside a long step)",
+            "launches": len(prof), "avg_launch_ms": round(ms / max(1, len(prof)), 4),
+            "traffic": None, "gemm_share_of_prefill": round(ms / mp, 4) if mp else None}
+    out = {"metric": METRIC, "value": round(tokens / (step_ms * 1e-3), 1), "unit": UNIT, "n_gpus": world,
+           "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_ms, 3), "higher_is_better": True,
+           "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+           "data": "synthetic (random-init N(0,0.02) 27B weights; uniform token ids, reference case seeds 26/27)",
+           "config": {"workload": f"B{B}xL{L} prefill into a fresh cache + B{B} decode at {L} context, 27B hybrid",
+                      "model": "Qwen3.8-27B hybrid geometry (48 GDN + 16 gated GQA), random init",
+                      "global_batch": world * B, "seq_len": L, "parallelism": f"replicas x{world} (requests sharded)",
+                      "l2": "inputs larger than L2 (54 GB of weights streamed per call)"},
+           "median_ms": {"prefill": round(mp, 3), "decode": round(md, 3)},
+           "e2e": {"value": round(tokens / (e2e_ms * 1e-3), 1), "unit": UNIT, "h2d_bytes_per_step": h2d,
+                   "d2h_bytes_per_step": d2h},
+           "gpu_launches": launches, "clocks": clocks, "roofline": roof}
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        out["cpu_baseline"] = cpu_baseline(B, L)
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    t0 = time.perf_counter()
+    cb = cpu_baseline(args.batch, args.length)
+    wall = time.perf_counter() - t0
+    out = {"metric": METRIC, "value": round(cb["value"], 2), "unit": UNIT, "impl": "reference",
+           "n_gpus": args.gpus, "steps": 1, "warmup": 0, "higher_is_better": True, "scaling": "weak",
+           "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+           "config": {"workload": f"B{args.batch}xL{args.length} prefill + B{args.batch} decode, 27B hybrid (CPU sample)"},
+           "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
+           "e2e": {"value": round(cb["value"], 2), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+           "wall_s": round(wall, 1)}
+    print(json.dumps(out), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--batch", type=int, default=32)
+    ap.add_argument("--length", type=int, default=1024)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "ours":
+        print("note: fewer than 3 warm-up steps", file=sys.stderr)
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_gpu(args)
+
+
+if __name__ == "__main__":
+    main()

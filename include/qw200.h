@@ -1,0 +1,142 @@
+/*
+ * qw200.h - C ABI of the B200 (sm_100a) kernels behind the hybrid Gated-DeltaNet /
+ * gated-GQA forward_step.
+ *
+ * Every entry point takes plain device pointers, sizes and strides (in elements), the
+ * CUDA stream to launch on, and returns 0 or a QW_ERR_* code. No entry point allocates
+ * device memory: callers pass every buffer, including workspaces. Kernels record
+ * device-side failures (a bounded wait that gave up, an index outside its range) in one
+ * library-wide error word that qw_take_device_error() reads and clears.
+ *
+ * Element types: "bf16" = __nv_bfloat16 bit patterns (uint16), "f32" = float,
+ * "i32"/"i64" = int32_t/int64_t. Row-major unless stated.
+ *
+ * Each declaration names the reference interface it replaces, as
+ * reference/qwen38_inference.py:<line> ("REF").
+ */
+#ifndef QW200_H
+#define QW200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* qw_stream_t;
+
+/* ---- status codes ------------------------------------------------------------------ */
+#define QW_OK 0
+#define QW_ERR_ARG 1         /* bad size, count or null pointer                          */
+#define QW_ERR_ALIGN 2       /* pointer or leading dimension not 16-byte aligned         */
+#define QW_ERR_UNSUPPORTED 3 /* head size / width with no compiled kernel                */
+#define QW_ERR_WORKSPACE 4   /* workspace smaller than qw_*_workspace_bytes()            */
+#define QW_ERR_DRIVER 5      /* cuTensorMapEncodeTiled unavailable or failed             */
+#define QW_ERR_CUDA_BASE 1000 /* + cudaError_t of a failed launch                       */
+
+/* device error word values */
+#define QW_DEV_ERR_TIMEOUT_GEMM 101
+#define QW_DEV_ERR_INDEX 102
+
+/* ---- library ----------------------------------------------------------------------- */
+int qw_version(void);
+/* Synchronizes the device, stores the device error word in *code and clears it. */
+int qw_take_device_error(int* code);
+
+/* ---- dense projections (REF:5054,5067,5069,5070,5087,5089,5092,5096: F.linear) ------ *
+ * y = x[M,K] . w[N,K]^T with fp32 accumulation on tcgen05 tensor cores.
+ *   out_kind QW_OUT_BF16:        y bf16 [M, ldy], N columns            (F.linear)
+ *   out_kind QW_OUT_F32_OF_BF16: y f32  [M, ldy] = float(bf16(acc))     (F.linear().float(), REF:5096)
+ *   out_kind QW_OUT_SWIGLU:      w = [gate; up] with N = 2*I rows, y bf16 [M, ldy] with I
+ *                                columns = bf16(silu(bf16(g)) * bf16(u)) (REF:5089-5091 + REF:2238-2281)
+ * Small M (decode) runs weight-streaming split-K tiles and needs a workspace of
+ * qw_gemm_workspace_bytes(M, N, K) bytes (0 for large M).
+ */
+#define QW_OUT_BF16 0
+#define QW_OUT_F32_OF_BF16 1
+#define QW_OUT_SWIGLU 2
+size_t qw_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K, int out_kind);
+int qw_gemm_bf16(const void* x, const void* w, void* y, int64_t M, int64_t N, int64_t K, int64_t ldx,
+                 int64_t ldw, int64_t ldy, int out_kind, void* workspace, size_t ws_bytes, qw_stream_t stream);
+
+/* ---- hidden-state norms ------------------------------------------------------------ */
+/* residual = table[tokens] (bf16 [T,H]); hidden = bf16(r * rsqrt(mean r^2 + eps) * (1 + w))
+ * (REF:5045 F.embedding + REF:5049-5050 sgl_kernel gemma_rmsnorm)                          */
+int qw_embed_rmsnorm(const int32_t* tokens, int64_t T, const void* table, int64_t vocab, int64_t H, const void* w,
+                     void* resid_out, void* hidden_out, float eps, qw_stream_t stream);
+/* in place: h = x + resid (fp32); resid = bf16(h); x = bf16(h * rsqrt(mean h^2 + eps) * (1 + w))
+ * (REF:5052, 5088: sgl_kernel gemma_fused_add_rmsnorm)                                      */
+int qw_add_rmsnorm(void* x, void* resid, const void* w, int64_t T, int64_t H, float eps, qw_stream_t stream);
+/* out[i] = norm(x[rows[i]] + resid[rows[i]]) for n_rows selected rows (rows == NULL: all T);
+ * inputs unchanged (REF:5093-5095: final add-norm + last-row select)                        */
+int qw_add_rmsnorm_rows(const void* x, const void* resid, const int32_t* rows, int64_t n_rows, int64_t T, int64_t H,
+                        const void* w, void* out, float eps, qw_stream_t stream);
+/* y = bf16(x * rsqrt(mean x^2 + eps) * w * z * sigmoid(z)) per head of D columns
+ * (REF:1804-2089 rms_norm_gated, norm_before_gate=True, swish)                             */
+int qw_gated_rmsnorm(const void* x, int64_t ldx, const void* z, int64_t ldz, const void* w, void* y, int64_t ldy,
+                     int64_t T, int64_t HV, int64_t D, float eps, qw_stream_t stream);
+
+/* ---- gated GQA attention ---------------------------------------------------------- */
+/* qkv bf16 [T, ldq] = per query head [q | gate] (2d), then k (nkv*d), then v (nkv*d).
+ * Gemma RMSNorm of every q and k head, NeoX RoPE on the first rotary_dim dims with the
+ * fp32 [cos | sin] table rope[rope_rows, rotary_dim] at positions[t]; q written back in
+ * place; k and v stored at cache row locations[t] of k_cache/v_cache [cache_rows, nkv, d]
+ * (REF:83-278 fused_qk_gemma_rmsnorm_rope_gate + REF:2656-2787 store_kvcache)              */
+int qw_qk_norm_rope_store(void* qkv, int64_t ldq, int64_t T, int64_t nq, int64_t nkv, int64_t d, const void* q_w,
+                          const void* k_w, const float* rope, int64_t rotary_dim, int64_t rope_rows,
+                          const int32_t* positions, const int32_t* locations, void* k_cache, void* v_cache,
+                          int64_t cache_rows, float eps, qw_stream_t stream);
+/* Causal varlen attention for prefill/extend; tiles = int32 pairs (request, first query)
+ * of 128-query tiles; request i owns query rows cu[i]..cu[i+1], has prefix[i] cached tokens
+ * and its keys start at cache row kv_base[i]. out bf16 [T, ldo] =
+ * bf16(bf16(softmax(q k^T * scale) v) * sigmoid(gate))
+ * (REF:5059-5066 trtllm_batch_context_with_kv_cache + fused_sigmoid_mul)                   */
+int qw_attn_prefill(const void* qkv, int64_t ldq, int64_t nq, int64_t nkv, int64_t d, const void* k_cache,
+                    const void* v_cache, const void* tiles, int64_t n_tiles, const int32_t* cu_seqlens,
+                    const int32_t* prefix, const int32_t* kv_base, void* out, int64_t ldo, float scale,
+                    qw_stream_t stream);
+/* One query per request against seq_len[b] keys from row kv_base[b], split over `splits`
+ * CTAs per (request, kv head) and combined (REF:5059-5062 trtllm_batch_decode_with_kv_cache
+ * + REF:5066 fused_sigmoid_mul)                                                              */
+size_t qw_attn_decode_workspace_bytes(int64_t B, int64_t nq, int64_t d, int64_t splits);
+int qw_attn_decode(const void* qkv, int64_t ldq, int64_t B, int64_t nq, int64_t nkv, int64_t d, const void* k_cache,
+                   const void* v_cache, const int32_t* seq_len, const int32_t* kv_base, int64_t max_len,
+                   int64_t splits, void* out, int64_t ldo, float scale, void* workspace, size_t ws_bytes,
+                   qw_stream_t stream);
+
+/* ---- Gated DeltaNet ------------------------------------------------------------------ */
+/* Prefill causal conv (width 4) + SiLU over the first 2*qk_dim+v_dim columns of x [T, ldx],
+ * L2 norm of q/k heads, token-major q,k [T, qk_dim], v [T, v_dim]; conv_state [S, C, 3]
+ * read when has_initial[b] and rewritten for every request
+ * (REF:704-1253 causal_conv1d_fn + REF:603-699 split + REF:1550-1638 l2norm)               */
+int qw_conv_prefill(const void* x, int64_t ldx, const void* conv_w, void* conv_state, const int32_t* cu_seqlens,
+                    const int32_t* slots, const int32_t* has_initial, int64_t B, int64_t n_slots, int64_t max_len,
+                    void* q_out, void* k_out, void* v_out, int64_t qk_dim, int64_t v_dim, int64_t head_dim,
+                    qw_stream_t stream);
+/* Chunked gated delta rule over varlen requests with the gating folded in; state
+ * [S, HV, dv, dk] fp32 read and written in place at slots[b]; out bf16 [T, HV, dv]
+ * (REF:5081-5085: fused_gdn_gating + flashinfer chunk_gated_delta_rule + index_copy_)      */
+int qw_gdn_prefill(const void* q, const void* k, const void* v, const void* ba, int64_t ldba, const float* A_log,
+                   const void* dt_bias, const int32_t* cu_seqlens, const int32_t* slots, int64_t B, int64_t n_slots,
+                   float* state, void* out, int64_t H, int64_t HV, int64_t dk, int64_t dv, float scale,
+                   qw_stream_t stream);
+/* Decode: conv update + L2 norm + gating + one recurrent step + gated RMSNorm, y bf16
+ * [B, HV*dv] (REF:5072-5075 fused_qkvzba_causal_conv1d_update + recurrent packed decode,
+ * REF:5086 rms_norm_gated)                                                                   */
+int qw_gdn_decode(const void* qkvz, int64_t ldx, const void* ba, int64_t ldba, const void* conv_w, void* conv_state,
+                  float* state, const int32_t* slots, int64_t B, int64_t n_slots, const float* A_log,
+                  const void* dt_bias, const void* norm_w, void* y, int64_t ldy, int64_t H, int64_t HV, int64_t dk,
+                  int64_t dv, float eps, qw_stream_t stream);
+
+/* ---- cache growth ------------------------------------------------------------------- */
+/* dst [S*new_cap + 64, row_elems] = live prefixes of src [S*old_cap + 64, row_elems]
+ * (rows 64 + s*old_cap + j, j < lengths[s]) moved to rows 64 + s*new_cap + j; every other
+ * row zero. Applied to K and V together (REF:4985-5001 _reserve; solution/cache_growth.py) */
+int qw_kv_grow(const void* src_k, const void* src_v, void* dst_k, void* dst_v, const int32_t* lengths, int64_t S,
+               int64_t old_cap, int64_t new_cap, int64_t row_elems, qw_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* QW200_H */

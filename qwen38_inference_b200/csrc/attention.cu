@@ -1,0 +1,564 @@
+// Gated GQA attention over the slot-contiguous paged KV cache.
+//
+//   qw_qk_norm_rope_store  per-head Gemma RMSNorm of q and k, NeoX RoPE on the first
+//                          rotary dims, q written back in place, k and v stored at their
+//                          cache rows (REF:83-190 fused with the KV store REF:2656-2687)
+//   qw_attn_prefill        causal varlen attention, tensor cores (mma.sync m16n8k16 bf16),
+//                          epilogue out = bf16(bf16(o) * sigmoid(gate)) (L5 + REF:2105-2121)
+//   qw_attn_decode         one query per request, split over the KV length, CUDA cores;
+//                          partials combined by qw_attn_decode's second kernel (L6 + K10)
+//
+// Cache layout (the reference's, REF:4966-4983): K and V are [rows, nkv, d] with rows
+// 64 + slot*capacity + position; page 0 (rows 0..63) is reserved. A request's keys are
+// therefore contiguous from row kv_base = 64 + slot*capacity, which is what the kernels
+// address; the page table of REF:5038-5040 is implied by that layout.
+#include "common.cuh"
+
+namespace qw {
+
+// ============================================================== q/k norm + rope + kv store
+template <int D>
+__global__ void qk_norm_rope_store_kernel(__nv_bfloat16* __restrict__ qkv, int64_t ldq, int nq, int nkv,
+                                          const __nv_bfloat16* __restrict__ q_w, const __nv_bfloat16* __restrict__ k_w,
+                                          const float* __restrict__ rope, int rd, int64_t rope_rows,
+                                          const int32_t* __restrict__ positions, const int32_t* __restrict__ locs,
+                                          __nv_bfloat16* __restrict__ kc, __nv_bfloat16* __restrict__ vc,
+                                          int64_t cache_rows, int T, float eps, int* err) {
+  constexpr int E = D / 32;
+  const int gw = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  const int heads = nq + nkv;
+  if (gw >= T * heads) return;
+  const int t = gw / heads, h = gw % heads;
+  const bool is_k = h >= nq;
+  const int kh = h - nq;
+  __nv_bfloat16* row = qkv + (int64_t)t * ldq;
+  __nv_bfloat16* src = is_k ? row + (int64_t)2 * nq * D + kh * D : row + (int64_t)h * 2 * D;
+  const __nv_bfloat16* wt = is_k ? k_w : q_w;
+  const int c0 = lane * E;
+  float x[E], w[E];
+#pragma unroll
+  for (int j = 0; j < E; ++j) {
+    x[j] = bf2f(src[c0 + j]);
+    w[j] = bf2f(wt[c0 + j]);
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < E; ++j) ss += x[j] * x[j];
+  ss = warp_sum(ss);
+  const float inv = rsqrtf(ss / (float)D + eps);
+  float xn[E];
+#pragma unroll
+  for (int j = 0; j < E; ++j) xn[j] = bf16_round(x[j] * inv * (w[j] + 1.0f));
+  // rotate-half on [0, rd): pair (i, i + rd/2); partner lane holds the matching elements
+  const int half = rd / 2;
+  const int off = half / E;  // lane distance between partners
+  int pos = positions[t];
+  if (pos < 0 || pos >= rope_rows) {
+    set_error(err, QW_DEV_ERR_INDEX);
+    pos = 0;
+  }
+  float o[E];
+#pragma unroll
+  for (int j = 0; j < E; ++j) {
+    const float partner = __shfl_sync(0xffffffffu, xn[j], (c0 < half) ? lane + off : lane - off);
+    const int c = c0 + j;
+    if (c < half) {
+      const float cs = rope[(int64_t)pos * rd + c], sn = rope[(int64_t)pos * rd + half + c];
+      o[j] = xn[j] * cs - partner * sn;
+    } else if (c < rd) {
+      const float cs = rope[(int64_t)pos * rd + c - half], sn = rope[(int64_t)pos * rd + c];
+      o[j] = xn[j] * cs + partner * sn;
+    } else {
+      o[j] = xn[j];
+    }
+  }
+  if (!is_k) {
+#pragma unroll
+    for (int j = 0; j < E; ++j) src[c0 + j] = f2bf(o[j]);
+    return;
+  }
+  const int64_t loc = locs[t];
+  if (loc < 0 || loc >= cache_rows) {
+    set_error(err, QW_DEV_ERR_INDEX);
+    return;
+  }
+  if (loc == 0) return;  // reserved row, skipped like the reference store (REF:2683)
+  __nv_bfloat16* kd = kc + (loc * nkv + kh) * D;
+  __nv_bfloat16* vd = vc + (loc * nkv + kh) * D;
+  const __nv_bfloat16* vs = row + (int64_t)2 * nq * D + (int64_t)nkv * D + kh * D;
+#pragma unroll
+  for (int j = 0; j < E; ++j) {
+    kd[c0 + j] = f2bf(o[j]);
+    vd[c0 + j] = vs[c0 + j];
+  }
+}
+
+// ============================================================== prefill attention (tensor cores)
+QW_DEV void ldmatrix_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+QW_DEV void ldmatrix_x4_trans(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+QW_DEV void mma_bf16_16816(float* d, const uint32_t* a, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+QW_DEV void cp_async16(uint32_t dst, const void* src, bool pred) {
+  const int n = pred ? 16 : 0;
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(n) : "memory");
+}
+QW_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+QW_DEV void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// byte offset of 16-byte chunk `c` of row `r` in a tile whose rows are D bf16 long,
+// with the chunk index XOR-swizzled by (r % 8) so ldmatrix reads are conflict free
+template <int D>
+QW_DEV uint32_t swz(int r, int c) {
+  return (uint32_t)(r * (D * 2) + ((c ^ (r & 7)) << 4));
+}
+
+struct PrefillTile {
+  int32_t req;    // request index
+  int32_t q0;     // first query (within the request) of this tile
+};
+
+template <int D, int BM, int BN>
+struct AttnSmem {
+  static constexpr int Q = BM * D * 2;
+  static constexpr int KV = BN * D * 2;
+  static constexpr int TOTAL = Q + 4 * KV;  // Q, then double-buffered K and V
+};
+
+// grid: (n_tiles, nq). 8 warps x 16 query rows.
+template <int D>
+__global__ void __launch_bounds__(256, 1)
+    attn_prefill_kernel(const __nv_bfloat16* __restrict__ qkv, int64_t ldq, int nq, int nkv,
+                        const __nv_bfloat16* __restrict__ kc, const __nv_bfloat16* __restrict__ vc,
+                        const PrefillTile* __restrict__ tiles, const int32_t* __restrict__ cu,
+                        const int32_t* __restrict__ prefix, const int32_t* __restrict__ kv_base,
+                        __nv_bfloat16* __restrict__ out, int64_t ldo, float scale_log2) {
+  constexpr int BM = 128, BN = 64, NW = 8;
+  constexpr int CH = D / 8;  // 16-byte chunks per row
+  using L = AttnSmem<D, BM, BN>;
+  extern __shared__ __align__(128) uint8_t smem[];
+  const uint32_t sQ = smem_u32(smem);
+  const uint32_t sK0 = sQ + L::Q;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const PrefillTile tile = tiles[blockIdx.x];
+  const int h = blockIdx.y;
+  const int kvh = h / (nq / nkv);
+  const int t0 = cu[tile.req], n = cu[tile.req + 1] - t0;
+  const int p = prefix[tile.req];
+  const int64_t kb = kv_base[tile.req];
+  const int q_end = min(n, tile.q0 + BM);            // exclusive, within request
+  const int kv_len = p + q_end;                      // keys needed by this tile
+  const int n_kv_tiles = (kv_len + BN - 1) / BN;
+
+  // ---- load Q tile (rows beyond the request are zero-filled)
+  for (int i = threadIdx.x; i < BM * CH; i += blockDim.x) {
+    const int r = i / CH, c = i % CH;
+    const int qi = tile.q0 + r;
+    const __nv_bfloat16* src = qkv + (int64_t)(t0 + min(qi, n - 1)) * ldq + (int64_t)h * 2 * D + c * 8;
+    cp_async16(sQ + swz<D>(r, c), src, qi < n);
+  }
+  auto load_kv = [&](int j, int buf) {
+    const uint32_t sK = sK0 + buf * 2 * L::KV;
+    const uint32_t sV = sK + L::KV;
+    for (int i = threadIdx.x; i < BN * CH; i += blockDim.x) {
+      const int r = i / CH, c = i % CH;
+      const int key = j * BN + r;
+      const int64_t rowi = kb + min(key, kv_len - 1);
+      const bool ok = key < kv_len;
+      cp_async16(sK + swz<D>(r, c), kc + (rowi * nkv + kvh) * D + c * 8, ok);
+      cp_async16(sV + swz<D>(r, c), vc + (rowi * nkv + kvh) * D + c * 8, ok);
+    }
+  };
+  load_kv(0, 0);
+  cp_async_commit();
+
+  float o[D / 8][4];
+#pragma unroll
+  for (int i = 0; i < D / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  float m_r[2] = {-INFINITY, -INFINITY}, l_r[2] = {0.f, 0.f};
+  const int g = lane >> 2, cq = lane & 3;
+  const int row0 = warp * 16;  // warp's first row in the tile
+  const int qpos0 = p + tile.q0 + row0 + g;  // absolute position of row g (and +8)
+
+  for (int j = 0; j < n_kv_tiles; ++j) {
+    if (j + 1 < n_kv_tiles) load_kv(j + 1, (j + 1) & 1);
+    cp_async_commit();
+    cp_async_wait<1>();
+    __syncthreads();
+    const uint32_t sK = sK0 + (j & 1) * 2 * L::KV;
+    const uint32_t sV = sK + L::KV;
+    // warps whose rows all precede this key tile skip the math (causal)
+    const bool active = (p + tile.q0 + row0 + 15) >= j * BN;
+    if (active) {
+      // ---- S = Q K^T  (16 x 64 per warp)
+      float s[8][4];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) s[i][0] = s[i][1] = s[i][2] = s[i][3] = 0.f;
+#pragma unroll
+      for (int kk = 0; kk < D / 16; ++kk) {
+        uint32_t a[4];
+        {
+          const int r = row0 + (lane & 15);
+          const int c = kk * 2 + (lane >> 4);
+          ldmatrix_x4(sQ + swz<D>(r, c), a[0], a[1], a[2], a[3]);
+        }
+#pragma unroll
+        for (int nt = 0; nt < 8; nt += 2) {
+          // matrices: keys nt*8..+7 (k lo, k hi), keys (nt+1)*8..+7 (k lo, k hi)
+          const int r = nt * 8 + (lane & 7) + ((lane >> 4) << 3);
+          const int c = kk * 2 + ((lane >> 3) & 1);
+          uint32_t b0, b1, b2, b3;
+          ldmatrix_x4(sK + swz<D>(r, c), b0, b1, b2, b3);
+          mma_bf16_16816(s[nt], a, b0, b1);
+          mma_bf16_16816(s[nt + 1], a, b2, b3);
+        }
+      }
+      // ---- mask + online softmax (rows g and g+8)
+      float mx[2] = {m_r[0], m_r[1]};
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int key = j * BN + nt * 8 + cq * 2 + (e & 1);
+          const int qpos = qpos0 + ((e >> 1) << 3);
+          float v = s[nt][e] * scale_log2;
+          if (key > qpos || key >= kv_len) v = -INFINITY;
+          s[nt][e] = v;
+          mx[e >> 1] = fmaxf(mx[e >> 1], v);
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 1));
+        mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 2));
+      }
+      float alpha[2], rs[2] = {0.f, 0.f};
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        alpha[r] = (mx[r] == -INFINITY) ? 1.f : exp2f(m_r[r] - mx[r]);
+        m_r[r] = mx[r];
+      }
+      uint32_t pa[4][4];  // P as A fragments, 4 k-steps of 16 keys
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt) {
+        float pv[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int r = e >> 1;
+          pv[e] = (m_r[r] == -INFINITY) ? 0.f : exp2f(s[nt][e] - m_r[r]);
+          rs[r] += pv[e];
+        }
+        const int ks = nt >> 1, hi = nt & 1;
+        pa[ks][hi * 2 + 0] = pack_bf16x2(pv[0], pv[1]);
+        pa[ks][hi * 2 + 1] = pack_bf16x2(pv[2], pv[3]);
+      }
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        rs[r] += __shfl_xor_sync(0xffffffffu, rs[r], 1);
+        rs[r] += __shfl_xor_sync(0xffffffffu, rs[r], 2);
+        l_r[r] = l_r[r] * alpha[r] + rs[r];
+      }
+#pragma unroll
+      for (int i = 0; i < D / 8; ++i) {
+        o[i][0] *= alpha[0];
+        o[i][1] *= alpha[0];
+        o[i][2] *= alpha[1];
+        o[i][3] *= alpha[1];
+      }
+      // ---- O += P V
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks) {
+        uint32_t a[4] = {pa[ks][0], pa[ks][1], pa[ks][2], pa[ks][3]};
+#pragma unroll
+        for (int dt = 0; dt < D / 8; dt += 2) {
+          // matrices (trans): keys ks*16+0..7 / +8..15 for d-tiles dt and dt+1
+          const int r = ks * 16 + (lane & 7) + (((lane >> 3) & 1) << 3);
+          const int c = dt + (lane >> 4);
+          uint32_t b0, b1, b2, b3;
+          ldmatrix_x4_trans(sV + swz<D>(r, c), b0, b1, b2, b3);
+          mma_bf16_16816(o[dt], a, b0, b1);
+          mma_bf16_16816(o[dt + 1], a, b2, b3);
+        }
+      }
+    }
+    __syncthreads();
+  }
+  cp_async_wait<0>();
+
+  // ---- epilogue: out = bf16(bf16(O / l) * sigmoid(gate))
+  float inv_l[2] = {l_r[0] > 0.f ? 1.f / l_r[0] : 0.f, l_r[1] > 0.f ? 1.f / l_r[1] : 0.f};
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const int qi = tile.q0 + row0 + g + r * 8;
+    if (qi >= n) continue;
+    const int64_t t = t0 + qi;
+    const __nv_bfloat16* gate = qkv + t * ldq + (int64_t)h * 2 * D + D;
+    __nv_bfloat16* dst = out + t * ldo + (int64_t)h * D;
+#pragma unroll
+    for (int dt = 0; dt < D / 8; ++dt) {
+      const int c = dt * 8 + cq * 2;
+      const float a0 = bf16_round(o[dt][r * 2 + 0] * inv_l[r]);
+      const float a1 = bf16_round(o[dt][r * 2 + 1] * inv_l[r]);
+      const float g0 = bf2f(gate[c]), g1 = bf2f(gate[c + 1]);
+      *reinterpret_cast<uint32_t*>(dst + c) = pack_bf16x2(a0 / (1.f + expf(-g0)), a1 / (1.f + expf(-g1)));
+    }
+  }
+}
+
+// ============================================================== decode attention (CUDA cores)
+// grid (B * nkv, splits); 4 warps; each warp takes 32 keys at a time, lane = key for the
+// scores, lane = 8-dim slice for the value accumulation.
+template <int D, int G>
+__global__ void __launch_bounds__(128) attn_decode_kernel(
+    const __nv_bfloat16* __restrict__ qkv, int64_t ldq, int nq, int nkv, const __nv_bfloat16* __restrict__ kc,
+    const __nv_bfloat16* __restrict__ vc, const int32_t* __restrict__ seq_len, const int32_t* __restrict__ kv_base,
+    int keys_per_split, float scale_log2, float* __restrict__ part_o, float* __restrict__ part_ml, int splits) {
+  constexpr int E = D / 32;
+  __shared__ float sq[G][D];
+  __shared__ float s_m[4][G], s_l[4][G];
+  __shared__ float s_o[4][G][D];
+  const int b = blockIdx.x / nkv, kvh = blockIdx.x % nkv;
+  const int split = blockIdx.y;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int L = seq_len[b];
+  const int64_t base = kv_base[b];
+  const int k_begin = split * keys_per_split;
+  const int k_end = min(L, k_begin + keys_per_split);
+  for (int i = threadIdx.x; i < G * D; i += blockDim.x) {
+    const int gi = i / D, d = i % D;
+    sq[gi][d] = bf2f(qkv[(int64_t)b * ldq + (int64_t)(kvh * G + gi) * 2 * D + d]);
+  }
+  __syncthreads();
+  float m[G], l[G], acc[G][E];
+#pragma unroll
+  for (int gi = 0; gi < G; ++gi) {
+    m[gi] = -INFINITY;
+    l[gi] = 0.f;
+#pragma unroll
+    for (int e = 0; e < E; ++e) acc[gi][e] = 0.f;
+  }
+  for (int k0 = k_begin + warp * 32; k0 < k_end; k0 += 128) {
+    const int key = k0 + lane;
+    const bool valid = key < k_end;
+    float s[G];
+#pragma unroll
+    for (int gi = 0; gi < G; ++gi) s[gi] = 0.f;
+    if (valid) {
+      const __nv_bfloat16* kr = kc + ((base + key) * nkv + kvh) * D;
+#pragma unroll 4
+      for (int c = 0; c < D; c += 8) {
+        float kf[8];
+        load_bf16x8(kr + c, kf);
+#pragma unroll
+        for (int gi = 0; gi < G; ++gi) {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) s[gi] += sq[gi][c + e] * kf[e];
+        }
+      }
+    }
+    float pw[G];
+#pragma unroll
+    for (int gi = 0; gi < G; ++gi) {
+      const float v = valid ? s[gi] * scale_log2 : -INFINITY;
+      const float mx = fmaxf(m[gi], warp_max(v));
+      const float alpha = (mx == -INFINITY) ? 1.f : exp2f(m[gi] - mx);
+      pw[gi] = valid ? exp2f(v - mx) : 0.f;
+      l[gi] = l[gi] * alpha + warp_sum(pw[gi]);
+      m[gi] = mx;
+#pragma unroll
+      for (int e = 0; e < E; ++e) acc[gi][e] *= alpha;
+    }
+    const int nk = min(32, k_end - k0);
+    for (int jj = 0; jj < nk; ++jj) {
+      const __nv_bfloat16* vr = vc + ((base + k0 + jj) * nkv + kvh) * D + lane * E;
+      float vf[E];
+#pragma unroll
+      for (int e = 0; e < E; ++e) vf[e] = bf2f(vr[e]);
+#pragma unroll
+      for (int gi = 0; gi < G; ++gi) {
+        const float pj = __shfl_sync(0xffffffffu, pw[gi], jj);
+#pragma unroll
+        for (int e = 0; e < E; ++e) acc[gi][e] += pj * vf[e];
+      }
+    }
+  }
+  // combine the 4 warps
+  if (lane == 0) {
+#pragma unroll
+    for (int gi = 0; gi < G; ++gi) {
+      s_m[warp][gi] = m[gi];
+      s_l[warp][gi] = l[gi];
+    }
+  }
+#pragma unroll
+  for (int gi = 0; gi < G; ++gi)
+#pragma unroll
+    for (int e = 0; e < E; ++e) s_o[warp][gi][lane * E + e] = acc[gi][e];
+  __syncthreads();
+  for (int i = threadIdx.x; i < G * D; i += blockDim.x) {
+    const int gi = i / D, d = i % D;
+    float mm = -INFINITY;
+    for (int w = 0; w < 4; ++w) mm = fmaxf(mm, s_m[w][gi]);
+    float ll = 0.f, oo = 0.f;
+    for (int w = 0; w < 4; ++w) {
+      const float f = (s_m[w][gi] == -INFINITY) ? 0.f : exp2f(s_m[w][gi] - mm);
+      ll += s_l[w][gi] * f;
+      oo += s_o[w][gi][d] * f;
+    }
+    const int h = kvh * G + gi;
+    const int64_t slot = ((int64_t)b * nq + h) * splits + split;
+    part_o[slot * D + d] = oo;
+    if (d == 0) {
+      part_ml[slot * 2 + 0] = mm;
+      part_ml[slot * 2 + 1] = ll;
+    }
+  }
+}
+
+template <int D>
+__global__ void attn_decode_combine_kernel(const float* __restrict__ part_o, const float* __restrict__ part_ml,
+                                           int splits, const __nv_bfloat16* __restrict__ qkv, int64_t ldq, int nq,
+                                           __nv_bfloat16* __restrict__ out, int64_t ldo) {
+  const int bh = blockIdx.x;  // b * nq + h
+  const int b = bh / nq, h = bh % nq;
+  float mm = -INFINITY;
+  for (int s = 0; s < splits; ++s) mm = fmaxf(mm, part_ml[((int64_t)bh * splits + s) * 2]);
+  for (int d = threadIdx.x; d < D; d += blockDim.x) {
+    float ll = 0.f, oo = 0.f;
+    for (int s = 0; s < splits; ++s) {
+      const int64_t slot = (int64_t)bh * splits + s;
+      const float ms = part_ml[slot * 2];
+      const float f = (ms == -INFINITY) ? 0.f : exp2f(ms - mm);
+      ll += part_ml[slot * 2 + 1] * f;
+      oo += part_o[slot * D + d] * f;
+    }
+    const float a = bf16_round(ll > 0.f ? oo / ll : 0.f);
+    const float gt = bf2f(qkv[(int64_t)b * ldq + (int64_t)h * 2 * D + D + d]);
+    out[(int64_t)b * ldo + (int64_t)h * D + d] = f2bf(a / (1.f + expf(-gt)));
+  }
+}
+
+}  // namespace qw
+
+using namespace qw;
+
+extern "C" int qw_qk_norm_rope_store(void* qkv, int64_t ldq, int64_t T, int64_t nq, int64_t nkv, int64_t d,
+                                     const void* q_w, const void* k_w, const float* rope, int64_t rotary_dim,
+                                     int64_t rope_rows, const int32_t* positions, const int32_t* locations,
+                                     void* k_cache, void* v_cache, int64_t cache_rows, float eps,
+                                     qw_stream_t stream) {
+  QW_CHECK_ARG(qkv && q_w && k_w && rope && positions && locations && k_cache && v_cache && T > 0, QW_ERR_ARG);
+  QW_CHECK_ARG(nq > 0 && nkv > 0 && nq % nkv == 0 && rotary_dim > 0 && rotary_dim <= d && rotary_dim % 2 == 0,
+               QW_ERR_ARG);
+  auto* s = reinterpret_cast<cudaStream_t>(stream);
+  const int64_t warps = T * (nq + nkv);
+  const unsigned blocks = (unsigned)((warps + 7) / 8);
+  auto* q = static_cast<__nv_bfloat16*>(qkv);
+  const auto* qw_ = static_cast<const __nv_bfloat16*>(q_w);
+  const auto* kw_ = static_cast<const __nv_bfloat16*>(k_w);
+  auto* kc = static_cast<__nv_bfloat16*>(k_cache);
+  auto* vc = static_cast<__nv_bfloat16*>(v_cache);
+  int* err = device_error_ptr();
+#define QW_ROPE_LAUNCH(DD)                                                                                          \
+  do {                                                                                                              \
+    QW_CHECK_ARG(((rotary_dim / 2) % (DD / 32)) == 0, QW_ERR_UNSUPPORTED);                                          \
+    qk_norm_rope_store_kernel<DD><<<blocks, 256, 0, s>>>(q, ldq, (int)nq, (int)nkv, qw_, kw_, rope, (int)rotary_dim, \
+                                                         rope_rows, positions, locations, kc, vc, cache_rows,       \
+                                                         (int)T, eps, err);                                         \
+  } while (0)
+  if (d == 256) QW_ROPE_LAUNCH(256);
+  else if (d == 128) QW_ROPE_LAUNCH(128);
+  else if (d == 64) QW_ROPE_LAUNCH(64);
+  else return QW_ERR_UNSUPPORTED;
+#undef QW_ROPE_LAUNCH
+  QW_LAUNCH_CHECK();
+  return QW_OK;
+}
+
+extern "C" int qw_attn_prefill(const void* qkv, int64_t ldq, int64_t nq, int64_t nkv, int64_t d, const void* k_cache,
+                               const void* v_cache, const void* tiles, int64_t n_tiles, const int32_t* cu_seqlens,
+                               const int32_t* prefix, const int32_t* kv_base, void* out, int64_t ldo, float scale,
+                               qw_stream_t stream) {
+  QW_CHECK_ARG(qkv && k_cache && v_cache && tiles && cu_seqlens && prefix && kv_base && out, QW_ERR_ARG);
+  QW_CHECK_ARG(n_tiles > 0 && nq > 0 && nkv > 0 && nq % nkv == 0, QW_ERR_ARG);
+  QW_CHECK_ARG(((uintptr_t)qkv % 16) == 0 && (ldq % 8) == 0, QW_ERR_ALIGN);
+  auto* s = reinterpret_cast<cudaStream_t>(stream);
+  const float sl2 = scale * 1.4426950408889634f;
+  dim3 grid((unsigned)n_tiles, (unsigned)nq);
+#define QW_ATTN_LAUNCH(DD)                                                                                          \
+  do {                                                                                                              \
+    constexpr int smem = AttnSmem<DD, 128, 64>::TOTAL;                                                              \
+    static bool cfg = false;                                                                                        \
+    if (!cfg) {                                                                                                     \
+      cudaFuncSetAttribute(attn_prefill_kernel<DD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);             \
+      cfg = true;                                                                                                   \
+    }                                                                                                               \
+    attn_prefill_kernel<DD><<<grid, 256, smem, s>>>(                                                                \
+        static_cast<const __nv_bfloat16*>(qkv), ldq, (int)nq, (int)nkv, static_cast<const __nv_bfloat16*>(k_cache), \
+        static_cast<const __nv_bfloat16*>(v_cache), static_cast<const PrefillTile*>(tiles), cu_seqlens, prefix,     \
+        kv_base, static_cast<__nv_bfloat16*>(out), ldo, sl2);                                                       \
+  } while (0)
+  if (d == 256) QW_ATTN_LAUNCH(256);
+  else if (d == 128) QW_ATTN_LAUNCH(128);
+  else if (d == 64) QW_ATTN_LAUNCH(64);
+  else return QW_ERR_UNSUPPORTED;
+#undef QW_ATTN_LAUNCH
+  QW_LAUNCH_CHECK();
+  return QW_OK;
+}
+
+extern "C" size_t qw_attn_decode_workspace_bytes(int64_t B, int64_t nq, int64_t d, int64_t splits) {
+  return (size_t)(B * nq * splits) * (size_t)(d + 2) * sizeof(float) + 256;
+}
+
+extern "C" int qw_attn_decode(const void* qkv, int64_t ldq, int64_t B, int64_t nq, int64_t nkv, int64_t d,
+                              const void* k_cache, const void* v_cache, const int32_t* seq_len,
+                              const int32_t* kv_base, int64_t max_len, int64_t splits, void* out, int64_t ldo,
+                              float scale, void* workspace, size_t ws_bytes, qw_stream_t stream) {
+  QW_CHECK_ARG(qkv && k_cache && v_cache && seq_len && kv_base && out && B > 0 && max_len > 0, QW_ERR_ARG);
+  QW_CHECK_ARG(nq > 0 && nkv > 0 && nq % nkv == 0 && splits >= 1, QW_ERR_ARG);
+  QW_CHECK_ARG(workspace && ws_bytes >= qw_attn_decode_workspace_bytes(B, nq, d, splits), QW_ERR_WORKSPACE);
+  auto* s = reinterpret_cast<cudaStream_t>(stream);
+  const int group = (int)(nq / nkv);
+  const int kps = (int)(((max_len + splits - 1) / splits + 31) / 32 * 32);
+  float* part_o = static_cast<float*>(workspace);
+  float* part_ml = part_o + B * nq * splits * d;
+  const float sl2 = scale * 1.4426950408889634f;
+  dim3 grid((unsigned)(B * nkv), (unsigned)splits);
+  const auto* q = static_cast<const __nv_bfloat16*>(qkv);
+  const auto* kc = static_cast<const __nv_bfloat16*>(k_cache);
+  const auto* vc = static_cast<const __nv_bfloat16*>(v_cache);
+  if (d == 256 && group == 6)
+    attn_decode_kernel<256, 6><<<grid, 128, 0, s>>>(q, ldq, (int)nq, (int)nkv, kc, vc, seq_len, kv_base, kps, sl2,
+                                                    part_o, part_ml, (int)splits);
+  else if (d == 64 && group == 2)
+    attn_decode_kernel<64, 2><<<grid, 128, 0, s>>>(q, ldq, (int)nq, (int)nkv, kc, vc, seq_len, kv_base, kps, sl2,
+                                                   part_o, part_ml, (int)splits);
+  else
+    return QW_ERR_UNSUPPORTED;
+  QW_LAUNCH_CHECK();
+  if (d == 256)
+    attn_decode_combine_kernel<256><<<(unsigned)(B * nq), 128, 0, s>>>(part_o, part_ml, (int)splits, q, ldq, (int)nq,
+                                                                       static_cast<__nv_bfloat16*>(out), ldo);
+  else
+    attn_decode_combine_kernel<64><<<(unsigned)(B * nq), 64, 0, s>>>(part_o, part_ml, (int)splits, q, ldq, (int)nq,
+                                                                     static_cast<__nv_bfloat16*>(out), ldo);
+  QW_LAUNCH_CHECK();
+  return QW_OK;
+}

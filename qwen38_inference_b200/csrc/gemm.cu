@@ -1,0 +1,515 @@
+// Dense bf16 projections on the 5th-generation tensor cores (tcgen05 + TMEM + TMA).
+//
+// Replaces the reference's cuBLAS F.linear calls (reference/qwen38_inference.py:5054,
+// 5067, 5069, 5070, 5087, 5089, 5092, 5096) and fuses the SwiGLU of REF:5091.
+//
+// One persistent, warp-specialized kernel computes D[a_rows, b_rows] = A[a_rows,K] . B[b_rows,K]^T:
+//   warp 0      TMA producer: 128 x 64 A tile and BN x 64 B tile per stage (SWIZZLE_128B)
+//   warp 1      TMEM allocator + single-thread tcgen05.mma issuer (M=128, N=BN, K=16)
+//   warps 2..5  epilogue: tcgen05.ld of the fp32 accumulator, rounding, stores
+// The accumulator is double-buffered in TMEM so the epilogue of one tile overlaps the
+// main loop of the next. Work units are (a_tile, b_tile, k_split) in a grouped raster.
+//
+// Prefill (M >= 65): A = activations, B = weights, BN = 256 (128 for SwiGLU halves).
+// Decode  (M <= 64): A = weights (weight-streaming), B = the few activation rows,
+//                    BN = M rounded up to 16, split over K to fill all SMs; fp32 partials
+//                    are summed by a small deterministic reduction kernel.
+// No TMA multicast is used (the same code runs in multi-GPU jobs).
+#include <mutex>
+
+#include "common.cuh"
+
+namespace qw {
+
+__device__ int g_device_error_word = 0;
+
+int* device_error_ptr() {
+  static int* ptrs[64] = {nullptr};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return nullptr;
+  if (!ptrs[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_device_error_word) == cudaSuccess) ptrs[dev] = static_cast<int*>(p);
+  }
+  return ptrs[dev];
+}
+
+enum Epi : int { EPI_BF16 = 0, EPI_F32 = 1, EPI_SWIGLU = 2, EPI_PARTIAL = 3 };
+
+struct GemmParams {
+  int a_rows, b_rows, K;
+  int a_tiles, b_tiles, k_splits, kb_per_split, kb_total;
+  int group;           // grouped raster width over a_tiles
+  int swap;            // 0: out[a_row][b_row]; 1: out[b_row][a_row]
+  int b_up_offset;     // SwiGLU: row offset of the "up" half inside B
+  void* out;
+  int64_t ldo;         // output row stride, elements
+  int64_t part_stride; // EPI_PARTIAL: elements between split slices
+  int* err;            // device error word
+  int vec_ok;          // output rows 16-byte aligned: vector stores allowed
+};
+
+constexpr int BM = 128;
+constexpr int BK = 64;  // 64 bf16 = 128 bytes = one SWIZZLE_128B row
+constexpr int kThreads = 192;
+
+template <int BN, int STAGES>
+struct GemmSmem {
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int BAR_OFFSET = STAGES * STAGE_BYTES;
+  static constexpr int TOTAL = BAR_OFFSET + 256 + 1024;  // barriers + alignment slack
+};
+
+QW_DEV void decode_unit(const GemmParams& p, int unit, int& at, int& bt, int& split) {
+  split = unit % p.k_splits;
+  int tile = unit / p.k_splits;
+  int per_group = p.group * p.b_tiles;
+  int g = tile / per_group;
+  int first = g * p.group;
+  int gsz = min(p.a_tiles - first, p.group);
+  int r = tile - g * per_group;
+  at = first + r % gsz;
+  bt = r / gsz;
+}
+
+template <int BN, int STAGES, int EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                        const GemmParams p) {
+  using L = GemmSmem<BN, STAGES>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::BAR_OFFSET);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;  // [2]
+  uint64_t* tempty = tfull + 2;      // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  const int units = p.a_tiles * p.b_tiles * p.k_splits;
+  constexpr uint32_t TMEM_COLS = (2 * BN <= 32) ? 32 : (2 * BN <= 64) ? 64 : (2 * BN <= 128) ? 128 : (2 * BN <= 256) ? 256 : 512;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 4);  // one arrive per epilogue warp
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- TMA producer
+    if (elect_one()) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+        int at, bt, split;
+        decode_unit(p, u, at, bt, split);
+        const int kb0 = split * p.kb_per_split;
+        const int kb1 = min(p.kb_total, kb0 + p.kb_per_split);
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, p.err, QW_DEV_ERR_TIMEOUT_GEMM)) { ok = false; break; }
+          uint8_t* sa = smem + stage * L::STAGE_BYTES;
+          uint8_t* sb = sa + L::A_BYTES;
+          mbar_arrive_expect_tx(&full[stage], L::STAGE_BYTES);
+          tma_load_2d(sa, &tmA, &full[stage], kb * BK, at * BM);
+          if constexpr (EPI == EPI_SWIGLU) {
+            tma_load_2d(sb, &tmB, &full[stage], kb * BK, bt * (BN / 2));
+            tma_load_2d(sb + (BN / 2) * BK * 2, &tmB, &full[stage], kb * BK, p.b_up_offset + bt * (BN / 2));
+          } else {
+            tma_load_2d(sb, &tmB, &full[stage], kb * BK, bt * BN);
+          }
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer
+    constexpr uint32_t IDESC = umma_idesc_bf16(BM, BN);
+    int stage = 0;
+    uint32_t phase = 0;
+    int tcount = 0;
+    bool ok = true;
+    for (int u = blockIdx.x; u < units && ok; u += gridDim.x, ++tcount) {
+      int at, bt, split;
+      decode_unit(p, u, at, bt, split);
+      const int kb0 = split * p.kb_per_split;
+      const int kb1 = min(p.kb_total, kb0 + p.kb_per_split);
+      const int buf = tcount & 1;
+      const uint32_t tphase = ((tcount >> 1) & 1) ^ 1;
+      if (!mbar_wait(&tempty[buf], tphase, abort_flag, p.err, QW_DEV_ERR_TIMEOUT_GEMM)) { ok = false; break; }
+      tc_fence_after();
+      const uint32_t d_tmem = tmem_base + buf * BN;
+      for (int kb = kb0; kb < kb1; ++kb) {
+        if (!mbar_wait(&full[stage], phase, abort_flag, p.err, QW_DEV_ERR_TIMEOUT_GEMM)) { ok = false; break; }
+        tc_fence_after();
+        if (elect_one()) {
+          const uint32_t sa = smem_u32(smem + stage * L::STAGE_BYTES);
+          const uint32_t sb = sa + L::A_BYTES;
+          const uint64_t da = umma_sdesc_sw128(sa);
+          const uint64_t db = umma_sdesc_sw128(sb);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            // advance the start address by 16 bf16 = 32 bytes inside the 128-byte swizzled row
+            umma_bf16(d_tmem, da + (uint64_t)(2 * k), db + (uint64_t)(2 * k), IDESC, (kb > kb0 || k > 0) ? 1u : 0u);
+          }
+          umma_commit(&empty[stage]);
+        }
+        __syncwarp();
+        if (++stage == STAGES) { stage = 0; phase ^= 1; }
+      }
+      if (!ok) break;
+      if (elect_one()) umma_commit(&tfull[buf]);
+      __syncwarp();
+    }
+  } else {
+    // ---------------------------------------------------------------- epilogue (warps 2..5)
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int row_in_tile = q * 32 + lane;
+    int tcount = 0;
+    for (int u = blockIdx.x; u < units; u += gridDim.x, ++tcount) {
+      int at, bt, split;
+      decode_unit(p, u, at, bt, split);
+      const int buf = tcount & 1;
+      if (!mbar_wait(&tfull[buf], (tcount >> 1) & 1, abort_flag, p.err, QW_DEV_ERR_TIMEOUT_GEMM)) break;
+      tc_fence_after();
+      const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + buf * BN;
+      const int a_row = at * BM + row_in_tile;
+      const bool a_ok = a_row < p.a_rows;
+      if constexpr (EPI == EPI_SWIGLU) {
+        // columns [0, BN/2) = gate, [BN/2, BN) = up of output columns bt*BN/2 ...
+        __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.out);
+#pragma unroll 1
+        for (int c = 0; c < BN / 2; c += 32) {
+          uint32_t g[32], v[32];
+          tmem_ld_32x32b_x32(t_row + c, g);
+          tmem_ld_32x32b_x32(t_row + BN / 2 + c, v);
+          tmem_ld_wait();
+          const int col0 = bt * (BN / 2) + c;
+          if (a_ok) {
+            float f[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const float gg = bf16_round(__uint_as_float(g[j]));
+              const float uu = bf16_round(__uint_as_float(v[j]));
+              f[j] = gg / (1.0f + expf(-gg)) * uu;
+            }
+            const int ncols = p.b_rows - col0;  // b_rows = I (output columns)
+            __nv_bfloat16* dst = out + (int64_t)a_row * p.ldo + col0;
+            if (ncols >= 32 && p.vec_ok) {
+#pragma unroll
+              for (int j = 0; j < 32; j += 8) store_bf16x8(dst + j, f + j);
+            } else {
+              for (int j = 0; j < ncols; ++j) dst[j] = f2bf(f[j]);
+            }
+          }
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+          uint32_t r[32];
+          if constexpr (BN >= 32) {
+            tmem_ld_32x32b_x32(t_row + c, r);
+          } else {
+            tmem_ld_32x32b_x16(t_row + c, r);
+          }
+          tmem_ld_wait();
+          if (!a_ok) continue;
+          const int b0 = bt * BN + c;
+          const int nb = min(32, p.b_rows - b0);
+          if (nb <= 0) continue;
+          if (!p.swap) {
+            if constexpr (EPI == EPI_BF16) {
+              __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.out) + (int64_t)a_row * p.ldo + b0;
+              float f[32];
+#pragma unroll
+              for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(r[j]);
+              if (nb == 32 && p.vec_ok) {
+#pragma unroll
+                for (int j = 0; j < 32; j += 8) store_bf16x8(dst + j, f + j);
+              } else {
+                for (int j = 0; j < nb; ++j) dst[j] = f2bf(f[j]);
+              }
+            } else if constexpr (EPI == EPI_F32) {
+              float* dst = reinterpret_cast<float*>(p.out) + (int64_t)a_row * p.ldo + b0;
+              if (nb == 32 && p.vec_ok) {
+#pragma unroll
+                for (int j = 0; j < 32; j += 4) {
+                  float4 v4 = make_float4(bf16_round(__uint_as_float(r[j])), bf16_round(__uint_as_float(r[j + 1])),
+                                          bf16_round(__uint_as_float(r[j + 2])), bf16_round(__uint_as_float(r[j + 3])));
+                  *reinterpret_cast<float4*>(dst + j) = v4;
+                }
+              } else {
+                for (int j = 0; j < nb; ++j) dst[j] = bf16_round(__uint_as_float(r[j]));
+              }
+            }
+          } else {
+            // swap: out[b_row][a_row]; lanes of a warp write 32 consecutive a_rows
+            if constexpr (EPI == EPI_BF16) {
+              __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.out) + a_row;
+              for (int j = 0; j < nb; ++j) dst[(int64_t)(b0 + j) * p.ldo] = f2bf(__uint_as_float(r[j]));
+            } else if constexpr (EPI == EPI_F32) {
+              float* dst = reinterpret_cast<float*>(p.out) + a_row;
+              for (int j = 0; j < nb; ++j) dst[(int64_t)(b0 + j) * p.ldo] = bf16_round(__uint_as_float(r[j]));
+            } else if constexpr (EPI == EPI_PARTIAL) {
+              float* dst = reinterpret_cast<float*>(p.out) + (int64_t)split * p.part_stride + a_row;
+              for (int j = 0; j < nb; ++j) dst[(int64_t)(b0 + j) * p.ldo] = __uint_as_float(r[j]);
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[buf]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+// Sum of split-K partials ws[s][m][n] (s = 0..splits-1 in order), then the output rounding.
+template <int EPI>
+__global__ void splitk_reduce_kernel(const float* __restrict__ ws, void* out, int M, int N_out, int64_t ldo,
+                                     int splits, int64_t part_stride, int64_t ldw, int up_offset) {
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (int64_t)M * N_out) return;
+  const int m = (int)(idx / N_out);
+  const int n = (int)(idx % N_out);
+  float acc = 0.f;
+  for (int s = 0; s < splits; ++s) acc += ws[s * part_stride + (int64_t)m * ldw + n];
+  if constexpr (EPI == EPI_SWIGLU) {
+    float up = 0.f;
+    for (int s = 0; s < splits; ++s) up += ws[s * part_stride + (int64_t)m * ldw + up_offset + n];
+    const float g = bf16_round(acc), u = bf16_round(up);
+    reinterpret_cast<__nv_bfloat16*>(out)[(int64_t)m * ldo + n] = f2bf(g / (1.0f + expf(-g)) * u);
+  } else if constexpr (EPI == EPI_F32) {
+    reinterpret_cast<float*>(out)[(int64_t)m * ldo + n] = bf16_round(acc);
+  } else {
+    reinterpret_cast<__nv_bfloat16*>(out)[(int64_t)m * ldo + n] = f2bf(acc);
+  }
+}
+
+// ------------------------------------------------------------------ host side
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn get_encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// 2-D bf16 K-major operand [rows, K] with leading dimension ld (elements), box [box_rows, 64].
+static int make_tmap(CUtensorMap* m, const void* ptr, int64_t rows, int64_t K, int64_t ld, int box_rows) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) return QW_ERR_DRIVER;
+  cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
+  cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
+  cuuint32_t es[2] = {1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, es,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? QW_OK : QW_ERR_DRIVER;
+}
+
+static int num_sms() {
+  static int n = 0;
+  if (n == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = 148;
+  }
+  return n;
+}
+
+template <int BN, int STAGES, int EPI>
+static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, cudaStream_t s) {
+  auto kern = gemm_tcgen05_kernel<BN, STAGES, EPI>;
+  const int smem = GemmSmem<BN, STAGES>::TOTAL;
+  static bool configured = false;  // one flag per instantiation
+  if (!configured) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    configured = true;
+  }
+  const int units = p.a_tiles * p.b_tiles * p.k_splits;
+  const int grid = units < num_sms() ? units : num_sms();
+  kern<<<grid, kThreads, smem, s>>>(ta, tb, p);
+  QW_LAUNCH_CHECK();
+  return QW_OK;
+}
+
+struct SkinnyPlan {
+  int bn, b_tiles, a_tiles, splits, kb_per_split, kb_total;
+};
+
+static SkinnyPlan plan_skinny(int64_t M, int64_t N, int64_t K) {
+  SkinnyPlan pl;
+  pl.bn = M <= 16 ? 16 : M <= 32 ? 32 : 64;
+  pl.b_tiles = 1;
+  pl.a_tiles = (int)((N + BM - 1) / BM);
+  pl.kb_total = (int)((K + BK - 1) / BK);
+  const int target = 2 * num_sms();
+  int splits = (target + pl.a_tiles - 1) / pl.a_tiles;
+  const int max_splits = pl.kb_total / 4 > 0 ? pl.kb_total / 4 : 1;  // keep >= 4 k-blocks per split
+  if (splits > max_splits) splits = max_splits;
+  if (splits < 1) splits = 1;
+  pl.kb_per_split = (pl.kb_total + splits - 1) / splits;
+  pl.splits = (pl.kb_total + pl.kb_per_split - 1) / pl.kb_per_split;
+  return pl;
+}
+
+static bool use_skinny(int64_t M) { return M <= 64; }
+
+}  // namespace qw
+
+using namespace qw;
+
+extern "C" size_t qw_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K, int out_kind) {
+  if (!use_skinny(M)) return 0;
+  SkinnyPlan pl = plan_skinny(M, N, K);
+  if (pl.splits == 1 && out_kind != QW_OUT_SWIGLU) return 0;
+  return (size_t)pl.splits * (size_t)M * (size_t)N * sizeof(float);
+}
+
+extern "C" int qw_gemm_bf16(const void* x, const void* w, void* y, int64_t M, int64_t N, int64_t K, int64_t ldx,
+                            int64_t ldw, int64_t ldy, int out_kind, void* workspace, size_t ws_bytes,
+                            qw_stream_t stream) {
+  QW_CHECK_ARG(x && w && y && M > 0 && N > 0 && K > 0, QW_ERR_ARG);
+  QW_CHECK_ARG(ldx >= K && ldw >= K, QW_ERR_ARG);
+  QW_CHECK_ARG(out_kind >= QW_OUT_BF16 && out_kind <= QW_OUT_SWIGLU, QW_ERR_ARG);
+  QW_CHECK_ARG(M < (1 << 30) && N < (1 << 30), QW_ERR_ARG);
+  QW_CHECK_ARG(((uintptr_t)x % 16) == 0 && ((uintptr_t)w % 16) == 0 && (ldx % 8) == 0 && (ldw % 8) == 0, QW_ERR_ALIGN);
+  const int64_t n_out = out_kind == QW_OUT_SWIGLU ? N / 2 : N;
+  QW_CHECK_ARG(out_kind != QW_OUT_SWIGLU || (N % 2 == 0), QW_ERR_ARG);
+  QW_CHECK_ARG(ldy >= n_out, QW_ERR_ARG);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  CUtensorMap ta, tb;
+  int rc;
+  GemmParams p{};
+  p.err = device_error_ptr();
+  p.K = (int)K;
+  p.kb_total = (int)((K + BK - 1) / BK);
+  p.group = 16;
+
+  if (!use_skinny(M)) {
+    // A = activations [M, K], B = weights [N, K]; out[m][n]
+    const bool swiglu = out_kind == QW_OUT_SWIGLU;
+    const int per16 = out_kind == QW_OUT_F32_OF_BF16 ? 4 : 8;  // elements per 16 bytes
+    p.vec_ok = ((uintptr_t)y % 16) == 0 && (ldy % per16) == 0;
+    constexpr int BN = 256;
+    if ((rc = make_tmap(&ta, x, M, K, ldx, BM)) != QW_OK) return rc;
+    if ((rc = make_tmap(&tb, w, N, K, ldw, swiglu ? BN / 2 : BN)) != QW_OK) return rc;
+    p.a_rows = (int)M;
+    p.b_rows = (int)n_out;
+    p.a_tiles = (int)((M + BM - 1) / BM);
+    p.b_tiles = swiglu ? (int)((n_out + BN / 2 - 1) / (BN / 2)) : (int)((N + BN - 1) / BN);
+    p.k_splits = 1;
+    p.kb_per_split = p.kb_total;
+    p.swap = 0;
+    p.b_up_offset = (int)n_out;
+    p.out = y;
+    p.ldo = ldy;
+    if (swiglu) return launch_gemm<BN, 4, EPI_SWIGLU>(ta, tb, p, s);
+    if (out_kind == QW_OUT_F32_OF_BF16) return launch_gemm<BN, 4, EPI_F32>(ta, tb, p, s);
+    return launch_gemm<BN, 4, EPI_BF16>(ta, tb, p, s);
+  }
+
+  // Skinny: A = weights [N, K] (streamed once), B = activations [M, K]
+  SkinnyPlan pl = plan_skinny(M, N, K);
+  if ((rc = make_tmap(&ta, w, N, K, ldw, BM)) != QW_OK) return rc;
+  if ((rc = make_tmap(&tb, x, M, K, ldx, pl.bn)) != QW_OK) return rc;
+  p.a_rows = (int)N;
+  p.b_rows = (int)M;
+  p.a_tiles = pl.a_tiles;
+  p.b_tiles = 1;
+  p.k_splits = pl.splits;
+  p.kb_per_split = pl.kb_per_split;
+  p.swap = 1;
+  p.group = 1;
+  const bool partial = pl.splits > 1 || out_kind == QW_OUT_SWIGLU;
+  if (!partial) {
+    p.out = y;
+    p.ldo = ldy;
+    const bool f32 = out_kind == QW_OUT_F32_OF_BF16;
+    switch (pl.bn) {
+      case 16: return f32 ? launch_gemm<16, 8, EPI_F32>(ta, tb, p, s) : launch_gemm<16, 8, EPI_BF16>(ta, tb, p, s);
+      case 32: return f32 ? launch_gemm<32, 8, EPI_F32>(ta, tb, p, s) : launch_gemm<32, 8, EPI_BF16>(ta, tb, p, s);
+      default: return f32 ? launch_gemm<64, 8, EPI_F32>(ta, tb, p, s) : launch_gemm<64, 8, EPI_BF16>(ta, tb, p, s);
+    }
+  }
+  const size_t need = (size_t)pl.splits * (size_t)M * (size_t)N * sizeof(float);
+  QW_CHECK_ARG(workspace != nullptr && ws_bytes >= need, QW_ERR_WORKSPACE);
+  QW_CHECK_ARG(((uintptr_t)workspace % 16) == 0, QW_ERR_ALIGN);
+  p.out = workspace;
+  p.ldo = N;  // partial rows are [M][N] per split
+  p.part_stride = (int64_t)M * N;
+  switch (pl.bn) {
+    case 16: rc = launch_gemm<16, 8, EPI_PARTIAL>(ta, tb, p, s); break;
+    case 32: rc = launch_gemm<32, 8, EPI_PARTIAL>(ta, tb, p, s); break;
+    default: rc = launch_gemm<64, 8, EPI_PARTIAL>(ta, tb, p, s); break;
+  }
+  if (rc != QW_OK) return rc;
+  const int64_t total = M * n_out;
+  const int threads = 256;
+  const int blocks = (int)((total + threads - 1) / threads);
+  const float* ws = reinterpret_cast<const float*>(workspace);
+  if (out_kind == QW_OUT_SWIGLU)
+    splitk_reduce_kernel<EPI_SWIGLU><<<blocks, threads, 0, s>>>(ws, y, (int)M, (int)n_out, ldy, pl.splits, p.part_stride, N, (int)n_out);
+  else if (out_kind == QW_OUT_F32_OF_BF16)
+    splitk_reduce_kernel<EPI_F32><<<blocks, threads, 0, s>>>(ws, y, (int)M, (int)n_out, ldy, pl.splits, p.part_stride, N, 0);
+  else
+    splitk_reduce_kernel<EPI_BF16><<<blocks, threads, 0, s>>>(ws, y, (int)M, (int)n_out, ldy, pl.splits, p.part_stride, N, 0);
+  QW_LAUNCH_CHECK();
+  return QW_OK;
+}
+
+extern "C" int qw_version(void) { return 1; }
+
+extern "C" int qw_take_device_error(int* code) {
+  if (!code) return QW_ERR_ARG;
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return QW_ERR_CUDA_BASE + (int)e;
+  int v = 0, zero = 0;
+  e = cudaMemcpyFromSymbol(&v, qw::g_device_error_word, sizeof(int));
+  if (e != cudaSuccess) return QW_ERR_CUDA_BASE + (int)e;
+  e = cudaMemcpyToSymbol(qw::g_device_error_word, &zero, sizeof(int));
+  if (e != cudaSuccess) return QW_ERR_CUDA_BASE + (int)e;
+  *code = v;
+  return QW_OK;
+}

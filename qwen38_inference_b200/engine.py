@@ -1,0 +1,158 @@
+"""The layer loop of ``forward_step`` on the sm_100a kernels (REF:5045-5099).
+
+Prefill (any call that is not pure decode, REF:5027) runs per layer:
+  norm -> [attention: qkv GEMM, q/k norm + RoPE + KV store, varlen attention (gated), o GEMM]
+       or [GDN: qkvz GEMM, ba GEMM, conv + split + L2 norm, chunked delta rule (gating
+           fused, state in place), gated RMSNorm, out GEMM]
+  -> add-norm -> gate_up GEMM with fused SwiGLU -> down GEMM
+then the final add-norm on the selected rows and the lm_head GEMM writing fp32 logits.
+Decode replaces the GDN middle by one fused kernel and attention by split-KV decode, and
+is replayed from a CUDA graph per (batch, cache) once captured.
+
+All per-call indices travel in one int32 upload (``build_metadata``).
+"""
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+from . import ops
+from .model import _Staging, build_metadata
+
+BF16 = torch.bfloat16
+
+
+class Engine:
+    def __init__(self, model):
+        self.m = model
+        self.c = model.cfg
+        self.dev = model.device
+        self.ws = ops.Workspace(self.dev, 1 << 20)
+        self.staging = _Staging()
+        self.graphs = {}
+        self.use_graphs = True
+
+    # ------------------------------------------------------------------ helpers
+    def _decode_splits(self, capacity):
+        return int(min(64, max(1, (capacity + 255) // 256)))
+
+    def _meta_views(self, dev, offs):
+        return {k: dev[o:o + n] for k, (o, n) in offs.items()}
+
+    # ------------------------------------------------------------------ entry
+    def forward(self, flat, slots, prefixes, lens, cache, is_decode, return_all_logits):
+        packed, offs, T = build_metadata(slots, prefixes, lens, cache.capacity)
+        tokens = np.asarray(flat, dtype=np.int32)
+        arr = np.concatenate([tokens, packed])
+        self.last_h2d_bytes = int(arr.nbytes)
+        if is_decode and not return_all_logits and self.use_graphs:
+            return self._decode_graph(arr, offs, T, slots, cache)
+        dev = self.staging.upload(arr, self.dev)
+        md = self._meta_views(dev[T:], offs)
+        md["tokens"] = dev[:T]
+        return self._run(md, T, len(slots), max(lens), cache, is_decode, return_all_logits)
+
+    # ------------------------------------------------------------------ decode graphs
+    def _decode_graph(self, arr, offs, T, slots, cache):
+        """Decode through a CUDA graph keyed by (batch, cache buffers).
+
+        The first decode of a key runs eagerly. The second runs eagerly too and then
+        captures the same launch sequence (capture records, it does not execute, and its
+        host cost overlaps the eager step on the GPU). Later calls copy the new indices into
+        the graph's input buffer and replay. A cache that is decoded once (a benchmark
+        repetition) therefore never pays for a capture.
+        """
+        B = len(slots)
+        key = (B, cache.capacity, len(cache.lengths), tuple(k.data_ptr() for k, _ in cache.kv.values()),
+               tuple(x.data_ptr() for x in cache.recurrent.values()), tuple(x.data_ptr() for x in cache.conv.values()))
+        ent = self.graphs.get(key)
+        if ent is None or ent.get("graph") is None:
+            if ent is None:
+                for k in [k for k in self.graphs if k[0] == B]:  # built on a grown or freed cache
+                    del self.graphs[k]
+            dev_in = torch.empty(arr.size, dtype=torch.int32, device=self.dev)
+            dev_in.copy_(torch.from_numpy(arr), non_blocking=True)
+            md = self._meta_views(dev_in[T:], offs)
+            md["tokens"] = dev_in[:T]
+            out = self._run(md, T, B, 1, cache, True, False)
+            if ent is None:
+                self.graphs[key] = {"graph": None}
+                return out
+            g = torch.cuda.CUDAGraph()
+            n0 = ops.LAUNCHES[0]
+            with torch.cuda.graph(g):
+                g_out = self._run(md, T, B, 1, cache, True, False)
+            n_launch = ops.LAUNCHES[0] - n0
+            ops.LAUNCHES[0] = n0  # captured launches do not execute
+            self.graphs[key] = {"graph": g, "input": dev_in, "out": g_out, "offs": offs, "launches": n_launch}
+            return out
+        if ent["offs"] != offs:
+            raise RuntimeError("decode metadata layout changed for a captured shape")
+        ent["input"].copy_(torch.from_numpy(arr))
+        ent["graph"].replay()
+        ops.LAUNCHES[0] += ent["launches"]
+        return ent["out"].clone()
+
+    # ------------------------------------------------------------------ the layer loop
+    def _run(self, md, T, B, max_len, cache, is_decode, return_all_logits):
+        m, c, dev, ws = self.m, self.c, self.dev, self.ws
+        H = c.hidden_size
+        eps = m.eps
+        resid = torch.empty(T, H, dtype=BF16, device=dev)
+        hidden = torch.empty(T, H, dtype=BF16, device=dev)
+        ops.embed_rmsnorm(md["tokens"], m.embedding, m.layers[0]["input_norm"], resid, hidden, eps)
+        nq, nkv, d = c.num_attention_heads, c.num_key_value_heads, c.head_dim
+        Hk, HV, dk, dv = c.linear_num_key_heads, c.linear_num_value_heads, c.linear_key_head_dim, c.linear_value_head_dim
+        big = max(c.qkv_dim, c.qkvz_dim)
+        proj = torch.empty(T, big, dtype=BF16, device=dev)
+        ba = torch.empty(T, c.ba_dim, dtype=BF16, device=dev)
+        mix = torch.empty(T, max(c.attn_out_dim, c.gdn_v_dim), dtype=BF16, device=dev)
+        act = torch.empty(T, c.intermediate_size, dtype=BF16, device=dev)
+        if not is_decode:
+            qb = torch.empty(T, c.gdn_qk_dim, dtype=BF16, device=dev)
+            kb = torch.empty(T, c.gdn_qk_dim, dtype=BF16, device=dev)
+            vb = torch.empty(T, c.gdn_v_dim, dtype=BF16, device=dev)
+            ob = torch.empty(T, c.gdn_v_dim, dtype=BF16, device=dev)
+        splits = self._decode_splits(cache.capacity)
+        for i, (kind, w) in enumerate(zip(m.layer_types, m.layers)):
+            if i > 0:
+                ops.add_rmsnorm(hidden, resid, w["input_norm"], eps)
+            if kind == "full_attention":
+                qkv = proj[:, :c.qkv_dim]
+                ops.gemm(hidden, w["qkv"], qkv, ws=ws)
+                kc, vc = cache.kv[i]
+                ops.qk_norm_rope_store(qkv, nq, nkv, d, w["q_norm"], w["k_norm"], m.rope, md["positions"],
+                                       md["locations"], kc, vc, eps)
+                att = mix[:, :c.attn_out_dim]
+                if is_decode:
+                    ops.attn_decode(qkv, B, nq, nkv, d, kc, vc, md["seq_len"], md["kv_base"], cache.capacity, splits,
+                                    att, d ** -0.5, ws)
+                else:
+                    ops.attn_prefill(qkv, nq, nkv, d, kc, vc, md["tiles"], md["cu"], md["prefix"], md["kv_base"],
+                                     att, d ** -0.5)
+                ops.gemm(att, w["out"], hidden, ws=ws)
+            else:
+                qkvz = proj[:, :c.qkvz_dim]
+                ops.gemm(hidden, w["qkvz"], qkvz, ws=ws)
+                ops.gemm(hidden, w["ba"], ba, ws=ws)
+                y = mix[:, :c.gdn_v_dim]
+                if is_decode:
+                    ops.gdn_decode(qkvz, ba, w["conv"], cache.conv[i], cache.recurrent[i], md["slots"], B, w["A_log"],
+                                   w["dt_bias"], w["norm"], y, Hk, HV, dk, dv, eps)
+                else:
+                    ops.conv_prefill(qkvz, w["conv"], cache.conv[i], md["cu"], md["slots"], md["has_initial"], B,
+                                     max_len, qb, kb, vb, c.gdn_qk_dim, c.gdn_v_dim, dk)
+                    ops.gdn_prefill(qb, kb, vb, ba, w["A_log"], w["dt_bias"], md["cu"], md["slots"], B,
+                                    cache.recurrent[i], ob, Hk, HV, dk, dv, dk ** -0.5)
+                    ops.gated_rmsnorm(ob, qkvz[:, c.conv_dim:], w["norm"], y, HV, dv, eps)
+                ops.gemm(y, w["out"], hidden, ws=ws)
+            ops.add_rmsnorm(hidden, resid, w["post_norm"], eps)
+            ops.gemm(hidden, w["gate_up"], act, out_kind=ops.OUT_SWIGLU, ws=ws)
+            ops.gemm(act, w["down"], hidden, ws=ws)
+        rows = None if return_all_logits else md["last_rows"]
+        R = T if return_all_logits else B
+        fin = torch.empty(R, H, dtype=BF16, device=dev)
+        ops.add_rmsnorm_rows(hidden, resid, m.final_norm, fin, eps, rows)
+        logits = torch.empty(R, c.vocab_size, dtype=torch.float32, device=dev)
+        ops.gemm(fin, m.lm_head, logits, out_kind=ops.OUT_F32_OF_BF16, ws=ws)
+        return logits

@@ -1,0 +1,174 @@
+"""Torch-facing wrappers over the C ABI (include/qw200.h).
+
+Each wrapper checks dtypes, devices and contiguity, passes raw pointers, sizes and the
+current CUDA stream to ``libqw200.so``, and raises on any nonzero status. There is no
+fallback path: every op runs the sm_100a kernel or fails.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+
+BF16 = torch.bfloat16
+OUT_BF16, OUT_F32_OF_BF16, OUT_SWIGLU = 0, 1, 2
+
+# Kernels launched through this module (a benchmark's claim of native launches), and an
+# optional list that, when set, receives (flops, start_event, end_event) per GEMM launch.
+LAUNCHES = [0]
+PROFILE = None
+
+
+def _ptr(t):
+    return t.data_ptr() if t is not None else None
+
+
+def _stream():
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _req(t, dtype, name):
+    if not isinstance(t, torch.Tensor) or not t.is_cuda or t.dtype != dtype:
+        raise TypeError(f"{name} must be a CUDA {dtype} tensor")
+
+
+class Workspace:
+    """A growable device scratch buffer owned by the caller (the library never allocates)."""
+
+    def __init__(self, device, nbytes: int = 0):
+        self.device = torch.device(device)
+        self.buf = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=self.device)
+
+    def get(self, nbytes: int) -> torch.Tensor:
+        if nbytes > self.buf.numel():
+            if torch.cuda.is_current_stream_capturing():
+                raise RuntimeError("workspace must be sized before CUDA-graph capture")
+            self.buf = torch.empty(int(nbytes * 1.25) + 256, dtype=torch.uint8, device=self.device)
+        return self.buf
+
+
+def gemm_workspace_bytes(M, N, K, out_kind=OUT_BF16) -> int:
+    return int(_lib.load().qw_gemm_workspace_bytes(M, N, K, out_kind))
+
+
+def gemm(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None, *, out_kind: int = OUT_BF16,
+         ws: Workspace | None = None) -> torch.Tensor:
+    """y = x . w^T (bf16, fp32 accumulation). x [M, K] (row stride >= K), w [N, K]."""
+    _req(x, BF16, "x")
+    _req(w, BF16, "w")
+    if x.dim() != 2 or w.dim() != 2 or x.shape[1] != w.shape[1] or x.stride(1) != 1 or w.stride(1) != 1:
+        raise ValueError("gemm expects x [M, K] and w [N, K] with unit inner stride")
+    M, K = x.shape
+    N = w.shape[0]
+    n_out = N // 2 if out_kind == OUT_SWIGLU else N
+    odt = torch.float32 if out_kind == OUT_F32_OF_BF16 else BF16
+    if out is None:
+        out = torch.empty(M, n_out, dtype=odt, device=x.device)
+    if out.dtype != odt or out.shape != (M, n_out) or out.stride(1) != 1:
+        raise ValueError("bad gemm output tensor")
+    need = gemm_workspace_bytes(M, N, K, out_kind)
+    wsp = None
+    if need:
+        if ws is None:
+            raise ValueError("this gemm shape needs a workspace")
+        wsp = ws.get(need)
+    prof = PROFILE
+    if prof is not None:
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+    _lib.call("qw_gemm_bf16", x.data_ptr(), w.data_ptr(), out.data_ptr(), M, N, K, x.stride(0), w.stride(0),
+              out.stride(0), out_kind, _ptr(wsp), need, _stream())
+    if prof is not None:
+        e1.record()
+        prof.append((2.0 * M * N * K, e0, e1))
+    LAUNCHES[0] += 2 if need else 1
+    return out
+
+
+# ----------------------------------------------------------------------------- norms
+def embed_rmsnorm(tokens, table, w, resid_out, hidden_out, eps):
+    T = tokens.numel()
+    LAUNCHES[0] += 1
+    _lib.call("qw_embed_rmsnorm", tokens.data_ptr(), T, table.data_ptr(), table.shape[0], table.shape[1],
+              w.data_ptr(), resid_out.data_ptr(), hidden_out.data_ptr(), eps, _stream())
+
+
+def add_rmsnorm(x, resid, w, eps):
+    T, H = x.shape
+    LAUNCHES[0] += 1
+    _lib.call("qw_add_rmsnorm", x.data_ptr(), resid.data_ptr(), w.data_ptr(), T, H, eps, _stream())
+
+
+def add_rmsnorm_rows(x, resid, w, out, eps, rows=None):
+    T, H = x.shape
+    n = rows.numel() if rows is not None else T
+    LAUNCHES[0] += 1
+    _lib.call("qw_add_rmsnorm_rows", x.data_ptr(), resid.data_ptr(), _ptr(rows), n, T, H, w.data_ptr(),
+              out.data_ptr(), eps, _stream())
+
+
+def gated_rmsnorm(x, z, w, y, HV, D, eps):
+    T = x.shape[0]
+    LAUNCHES[0] += 1
+    _lib.call("qw_gated_rmsnorm", x.data_ptr(), x.stride(0), z.data_ptr(), z.stride(0), w.data_ptr(), y.data_ptr(),
+              y.stride(0), T, HV, D, eps, _stream())
+
+
+# ----------------------------------------------------------------------------- attention
+def qk_norm_rope_store(qkv, nq, nkv, d, q_w, k_w, rope, positions, locations, kc, vc, eps):
+    T = qkv.shape[0]
+    LAUNCHES[0] += 1
+    _lib.call("qw_qk_norm_rope_store", qkv.data_ptr(), qkv.stride(0), T, nq, nkv, d, q_w.data_ptr(), k_w.data_ptr(),
+              rope.data_ptr(), rope.shape[1], rope.shape[0], positions.data_ptr(), locations.data_ptr(),
+              kc.data_ptr(), vc.data_ptr(), kc.shape[0], eps, _stream())
+
+
+def attn_prefill(qkv, nq, nkv, d, kc, vc, tiles, cu, prefix, kv_base, out, scale):
+    LAUNCHES[0] += 1
+    _lib.call("qw_attn_prefill", qkv.data_ptr(), qkv.stride(0), nq, nkv, d, kc.data_ptr(), vc.data_ptr(),
+              tiles.data_ptr(), tiles.numel() // 2, cu.data_ptr(), prefix.data_ptr(), kv_base.data_ptr(),
+              out.data_ptr(), out.stride(0), scale, _stream())
+
+
+def attn_decode_workspace_bytes(B, nq, d, splits):
+    return int(_lib.load().qw_attn_decode_workspace_bytes(B, nq, d, splits))
+
+
+def attn_decode(qkv, B, nq, nkv, d, kc, vc, seq_len, kv_base, max_len, splits, out, scale, ws: Workspace):
+    need = attn_decode_workspace_bytes(B, nq, d, splits)
+    buf = ws.get(need)
+    LAUNCHES[0] += 2
+    _lib.call("qw_attn_decode", qkv.data_ptr(), qkv.stride(0), B, nq, nkv, d, kc.data_ptr(), vc.data_ptr(),
+              seq_len.data_ptr(), kv_base.data_ptr(), max_len, splits, out.data_ptr(), out.stride(0), scale,
+              buf.data_ptr(), need, _stream())
+
+
+# ----------------------------------------------------------------------------- gated deltanet
+def conv_prefill(x, conv_w, conv_state, cu, slots, has_initial, B, max_len, q_out, k_out, v_out, qk_dim, v_dim,
+                 head_dim):
+    LAUNCHES[0] += 1
+    _lib.call("qw_conv_prefill", x.data_ptr(), x.stride(0), conv_w.data_ptr(), conv_state.data_ptr(), cu.data_ptr(),
+              slots.data_ptr(), has_initial.data_ptr(), B, conv_state.shape[0], max_len, q_out.data_ptr(),
+              k_out.data_ptr(), v_out.data_ptr(), qk_dim, v_dim, head_dim, _stream())
+
+
+def gdn_prefill(q, k, v, ba, A_log, dt_bias, cu, slots, B, state, out, H, HV, dk, dv, scale):
+    LAUNCHES[0] += 1
+    _lib.call("qw_gdn_prefill", q.data_ptr(), k.data_ptr(), v.data_ptr(), ba.data_ptr(), ba.stride(0),
+              A_log.data_ptr(), dt_bias.data_ptr(), cu.data_ptr(), slots.data_ptr(), B, state.shape[0],
+              state.data_ptr(), out.data_ptr(), H, HV, dk, dv, scale, _stream())
+
+
+def gdn_decode(qkvz, ba, conv_w, conv_state, state, slots, B, A_log, dt_bias, norm_w, y, H, HV, dk, dv, eps):
+    LAUNCHES[0] += 1
+    _lib.call("qw_gdn_decode", qkvz.data_ptr(), qkvz.stride(0), ba.data_ptr(), ba.stride(0), conv_w.data_ptr(),
+              conv_state.data_ptr(), state.data_ptr(), slots.data_ptr(), B, state.shape[0], A_log.data_ptr(),
+              dt_bias.data_ptr(), norm_w.data_ptr(), y.data_ptr(), y.stride(0), H, HV, dk, dv, eps, _stream())
+
+
+# ----------------------------------------------------------------------------- cache
+def kv_grow(src_k, src_v, dst_k, dst_v, lengths, S, old_cap, new_cap):
+    row_elems = src_k[0].numel()
+    LAUNCHES[0] += 1
+    _lib.call("qw_kv_grow", src_k.data_ptr(), src_v.data_ptr(), dst_k.data_ptr(), dst_v.data_ptr(),
+              lengths.data_ptr(), S, old_cap, new_cap, row_elems, _stream())

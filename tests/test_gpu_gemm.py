@@ -1,0 +1,103 @@
+"""tcgen05 GEMM parity against a float64 torch reference of the same op (bf16 in, fp32
+accumulation, bf16 rounding of the output).
+
+Tolerance: an fp32 sum in a different order than any reference differs from the exact
+sum by a few units of 2^-24 times the sum of |x_k w_k|, so after rounding to bf16 an
+element may sit one bf16 ulp from bf16(exact) (two near cancellation). The bound per
+element is 1.01 ulp_bf16(max(|exact|, |got|)) + 8 sqrt(K) 2^-24 sum_k |x_k w_k|, and at
+most 1% of elements may differ from bf16(exact) at all.
+"""
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def ulp_bf16(x):
+    x = x.float().abs().clamp_min(2.0 ** -126)
+    return torch.exp2(torch.floor(torch.log2(x)) - 7)
+
+
+def fp32_sum_bound(x, w):
+    K = x.shape[1]
+    return 8.0 * K ** 0.5 * 2.0 ** -24 * (x.double().abs() @ w.double().abs().t())
+
+
+def check_bf16(got, x, w, frac=0.01):
+    ref = x.double() @ w.double().t()
+    exp = ref.to(torch.bfloat16).double()
+    diff = (got.double() - exp).abs()
+    bound = torch.maximum(ulp_bf16(ref), ulp_bf16(got)).double() * 1.01 + fp32_sum_bound(x, w)
+    bad = diff > bound
+    assert not bool(bad.any()), f"{int(bad.sum())} elements beyond bound, max diff {diff.max().item()}"
+    assert (diff > 0).double().mean().item() <= frac
+
+
+@pytest.fixture(scope="module")
+def ops():
+    from qwen38_inference_b200 import ops as o
+    return o
+
+
+SHAPES = [
+    (256, 512, 320),      # exact tiles, K tail of 64
+    (300, 1000, 5120),    # ragged M and N
+    (1024, 768, 256),
+    (129, 96, 5120),      # the ba projection shape, M tail
+    (4096, 2048, 1024),   # many tiles per CTA (persistent loop, TMEM double buffer)
+    (32, 1024, 512),      # skinny: weight streaming
+    (1, 96, 5120),
+    (5, 5120, 6144),      # skinny split-K
+    (64, 4096, 17408),
+    (17, 248, 512),
+]
+
+
+@pytest.mark.parametrize("M,N,K", SHAPES)
+def test_gemm_bf16(ops, M, N, K):
+    g = torch.Generator(device="cuda").manual_seed(M * 7 + N * 13 + K)
+    x = (torch.randn(M, K, device="cuda", generator=g)).to(torch.bfloat16)
+    w = (torch.randn(N, K, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+    ws = ops.Workspace("cuda")
+    y = ops.gemm(x, w, ws=ws)
+    torch.cuda.synchronize()
+    check_bf16(y, x, w)
+    from qwen38_inference_b200 import _lib
+    assert _lib.take_device_error() == 0
+
+
+@pytest.mark.parametrize("M,N,K", [(300, 1000, 512), (8, 2048, 1024), (2, 248320 // 64, 256)])
+def test_gemm_f32_logits(ops, M, N, K):
+    g = torch.Generator(device="cuda").manual_seed(5)
+    x = torch.randn(M, K, device="cuda", generator=g).to(torch.bfloat16)
+    w = (torch.randn(N, K, device="cuda", generator=g) * 0.05).to(torch.bfloat16)
+    y = ops.gemm(x, w, out_kind=ops.OUT_F32_OF_BF16, ws=ops.Workspace("cuda"))
+    assert y.dtype == torch.float32
+    check_bf16(y, x, w)
+
+
+@pytest.mark.parametrize("M,I,K", [(300, 384, 512), (128, 1024, 256), (32, 512, 1024), (3, 256, 512)])
+def test_gemm_swiglu(ops, M, I, K):
+    g = torch.Generator(device="cuda").manual_seed(9)
+    x = torch.randn(M, K, device="cuda", generator=g).to(torch.bfloat16)
+    w = (torch.randn(2 * I, K, device="cuda", generator=g) * 0.05).to(torch.bfloat16)
+    y = ops.gemm(x, w, out_kind=ops.OUT_SWIGLU, ws=ops.Workspace("cuda"))
+    gu = (x.double() @ w.double().t()).to(torch.bfloat16).double()
+    gate, up = gu[:, :I], gu[:, I:]
+    ref = gate / (1 + torch.exp(-gate)) * up
+    # the rounding of g and u may flip (one ulp each), then the product rounds once more
+    sb = fp32_sum_bound(x, w)
+    slack = ulp_bf16(gu).double() + sb
+    bound = 1.01 * ulp_bf16(ref).double() + (slack[:, :I] * up.abs() + slack[:, I:] * gate.abs()) * 1.2
+    diff = (y.double() - ref.to(torch.bfloat16).double()).abs()
+    assert bool((diff <= bound).all()), f"max diff {diff.max().item()}"
+    assert (diff > 0).double().mean().item() <= 0.02
+
+
+def test_gemm_strided_input(ops):
+    g = torch.Generator(device="cuda").manual_seed(3)
+    big = torch.randn(200, 1024, device="cuda", generator=g).to(torch.bfloat16)
+    x = big[:, 128:128 + 512]  # row stride 1024
+    w = (torch.randn(640, 512, device="cuda", generator=g) * 0.05).to(torch.bfloat16)
+    y = ops.gemm(x, w)
+    check_bf16(y, x, w)

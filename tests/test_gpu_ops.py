@@ -1,0 +1,296 @@
+"""Per-kernel parity: every sm_100a op against the CPU oracle op (oracle/ops.py) on the same
+seeded inputs, with the 27B per-head geometry.
+
+Tolerances (bf16 outputs): an element may differ from the oracle by a few bf16 ulps of its
+magnitude plus a small absolute term; the fraction of differing elements is bounded. The
+oracle computes in fp32 with the reference's rounding points; the kernels reach the same
+rounding points with a different fp32 summation order, so isolated last-ulp flips are
+expected. Cache bookkeeping (rows written, state shifts, growth copies) is bit-exact.
+"""
+import pytest
+import torch
+
+from oracle import ops as O
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+@pytest.fixture(scope="module")
+def K():
+    from qwen38_inference_b200 import ops
+    return ops
+
+
+def bf(t):
+    return t.to(torch.bfloat16)
+
+
+def ulp(x):
+    x = x.float().abs().clamp_min(2.0 ** -126)
+    return torch.exp2(torch.floor(torch.log2(x)) - 7)
+
+
+def close(got, exp, n_ulp=2.0, atol=1e-5, max_frac=0.05):
+    got, exp = got.float().cpu(), exp.float().cpu()
+    d = (got - exp).abs()
+    bound = n_ulp * torch.maximum(ulp(got), ulp(exp)) + atol
+    bad = d > bound
+    assert not bool(bad.any()), f"{int(bad.sum())}/{d.numel()} beyond bound; max diff {d.max().item():.3g}"
+    frac = (d > 0).float().mean().item()
+    assert frac <= max_frac, f"{frac:.3f} of elements differ"
+
+
+def gen(seed):
+    return torch.Generator().manual_seed(seed)
+
+
+def test_embed_and_add_rmsnorm(K):
+    g = gen(1)
+    V, H, T = 500, 5120, 37
+    table = bf(torch.randn(V, H, generator=g))
+    w = bf(torch.randn(H, generator=g) * 0.1)
+    tok = torch.randint(V, (T,), generator=g, dtype=torch.int32)
+    resid = torch.empty(T, H, dtype=torch.bfloat16, device=DEV)
+    hid = torch.empty_like(resid)
+    K.embed_rmsnorm(tok.to(DEV), table.to(DEV), w.to(DEV), resid, hid, 1e-6)
+    assert torch.equal(resid.cpu(), table[tok.long()])
+    close(hid, O.gemma_rmsnorm(table[tok.long()], w, 1e-6, O.bf16), n_ulp=1)
+    x = bf(torch.randn(T, H, generator=g))
+    r = bf(torch.randn(T, H, generator=g))
+    xd, rd = x.to(DEV), r.to(DEV)
+    K.add_rmsnorm(xd, rd, w.to(DEV), 1e-6)
+    ex, er = O.gemma_add_rmsnorm(x, r, w, 1e-6, O.bf16)
+    assert torch.equal(rd.cpu().float(), er)  # residual = bf16(x + r) exactly
+    close(xd, ex, n_ulp=1)
+    rows = torch.tensor([3, 0, 36], dtype=torch.int32)
+    out = torch.empty(3, H, dtype=torch.bfloat16, device=DEV)
+    K.add_rmsnorm_rows(x.to(DEV), r.to(DEV), w.to(DEV), out, 1e-6, rows.to(DEV))
+    close(out, ex[rows.long()], n_ulp=1)
+
+
+def test_gated_rmsnorm(K):
+    g = gen(2)
+    T, HV, D = 19, 48, 128
+    x = bf(torch.randn(T, HV * D, generator=g))
+    zbuf = bf(torch.randn(T, 3 * HV * D, generator=g))
+    z = zbuf[:, HV * D:2 * HV * D]
+    w = bf(torch.randn(D, generator=g) * 0.3 + 1)
+    y = torch.empty(T, HV * D, dtype=torch.bfloat16, device=DEV)
+    zd = zbuf.to(DEV)[:, HV * D:2 * HV * D]
+    K.gated_rmsnorm(x.to(DEV), zd, w.to(DEV), y, HV, D, 1e-6)
+    exp = O.gated_rmsnorm(x.reshape(-1, D), w, z.reshape(-1, D), 1e-6, O.bf16).reshape(T, -1)
+    close(y, exp, n_ulp=2)
+
+
+@pytest.mark.parametrize("nq,nkv,d,rd", [(24, 4, 256, 64), (6, 1, 256, 64), (4, 2, 64, 16)])
+def test_qk_norm_rope_store(K, nq, nkv, d, rd):
+    from qwen38_inference_b200.config import rope_table, HybridConfig
+    g = gen(3)
+    T, rows = 11, 200
+    cfg = HybridConfig(hidden_size=64, intermediate_size=64, num_attention_heads=nq, num_key_value_heads=nkv,
+                       head_dim=d, linear_num_key_heads=1, linear_num_value_heads=1, linear_key_head_dim=128,
+                       linear_value_head_dim=128, linear_conv_kernel_dim=4, num_hidden_layers=4, vocab_size=8,
+                       partial_rotary_factor=rd / d)
+    rope = rope_table(cfg, 1024, DEV)
+    qkv = bf(torch.randn(T, 2 * nq * d + 2 * nkv * d, generator=g))
+    qw, kw = bf(torch.randn(d, generator=g) * 0.1), bf(torch.randn(d, generator=g) * 0.1)
+    pos = torch.randint(0, 1024, (T,), generator=g, dtype=torch.int32)
+    loc = torch.randperm(rows - 64, generator=g)[:T].to(torch.int32) + 64
+    kc = torch.full((rows, nkv, d), float("nan"), dtype=torch.bfloat16, device=DEV)  # poisoned
+    vc = torch.full_like(kc, float("nan"))
+    qd = qkv.to(DEV)
+    K.qk_norm_rope_store(qd, nq, nkv, d, qw.to(DEV), kw.to(DEV), rope, pos.to(DEV), loc.to(DEV), kc, vc, 1e-6)
+    qg, k, v = qkv.float().split([2 * nq * d, nkv * d, nkv * d], dim=-1)
+    eq, ek, _ = O.qk_norm_rope_gate(qg, k, qw, kw, rope.cpu(), pos.long(), 1e-6, nq, nkv, d, rd, O.bf16)
+    got_q = qd.cpu().float()[:, :2 * nq * d].view(T, nq, 2 * d)
+    close(got_q[..., :d], eq, n_ulp=1)
+    assert torch.equal(got_q[..., d:], qg.view(T, nq, 2 * d)[..., d:])  # gate untouched
+    close(kc.cpu()[loc.long()], ek, n_ulp=1)
+    assert torch.equal(vc.cpu()[loc.long()].float(), v.view(T, nkv, d))
+    untouched = torch.ones(rows, dtype=torch.bool)
+    untouched[loc.long()] = False
+    assert bool(torch.isnan(kc.cpu()[untouched].float()).all())
+
+
+def _attn_case(g, nq, nkv, d, prefixes, lens, cap=512):
+    S = len(lens)
+    rows = S * cap + 64
+    kc = bf(torch.randn(rows, nkv, d, generator=g))
+    vc = bf(torch.randn(rows, nkv, d, generator=g))
+    T = sum(lens)
+    qkv = bf(torch.randn(T, 2 * nq * d + 2 * nkv * d, generator=g))
+    starts = [64 + s * cap for s in range(S)]
+    return kc, vc, qkv, starts
+
+
+@pytest.mark.parametrize("nq,nkv,d", [(24, 4, 256), (6, 1, 256), (4, 2, 64)])
+def test_attn_prefill(K, nq, nkv, d):
+    from qwen38_inference_b200.model import build_metadata
+    g = gen(4)
+    prefixes, lens = [0, 37, 130, 0], [200, 1, 77, 129]
+    kc, vc, qkv, starts = _attn_case(g, nq, nkv, d, prefixes, lens)
+    packed, offs, T = build_metadata(list(range(len(lens))), prefixes, lens, 512)
+    md = {k: torch.from_numpy(packed[o:o + n]).to(DEV) for k, (o, n) in offs.items()}
+    out = torch.empty(T, nq * d, dtype=torch.bfloat16, device=DEV)
+    K.attn_prefill(qkv.to(DEV), nq, nkv, d, kc.to(DEV), vc.to(DEV), md["tiles"], md["cu"], md["prefix"],
+                   md["kv_base"], out, d ** -0.5)
+    q = qkv.float()[:, :2 * nq * d].view(T, nq, 2 * d)
+    att = O.paged_attention(q[..., :d], kc, vc, starts, prefixes, lens, d ** -0.5, O.bf16)
+    exp = O.sigmoid_mul(att.reshape(T, -1), q[..., d:].reshape(T, -1), O.bf16)
+    # P is rounded to bf16 before the PV product (tensor cores): allow a few ulps
+    close(out, exp, n_ulp=4, atol=2e-3, max_frac=0.5)
+
+
+@pytest.mark.parametrize("nq,nkv,d", [(24, 4, 256), (4, 2, 64)])
+@pytest.mark.parametrize("splits", [1, 3])
+def test_attn_decode(K, nq, nkv, d, splits):
+    g = gen(5)
+    lens = [1] * 5
+    prefixes = [1, 63, 64, 300, 511]
+    kc, vc, qkv, starts = _attn_case(g, nq, nkv, d, prefixes, lens)
+    B = len(lens)
+    seq_len = torch.tensor([p + 1 for p in prefixes], dtype=torch.int32)
+    kv_base = torch.tensor(starts, dtype=torch.int32)
+    out = torch.empty(B, nq * d, dtype=torch.bfloat16, device=DEV)
+    ws = K.Workspace(DEV)
+    K.attn_decode(qkv.to(DEV), B, nq, nkv, d, kc.to(DEV), vc.to(DEV), seq_len.to(DEV), kv_base.to(DEV), 512, splits,
+                  out, d ** -0.5, ws)
+    q = qkv.float()[:, :2 * nq * d].view(B, nq, 2 * d)
+    att = O.paged_attention(q[..., :d], kc, vc, starts, prefixes, lens, d ** -0.5, O.bf16)
+    exp = O.sigmoid_mul(att.reshape(B, -1), q[..., d:].reshape(B, -1), O.bf16)
+    close(out, exp, n_ulp=2, atol=1e-4, max_frac=0.2)
+
+
+def test_conv_prefill(K):
+    g = gen(6)
+    H, HV, dk = 2, 6, 128
+    qk, vd = H * dk, HV * dk
+    C = 2 * qk + vd
+    lens, has, slots = [5, 2, 1, 70, 3, 130], [1, 1, 0, 1, 0, 1], [3, 0, 1, 4, 2, 5]
+    T = sum(lens)
+    x = bf(torch.randn(T, C + vd, generator=g))
+    w = bf(torch.randn(C, 4, generator=g) * 0.5)
+    st = bf(torch.randn(6, C, 3, generator=g))
+    cu = [0]
+    for n in lens:
+        cu.append(cu[-1] + n)
+    std = st.to(DEV)
+    qo = torch.empty(T, qk, dtype=torch.bfloat16, device=DEV)
+    ko, vo = torch.empty_like(qo), torch.empty(T, vd, dtype=torch.bfloat16, device=DEV)
+    t32 = lambda a: torch.tensor(a, dtype=torch.int32, device=DEV)
+    K.conv_prefill(x.to(DEV), w.to(DEV), std, t32(cu), t32(slots), t32(has), len(lens), max(lens), qo, ko, vo, qk, vd,
+                   dk)
+    ex_st = st.clone()
+    y = O.conv_prefill(x[:, :C], w, ex_st, cu, slots, [bool(h) for h in has], O.bf16)
+    assert torch.equal(std.cpu(), ex_st)  # conv state = last 3 raw inputs, bit-exact
+    close(vo, y[:, 2 * qk:], n_ulp=1, max_frac=0.02)
+    eq = O.bf16(O.l2norm(y[:, :qk].reshape(T, H, dk))).reshape(T, qk)
+    ek = O.bf16(O.l2norm(y[:, qk:2 * qk].reshape(T, H, dk))).reshape(T, qk)
+    close(qo, eq, n_ulp=2, max_frac=0.05)
+    close(ko, ek, n_ulp=2, max_frac=0.05)
+
+
+def _gdn_inputs(g, lens, H=2, HV=6, S=None):
+    dk = 128
+    T = sum(lens)
+    S = S or len(lens)
+    q = bf(O.l2norm(torch.randn(T, H, dk, generator=g)))
+    k = bf(O.l2norm(torch.randn(T, H, dk, generator=g)))
+    v = bf(torch.randn(T, HV, dk, generator=g))
+    ba = bf(torch.randn(T, 2 * HV, generator=g))
+    A_log = torch.randn(HV, generator=g) * 0.5
+    dt = bf(torch.randn(HV, generator=g) * 0.5)
+    state = torch.randn(S, HV, dk, dk, generator=g) * 0.05
+    return q, k, v, ba, A_log, dt, state
+
+
+@pytest.mark.parametrize("lens", [[64], [1, 63, 65, 130], [200, 7], [257]])
+def test_gdn_prefill_chunked(K, lens):
+    g = gen(7)
+    H, HV, dk = 2, 6, 128
+    q, k, v, ba, A_log, dt, state = _gdn_inputs(g, lens, H, HV, S=len(lens) + 1)
+    slots = list(range(len(lens)))[::-1]
+    cu = [0]
+    for n in lens:
+        cu.append(cu[-1] + n)
+    T = cu[-1]
+    sd = state.to(DEV)
+    out = torch.empty(T, HV * dk, dtype=torch.bfloat16, device=DEV)
+    t32 = lambda a: torch.tensor(a, dtype=torch.int32, device=DEV)
+    K.gdn_prefill(q.to(DEV), k.to(DEV), v.to(DEV), ba.to(DEV), A_log.to(DEV), dt.to(DEV), t32(cu), t32(slots),
+                  len(lens), sd, out, H, HV, dk, dk, dk ** -0.5)
+    gg, beta = O.gdn_gating(A_log, ba[:, HV:], ba[:, :HV], dt, O.bf16)
+    exp_state = state.clone()
+    exp_o = torch.empty(T, HV, dk)
+    for i, s in enumerate(slots):
+        a0, a1 = cu[i], cu[i + 1]
+        exp_o[a0:a1], exp_state[s] = O.gdn_recurrence(q[a0:a1], k[a0:a1], v[a0:a1], gg[a0:a1], beta[a0:a1],
+                                                      state[s], dk ** -0.5, HV // H)
+    # chunk products use bf16 operands (as the reference's chunked kernel): compare with a
+    # tolerance relative to the output scale
+    got, exp = out.cpu().float().view(T, HV, dk), O.bf16(exp_o)
+    scale = exp.abs().amax(dim=-1, keepdim=True).clamp_min(1e-3)
+    err = ((got - exp).abs() / scale).max().item()
+    assert err < 3e-2, f"relative output error {err}"
+    serr = ((sd.cpu() - exp_state).abs().max() / exp_state.abs().max()).item()
+    assert serr < 2e-2, f"relative state error {serr}"
+    untouched = [s for s in range(len(lens) + 1) if s not in slots]
+    for s in untouched:
+        assert torch.equal(sd.cpu()[s], state[s])
+
+
+def test_gdn_decode_fused(K):
+    g = gen(8)
+    H, HV, dk = 2, 6, 128
+    B, S = 4, 6
+    C = 2 * H * dk + HV * dk
+    qkvz = bf(torch.randn(B, C + HV * dk, generator=g))
+    ba = bf(torch.randn(B, 2 * HV, generator=g))
+    conv_w = bf(torch.randn(C, 4, generator=g) * 0.5)
+    conv_state = bf(torch.randn(S, C, 3, generator=g))
+    state = torch.randn(S, HV, dk, dk, generator=g) * 0.05
+    A_log, dt = torch.randn(HV, generator=g) * 0.5, bf(torch.randn(HV, generator=g) * 0.5)
+    norm_w = bf(torch.randn(dk, generator=g) * 0.3 + 1)
+    slots = [4, 0, 5, 2]
+    csd, sd = conv_state.to(DEV), state.to(DEV)
+    y = torch.empty(B, HV * dk, dtype=torch.bfloat16, device=DEV)
+    K.gdn_decode(qkvz.to(DEV), ba.to(DEV), conv_w.to(DEV), csd, sd, torch.tensor(slots, dtype=torch.int32, device=DEV),
+                 B, A_log.to(DEV), dt.to(DEV), norm_w.to(DEV), y, H, HV, dk, dk, 1e-6)
+    ecs, est = conv_state.clone(), state.clone()
+    mixed = O.conv_decode(qkvz[:, :C], conv_w, ecs, slots, O.bf16)
+    assert torch.equal(csd.cpu(), ecs)
+    gg, beta = O.gdn_gating(A_log, ba[:, HV:], ba[:, :HV], dt, O.bf16)
+    qn = O.l2norm(mixed[:, :H * dk].reshape(B, H, dk))
+    kn = O.l2norm(mixed[:, H * dk:2 * H * dk].reshape(B, H, dk))
+    v = mixed[:, 2 * H * dk:].reshape(B, HV, dk)
+    o = torch.empty(B, HV, dk)
+    for i, s in enumerate(slots):
+        oo, est[s] = O.gdn_recurrence(qn[i:i + 1], kn[i:i + 1], v[i:i + 1], gg[i:i + 1], beta[i:i + 1], est[s],
+                                      dk ** -0.5, HV // H)
+        o[i] = oo[0]
+    exp = O.gated_rmsnorm(O.bf16(o).reshape(-1, dk), norm_w, qkvz[:, C:].reshape(-1, dk), 1e-6, O.bf16).reshape(B, -1)
+    close(y, exp, n_ulp=2, atol=1e-4, max_frac=0.05)
+    torch.testing.assert_close(sd.cpu(), est, rtol=1e-4, atol=1e-5)
+
+
+def test_kv_grow(K):
+    g = gen(9)
+    S, old, new, nkv, d = 3, 64, 192, 4, 256
+    src_k = bf(torch.randn(S * old + 64, nkv, d, generator=g))
+    src_v = bf(torch.randn(S * old + 64, nkv, d, generator=g))
+    lengths = [10, 0, 64]
+    dk_, dv_ = (torch.full((S * new + 64, nkv, d), 7.0, dtype=torch.bfloat16, device=DEV) for _ in range(2))
+    K.kv_grow(src_k.to(DEV), src_v.to(DEV), dk_, dv_, torch.tensor(lengths, dtype=torch.int32, device=DEV), S, old, new)
+    exp_k = torch.zeros(S * new + 64, nkv, d, dtype=torch.bfloat16)
+    exp_v = torch.zeros_like(exp_k)
+    for s, L in enumerate(lengths):
+        exp_k[64 + s * new:64 + s * new + L] = src_k[64 + s * old:64 + s * old + L]
+        exp_v[64 + s * new:64 + s * new + L] = src_v[64 + s * old:64 + s * old + L]
+    assert torch.equal(dk_.cpu(), exp_k)
+    assert torch.equal(dv_.cpu(), exp_v)
+
+
+def test_no_device_error_after_ops(K):
+    from qwen38_inference_b200 import _lib
+    assert _lib.take_device_error() == 0
