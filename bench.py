@@ -233,12 +233,15 @@ def run_gpu(args):
         t0 = time.perf_counter()
         ev[0].record(stream)
         lg = model.forward_step(prefill, cache)
+        t_issue_p = time.perf_counter()
         ev[1].record(stream)
         h2d = model._engine.last_h2d_bytes
         host_p = lg.cpu()
         t1 = time.perf_counter()
+        t_dec = time.perf_counter()
         ev[2].record(stream)
         lg = model.forward_step(decode, cache)
+        t_issue_d = time.perf_counter()
         ev[3].record(stream)
         h2d += model._engine.last_h2d_bytes
         host_d = lg.cpu()
@@ -249,10 +252,12 @@ def run_gpu(args):
             record["d"].append(ev[2].elapsed_time(ev[3]))
             record["p_wall"].append((t1 - t0) * 1e3)
             record["d_wall"].append((t2 - t1) * 1e3)
+            record["p_issue"].append((t_issue_p - t0) * 1e3)
+            record["d_issue"].append((t_issue_d - t_dec) * 1e3)
         return h2d, host_p.numel() * 4 + host_d.numel() * 4
     for _ in range(args.warmup):
         one_step(None)
-    rec = {"p": [], "d": [], "p_wall": [], "d_wall": []}
+    rec = {"p": [], "d": [], "p_wall": [], "d_wall": [], "p_issue": [], "d_issue": []}
     ops.LAUNCHES[0] = 0
     barrier()
     with ClockSampler(local) as clk:
@@ -294,7 +299,9 @@ def run_gpu(args):
                       "model": "Qwen3.8-27B hybrid geometry (48 GDN + 16 gated GQA), random init",
                       "global_batch": world * B, "seq_len": L, "parallelism": f"replicas x{world} (requests sharded)",
                       "l2": "inputs larger than L2 (54 GB of weights streamed per call)"},
-           "median_ms": {"prefill": round(mp, 3), "decode": round(md, 3)},
+           "median_ms": {"prefill": round(mp, 3), "decode": round(md, 3),
+                         "prefill_host_issue": round(statistics.median(rec["p_issue"]), 3),
+                         "decode_host_issue": round(statistics.median(rec["d_issue"]), 3)},
            "e2e": {"value": round(tokens / (e2e_ms * 1e-3), 1), "unit": UNIT, "h2d_bytes_per_step": h2d,
                    "d2h_bytes_per_step": d2h},
            "gpu_launches": launches, "clocks": clocks, "roofline": roof}

@@ -2,9 +2,12 @@
 // projection, the split into token-major q, k, v, the L2 norm of q and k, and the conv
 // state update (REF:704-1253 conv, REF:603-699 split, REF:1550-1638 l2norm).
 //
-// Grid (request, chunk of 64 tokens, 128-channel block). Only chunk 0 of a request reads
-// its previous conv state (when has_initial) and writes the new one (the last W-1 raw
-// inputs of [old state | x]), so no other CTA touches that request's state. Per channel:
+// Grid (request, chunk of 64 tokens, 128-channel block), 256 threads. The CTA stages the
+// 3 history rows + 64 token rows of its 128 channels in shared memory with 16-byte loads
+// (all in flight together), convolves from shared memory, normalizes q/k heads per token
+// (one warp per token) and writes 16-byte-aligned rows. Only chunk 0 of a request reads
+// its previous conv state (when has_initial) and writes the new one (the last 3 raw inputs
+// of [old state | x]), so no other CTA touches that request's state. Per channel:
 // acc = sum_j bf16(x[t-3+j] * w[j]) for j = 0..3 in order, y = bf16(silu(acc)); q and k
 // heads then become bf16(y / sqrt(sum y^2 + 1e-6)).
 #include "common.cuh"
@@ -12,77 +15,84 @@
 namespace qw {
 
 template <int HD>
-__global__ void __launch_bounds__(128) conv_prefill_kernel(
+__global__ void __launch_bounds__(256) conv_prefill_kernel(
     const __nv_bfloat16* __restrict__ x, int64_t ldx, const __nv_bfloat16* __restrict__ w,
     __nv_bfloat16* __restrict__ conv_state, const int32_t* __restrict__ cu, const int32_t* __restrict__ slots,
     const int32_t* __restrict__ has_initial, int n_slots, __nv_bfloat16* __restrict__ q_out,
     __nv_bfloat16* __restrict__ k_out, __nv_bfloat16* __restrict__ v_out, int qk_dim, int v_dim, int* err) {
-  constexpr int BT = 64, BC = 128, W = 4;
-  __shared__ float sy[BT][BC + 1];
+  constexpr int BT = 64, BC = 128, W = 4, HIST = W - 1;
+  __shared__ __align__(16) __nv_bfloat16 sx[BT + HIST][BC];
+  __shared__ __align__(16) __nv_bfloat16 sy[BT][BC];  // bf16(silu(conv)), exact
   const int seq = blockIdx.x, chunk = blockIdx.y, cb = blockIdx.z;
   const int t0 = cu[seq], n = cu[seq + 1] - t0;
   const int tb = chunk * BT;
   if (tb >= n) return;
   const int C = 2 * qk_dim + v_dim;
   const int tid = threadIdx.x;
-  const int c = cb * BC + tid;
+  const int c0 = cb * BC;
   const int slot = slots[seq];
   if (slot < 0 || slot >= n_slots) {
     if (tid == 0) set_error(err, QW_DEV_ERR_INDEX);
     return;
   }
-  const float w0 = bf2f(w[(int64_t)c * W + 0]), w1 = bf2f(w[(int64_t)c * W + 1]);
-  const float w2 = bf2f(w[(int64_t)c * W + 2]), w3 = bf2f(w[(int64_t)c * W + 3]);
-  float h0, h1, h2;  // x[t-3], x[t-2], x[t-1]
-  __nv_bfloat16* st = conv_state + ((int64_t)slot * C + c) * (W - 1);
-  if (chunk == 0) {
-    if (has_initial[seq]) {
-      h0 = bf2f(st[0]);
-      h1 = bf2f(st[1]);
-      h2 = bf2f(st[2]);
-    } else {
-      h0 = h1 = h2 = 0.f;
-    }
-    // new state = last 3 entries of [history | x]
-    __nv_bfloat16 ns[3];
-#pragma unroll
-    for (int i = 0; i < 3; ++i) {
-      const int pos = n - 3 + i;  // index into x of this request; negative = history
-      if (pos >= 0) ns[i] = x[(int64_t)(t0 + pos) * ldx + c];
-      else ns[i] = f2bf(pos == -1 ? h2 : pos == -2 ? h1 : h0);
-    }
-    st[0] = ns[0];
-    st[1] = ns[1];
-    st[2] = ns[2];
-  } else {
-    h0 = bf2f(x[(int64_t)(t0 + tb - 3) * ldx + c]);
-    h1 = bf2f(x[(int64_t)(t0 + tb - 2) * ldx + c]);
-    h2 = bf2f(x[(int64_t)(t0 + tb - 1) * ldx + c]);
-  }
   const int nt = min(BT, n - tb);
-  for (int j = 0; j < nt; ++j) {
-    const float xv = bf2f(x[(int64_t)(t0 + tb + j) * ldx + c]);
-    float acc = 0.f;
-    acc += bf16_round(h0 * w0);
-    acc += bf16_round(h1 * w1);
-    acc += bf16_round(h2 * w2);
-    acc += bf16_round(xv * w3);
-    sy[j][tid] = bf16_round(acc / (1.0f + __expf(-acc)));
-    h0 = h1;
-    h1 = h2;
-    h2 = xv;
+  // ---- stage rows tb-3 .. tb+nt-1 (16-byte vectors; 16 per row)
+  for (int i = tid; i < (BT + HIST) * 16; i += 256) {
+    const int r = i >> 4, v = i & 15;
+    const int tok = tb - HIST + r;  // index within the request
+    uint4 val = make_uint4(0, 0, 0, 0);
+    if (tok >= 0 && tok < tb + nt) val = *reinterpret_cast<const uint4*>(x + (int64_t)(t0 + tok) * ldx + c0 + v * 8);
+    *reinterpret_cast<uint4*>(&sx[r][v * 8]) = val;
+  }
+  __nv_bfloat16* st = conv_state + ((int64_t)slot * C + c0) * (W - 1);
+  if (chunk == 0) {
+    // history rows from the old state when the request has one (zeros otherwise)
+    if (has_initial[seq] && tid < BC) {
+#pragma unroll
+      for (int j = 0; j < HIST; ++j) sx[j][tid] = st[tid * (W - 1) + j];
+    }
   }
   __syncthreads();
-  // ---- outputs: 4 warps x 16 tokens; lane owns 4 channels of the 128-channel block
+  if (chunk == 0 && tid < BC) {
+    // new state = last 3 entries of [history | x] (history is in sx rows 0..2)
+    __nv_bfloat16 ns[HIST];
+#pragma unroll
+    for (int i = 0; i < HIST; ++i) {
+      const int pos = n - HIST + i;  // index within the request; negative = history row
+      ns[i] = pos >= 0 ? x[(int64_t)(t0 + pos) * ldx + c0 + tid] : sx[pos + HIST][tid];
+    }
+#pragma unroll
+    for (int i = 0; i < HIST; ++i) st[tid * (W - 1) + i] = ns[i];
+  }
+  // ---- convolution: thread = (channel, half of the tokens)
+  {
+    const int c = tid & (BC - 1), half = tid >> 7;
+    const float w0 = bf2f(w[(int64_t)(c0 + c) * W + 0]), w1 = bf2f(w[(int64_t)(c0 + c) * W + 1]);
+    const float w2 = bf2f(w[(int64_t)(c0 + c) * W + 2]), w3 = bf2f(w[(int64_t)(c0 + c) * W + 3]);
+    const int j0 = half * (BT / 2);
+    float h0 = bf2f(sx[j0][c]), h1 = bf2f(sx[j0 + 1][c]), h2 = bf2f(sx[j0 + 2][c]);
+    for (int j = j0; j < j0 + BT / 2 && j < nt; ++j) {
+      const float xv = bf2f(sx[j + HIST][c]);
+      float acc = 0.f;
+      acc += bf16_round(h0 * w0);
+      acc += bf16_round(h1 * w1);
+      acc += bf16_round(h2 * w2);
+      acc += bf16_round(xv * w3);
+      sy[j][c] = f2bf(acc / (1.0f + __expf(-acc)));
+      h0 = h1;
+      h1 = h2;
+      h2 = xv;
+    }
+  }
+  __syncthreads();
+  // ---- outputs: one warp per token row; lane owns 4 channels of the 128-channel block
   const int warp = tid >> 5, lane = tid & 31;
-  const int c0 = cb * BC;
   const bool is_v = c0 >= 2 * qk_dim;
-  for (int j = warp; j < nt; j += 4) {
+  for (int j = warp; j < nt; j += 8) {
     float y[4];
 #pragma unroll
-    for (int e = 0; e < 4; ++e) y[e] = sy[j][lane * 4 + e];
+    for (int e = 0; e < 4; ++e) y[e] = bf2f(sy[j][lane * 4 + e]);
     if (!is_v) {
-      // L2 norm per head of HD channels (HD = 128: whole warp; HD = 64: half warp)
       float ss = 0.f;
 #pragma unroll
       for (int e = 0; e < 4; ++e) ss += y[e] * y[e];
@@ -115,6 +125,7 @@ extern "C" int qw_conv_prefill(const void* x, int64_t ldx, const void* conv_w, v
   QW_CHECK_ARG(x && conv_w && conv_state && cu_seqlens && slots && has_initial && q_out && k_out && v_out, QW_ERR_ARG);
   QW_CHECK_ARG(B > 0 && max_len > 0 && n_slots > 0, QW_ERR_ARG);
   QW_CHECK_ARG(qk_dim % 128 == 0 && v_dim % 128 == 0, QW_ERR_UNSUPPORTED);
+  QW_CHECK_ARG(((uintptr_t)x % 16) == 0 && (ldx % 8) == 0, QW_ERR_ALIGN);
   QW_CHECK_ARG(((uintptr_t)q_out % 8) == 0 && ((uintptr_t)k_out % 8) == 0 && ((uintptr_t)v_out % 8) == 0, QW_ERR_ALIGN);
   auto* s = reinterpret_cast<cudaStream_t>(stream);
   const int C = (int)(2 * qk_dim + v_dim);
@@ -126,10 +137,10 @@ extern "C" int qw_conv_prefill(const void* x, int64_t ldx, const void* conv_w, v
   auto* ko = static_cast<__nv_bfloat16*>(k_out);
   auto* vo = static_cast<__nv_bfloat16*>(v_out);
   if (head_dim == 128)
-    conv_prefill_kernel<128><<<grid, 128, 0, s>>>(xp, ldx, wp, cs, cu_seqlens, slots, has_initial, (int)n_slots, qo, ko,
+    conv_prefill_kernel<128><<<grid, 256, 0, s>>>(xp, ldx, wp, cs, cu_seqlens, slots, has_initial, (int)n_slots, qo, ko,
                                                   vo, (int)qk_dim, (int)v_dim, device_error_ptr());
   else if (head_dim == 64)
-    conv_prefill_kernel<64><<<grid, 128, 0, s>>>(xp, ldx, wp, cs, cu_seqlens, slots, has_initial, (int)n_slots, qo, ko,
+    conv_prefill_kernel<64><<<grid, 256, 0, s>>>(xp, ldx, wp, cs, cu_seqlens, slots, has_initial, (int)n_slots, qo, ko,
                                                  vo, (int)qk_dim, (int)v_dim, device_error_ptr());
   else
     return QW_ERR_UNSUPPORTED;

@@ -66,6 +66,14 @@ class Engine:
         key = (B, cache.capacity, len(cache.lengths), tuple(k.data_ptr() for k, _ in cache.kv.values()),
                tuple(x.data_ptr() for x in cache.recurrent.values()), tuple(x.data_ptr() for x in cache.conv.values()))
         ent = self.graphs.get(key)
+        # decodes of this shape on this cache object (the allocator may hand a new cache the
+        # addresses of a freed one, so the count lives on the cache, not on the key)
+        seen = getattr(cache, "_decode_counts", None)
+        if seen is None:
+            seen = {}
+            cache._decode_counts = seen
+        n_prev = seen.get(key, 0)
+        seen[key] = n_prev + 1
         if ent is None or ent.get("graph") is None:
             if ent is None:
                 for k in [k for k in self.graphs if k[0] == B]:  # built on a grown or freed cache
@@ -75,7 +83,7 @@ class Engine:
             md = self._meta_views(dev_in[T:], offs)
             md["tokens"] = dev_in[:T]
             out = self._run(md, T, B, 1, cache, True, False)
-            if ent is None:
+            if n_prev == 0:
                 self.graphs[key] = {"graph": None}
                 return out
             g = torch.cuda.CUDAGraph()
