@@ -275,12 +275,24 @@ def run_gpu(args):
     tokens = world * (B * L + B)
 
     # ---- roofline of the dominant kernel (the tcgen05 GEMM): one instrumented prefill
-    prof = []
-    ops.PROFILE = prof
+    from qwen38_inference_b200 import _lib
+    prof, per_op = [], []
+    ops.PROFILE, _lib.PROFILE = prof, per_op
     cache = model.new_cache(B, initial_capacity=64)
     model.forward_step(prefill, cache)
     torch.cuda.synchronize()
-    ops.PROFILE = None
+    ops.PROFILE, _lib.PROFILE = None, None
+    breakdown = {}
+    for name, a, b in per_op:
+        breakdown[name] = breakdown.get(name, 0.0) + a.elapsed_time(b)
+    dec_ops = []
+    _lib.PROFILE = dec_ops
+    model.forward_step(decode, cache)
+    torch.cuda.synchronize()
+    _lib.PROFILE = None
+    dec_breakdown = {}
+    for name, a, b in dec_ops:
+        dec_breakdown[name] = dec_breakdown.get(name, 0.0) + a.elapsed_time(b)
     flops = sum(f for f, _, _ in prof)
     ms = sum(a.elapsed_time(b) for _, a, b in prof)
     hbm, tf_burst, tf_sust, src = _peaks()
@@ -304,7 +316,9 @@ def run_gpu(args):
                          "decode_host_issue": round(statistics.median(rec["d_issue"]), 3)},
            "e2e": {"value": round(tokens / (e2e_ms * 1e-3), 1), "unit": UNIT, "h2d_bytes_per_step": h2d,
                    "d2h_bytes_per_step": d2h},
-           "gpu_launches": launches, "clocks": clocks, "roofline": roof}
+           "gpu_launches": launches, "clocks": clocks, "roofline": roof,
+           "op_ms": {"prefill": {k[3:]: round(v, 2) for k, v in sorted(breakdown.items(), key=lambda x: -x[1])},
+                     "decode": {k[3:]: round(v, 3) for k, v in sorted(dec_breakdown.items(), key=lambda x: -x[1])}}}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         out["cpu_baseline"] = cpu_baseline(B, L)
     if rank == 0:

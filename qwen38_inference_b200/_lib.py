@@ -33,7 +33,8 @@ SIGNATURES = {
     "qw_attn_decode_workspace_bytes": (SZ, [I64, I64, I64, I64]),
     "qw_attn_decode": (I32, [P, I64, I64, I64, I64, I64, P, P, P, P, I64, I64, P, I64, F32, P, SZ, P]),
     "qw_conv_prefill": (I32, [P, I64, P, P, P, P, P, I64, I64, I64, P, P, P, I64, I64, I64, P]),
-    "qw_gdn_prefill": (I32, [P, P, P, P, I64, P, P, P, P, I64, I64, P, P, I64, I64, I64, I64, F32, P]),
+    "qw_gdn_prefill": (I32, [P, P, P, P, I64, P, P, P, P, I64, I64, P, P, I64, P, P, I64, I64, I64, I64, I64, F32,
+                             F32, P]),
     "qw_gdn_decode": (I32, [P, I64, P, I64, P, P, P, P, I64, I64, P, P, P, P, I64, I64, I64, I64, I64, F32, P]),
     "qw_kv_grow": (I32, [P, P, P, P, P, I64, I64, I64, I64, P]),
 }
@@ -66,8 +67,22 @@ def check(rc: int, what: str) -> None:
         raise QwError(f"{what} failed: {name}")
 
 
+# When set to a list, every entry-point call appends (name, start_event, end_event) recorded
+# on the current stream around it (the benchmark's per-op breakdown).
+PROFILE = None
+
+
 def call(name: str, *args) -> None:
+    prof = PROFILE
+    if prof is None:
+        check(getattr(load(), name)(*args), name)
+        return
+    import torch
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
     check(getattr(load(), name)(*args), name)
+    e1.record()
+    prof.append((name, e0, e1))
 
 
 def take_device_error() -> int:

@@ -98,34 +98,51 @@ QW_DEV void store_tile_bf16(uint8_t* smem_base, float (*acc)[4], int m0, int n0,
         pack_bf16x2(acc[nt][2] * mul, acc[nt][3] * mul);
   }
 }
-
 constexpr int CH = 64;   // chunk length
 constexpr int DKc = 128; // key / value head dim
 constexpr int LDA = 65;  // fp32 row stride of the A / T matrices
 
 struct GdnSmem {
-  static constexpr int TILE = CH * DKc * 2;  // 16 KB
-  static constexpr int Q = 0;
-  static constexpr int K = Q + TILE;
-  static constexpr int V = K + TILE;     // V, then b*V in place
-  static constexpr int KB = V + TILE;    // b e^G K, later e^{G_C-G} K
-  static constexpr int W = KB + TILE;    // -W
-  static constexpr int U = W + TILE;
-  static constexpr int S = U + TILE;     // S0 bf16 [dv][dk], 32 KB
-  static constexpr int P = S + 2 * TILE; // [t][s] bf16, 8 KB
+  static constexpr int TILE = CH * DKc * 2;       // 16 KB
+  static constexpr int QKV = 0;                   // [2 buffers][Q | K | V]
+  static constexpr int KB = QKV + 6 * TILE;       // b e^G K, later e^{G_C-G} K
+  static constexpr int R = KB + TILE;             // A32 | T32 during the inverse; then -W | U
+  static constexpr int W = R;
+  static constexpr int U = R + TILE;
+  static constexpr int A32 = R;
+  static constexpr int T32 = R + CH * LDA * 4;
+  static constexpr int R_BYTES = 2 * CH * LDA * 4;  // >= 2 * TILE
+  static constexpr int S = R + R_BYTES;           // S0 bf16 [dv][dk], 32 KB
+  static constexpr int P = S + 2 * TILE;          // [t][s] bf16, 8 KB
   static constexpr int T = P + CH * CH * 2;
-  static constexpr int A32 = T + CH * CH * 2;  // fp32 [64][LDA]
-  static constexpr int T32 = A32 + CH * LDA * 4;
-  static constexpr int X32 = T32 + CH * LDA * 4;  // 3 x 16 x 16 fp32 scratch
-  static constexpr int VEC = X32 + 3 * 256 * 4;   // G, eG, eGl, beta, g: 5 x 64 fp32
-  static constexpr int TOTAL = VEC + 5 * CH * 4;
+  static constexpr int X32 = T + CH * CH * 2;     // 3 x 16 x 16 fp32 scratch
+  static constexpr int VEC = X32 + 3 * 256 * 4;   // G, eG, eGl, beta: 4 x 64 fp32; row sums 2 x 64
+  static constexpr int TOTAL = VEC + 6 * CH * 4;
 };
+static_assert(GdnSmem::R_BYTES >= 2 * GdnSmem::TILE, "W and U must fit in the inverse's scratch");
+
+// Issue the loads of chunk `ch` (rows beyond the request are zero-filled) into buffer `b`.
+QW_DEV void gdn_load_chunk(uint32_t s0, int b, const __nv_bfloat16* q, const __nv_bfloat16* k,
+                           const __nv_bfloat16* v, int64_t tc, int nc, int h, int hv, int H, int HV, int tid) {
+  const uint32_t base = s0 + GdnSmem::QKV + b * 3 * GdnSmem::TILE;
+  for (int i = tid; i < CH * 16; i += 256) {
+    const int r = i >> 4, c = i & 15;
+    const bool ok = r < nc;
+    const int64_t t = tc + (ok ? r : 0);
+    cpa16(base + sw<DKc>(r, c), q + (t * H + h) * DKc + c * 8, ok);
+    cpa16(base + GdnSmem::TILE + sw<DKc>(r, c), k + (t * H + h) * DKc + c * 8, ok);
+    cpa16(base + 2 * GdnSmem::TILE + sw<DKc>(r, c), v + (t * HV + hv) * DKc + c * 8, ok);
+  }
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
 
 __global__ void __launch_bounds__(256, 1) gdn_prefill_kernel(
     const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k, const __nv_bfloat16* __restrict__ v,
     const __nv_bfloat16* __restrict__ ba, int64_t ldba, const float* __restrict__ A_log,
     const __nv_bfloat16* __restrict__ dt_bias, const int32_t* __restrict__ cu, const int32_t* __restrict__ slots,
-    int n_slots, float* __restrict__ state, __nv_bfloat16* __restrict__ out, int H, int HV, float scale, int* err) {
+    int n_slots, float* __restrict__ state, const __nv_bfloat16* __restrict__ z, int64_t ldz,
+    const __nv_bfloat16* __restrict__ norm_w, __nv_bfloat16* __restrict__ y, int64_t ldy, int H, int HV, float scale,
+    float eps, int* err) {
   extern __shared__ __align__(128) uint8_t smem[];
   const uint32_t s0 = smem_u32(smem);
   float* A32 = reinterpret_cast<float*>(smem + GdnSmem::A32);
@@ -135,7 +152,7 @@ __global__ void __launch_bounds__(256, 1) gdn_prefill_kernel(
   float* sEG = sG + CH;
   float* sEGl = sEG + CH;
   float* sBeta = sEGl + CH;
-  float* sg = sBeta + CH;
+  float* sSS = sBeta + CH;  // [2][64] partial sums of squares of the output rows
 
   const int seq = blockIdx.x, hv = blockIdx.y;
   const int h = hv / (HV / H);
@@ -150,6 +167,8 @@ __global__ void __launch_bounds__(256, 1) gdn_prefill_kernel(
   float* Sg = state + ((int64_t)slot * HV + hv) * DKc * DKc;
   const float a_log = expf(A_log[hv]);
   const float dtb = bf2f(dt_bias[hv]);
+  const int n_chunks = (n + CH - 1) / CH;
+  gdn_load_chunk(s0, 0, q, k, v, t_begin, min(CH, n), h, hv, H, HV, tid);
 
   // state accumulator: warp w owns dv rows [16w, 16w+16), all 128 dk columns
   float sacc[16][4];
@@ -164,21 +183,22 @@ __global__ void __launch_bounds__(256, 1) gdn_prefill_kernel(
     sacc[nt][3] = hi.y;
   }
   store_tile_bf16<16, DKc>(smem + GdnSmem::S, sacc, warp * 16, 0, lane, 1.f);
+  const int mt = warp & 3, nh = warp >> 2;  // 64-row products: m-tile and column half
 
-  const int n_chunks = (n + CH - 1) / CH;
   for (int ch = 0; ch < n_chunks; ++ch) {
     const int tc = t_begin + ch * CH;
     const int nc = min(CH, n - ch * CH);
-    // ---------------------------------------------------------------- load Q, K, V
-    for (int i = tid; i < CH * 16; i += 256) {
-      const int r = i >> 4, c = i & 15;
-      const bool ok = r < nc;
-      const int64_t t = tc + (ok ? r : 0);
-      cpa16(s0 + GdnSmem::Q + sw<DKc>(r, c), q + (t * H + h) * DKc + c * 8, ok);
-      cpa16(s0 + GdnSmem::K + sw<DKc>(r, c), k + (t * H + h) * DKc + c * 8, ok);
-      cpa16(s0 + GdnSmem::V + sw<DKc>(r, c), v + (t * HV + hv) * DKc + c * 8, ok);
+    const int b = ch & 1;
+    const uint32_t sQ = s0 + GdnSmem::QKV + b * 3 * GdnSmem::TILE;
+    const uint32_t sK = sQ + GdnSmem::TILE, sV = sK + GdnSmem::TILE;
+    uint8_t* pK = smem + GdnSmem::QKV + b * 3 * GdnSmem::TILE + GdnSmem::TILE;
+    uint8_t* pV = pK + GdnSmem::TILE;
+    // prefetch the next chunk into the other buffer (its previous contents are dead)
+    if (ch + 1 < n_chunks) {
+      gdn_load_chunk(s0, b ^ 1, q, k, v, tc + CH, min(CH, n - (ch + 1) * CH), h, hv, H, HV, tid);
+    } else {
+      asm volatile("cp.async.commit_group;" ::: "memory");
     }
-    asm volatile("cp.async.commit_group;" ::: "memory");
     // gating (threads 0..63) and the within-chunk cumulative log decay
     if (tid < CH) {
       float gg = 0.f, bb = 0.f;
@@ -189,51 +209,31 @@ __global__ void __launch_bounds__(256, 1) gdn_prefill_kernel(
         gg = -a_log * sp;
         bb = bf16_round(1.f / (1.f + expf(-bf2f(ba[t * ldba + hv]))));
       }
-      sg[tid] = gg;
       sBeta[tid] = bb;
-      // inclusive scan within each warp, then add the first warp's total
       float x = gg;
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
-        const float y = __shfl_up_sync(0xffffffffu, x, o);
-        if (lane >= o) x += y;
+        const float yv = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += yv;
       }
       sG[tid] = x;
     }
+    asm volatile("cp.async.wait_group 1;" ::: "memory");  // this chunk's tiles have landed
     __syncthreads();
     if (tid >= 32 && tid < CH) sG[tid] += sG[31];
-    asm volatile("cp.async.wait_group 0;" ::: "memory");
     __syncthreads();
     const float G_last = sG[CH - 1];
     if (tid < CH) {
       sEG[tid] = expf(sG[tid]);
       sEGl[tid] = expf(G_last - sG[tid]);
     }
-    __syncthreads();
-
-    // ---------------------------------------------------------------- b e^G K, b V (in place)
-    for (int i = tid; i < CH * 16; i += 256) {
-      const int r = i >> 4, c = i & 15;
-      float kf[8], vf[8];
-      load_bf16x8(reinterpret_cast<const __nv_bfloat16*>(smem + GdnSmem::K + sw<DKc>(r, c)), kf);
-      load_bf16x8(reinterpret_cast<const __nv_bfloat16*>(smem + GdnSmem::V + sw<DKc>(r, c)), vf);
-      const float fk = sBeta[r] * sEG[r], fv = sBeta[r];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        kf[j] *= fk;
-        vf[j] *= fv;
-      }
-      store_bf16x8(reinterpret_cast<__nv_bfloat16*>(smem + GdnSmem::KB + sw<DKc>(r, c)), kf);
-      store_bf16x8(reinterpret_cast<__nv_bfloat16*>(smem + GdnSmem::V + sw<DKc>(r, c)), vf);
-    }
     // ---------------------------------------------------------------- K K^T -> A,  Q K^T -> P
     {
-      const int mt = warp & 3, nh = warp >> 2;
       float kk[4][4], qk[4][4];
 #pragma unroll
       for (int i = 0; i < 4; ++i) kk[i][0] = kk[i][1] = kk[i][2] = kk[i][3] = qk[i][0] = qk[i][1] = qk[i][2] = qk[i][3] = 0.f;
-      mma_tile<4, 8, DKc, DKc, false, false>(kk, s0 + GdnSmem::K, s0 + GdnSmem::K, mt * 16, nh * 32, lane);
-      mma_tile<4, 8, DKc, DKc, false, false>(qk, s0 + GdnSmem::Q, s0 + GdnSmem::K, mt * 16, nh * 32, lane);
+      mma_tile<4, 8, DKc, DKc, false, false>(kk, sK, sK, mt * 16, nh * 32, lane);
+      mma_tile<4, 8, DKc, DKc, false, false>(qk, sQ, sK, mt * 16, nh * 32, lane);
 #pragma unroll
       for (int nt = 0; nt < 4; ++nt) {
 #pragma unroll
@@ -252,20 +252,36 @@ __global__ void __launch_bounds__(256, 1) gdn_prefill_kernel(
     // ---------------------------------------------------------------- T = (I + A)^-1, blocked
     if (warp < 4) {
       // invert the unit lower-triangular diagonal block b = warp; lane j < 16 owns column j
-      const int b = warp, j = lane;
+      const int bb = warp, j = lane;
       float tcol[16];
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
         float acc = 0.f;
 #pragma unroll
         for (int kx = 0; kx < 16; ++kx) {
-          if (kx < i && j < 16 && kx >= j) acc += A32[(b * 16 + i) * LDA + b * 16 + kx] * tcol[kx];
+          if (kx < i && j < 16 && kx >= j) acc += A32[(bb * 16 + i) * LDA + bb * 16 + kx] * tcol[kx];
         }
         tcol[i] = (i == j) ? 1.f : (i > j ? -acc : 0.f);
       }
       if (j < 16) {
 #pragma unroll
-        for (int i = 0; i < 16; ++i) T32[(b * 16 + i) * LDA + b * 16 + j] = tcol[i];
+        for (int i = 0; i < 16; ++i) T32[(bb * 16 + i) * LDA + bb * 16 + j] = tcol[i];
+      }
+    } else {
+      // meanwhile: b e^G K into KB and b V in place (inputs of W and U)
+      for (int i = tid - 128; i < CH * 16; i += 128) {
+        const int r = i >> 4, c = i & 15;
+        float kf[8], vf[8];
+        load_bf16x8(reinterpret_cast<const __nv_bfloat16*>(pK + sw<DKc>(r, c)), kf);
+        load_bf16x8(reinterpret_cast<const __nv_bfloat16*>(pV + sw<DKc>(r, c)), vf);
+        const float fk = sBeta[r] * sEG[r], fv = sBeta[r];
+#pragma unroll
+        for (int jj = 0; jj < 8; ++jj) {
+          kf[jj] *= fk;
+          vf[jj] *= fv;
+        }
+        store_bf16x8(reinterpret_cast<__nv_bfloat16*>(smem + GdnSmem::KB + sw<DKc>(r, c)), kf);
+        store_bf16x8(reinterpret_cast<__nv_bfloat16*>(pV + sw<DKc>(r, c)), vf);
       }
     }
     __syncthreads();
@@ -304,7 +320,6 @@ __global__ void __launch_bounds__(256, 1) gdn_prefill_kernel(
     __syncthreads();
 
     // ---------------------------------------------------------------- W = T (b e^G K), stored negated
-    const int mt = warp & 3, nh = warp >> 2;
     {
       float w[8][4];
 #pragma unroll
@@ -318,17 +333,17 @@ __global__ void __launch_bounds__(256, 1) gdn_prefill_kernel(
       float u[8][4];
 #pragma unroll
       for (int i = 0; i < 8; ++i) u[i][0] = u[i][1] = u[i][2] = u[i][3] = 0.f;
-      mma_tile<8, 4, CH, DKc, false, true>(u, s0 + GdnSmem::T, s0 + GdnSmem::V, mt * 16, nh * 64, lane);
+      mma_tile<8, 4, CH, DKc, false, true>(u, s0 + GdnSmem::T, sV, mt * 16, nh * 64, lane);
       mma_tile<8, 8, DKc, DKc, false, false>(u, s0 + GdnSmem::W, s0 + GdnSmem::S, mt * 16, nh * 64, lane);
       store_tile_bf16<8, DKc>(smem + GdnSmem::U, u, mt * 16, nh * 64, lane, 1.f);
     }
     __syncthreads();
-    // ---------------------------------------------------------------- O; e^{G_C - G} K into KB
+    // ---------------------------------------------------------------- O, gated RMSNorm; e^{G_C - G} K into KB
     {
       float o[8][4];
 #pragma unroll
       for (int i = 0; i < 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
-      mma_tile<8, 8, DKc, DKc, false, false>(o, s0 + GdnSmem::Q, s0 + GdnSmem::S, mt * 16, nh * 64, lane);
+      mma_tile<8, 8, DKc, DKc, false, false>(o, sQ, s0 + GdnSmem::S, mt * 16, nh * 64, lane);
       const float f0 = scale * sEG[mt * 16 + g4], f1 = scale * sEG[mt * 16 + g4 + 8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
@@ -338,26 +353,55 @@ __global__ void __launch_bounds__(256, 1) gdn_prefill_kernel(
         o[i][3] *= f1;
       }
       mma_tile<8, 4, CH, DKc, false, true>(o, s0 + GdnSmem::P, s0 + GdnSmem::U, mt * 16, nh * 64, lane);
+      // o rounds to bf16 (the reference's GDN output dtype), then y = o rstd w z sigmoid(z)
+      float ss[2] = {0.f, 0.f};
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          o[i][e] = bf16_round(o[i][e]);
+          ss[e >> 1] += o[i][e] * o[i][e];
+        }
+      }
+#pragma unroll
+      for (int rr = 0; rr < 2; ++rr) {
+        ss[rr] += __shfl_xor_sync(0xffffffffu, ss[rr], 1);
+        ss[rr] += __shfl_xor_sync(0xffffffffu, ss[rr], 2);
+      }
+      if (c4 == 0) {
+        sSS[nh * CH + mt * 16 + g4] = ss[0];
+        sSS[nh * CH + mt * 16 + g4 + 8] = ss[1];
+      }
+      for (int i = tid; i < CH * 16; i += 256) {
+        const int r = i >> 4, c = i & 15;
+        float kf[8];
+        load_bf16x8(reinterpret_cast<const __nv_bfloat16*>(pK + sw<DKc>(r, c)), kf);
+        const float f = sEGl[r];
+#pragma unroll
+        for (int jj = 0; jj < 8; ++jj) kf[jj] *= f;
+        store_bf16x8(reinterpret_cast<__nv_bfloat16*>(smem + GdnSmem::KB + sw<DKc>(r, c)), kf);
+      }
+      __syncthreads();
 #pragma unroll
       for (int rr = 0; rr < 2; ++rr) {
         const int t = mt * 16 + g4 + rr * 8;
         if (t >= nc) continue;
-        __nv_bfloat16* dst = out + ((int64_t)(tc + t) * HV + hv) * DKc + nh * 64;
+        const float rstd = rsqrtf((sSS[t] + sSS[CH + t]) / (float)DKc + eps);
+        const int64_t tok = tc + t;
+        const __nv_bfloat16* zr = z + tok * ldz + (int64_t)hv * DKc + nh * 64;
+        __nv_bfloat16* dst = y + tok * ldy + (int64_t)hv * DKc + nh * 64;
 #pragma unroll
-        for (int nt = 0; nt < 8; ++nt)
-          *reinterpret_cast<uint32_t*>(dst + nt * 8 + c4 * 2) = pack_bf16x2(o[nt][rr * 2], o[nt][rr * 2 + 1]);
+        for (int nt = 0; nt < 8; ++nt) {
+          const int col = nt * 8 + c4 * 2;
+          float z0, z1, w0, w1;
+          unpack_bf16x2(*reinterpret_cast<const uint32_t*>(zr + col), z0, z1);
+          unpack_bf16x2(*reinterpret_cast<const uint32_t*>(norm_w + nh * 64 + col), w0, w1);
+          const float y0 = o[nt][rr * 2] * rstd * w0 * (z0 / (1.f + __expf(-z0)));
+          const float y1 = o[nt][rr * 2 + 1] * rstd * w1 * (z1 / (1.f + __expf(-z1)));
+          *reinterpret_cast<uint32_t*>(dst + col) = pack_bf16x2(y0, y1);
+        }
       }
     }
-    for (int i = tid; i < CH * 16; i += 256) {
-      const int r = i >> 4, c = i & 15;
-      float kf[8];
-      load_bf16x8(reinterpret_cast<const __nv_bfloat16*>(smem + GdnSmem::K + sw<DKc>(r, c)), kf);
-      const float f = sEGl[r];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) kf[j] *= f;
-      store_bf16x8(reinterpret_cast<__nv_bfloat16*>(smem + GdnSmem::KB + sw<DKc>(r, c)), kf);
-    }
-    __syncthreads();
     // ---------------------------------------------------------------- S <- e^{G_C} S + U^T (e^{G_C-G} K)
     {
       const float eC = expf(G_last);
@@ -373,6 +417,7 @@ __global__ void __launch_bounds__(256, 1) gdn_prefill_kernel(
     }
     __syncthreads();
   }
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
   // ---------------------------------------------------------------- final state, in place
 #pragma unroll
   for (int nt = 0; nt < 16; ++nt) {
@@ -388,13 +433,15 @@ using namespace qw;
 
 extern "C" int qw_gdn_prefill(const void* q, const void* k, const void* v, const void* ba, int64_t ldba,
                               const float* A_log, const void* dt_bias, const int32_t* cu_seqlens,
-                              const int32_t* slots, int64_t B, int64_t n_slots, float* state, void* out, int64_t H,
-                              int64_t HV, int64_t dk, int64_t dv, float scale, qw_stream_t stream) {
-  QW_CHECK_ARG(q && k && v && ba && A_log && dt_bias && cu_seqlens && slots && state && out, QW_ERR_ARG);
+                              const int32_t* slots, int64_t B, int64_t n_slots, float* state, const void* z,
+                              int64_t ldz, const void* norm_w, void* y, int64_t ldy, int64_t H, int64_t HV,
+                              int64_t dk, int64_t dv, float scale, float eps, qw_stream_t stream) {
+  QW_CHECK_ARG(q && k && v && ba && A_log && dt_bias && cu_seqlens && slots && state && z && norm_w && y, QW_ERR_ARG);
   QW_CHECK_ARG(B > 0 && H > 0 && HV % H == 0 && n_slots > 0, QW_ERR_ARG);
   if (dk != 128 || dv != 128) return QW_ERR_UNSUPPORTED;
   QW_CHECK_ARG(((uintptr_t)q % 16) == 0 && ((uintptr_t)k % 16) == 0 && ((uintptr_t)v % 16) == 0 &&
-                   ((uintptr_t)state % 16) == 0,
+                   ((uintptr_t)state % 16) == 0 && ((uintptr_t)z % 4) == 0 && ((uintptr_t)y % 4) == 0 &&
+                   (ldz % 2) == 0 && (ldy % 2) == 0,
                QW_ERR_ALIGN);
   auto* s = reinterpret_cast<cudaStream_t>(stream);
   static bool cfg = false;
@@ -406,7 +453,9 @@ extern "C" int qw_gdn_prefill(const void* q, const void* k, const void* v, const
   gdn_prefill_kernel<<<grid, 256, GdnSmem::TOTAL, s>>>(
       static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(k), static_cast<const __nv_bfloat16*>(v),
       static_cast<const __nv_bfloat16*>(ba), ldba, A_log, static_cast<const __nv_bfloat16*>(dt_bias), cu_seqlens,
-      slots, (int)n_slots, state, static_cast<__nv_bfloat16*>(out), (int)H, (int)HV, scale, device_error_ptr());
+      slots, (int)n_slots, state, static_cast<const __nv_bfloat16*>(z), ldz,
+      static_cast<const __nv_bfloat16*>(norm_w), static_cast<__nv_bfloat16*>(y), ldy, (int)H, (int)HV, scale, eps,
+      device_error_ptr());
   QW_LAUNCH_CHECK();
   return QW_OK;
 }

@@ -15,6 +15,7 @@
 //                    BN = M rounded up to 16, split over K to fill all SMs; fp32 partials
 //                    are summed by a small deterministic reduction kernel.
 // No TMA multicast is used (the same code runs in multi-GPU jobs).
+#include <cstdlib>
 #include <mutex>
 
 #include "common.cuh"
@@ -50,13 +51,18 @@ struct GemmParams {
   int vec_ok;          // output rows 16-byte aligned: vector stores allowed
 };
 
-constexpr int BM = 128;
-constexpr int BK = 64;  // 64 bf16 = 128 bytes = one SWIZZLE_128B row
-constexpr int kThreads = 192;
+constexpr int BM = 128;  // rows of one MMA (one TMEM accumulator)
+constexpr int BK = 64;   // 64 bf16 = 128 bytes = one SWIZZLE_128B row
 
-template <int BN, int STAGES>
+// MT = number of 128-row A sub-tiles per CTA sharing each B tile (1 or 2). MT = 2 gives a
+// 256 x BN tile: a third fewer operand bytes per FLOP than 128 x BN, at the cost of a
+// single-buffered accumulator when 2 * BN columns fill TMEM.
+template <int MT>
+constexpr int gemm_threads() { return 64 + 128 * MT; }
+
+template <int BN, int STAGES, int MT = 1>
 struct GemmSmem {
-  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int A_BYTES = MT * BM * BK * 2;
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int BAR_OFFSET = STAGES * STAGE_BYTES;
@@ -75,11 +81,13 @@ QW_DEV void decode_unit(const GemmParams& p, int unit, int& at, int& bt, int& sp
   bt = r / gsz;
 }
 
-template <int BN, int STAGES, int EPI>
-__global__ void __launch_bounds__(kThreads, 1)
+template <int BN, int STAGES, int EPI, int MT>
+__global__ void __launch_bounds__(gemm_threads<MT>(), 1)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                         const GemmParams p) {
-  using L = GemmSmem<BN, STAGES>;
+  using L = GemmSmem<BN, STAGES, MT>;
+  constexpr int NBUF = (2 * MT * BN <= 512) ? 2 : 1;  // TMEM accumulator buffers
+  constexpr int ACC = MT * BN;                        // TMEM columns of one buffer
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::BAR_OFFSET);
@@ -92,7 +100,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
   const int units = p.a_tiles * p.b_tiles * p.k_splits;
-  constexpr uint32_t TMEM_COLS = (2 * BN <= 32) ? 32 : (2 * BN <= 64) ? 64 : (2 * BN <= 128) ? 128 : (2 * BN <= 256) ? 256 : 512;
+  constexpr int NCOL = NBUF * ACC;
+  constexpr uint32_t TMEM_COLS = (NCOL <= 32) ? 32 : (NCOL <= 64) ? 64 : (NCOL <= 128) ? 128 : (NCOL <= 256) ? 256 : 512;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -101,7 +110,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], 4);  // one arrive per epilogue warp
+      mbar_init(&tempty[b], 4 * MT);  // one arrive per epilogue warp
     }
     *abort_flag = 0;
     fence_barrier_init();
@@ -133,7 +142,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint8_t* sa = smem + stage * L::STAGE_BYTES;
           uint8_t* sb = sa + L::A_BYTES;
           mbar_arrive_expect_tx(&full[stage], L::STAGE_BYTES);
-          tma_load_2d(sa, &tmA, &full[stage], kb * BK, at * BM);
+          tma_load_2d(sa, &tmA, &full[stage], kb * BK, at * (BM * MT));
           if constexpr (EPI == EPI_SWIGLU) {
             tma_load_2d(sb, &tmB, &full[stage], kb * BK, bt * (BN / 2));
             tma_load_2d(sb + (BN / 2) * BK * 2, &tmB, &full[stage], kb * BK, p.b_up_offset + bt * (BN / 2));
@@ -156,11 +165,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       decode_unit(p, u, at, bt, split);
       const int kb0 = split * p.kb_per_split;
       const int kb1 = min(p.kb_total, kb0 + p.kb_per_split);
-      const int buf = tcount & 1;
-      const uint32_t tphase = ((tcount >> 1) & 1) ^ 1;
+      const int buf = tcount % NBUF;
+      const uint32_t tphase = ((tcount / NBUF) & 1) ^ 1;
       if (!mbar_wait(&tempty[buf], tphase, abort_flag, p.err, QW_DEV_ERR_TIMEOUT_GEMM)) { ok = false; break; }
       tc_fence_after();
-      const uint32_t d_tmem = tmem_base + buf * BN;
+      const uint32_t d_tmem = tmem_base + buf * ACC;
       for (int kb = kb0; kb < kb1; ++kb) {
         if (!mbar_wait(&full[stage], phase, abort_flag, p.err, QW_DEV_ERR_TIMEOUT_GEMM)) { ok = false; break; }
         tc_fence_after();
@@ -171,8 +180,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint64_t db = umma_sdesc_sw128(sb);
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k) {
-            // advance the start address by 16 bf16 = 32 bytes inside the 128-byte swizzled row
-            umma_bf16(d_tmem, da + (uint64_t)(2 * k), db + (uint64_t)(2 * k), IDESC, (kb > kb0 || k > 0) ? 1u : 0u);
+            // advance the start address by 16 bf16 = 32 bytes inside the 128-byte swizzled row;
+            // sub-tile mt of A starts 128 rows (16 KB, 1024 descriptor units) further
+#pragma unroll
+            for (int mt = 0; mt < MT; ++mt)
+              umma_bf16(d_tmem + mt * BN, da + (uint64_t)(2 * k + mt * 1024), db + (uint64_t)(2 * k), IDESC,
+                        (kb > kb0 || k > 0) ? 1u : 0u);
           }
           umma_commit(&empty[stage]);
         }
@@ -184,18 +197,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
     }
   } else {
-    // ---------------------------------------------------------------- epilogue (warps 2..5)
-    const int q = warp & 3;  // TMEM lane quarter this warp may access
-    const int row_in_tile = q * 32 + lane;
+    // ---------------------------------------------------------------- epilogue (warps 2..)
+    const int q = warp & 3;             // TMEM lane quarter this warp may access
+    const int msub = (warp - 2) >> 2;   // which 128-row accumulator this warp drains
+    const int row_in_tile = msub * BM + q * 32 + lane;
     int tcount = 0;
     for (int u = blockIdx.x; u < units; u += gridDim.x, ++tcount) {
       int at, bt, split;
       decode_unit(p, u, at, bt, split);
-      const int buf = tcount & 1;
-      if (!mbar_wait(&tfull[buf], (tcount >> 1) & 1, abort_flag, p.err, QW_DEV_ERR_TIMEOUT_GEMM)) break;
+      const int buf = tcount % NBUF;
+      if (!mbar_wait(&tfull[buf], (tcount / NBUF) & 1, abort_flag, p.err, QW_DEV_ERR_TIMEOUT_GEMM)) break;
       tc_fence_after();
-      const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + buf * BN;
-      const int a_row = at * BM + row_in_tile;
+      const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + buf * ACC + msub * BN;
+      const int a_row = at * (BM * MT) + row_in_tile;
       const bool a_ok = a_row < p.a_rows;
       if constexpr (EPI == EPI_SWIGLU) {
         // columns [0, BN/2) = gate, [BN/2, BN) = up of output columns bt*BN/2 ...
@@ -358,10 +372,10 @@ static int num_sms() {
   return n;
 }
 
-template <int BN, int STAGES, int EPI>
+template <int BN, int STAGES, int EPI, int MT = 1>
 static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, cudaStream_t s) {
-  auto kern = gemm_tcgen05_kernel<BN, STAGES, EPI>;
-  const int smem = GemmSmem<BN, STAGES>::TOTAL;
+  auto kern = gemm_tcgen05_kernel<BN, STAGES, EPI, MT>;
+  const int smem = GemmSmem<BN, STAGES, MT>::TOTAL;
   static bool configured = false;  // one flag per instantiation
   if (!configured) {
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
@@ -369,7 +383,7 @@ static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmP
   }
   const int units = p.a_tiles * p.b_tiles * p.k_splits;
   const int grid = units < num_sms() ? units : num_sms();
-  kern<<<grid, kThreads, smem, s>>>(ta, tb, p);
+  kern<<<grid, gemm_threads<MT>(), smem, s>>>(ta, tb, p);
   QW_LAUNCH_CHECK();
   return QW_OK;
 }
@@ -395,6 +409,17 @@ static SkinnyPlan plan_skinny(int64_t M, int64_t N, int64_t K) {
 }
 
 static bool use_skinny(int64_t M) { return M <= 64; }
+
+// Rows of A per CTA for large-M GEMMs: 256 (two accumulators share each B tile) unless the
+// environment variable QW_GEMM_TILE_ROWS=128 selects the double-buffered 128-row tile.
+static int gemm_tile_rows() {
+  static int rows = 0;
+  if (rows == 0) {
+    const char* e = getenv("QW_GEMM_TILE_ROWS");
+    rows = (e && atoi(e) == 128) ? 128 : 256;
+  }
+  return rows;
+}
 
 }  // namespace qw
 
@@ -433,11 +458,16 @@ extern "C" int qw_gemm_bf16(const void* x, const void* w, void* y, int64_t M, in
     const int per16 = out_kind == QW_OUT_F32_OF_BF16 ? 4 : 8;  // elements per 16 bytes
     p.vec_ok = ((uintptr_t)y % 16) == 0 && (ldy % per16) == 0;
     constexpr int BN = 256;
-    if ((rc = make_tmap(&ta, x, M, K, ldx, BM)) != QW_OK) return rc;
+    // 256-row tiles win when the main loop is long enough to hide their single-buffered
+    // epilogue (measured on B200: K = 17408 +14%, N = 16384 +3%; SwiGLU, N = 5120 and
+    // N = 14336 with K <= 6144 lose 3-5%)
+    const bool big_tile = !swiglu && (K >= 8192 || N >= 16384);
+    const int mt = (M >= 256 && big_tile && gemm_tile_rows() == 256) ? 2 : 1;
+    if ((rc = make_tmap(&ta, x, M, K, ldx, BM * mt)) != QW_OK) return rc;
     if ((rc = make_tmap(&tb, w, N, K, ldw, swiglu ? BN / 2 : BN)) != QW_OK) return rc;
     p.a_rows = (int)M;
     p.b_rows = (int)n_out;
-    p.a_tiles = (int)((M + BM - 1) / BM);
+    p.a_tiles = (int)((M + BM * mt - 1) / (BM * mt));
     p.b_tiles = swiglu ? (int)((n_out + BN / 2 - 1) / (BN / 2)) : (int)((N + BN - 1) / BN);
     p.k_splits = 1;
     p.kb_per_split = p.kb_total;
@@ -445,6 +475,12 @@ extern "C" int qw_gemm_bf16(const void* x, const void* w, void* y, int64_t M, in
     p.b_up_offset = (int)n_out;
     p.out = y;
     p.ldo = ldy;
+    if (mt == 2) {
+      p.group = 8;
+      if (swiglu) return launch_gemm<BN, 3, EPI_SWIGLU, 2>(ta, tb, p, s);
+      if (out_kind == QW_OUT_F32_OF_BF16) return launch_gemm<BN, 3, EPI_F32, 2>(ta, tb, p, s);
+      return launch_gemm<BN, 3, EPI_BF16, 2>(ta, tb, p, s);
+    }
     if (swiglu) return launch_gemm<BN, 4, EPI_SWIGLU>(ta, tb, p, s);
     if (out_kind == QW_OUT_F32_OF_BF16) return launch_gemm<BN, 4, EPI_F32>(ta, tb, p, s);
     return launch_gemm<BN, 4, EPI_BF16>(ta, tb, p, s);

@@ -120,7 +120,6 @@ class Engine:
             qb = torch.empty(T, c.gdn_qk_dim, dtype=BF16, device=dev)
             kb = torch.empty(T, c.gdn_qk_dim, dtype=BF16, device=dev)
             vb = torch.empty(T, c.gdn_v_dim, dtype=BF16, device=dev)
-            ob = torch.empty(T, c.gdn_v_dim, dtype=BF16, device=dev)
         splits = self._decode_splits(cache.capacity)
         for i, (kind, w) in enumerate(zip(m.layer_types, m.layers)):
             if i > 0:
@@ -151,8 +150,8 @@ class Engine:
                     ops.conv_prefill(qkvz, w["conv"], cache.conv[i], md["cu"], md["slots"], md["has_initial"], B,
                                      max_len, qb, kb, vb, c.gdn_qk_dim, c.gdn_v_dim, dk)
                     ops.gdn_prefill(qb, kb, vb, ba, w["A_log"], w["dt_bias"], md["cu"], md["slots"], B,
-                                    cache.recurrent[i], ob, Hk, HV, dk, dv, dk ** -0.5)
-                    ops.gated_rmsnorm(ob, qkvz[:, c.conv_dim:], w["norm"], y, HV, dv, eps)
+                                    cache.recurrent[i], qkvz[:, c.conv_dim:], w["norm"], y, Hk, HV, dk, dv,
+                                    dk ** -0.5, eps)
                 ops.gemm(y, w["out"], hidden, ws=ws)
             ops.add_rmsnorm(hidden, resid, w["post_norm"], eps)
             ops.gemm(hidden, w["gate_up"], act, out_kind=ops.OUT_SWIGLU, ws=ws)

@@ -152,11 +152,13 @@ def conv_prefill(x, conv_w, conv_state, cu, slots, has_initial, B, max_len, q_ou
               k_out.data_ptr(), v_out.data_ptr(), qk_dim, v_dim, head_dim, _stream())
 
 
-def gdn_prefill(q, k, v, ba, A_log, dt_bias, cu, slots, B, state, out, H, HV, dk, dv, scale):
+def gdn_prefill(q, k, v, ba, A_log, dt_bias, cu, slots, B, state, z, norm_w, y, H, HV, dk, dv, scale, eps):
+    """Chunked delta rule + gated RMSNorm: y = norm(o) * w * silu(z), o never leaves the SM."""
     LAUNCHES[0] += 1
     _lib.call("qw_gdn_prefill", q.data_ptr(), k.data_ptr(), v.data_ptr(), ba.data_ptr(), ba.stride(0),
               A_log.data_ptr(), dt_bias.data_ptr(), cu.data_ptr(), slots.data_ptr(), B, state.shape[0],
-              state.data_ptr(), out.data_ptr(), H, HV, dk, dv, scale, _stream())
+              state.data_ptr(), z.data_ptr(), z.stride(0), norm_w.data_ptr(), y.data_ptr(), y.stride(0), H, HV, dk,
+              dv, scale, eps, _stream())
 
 
 def gdn_decode(qkvz, ba, conv_w, conv_state, state, slots, B, A_log, dt_bias, norm_w, y, H, HV, dk, dv, eps):

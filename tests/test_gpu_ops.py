@@ -215,11 +215,14 @@ def test_gdn_prefill_chunked(K, lens):
     for n in lens:
         cu.append(cu[-1] + n)
     T = cu[-1]
+    zbuf = bf(torch.randn(T, 2 * HV * dk, generator=g))  # z is a strided view, as in the qkvz buffer
+    norm_w = bf(torch.randn(dk, generator=g) * 0.3 + 1)
     sd = state.to(DEV)
-    out = torch.empty(T, HV * dk, dtype=torch.bfloat16, device=DEV)
+    y = torch.empty(T, HV * dk, dtype=torch.bfloat16, device=DEV)
     t32 = lambda a: torch.tensor(a, dtype=torch.int32, device=DEV)
+    zd = zbuf.to(DEV)[:, HV * dk:]
     K.gdn_prefill(q.to(DEV), k.to(DEV), v.to(DEV), ba.to(DEV), A_log.to(DEV), dt.to(DEV), t32(cu), t32(slots),
-                  len(lens), sd, out, H, HV, dk, dk, dk ** -0.5)
+                  len(lens), sd, zd, norm_w.to(DEV), y, H, HV, dk, dk, dk ** -0.5, 1e-6)
     gg, beta = O.gdn_gating(A_log, ba[:, HV:], ba[:, :HV], dt, O.bf16)
     exp_state = state.clone()
     exp_o = torch.empty(T, HV, dk)
@@ -227,17 +230,20 @@ def test_gdn_prefill_chunked(K, lens):
         a0, a1 = cu[i], cu[i + 1]
         exp_o[a0:a1], exp_state[s] = O.gdn_recurrence(q[a0:a1], k[a0:a1], v[a0:a1], gg[a0:a1], beta[a0:a1],
                                                       state[s], dk ** -0.5, HV // H)
-    # chunk products use bf16 operands (as the reference's chunked kernel): compare with a
-    # tolerance relative to the output scale
-    got, exp = out.cpu().float().view(T, HV, dk), O.bf16(exp_o)
-    scale = exp.abs().amax(dim=-1, keepdim=True).clamp_min(1e-3)
-    err = ((got - exp).abs() / scale).max().item()
+    exp_y = O.gated_rmsnorm(O.bf16(exp_o).reshape(-1, dk), norm_w, zbuf[:, HV * dk:].reshape(-1, dk), 1e-6,
+                            O.bf16).reshape(T, HV, dk)
+    # the chunk products use bf16 operands (like the reference's chunked kernel), so the
+    # comparison is relative to each head's output scale
+    got = y.cpu().float().view(T, HV, dk)
+    scale = exp_y.abs().amax(dim=-1, keepdim=True).clamp_min(1e-3)
+    err = ((got - exp_y).abs() / scale).max().item()
     assert err < 3e-2, f"relative output error {err}"
     serr = ((sd.cpu() - exp_state).abs().max() / exp_state.abs().max()).item()
     assert serr < 2e-2, f"relative state error {serr}"
     untouched = [s for s in range(len(lens) + 1) if s not in slots]
     for s in untouched:
         assert torch.equal(sd.cpu()[s], state[s])
+    print("gdn chunked: max relative output error", round(err, 5), "state", round(serr, 6))
 
 
 def test_gdn_decode_fused(K):
