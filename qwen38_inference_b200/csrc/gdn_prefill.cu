@@ -117,7 +117,9 @@ struct GdnSmem {
   static constexpr int T = P + CH * CH * 2;
   static constexpr int X32 = T + CH * CH * 2;     // 3 x 16 x 16 fp32 scratch
   static constexpr int VEC = X32 + 3 * 256 * 4;   // G, eG, eGl, beta: 4 x 64 fp32; row sums 2 x 64
-  static constexpr int TOTAL = VEC + 6 * CH * 4;
+  static constexpr int ZLD = DKc + 8;             // padded row of the z tile (bf16)
+  static constexpr int Z = VEC + 6 * CH * 4;      // z rows of the chunk [64][ZLD] bf16
+  static constexpr int TOTAL = Z + CH * ZLD * 2;
 };
 static_assert(GdnSmem::R_BYTES >= 2 * GdnSmem::TILE, "W and U must fit in the inverse's scratch");
 
@@ -169,6 +171,10 @@ __global__ void __launch_bounds__(256, 1) gdn_prefill_kernel(
   const float dtb = bf2f(dt_bias[hv]);
   const int n_chunks = (n + CH - 1) / CH;
   gdn_load_chunk(s0, 0, q, k, v, t_begin, min(CH, n), h, hv, H, HV, tid);
+  const __nv_bfloat16* zrow = z + (int64_t)hv * DKc;
+  uint32_t wpair[8];  // norm weight pairs of this thread's output columns
+#pragma unroll
+  for (int nt = 0; nt < 8; ++nt) wpair[nt] = *reinterpret_cast<const uint32_t*>(norm_w + (warp >> 2) * 64 + nt * 8 + (lane & 3) * 2);
 
   // state accumulator: warp w owns dv rows [16w, 16w+16), all 128 dk columns
   float sacc[16][4];
@@ -193,7 +199,14 @@ __global__ void __launch_bounds__(256, 1) gdn_prefill_kernel(
     const uint32_t sK = sQ + GdnSmem::TILE, sV = sK + GdnSmem::TILE;
     uint8_t* pK = smem + GdnSmem::QKV + b * 3 * GdnSmem::TILE + GdnSmem::TILE;
     uint8_t* pV = pK + GdnSmem::TILE;
-    // prefetch the next chunk into the other buffer (its previous contents are dead)
+    // z rows of this chunk (consumed by the epilogue), then the next chunk's q/k/v into the
+    // other buffer (its previous contents are dead)
+    for (int i = tid; i < CH * 16; i += 256) {
+      const int r = i >> 4, c = i & 15;
+      const bool ok = r < nc;
+      cpa16(s0 + GdnSmem::Z + (uint32_t)(r * GdnSmem::ZLD + c * 8) * 2, zrow + (int64_t)(tc + (ok ? r : 0)) * ldz + c * 8, ok);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
     if (ch + 1 < n_chunks) {
       gdn_load_chunk(s0, b ^ 1, q, k, v, tc + CH, min(CH, n - (ch + 1) * CH), h, hv, H, HV, tid);
     } else {
@@ -218,7 +231,7 @@ __global__ void __launch_bounds__(256, 1) gdn_prefill_kernel(
       }
       sG[tid] = x;
     }
-    asm volatile("cp.async.wait_group 1;" ::: "memory");  // this chunk's tiles have landed
+    asm volatile("cp.async.wait_group 2;" ::: "memory");  // this chunk's q/k/v tiles have landed
     __syncthreads();
     if (tid >= 32 && tid < CH) sG[tid] += sG[31];
     __syncthreads();
@@ -381,21 +394,23 @@ __global__ void __launch_bounds__(256, 1) gdn_prefill_kernel(
         for (int jj = 0; jj < 8; ++jj) kf[jj] *= f;
         store_bf16x8(reinterpret_cast<__nv_bfloat16*>(smem + GdnSmem::KB + sw<DKc>(r, c)), kf);
       }
+      asm volatile("cp.async.wait_group 1;" ::: "memory");  // this chunk's z rows
       __syncthreads();
+      const __nv_bfloat16* sZ = reinterpret_cast<const __nv_bfloat16*>(smem + GdnSmem::Z);
 #pragma unroll
       for (int rr = 0; rr < 2; ++rr) {
         const int t = mt * 16 + g4 + rr * 8;
         if (t >= nc) continue;
         const float rstd = rsqrtf((sSS[t] + sSS[CH + t]) / (float)DKc + eps);
         const int64_t tok = tc + t;
-        const __nv_bfloat16* zr = z + tok * ldz + (int64_t)hv * DKc + nh * 64;
+        const __nv_bfloat16* zr = sZ + t * GdnSmem::ZLD + nh * 64;
         __nv_bfloat16* dst = y + tok * ldy + (int64_t)hv * DKc + nh * 64;
 #pragma unroll
         for (int nt = 0; nt < 8; ++nt) {
           const int col = nt * 8 + c4 * 2;
           float z0, z1, w0, w1;
           unpack_bf16x2(*reinterpret_cast<const uint32_t*>(zr + col), z0, z1);
-          unpack_bf16x2(*reinterpret_cast<const uint32_t*>(norm_w + nh * 64 + col), w0, w1);
+          unpack_bf16x2(wpair[nt], w0, w1);
           const float y0 = o[nt][rr * 2] * rstd * w0 * (z0 / (1.f + __expf(-z0)));
           const float y1 = o[nt][rr * 2 + 1] * rstd * w1 * (z1 / (1.f + __expf(-z1)));
           *reinterpret_cast<uint32_t*>(dst + col) = pack_bf16x2(y0, y1);
@@ -440,8 +455,8 @@ extern "C" int qw_gdn_prefill(const void* q, const void* k, const void* v, const
   QW_CHECK_ARG(B > 0 && H > 0 && HV % H == 0 && n_slots > 0, QW_ERR_ARG);
   if (dk != 128 || dv != 128) return QW_ERR_UNSUPPORTED;
   QW_CHECK_ARG(((uintptr_t)q % 16) == 0 && ((uintptr_t)k % 16) == 0 && ((uintptr_t)v % 16) == 0 &&
-                   ((uintptr_t)state % 16) == 0 && ((uintptr_t)z % 4) == 0 && ((uintptr_t)y % 4) == 0 &&
-                   (ldz % 2) == 0 && (ldy % 2) == 0,
+                   ((uintptr_t)state % 16) == 0 && ((uintptr_t)y % 4) == 0 &&
+                   ((uintptr_t)z % 16) == 0 && (ldz % 8) == 0 && (ldy % 2) == 0,
                QW_ERR_ALIGN);
   auto* s = reinterpret_cast<cudaStream_t>(stream);
   static bool cfg = false;

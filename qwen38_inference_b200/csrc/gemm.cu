@@ -307,6 +307,212 @@ __global__ void __launch_bounds__(gemm_threads<MT>(), 1)
   }
 }
 
+// ------------------------------------------------------------------ CTA-pair GEMM (cta_group::2)
+// A cluster of 2 CTAs computes a 256 x 256 output tile with M=256 tcgen05.mma issued by the
+// pair leader: CTA r stages A rows [128r, 128r+128) and B rows [128r, 128r+128) of the tile
+// (32 KB per k-block instead of 48 KB for a 128 x 256 tile per CTA) and receives output rows
+// [128r, 128r+128) x 256 in its own TMEM, double-buffered. Both CTAs' TMA loads complete on
+// the leader's full barrier; the leader's MMA commits arrive on both CTAs' empty / tmem-full
+// barriers; both epilogues release the accumulator on the leader's tmem-empty barrier.
+// SwiGLU: CTA 0 stages the gate rows and CTA 1 the matching up rows, so accumulator columns
+// [0,128) are gate and [128,256) up, exactly as in the single-CTA kernel.
+constexpr int P_BN = 256, P_STAGES = 6;
+constexpr int P_A_BYTES = BM * BK * 2, P_B_BYTES = (P_BN / 2) * BK * 2, P_STAGE = P_A_BYTES + P_B_BYTES;
+constexpr int P_BAR = P_STAGES * P_STAGE;
+constexpr int P_SMEM = P_BAR + 256 + 1024;
+
+template <int EPI>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     const GemmParams p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + P_BAR);
+  uint64_t* empty = full + P_STAGES;
+  uint64_t* tfull = empty + P_STAGES;  // [2]
+  uint64_t* tempty = tfull + 2;        // [2], used in the leader
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+  const int units = p.a_tiles * p.b_tiles;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < P_STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 8);  // 4 epilogue warps in each CTA
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, 512);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync_all();  // barriers initialized and TMEM allocated in both CTAs
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- TMA producer (both CTAs)
+    if (elect_one()) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int u = pair; u < units && ok; u += npairs) {
+        int at, bt, split;
+        decode_unit(p, u, at, bt, split);
+        for (int kb = 0; kb < p.kb_total; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, p.err, QW_DEV_ERR_TIMEOUT_GEMM)) { ok = false; break; }
+          uint8_t* sa = smem + stage * P_STAGE;
+          uint8_t* sb = sa + P_A_BYTES;
+          const uint32_t bar = mapa_shared(smem_u32(&full[stage]), 0);
+          if (leader) mbar_arrive_expect_tx(&full[stage], 2 * P_STAGE);
+          tma_load_2d_pair(sa, &tmA, bar, kb * BK, at * 256 + (int)rank * BM);
+          if constexpr (EPI == EPI_SWIGLU) {
+            tma_load_2d_pair(sb, &tmB, bar, kb * BK, (rank ? p.b_up_offset : 0) + bt * (P_BN / 2));
+          } else {
+            tma_load_2d_pair(sb, &tmB, bar, kb * BK, bt * P_BN + (int)rank * (P_BN / 2));
+          }
+          if (++stage == P_STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer (leader only)
+    if (leader) {
+      constexpr uint32_t IDESC = umma_idesc_bf16(256, P_BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int tcount = 0;
+      bool ok = true;
+      for (int u = pair; u < units && ok; u += npairs, ++tcount) {
+        const int buf = tcount & 1;
+        if (!mbar_wait(&tempty[buf], ((tcount >> 1) & 1) ^ 1, abort_flag, p.err, QW_DEV_ERR_TIMEOUT_GEMM)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + buf * P_BN;
+        for (int kb = 0; kb < p.kb_total; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag, p.err, QW_DEV_ERR_TIMEOUT_GEMM)) { ok = false; break; }
+          tc_fence_after();
+          if (elect_one()) {
+            const uint32_t sa = smem_u32(smem + stage * P_STAGE);
+            const uint64_t da = umma_sdesc_sw128(sa);
+            const uint64_t db = umma_sdesc_sw128(sa + P_A_BYTES);
+#pragma unroll
+            for (int k = 0; k < BK / 16; ++k)
+              umma_bf16_pair(d_tmem, da + (uint64_t)(2 * k), db + (uint64_t)(2 * k), IDESC, (kb > 0 || k > 0) ? 1u : 0u);
+            umma_commit_pair(&empty[stage], 0x3);
+          }
+          __syncwarp();
+          if (++stage == P_STAGES) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) break;
+        if (elect_one()) umma_commit_pair(&tfull[buf], 0x3);
+        __syncwarp();
+      }
+    }
+  } else {
+    // ---------------------------------------------------------------- epilogue (warps 2..5, both CTAs)
+    const int q = warp & 3;
+    const int row_in_tile = (int)rank * BM + q * 32 + lane;
+    const uint32_t tempty_leader0 = mapa_shared(smem_u32(&tempty[0]), 0);
+    int tcount = 0;
+    for (int u = pair; u < units; u += npairs, ++tcount) {
+      int at, bt, split;
+      decode_unit(p, u, at, bt, split);
+      const int buf = tcount & 1;
+      if (!mbar_wait(&tfull[buf], (tcount >> 1) & 1, abort_flag, p.err, QW_DEV_ERR_TIMEOUT_GEMM)) break;
+      tc_fence_after();
+      const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + buf * P_BN;
+      const int a_row = at * 256 + row_in_tile;
+      const bool a_ok = a_row < p.a_rows;
+      if constexpr (EPI == EPI_SWIGLU) {
+        __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.out);
+#pragma unroll 1
+        for (int c = 0; c < P_BN / 2; c += 32) {
+          uint32_t g[32], v[32];
+          tmem_ld_32x32b_x32(t_row + c, g);
+          tmem_ld_32x32b_x32(t_row + P_BN / 2 + c, v);
+          tmem_ld_wait();
+          const int col0 = bt * (P_BN / 2) + c;
+          if (a_ok) {
+            float f[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const float gg = bf16_round(__uint_as_float(g[j]));
+              const float uu = bf16_round(__uint_as_float(v[j]));
+              f[j] = gg / (1.0f + expf(-gg)) * uu;
+            }
+            const int ncols = p.b_rows - col0;
+            __nv_bfloat16* dst = out + (int64_t)a_row * p.ldo + col0;
+            if (ncols >= 32 && p.vec_ok) {
+#pragma unroll
+              for (int j = 0; j < 32; j += 8) store_bf16x8(dst + j, f + j);
+            } else {
+              for (int j = 0; j < ncols && j < 32; ++j) dst[j] = f2bf(f[j]);
+            }
+          }
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < P_BN; c += 32) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(t_row + c, r);
+          tmem_ld_wait();
+          if (!a_ok) continue;
+          const int b0 = bt * P_BN + c;
+          const int nb = min(32, p.b_rows - b0);
+          if (nb <= 0) continue;
+          if constexpr (EPI == EPI_BF16) {
+            __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.out) + (int64_t)a_row * p.ldo + b0;
+            float f[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(r[j]);
+            if (nb == 32 && p.vec_ok) {
+#pragma unroll
+              for (int j = 0; j < 32; j += 8) store_bf16x8(dst + j, f + j);
+            } else {
+              for (int j = 0; j < nb; ++j) dst[j] = f2bf(f[j]);
+            }
+          } else {
+            float* dst = reinterpret_cast<float*>(p.out) + (int64_t)a_row * p.ldo + b0;
+            if (nb == 32 && p.vec_ok) {
+#pragma unroll
+              for (int j = 0; j < 32; j += 4)
+                *reinterpret_cast<float4*>(dst + j) =
+                    make_float4(bf16_round(__uint_as_float(r[j])), bf16_round(__uint_as_float(r[j + 1])),
+                                bf16_round(__uint_as_float(r[j + 2])), bf16_round(__uint_as_float(r[j + 3])));
+            } else {
+              for (int j = 0; j < nb; ++j) dst[j] = bf16_round(__uint_as_float(r[j]));
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(tempty_leader0 + buf * 8);  // the leader's tempty[buf]
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // no MMA or TMEM read in flight in either CTA
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, 512);
+  }
+}
+
 // Sum of split-K partials ws[s][m][n] (s = 0..splits-1 in order), then the output rounding.
 template <int EPI>
 __global__ void splitk_reduce_kernel(const float* __restrict__ ws, void* out, int M, int N_out, int64_t ldo,
@@ -388,6 +594,33 @@ static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmP
   return QW_OK;
 }
 
+template <int EPI>
+static int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, cudaStream_t s) {
+  auto kern = gemm_pair_kernel<EPI>;
+  static bool configured = false;
+  if (!configured) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, P_SMEM);
+    configured = true;
+  }
+  const int units = p.a_tiles * p.b_tiles;
+  int grid = 2 * units;
+  const int max_ctas = (num_sms() / 2) * 2;
+  if (grid > max_ctas) grid = max_ctas;
+  kern<<<grid, 192, P_SMEM, s>>>(ta, tb, p);
+  QW_LAUNCH_CHECK();
+  return QW_OK;
+}
+
+// CTA-pair GEMM for large M unless QW_GEMM_PAIR=0 selects the single-CTA kernels.
+static bool gemm_use_pairs() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("QW_GEMM_PAIR");
+    v = (e && atoi(e) == 0) ? 0 : 1;
+  }
+  return v == 1;
+}
+
 struct SkinnyPlan {
   int bn, b_tiles, a_tiles, splits, kb_per_split, kb_total;
 };
@@ -458,6 +691,24 @@ extern "C" int qw_gemm_bf16(const void* x, const void* w, void* y, int64_t M, in
     const int per16 = out_kind == QW_OUT_F32_OF_BF16 ? 4 : 8;  // elements per 16 bytes
     p.vec_ok = ((uintptr_t)y % 16) == 0 && (ldy % per16) == 0;
     constexpr int BN = 256;
+    if (M >= 256 && gemm_use_pairs()) {
+      if ((rc = make_tmap(&ta, x, M, K, ldx, BM)) != QW_OK) return rc;
+      if ((rc = make_tmap(&tb, w, N, K, ldw, P_BN / 2)) != QW_OK) return rc;
+      p.a_rows = (int)M;
+      p.b_rows = (int)n_out;
+      p.a_tiles = (int)((M + 255) / 256);
+      p.b_tiles = swiglu ? (int)((n_out + P_BN / 2 - 1) / (P_BN / 2)) : (int)((N + P_BN - 1) / P_BN);
+      p.k_splits = 1;
+      p.kb_per_split = p.kb_total;
+      p.swap = 0;
+      p.group = 8;
+      p.b_up_offset = (int)n_out;
+      p.out = y;
+      p.ldo = ldy;
+      if (swiglu) return launch_pair<EPI_SWIGLU>(ta, tb, p, s);
+      if (out_kind == QW_OUT_F32_OF_BF16) return launch_pair<EPI_F32>(ta, tb, p, s);
+      return launch_pair<EPI_BF16>(ta, tb, p, s);
+    }
     // 256-row tiles win when the main loop is long enough to hide their single-buffered
     // epilogue (measured on B200: K = 17408 +14%, N = 16384 +3%; SwiGLU, N = 5120 and
     // N = 14336 with K <= 6144 lose 3-5%)
