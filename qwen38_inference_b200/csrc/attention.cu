@@ -17,6 +17,34 @@
 namespace qw {
 
 // ============================================================== q/k norm + rope + kv store
+// E consecutive bf16 per lane moved as one vector (E = 8: 16 bytes, 4: 8 bytes, 2: 4 bytes)
+template <int E>
+QW_DEV void ld_vec(const __nv_bfloat16* p, float* f) {
+  if constexpr (E == 8) {
+    load_bf16x8(p, f);
+  } else if constexpr (E == 4) {
+    const uint2 u = *reinterpret_cast<const uint2*>(p);
+    unpack_bf16x2(u.x, f[0], f[1]);
+    unpack_bf16x2(u.y, f[2], f[3]);
+  } else {
+    unpack_bf16x2(*reinterpret_cast<const uint32_t*>(p), f[0], f[1]);
+  }
+}
+template <int E>
+QW_DEV void st_vec(__nv_bfloat16* p, const float* f) {
+  if constexpr (E == 8) {
+    store_bf16x8(p, f);
+  } else if constexpr (E == 4) {
+    uint2 u;
+    u.x = pack_bf16x2(f[0], f[1]);
+    u.y = pack_bf16x2(f[2], f[3]);
+    *reinterpret_cast<uint2*>(p) = u;
+  } else {
+    *reinterpret_cast<uint32_t*>(p) = pack_bf16x2(f[0], f[1]);
+  }
+}
+
+// One warp per (token, head); lane owns E = D/32 consecutive dims.
 template <int D>
 __global__ void qk_norm_rope_store_kernel(__nv_bfloat16* __restrict__ qkv, int64_t ldq, int nq, int nkv,
                                           const __nv_bfloat16* __restrict__ q_w, const __nv_bfloat16* __restrict__ k_w,
@@ -37,11 +65,8 @@ __global__ void qk_norm_rope_store_kernel(__nv_bfloat16* __restrict__ qkv, int64
   const __nv_bfloat16* wt = is_k ? k_w : q_w;
   const int c0 = lane * E;
   float x[E], w[E];
-#pragma unroll
-  for (int j = 0; j < E; ++j) {
-    x[j] = bf2f(src[c0 + j]);
-    w[j] = bf2f(wt[c0 + j]);
-  }
+  ld_vec<E>(src + c0, x);
+  ld_vec<E>(wt + c0, w);
   float ss = 0.f;
 #pragma unroll
   for (int j = 0; j < E; ++j) ss += x[j] * x[j];
@@ -59,23 +84,23 @@ __global__ void qk_norm_rope_store_kernel(__nv_bfloat16* __restrict__ qkv, int64
     pos = 0;
   }
   float o[E];
+  float partner[E];
 #pragma unroll
-  for (int j = 0; j < E; ++j) {
-    const float partner = __shfl_sync(0xffffffffu, xn[j], (c0 < half) ? lane + off : lane - off);
-    const int c = c0 + j;
-    if (c < half) {
-      const float cs = rope[(int64_t)pos * rd + c], sn = rope[(int64_t)pos * rd + half + c];
-      o[j] = xn[j] * cs - partner * sn;
-    } else if (c < rd) {
-      const float cs = rope[(int64_t)pos * rd + c - half], sn = rope[(int64_t)pos * rd + c];
-      o[j] = xn[j] * cs + partner * sn;
-    } else {
-      o[j] = xn[j];
-    }
+  for (int j = 0; j < E; ++j) partner[j] = __shfl_sync(0xffffffffu, xn[j], (c0 < half) ? lane + off : lane - off);
+  if (c0 < rd) {
+    // this lane's E dims are all rotary (rd is a multiple of 2E); cos/sin index = dim mod half
+    const int ci = c0 < half ? c0 : c0 - half;
+    const float* cs = rope + (int64_t)pos * rd + ci;
+    const float* sn = cs + half;
+    const float sign = c0 < half ? -1.f : 1.f;
+#pragma unroll
+    for (int j = 0; j < E; ++j) o[j] = xn[j] * cs[j] + sign * partner[j] * sn[j];
+  } else {
+#pragma unroll
+    for (int j = 0; j < E; ++j) o[j] = xn[j];
   }
   if (!is_k) {
-#pragma unroll
-    for (int j = 0; j < E; ++j) src[c0 + j] = f2bf(o[j]);
+    st_vec<E>(src + c0, o);
     return;
   }
   const int64_t loc = locs[t];
@@ -84,13 +109,14 @@ __global__ void qk_norm_rope_store_kernel(__nv_bfloat16* __restrict__ qkv, int64
     return;
   }
   if (loc == 0) return;  // reserved row, skipped like the reference store (REF:2683)
-  __nv_bfloat16* kd = kc + (loc * nkv + kh) * D;
-  __nv_bfloat16* vd = vc + (loc * nkv + kh) * D;
   const __nv_bfloat16* vs = row + (int64_t)2 * nq * D + (int64_t)nkv * D + kh * D;
-#pragma unroll
-  for (int j = 0; j < E; ++j) {
-    kd[c0 + j] = f2bf(o[j]);
-    vd[c0 + j] = vs[c0 + j];
+  st_vec<E>(kc + (loc * nkv + kh) * D + c0, o);
+  if constexpr (E == 8) {
+    *reinterpret_cast<uint4*>(vc + (loc * nkv + kh) * D + c0) = *reinterpret_cast<const uint4*>(vs + c0);
+  } else {
+    float vv[E];
+    ld_vec<E>(vs + c0, vv);
+    st_vec<E>(vc + (loc * nkv + kh) * D + c0, vv);
   }
 }
 

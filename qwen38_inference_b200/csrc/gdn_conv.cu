@@ -64,21 +64,33 @@ __global__ void __launch_bounds__(256) conv_prefill_kernel(
 #pragma unroll
     for (int i = 0; i < HIST; ++i) st[tid * (W - 1) + i] = ns[i];
   }
-  // ---- convolution: thread = (channel, half of the tokens)
+  // ---- convolution: thread = (channel pair, quarter of the tokens). Products are
+  // bf16 x bf16 rounded to bf16 (mul.rn.bf16x2, as the reference's bf16 multiply), summed in
+  // fp32 in tap order; silu uses the approximate divide of the reference's Triton kernels.
   {
-    const int c = tid & (BC - 1), half = tid >> 7;
-    const float w0 = bf2f(w[(int64_t)(c0 + c) * W + 0]), w1 = bf2f(w[(int64_t)(c0 + c) * W + 1]);
-    const float w2 = bf2f(w[(int64_t)(c0 + c) * W + 2]), w3 = bf2f(w[(int64_t)(c0 + c) * W + 3]);
-    const int j0 = half * (BT / 2);
-    float h0 = bf2f(sx[j0][c]), h1 = bf2f(sx[j0 + 1][c]), h2 = bf2f(sx[j0 + 2][c]);
-    for (int j = j0; j < j0 + BT / 2 && j < nt; ++j) {
-      const float xv = bf2f(sx[j + HIST][c]);
-      float acc = 0.f;
-      acc += bf16_round(h0 * w0);
-      acc += bf16_round(h1 * w1);
-      acc += bf16_round(h2 * w2);
-      acc += bf16_round(xv * w3);
-      sy[j][c] = f2bf(acc / (1.0f + __expf(-acc)));
+    const int cp = tid & (BC / 2 - 1), quarter = tid >> 6;
+    const int c = 2 * cp;
+    __nv_bfloat162 wv[W];
+#pragma unroll
+    for (int j = 0; j < W; ++j)
+      wv[j] = __halves2bfloat162(w[(int64_t)(c0 + c) * W + j], w[(int64_t)(c0 + c + 1) * W + j]);
+    const int j0 = quarter * (BT / 4);
+    __nv_bfloat162 h0 = *reinterpret_cast<const __nv_bfloat162*>(&sx[j0][c]);
+    __nv_bfloat162 h1 = *reinterpret_cast<const __nv_bfloat162*>(&sx[j0 + 1][c]);
+    __nv_bfloat162 h2 = *reinterpret_cast<const __nv_bfloat162*>(&sx[j0 + 2][c]);
+    for (int j = j0; j < j0 + BT / 4 && j < nt; ++j) {
+      const __nv_bfloat162 xv = *reinterpret_cast<const __nv_bfloat162*>(&sx[j + HIST][c]);
+      const float2 p0 = __bfloat1622float2(__hmul2(h0, wv[0]));
+      const float2 p1 = __bfloat1622float2(__hmul2(h1, wv[1]));
+      const float2 p2 = __bfloat1622float2(__hmul2(h2, wv[2]));
+      const float2 p3 = __bfloat1622float2(__hmul2(xv, wv[3]));
+      float a0 = 0.f, a1 = 0.f;
+      a0 += p0.x; a1 += p0.y;
+      a0 += p1.x; a1 += p1.y;
+      a0 += p2.x; a1 += p2.y;
+      a0 += p3.x; a1 += p3.y;
+      *reinterpret_cast<__nv_bfloat162*>(&sy[j][c]) =
+          __floats2bfloat162_rn(__fdividef(a0, 1.0f + __expf(-a0)), __fdividef(a1, 1.0f + __expf(-a1)));
       h0 = h1;
       h1 = h2;
       h2 = xv;

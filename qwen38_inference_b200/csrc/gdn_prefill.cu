@@ -116,18 +116,19 @@ struct GdnSmem {
   static constexpr int P = S + 2 * TILE;          // [t][s] bf16, 8 KB
   static constexpr int T = P + CH * CH * 2;
   static constexpr int X32 = T + CH * CH * 2;     // 3 x 16 x 16 fp32 scratch
-  static constexpr int VEC = X32 + 3 * 256 * 4;   // G, eG, eGl, beta: 4 x 64 fp32; row sums 2 x 64
+  static constexpr int VEC = X32 + 3 * 256 * 4;   // G, eG, eGl, beta: 4 x 64 fp32; row sums 4 x 64
   static constexpr int ZLD = DKc + 8;             // padded row of the z tile (bf16)
-  static constexpr int Z = VEC + 6 * CH * 4;      // z rows of the chunk [64][ZLD] bf16
+  static constexpr int Z = VEC + 8 * CH * 4;      // z rows of the chunk [64][ZLD] bf16
   static constexpr int TOTAL = Z + CH * ZLD * 2;
 };
 static_assert(GdnSmem::R_BYTES >= 2 * GdnSmem::TILE, "W and U must fit in the inverse's scratch");
 
 // Issue the loads of chunk `ch` (rows beyond the request are zero-filled) into buffer `b`.
+template <int NTHR>
 QW_DEV void gdn_load_chunk(uint32_t s0, int b, const __nv_bfloat16* q, const __nv_bfloat16* k,
                            const __nv_bfloat16* v, int64_t tc, int nc, int h, int hv, int H, int HV, int tid) {
   const uint32_t base = s0 + GdnSmem::QKV + b * 3 * GdnSmem::TILE;
-  for (int i = tid; i < CH * 16; i += 256) {
+  for (int i = tid; i < CH * 16; i += NTHR) {
     const int r = i >> 4, c = i & 15;
     const bool ok = r < nc;
     const int64_t t = tc + (ok ? r : 0);
@@ -138,7 +139,10 @@ QW_DEV void gdn_load_chunk(uint32_t s0, int b, const __nv_bfloat16* q, const __n
   asm volatile("cp.async.commit_group;" ::: "memory");
 }
 
-__global__ void __launch_bounds__(256, 1) gdn_prefill_kernel(
+// NW warps per CTA (8 or 16): the 64-row products are split into 4 m-tiles x NW/4 column
+// groups, the 128 x 128 state into 8 m-tiles x NW/8 column groups.
+template <int NW>
+__global__ void __launch_bounds__(NW * 32, 1) gdn_prefill_kernel(
     const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k, const __nv_bfloat16* __restrict__ v,
     const __nv_bfloat16* __restrict__ ba, int64_t ldba, const float* __restrict__ A_log,
     const __nv_bfloat16* __restrict__ dt_bias, const int32_t* __restrict__ cu, const int32_t* __restrict__ slots,
@@ -154,7 +158,12 @@ __global__ void __launch_bounds__(256, 1) gdn_prefill_kernel(
   float* sEG = sG + CH;
   float* sEGl = sEG + CH;
   float* sBeta = sEGl + CH;
-  float* sSS = sBeta + CH;  // [2][64] partial sums of squares of the output rows
+  float* sSS = sBeta + CH;  // [NW/4][64] partial sums of squares of the output rows
+  constexpr int NT_ = NW * 32;          // threads
+  constexpr int NQ = NW / 4;            // column groups of the 64-row products
+  constexpr int KK_NT = 8 / NQ;         // n-tiles per warp, 64-column outputs
+  constexpr int V_NT = 16 / NQ;         // n-tiles per warp, 128-column outputs
+  constexpr int S_NT = 16 / (NW / 8);   // n-tiles per warp of the state
 
   const int seq = blockIdx.x, hv = blockIdx.y;
   const int h = hv / (HV / H);
@@ -170,26 +179,28 @@ __global__ void __launch_bounds__(256, 1) gdn_prefill_kernel(
   const float a_log = expf(A_log[hv]);
   const float dtb = bf2f(dt_bias[hv]);
   const int n_chunks = (n + CH - 1) / CH;
-  gdn_load_chunk(s0, 0, q, k, v, t_begin, min(CH, n), h, hv, H, HV, tid);
+  gdn_load_chunk<NT_>(s0, 0, q, k, v, t_begin, min(CH, n), h, hv, H, HV, tid);
   const __nv_bfloat16* zrow = z + (int64_t)hv * DKc;
-  uint32_t wpair[8];  // norm weight pairs of this thread's output columns
+  const int mt = warp & 3, nh = warp >> 2;  // 64-row products: m-tile and column group
+  uint32_t wpair[V_NT];  // norm weight pairs of this thread's output columns
 #pragma unroll
-  for (int nt = 0; nt < 8; ++nt) wpair[nt] = *reinterpret_cast<const uint32_t*>(norm_w + (warp >> 2) * 64 + nt * 8 + (lane & 3) * 2);
+  for (int nt = 0; nt < V_NT; ++nt)
+    wpair[nt] = *reinterpret_cast<const uint32_t*>(norm_w + nh * (V_NT * 8) + nt * 8 + c4 * 2);
 
-  // state accumulator: warp w owns dv rows [16w, 16w+16), all 128 dk columns
-  float sacc[16][4];
+  // state accumulator: warp w owns dv rows [16 (w % 8), +16) and dk columns of group w / 8
+  const int smt = warp & 7, sng = warp >> 3;
+  float sacc[S_NT][4];
 #pragma unroll
-  for (int nt = 0; nt < 16; ++nt) {
-    const int col = nt * 8 + c4 * 2;
-    const float2 lo = *reinterpret_cast<const float2*>(Sg + (int64_t)(warp * 16 + g4) * DKc + col);
-    const float2 hi = *reinterpret_cast<const float2*>(Sg + (int64_t)(warp * 16 + g4 + 8) * DKc + col);
+  for (int nt = 0; nt < S_NT; ++nt) {
+    const int col = sng * (S_NT * 8) + nt * 8 + c4 * 2;
+    const float2 lo = *reinterpret_cast<const float2*>(Sg + (int64_t)(smt * 16 + g4) * DKc + col);
+    const float2 hi = *reinterpret_cast<const float2*>(Sg + (int64_t)(smt * 16 + g4 + 8) * DKc + col);
     sacc[nt][0] = lo.x;
     sacc[nt][1] = lo.y;
     sacc[nt][2] = hi.x;
     sacc[nt][3] = hi.y;
   }
-  store_tile_bf16<16, DKc>(smem + GdnSmem::S, sacc, warp * 16, 0, lane, 1.f);
-  const int mt = warp & 3, nh = warp >> 2;  // 64-row products: m-tile and column half
+  store_tile_bf16<S_NT, DKc>(smem + GdnSmem::S, sacc, smt * 16, sng * (S_NT * 8), lane, 1.f);
 
   for (int ch = 0; ch < n_chunks; ++ch) {
     const int tc = t_begin + ch * CH;
@@ -201,14 +212,14 @@ __global__ void __launch_bounds__(256, 1) gdn_prefill_kernel(
     uint8_t* pV = pK + GdnSmem::TILE;
     // z rows of this chunk (consumed by the epilogue), then the next chunk's q/k/v into the
     // other buffer (its previous contents are dead)
-    for (int i = tid; i < CH * 16; i += 256) {
+    for (int i = tid; i < CH * 16; i += NT_) {
       const int r = i >> 4, c = i & 15;
       const bool ok = r < nc;
       cpa16(s0 + GdnSmem::Z + (uint32_t)(r * GdnSmem::ZLD + c * 8) * 2, zrow + (int64_t)(tc + (ok ? r : 0)) * ldz + c * 8, ok);
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
     if (ch + 1 < n_chunks) {
-      gdn_load_chunk(s0, b ^ 1, q, k, v, tc + CH, min(CH, n - (ch + 1) * CH), h, hv, H, HV, tid);
+      gdn_load_chunk<NT_>(s0, b ^ 1, q, k, v, tc + CH, min(CH, n - (ch + 1) * CH), h, hv, H, HV, tid);
     } else {
       asm volatile("cp.async.commit_group;" ::: "memory");
     }
@@ -242,23 +253,23 @@ __global__ void __launch_bounds__(256, 1) gdn_prefill_kernel(
     }
     // ---------------------------------------------------------------- K K^T -> A,  Q K^T -> P
     {
-      float kk[4][4], qk[4][4];
+      float kk[KK_NT][4], qk[KK_NT][4];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) kk[i][0] = kk[i][1] = kk[i][2] = kk[i][3] = qk[i][0] = qk[i][1] = qk[i][2] = qk[i][3] = 0.f;
-      mma_tile<4, 8, DKc, DKc, false, false>(kk, sK, sK, mt * 16, nh * 32, lane);
-      mma_tile<4, 8, DKc, DKc, false, false>(qk, sQ, sK, mt * 16, nh * 32, lane);
+      for (int i = 0; i < KK_NT; ++i) kk[i][0] = kk[i][1] = kk[i][2] = kk[i][3] = qk[i][0] = qk[i][1] = qk[i][2] = qk[i][3] = 0.f;
+      mma_tile<KK_NT, 8, DKc, DKc, false, false>(kk, sK, sK, mt * 16, nh * (KK_NT * 8), lane);
+      mma_tile<KK_NT, 8, DKc, DKc, false, false>(qk, sQ, sK, mt * 16, nh * (KK_NT * 8), lane);
 #pragma unroll
-      for (int nt = 0; nt < 4; ++nt) {
+      for (int nt = 0; nt < KK_NT; ++nt) {
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const int t = mt * 16 + g4 + ((e >> 1) << 3);
-          const int s = nh * 32 + nt * 8 + c4 * 2 + (e & 1);
+          const int s = nh * (KK_NT * 8) + nt * 8 + c4 * 2 + (e & 1);
           const float dec = (s <= t) ? expf(sG[t] - sG[s]) : 0.f;
           A32[t * LDA + s] = (s < t) ? sBeta[t] * dec * kk[nt][e] : 0.f;
           qk[nt][e] = (s <= t) ? scale * dec * qk[nt][e] : 0.f;
         }
       }
-      store_tile_bf16<4, CH>(smem + GdnSmem::P, qk, mt * 16, nh * 32, lane, 1.f);
+      store_tile_bf16<KK_NT, CH>(smem + GdnSmem::P, qk, mt * 16, nh * (KK_NT * 8), lane, 1.f);
     }
     __syncthreads();
 
@@ -282,7 +293,7 @@ __global__ void __launch_bounds__(256, 1) gdn_prefill_kernel(
       }
     } else {
       // meanwhile: b e^G K into KB and b V in place (inputs of W and U)
-      for (int i = tid - 128; i < CH * 16; i += 128) {
+      for (int i = tid - 128; i < CH * 16; i += NT_ - 128) {
         const int r = i >> 4, c = i & 15;
         float kf[8], vf[8];
         load_bf16x8(reinterpret_cast<const __nv_bfloat16*>(pK + sw<DKc>(r, c)), kf);
@@ -302,7 +313,7 @@ __global__ void __launch_bounds__(256, 1) gdn_prefill_kernel(
 #pragma unroll 1
     for (int d = 1; d < 4; ++d) {
       const int nb = 4 - d;  // number of blocks at this distance
-      for (int e = tid; e < nb * 256; e += 256) {
+      for (int e = tid; e < nb * 256; e += NT_) {
         const int bi = e >> 8, r = (e >> 4) & 15, c = e & 15;
         const int j = bi, i = bi + d;
         float acc = 0.f;
@@ -313,7 +324,7 @@ __global__ void __launch_bounds__(256, 1) gdn_prefill_kernel(
         X32[bi * 256 + r * 16 + c] = acc;
       }
       __syncthreads();
-      for (int e = tid; e < nb * 256; e += 256) {
+      for (int e = tid; e < nb * 256; e += NT_) {
         const int bi = e >> 8, r = (e >> 4) & 15, c = e & 15;
         const int j = bi, i = bi + d;
         float acc = 0.f;
@@ -324,7 +335,7 @@ __global__ void __launch_bounds__(256, 1) gdn_prefill_kernel(
       __syncthreads();
     }
     // T (lower triangle incl. diagonal) -> bf16 [t][s]
-    for (int i = tid; i < CH * CH / 2; i += 256) {
+    for (int i = tid; i < CH * CH / 2; i += NT_) {
       const int r = i / (CH / 2), cc = (i % (CH / 2)) * 2;
       const float a0 = (cc <= r) ? T32[r * LDA + cc] : 0.f;
       const float a1 = (cc + 1 <= r) ? T32[r * LDA + cc + 1] : 0.f;
@@ -334,42 +345,42 @@ __global__ void __launch_bounds__(256, 1) gdn_prefill_kernel(
 
     // ---------------------------------------------------------------- W = T (b e^G K), stored negated
     {
-      float w[8][4];
+      float w[V_NT][4];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) w[i][0] = w[i][1] = w[i][2] = w[i][3] = 0.f;
-      mma_tile<8, 4, CH, DKc, false, true>(w, s0 + GdnSmem::T, s0 + GdnSmem::KB, mt * 16, nh * 64, lane);
-      store_tile_bf16<8, DKc>(smem + GdnSmem::W, w, mt * 16, nh * 64, lane, -1.f);
+      for (int i = 0; i < V_NT; ++i) w[i][0] = w[i][1] = w[i][2] = w[i][3] = 0.f;
+      mma_tile<V_NT, 4, CH, DKc, false, true>(w, s0 + GdnSmem::T, s0 + GdnSmem::KB, mt * 16, nh * (V_NT * 8), lane);
+      store_tile_bf16<V_NT, DKc>(smem + GdnSmem::W, w, mt * 16, nh * (V_NT * 8), lane, -1.f);
     }
     __syncthreads();
     // ---------------------------------------------------------------- U = T (b V) - W S0^T
     {
-      float u[8][4];
+      float u[V_NT][4];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) u[i][0] = u[i][1] = u[i][2] = u[i][3] = 0.f;
-      mma_tile<8, 4, CH, DKc, false, true>(u, s0 + GdnSmem::T, sV, mt * 16, nh * 64, lane);
-      mma_tile<8, 8, DKc, DKc, false, false>(u, s0 + GdnSmem::W, s0 + GdnSmem::S, mt * 16, nh * 64, lane);
-      store_tile_bf16<8, DKc>(smem + GdnSmem::U, u, mt * 16, nh * 64, lane, 1.f);
+      for (int i = 0; i < V_NT; ++i) u[i][0] = u[i][1] = u[i][2] = u[i][3] = 0.f;
+      mma_tile<V_NT, 4, CH, DKc, false, true>(u, s0 + GdnSmem::T, sV, mt * 16, nh * (V_NT * 8), lane);
+      mma_tile<V_NT, 8, DKc, DKc, false, false>(u, s0 + GdnSmem::W, s0 + GdnSmem::S, mt * 16, nh * (V_NT * 8), lane);
+      store_tile_bf16<V_NT, DKc>(smem + GdnSmem::U, u, mt * 16, nh * (V_NT * 8), lane, 1.f);
     }
     __syncthreads();
     // ---------------------------------------------------------------- O, gated RMSNorm; e^{G_C - G} K into KB
     {
-      float o[8][4];
+      float o[V_NT][4];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
-      mma_tile<8, 8, DKc, DKc, false, false>(o, sQ, s0 + GdnSmem::S, mt * 16, nh * 64, lane);
+      for (int i = 0; i < V_NT; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+      mma_tile<V_NT, 8, DKc, DKc, false, false>(o, sQ, s0 + GdnSmem::S, mt * 16, nh * (V_NT * 8), lane);
       const float f0 = scale * sEG[mt * 16 + g4], f1 = scale * sEG[mt * 16 + g4 + 8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
+      for (int i = 0; i < V_NT; ++i) {
         o[i][0] *= f0;
         o[i][1] *= f0;
         o[i][2] *= f1;
         o[i][3] *= f1;
       }
-      mma_tile<8, 4, CH, DKc, false, true>(o, s0 + GdnSmem::P, s0 + GdnSmem::U, mt * 16, nh * 64, lane);
+      mma_tile<V_NT, 4, CH, DKc, false, true>(o, s0 + GdnSmem::P, s0 + GdnSmem::U, mt * 16, nh * (V_NT * 8), lane);
       // o rounds to bf16 (the reference's GDN output dtype), then y = o rstd w z sigmoid(z)
       float ss[2] = {0.f, 0.f};
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
+      for (int i = 0; i < V_NT; ++i) {
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           o[i][e] = bf16_round(o[i][e]);
@@ -385,7 +396,7 @@ __global__ void __launch_bounds__(256, 1) gdn_prefill_kernel(
         sSS[nh * CH + mt * 16 + g4] = ss[0];
         sSS[nh * CH + mt * 16 + g4 + 8] = ss[1];
       }
-      for (int i = tid; i < CH * 16; i += 256) {
+      for (int i = tid; i < CH * 16; i += NT_) {
         const int r = i >> 4, c = i & 15;
         float kf[8];
         load_bf16x8(reinterpret_cast<const __nv_bfloat16*>(pK + sw<DKc>(r, c)), kf);
@@ -401,12 +412,15 @@ __global__ void __launch_bounds__(256, 1) gdn_prefill_kernel(
       for (int rr = 0; rr < 2; ++rr) {
         const int t = mt * 16 + g4 + rr * 8;
         if (t >= nc) continue;
-        const float rstd = rsqrtf((sSS[t] + sSS[CH + t]) / (float)DKc + eps);
-        const int64_t tok = tc + t;
-        const __nv_bfloat16* zr = sZ + t * GdnSmem::ZLD + nh * 64;
-        __nv_bfloat16* dst = y + tok * ldy + (int64_t)hv * DKc + nh * 64;
+        float ssum = 0.f;
 #pragma unroll
-        for (int nt = 0; nt < 8; ++nt) {
+        for (int gq = 0; gq < NQ; ++gq) ssum += sSS[gq * CH + t];
+        const float rstd = rsqrtf(ssum / (float)DKc + eps);
+        const int64_t tok = tc + t;
+        const __nv_bfloat16* zr = sZ + t * GdnSmem::ZLD + nh * (V_NT * 8);
+        __nv_bfloat16* dst = y + tok * ldy + (int64_t)hv * DKc + nh * (V_NT * 8);
+#pragma unroll
+        for (int nt = 0; nt < V_NT; ++nt) {
           const int col = nt * 8 + c4 * 2;
           float z0, z1, w0, w1;
           unpack_bf16x2(*reinterpret_cast<const uint32_t*>(zr + col), z0, z1);
@@ -421,24 +435,24 @@ __global__ void __launch_bounds__(256, 1) gdn_prefill_kernel(
     {
       const float eC = expf(G_last);
 #pragma unroll
-      for (int nt = 0; nt < 16; ++nt) {
+      for (int nt = 0; nt < S_NT; ++nt) {
         sacc[nt][0] *= eC;
         sacc[nt][1] *= eC;
         sacc[nt][2] *= eC;
         sacc[nt][3] *= eC;
       }
-      mma_tile<16, 4, DKc, DKc, true, true>(sacc, s0 + GdnSmem::U, s0 + GdnSmem::KB, warp * 16, 0, lane);
-      store_tile_bf16<16, DKc>(smem + GdnSmem::S, sacc, warp * 16, 0, lane, 1.f);
+      mma_tile<S_NT, 4, DKc, DKc, true, true>(sacc, s0 + GdnSmem::U, s0 + GdnSmem::KB, smt * 16, sng * (S_NT * 8), lane);
+      store_tile_bf16<S_NT, DKc>(smem + GdnSmem::S, sacc, smt * 16, sng * (S_NT * 8), lane, 1.f);
     }
     __syncthreads();
   }
   asm volatile("cp.async.wait_group 0;" ::: "memory");
   // ---------------------------------------------------------------- final state, in place
 #pragma unroll
-  for (int nt = 0; nt < 16; ++nt) {
-    const int col = nt * 8 + c4 * 2;
-    *reinterpret_cast<float2*>(Sg + (int64_t)(warp * 16 + g4) * DKc + col) = make_float2(sacc[nt][0], sacc[nt][1]);
-    *reinterpret_cast<float2*>(Sg + (int64_t)(warp * 16 + g4 + 8) * DKc + col) = make_float2(sacc[nt][2], sacc[nt][3]);
+  for (int nt = 0; nt < S_NT; ++nt) {
+    const int col = sng * (S_NT * 8) + nt * 8 + c4 * 2;
+    *reinterpret_cast<float2*>(Sg + (int64_t)(smt * 16 + g4) * DKc + col) = make_float2(sacc[nt][0], sacc[nt][1]);
+    *reinterpret_cast<float2*>(Sg + (int64_t)(smt * 16 + g4 + 8) * DKc + col) = make_float2(sacc[nt][2], sacc[nt][3]);
   }
 }
 
@@ -459,13 +473,14 @@ extern "C" int qw_gdn_prefill(const void* q, const void* k, const void* v, const
                    ((uintptr_t)z % 16) == 0 && (ldz % 8) == 0 && (ldy % 2) == 0,
                QW_ERR_ALIGN);
   auto* s = reinterpret_cast<cudaStream_t>(stream);
+  constexpr int NW = 16;
   static bool cfg = false;
   if (!cfg) {
-    cudaFuncSetAttribute(gdn_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, GdnSmem::TOTAL);
+    cudaFuncSetAttribute(gdn_prefill_kernel<NW>, cudaFuncAttributeMaxDynamicSharedMemorySize, GdnSmem::TOTAL);
     cfg = true;
   }
   dim3 grid((unsigned)B, (unsigned)HV);
-  gdn_prefill_kernel<<<grid, 256, GdnSmem::TOTAL, s>>>(
+  gdn_prefill_kernel<NW><<<grid, NW * 32, GdnSmem::TOTAL, s>>>(
       static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(k), static_cast<const __nv_bfloat16*>(v),
       static_cast<const __nv_bfloat16*>(ba), ldba, A_log, static_cast<const __nv_bfloat16*>(dt_bias), cu_seqlens,
       slots, (int)n_slots, state, static_cast<const __nv_bfloat16*>(z), ldz,

@@ -691,7 +691,11 @@ extern "C" int qw_gemm_bf16(const void* x, const void* w, void* y, int64_t M, in
     const int per16 = out_kind == QW_OUT_F32_OF_BF16 ? 4 : 8;  // elements per 16 bytes
     p.vec_ok = ((uintptr_t)y % 16) == 0 && (ldy % per16) == 0;
     constexpr int BN = 256;
-    if (M >= 256 && gemm_use_pairs()) {
+    // Kernel choice per shape, from sustained (power-capped) runs of a whole prefill's
+    // projections on B200: CTA pairs win for K <= 6144 plain outputs (qkvz, qkv, out_proj,
+    // o_proj: 5-11%); the SwiGLU epilogue and K >= 8192 do better on one CTA (the pair's
+    // cross-SM accumulator handshake costs more than it saves there).
+    if (M >= 256 && !swiglu && K < 8192 && gemm_use_pairs()) {
       if ((rc = make_tmap(&ta, x, M, K, ldx, BM)) != QW_OK) return rc;
       if ((rc = make_tmap(&tb, w, N, K, ldw, P_BN / 2)) != QW_OK) return rc;
       p.a_rows = (int)M;
