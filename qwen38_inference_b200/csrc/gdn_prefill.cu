@@ -115,8 +115,8 @@ struct GdnSmem {
   static constexpr int S = R + R_BYTES;           // S0 bf16 [dv][dk], 32 KB
   static constexpr int P = S + 2 * TILE;          // [t][s] bf16, 8 KB
   static constexpr int T = P + CH * CH * 2;
-  static constexpr int X32 = T + CH * CH * 2;     // 3 x 16 x 16 fp32 scratch
-  static constexpr int VEC = X32 + 3 * 256 * 4;   // G, eG, eGl, beta: 4 x 64 fp32; row sums 4 x 64
+  static constexpr int X32 = T + CH * CH * 2;     // 6 x 16 x 16 fp32 scratch (T_ii A_ik)
+  static constexpr int VEC = X32 + 6 * 256 * 4;   // G, eG, eGl, beta: 4 x 64 fp32; row sums 4 x 64
   static constexpr int ZLD = DKc + 8;             // padded row of the z tile (bf16)
   static constexpr int Z = VEC + 8 * CH * 4;      // z rows of the chunk [64][ZLD] bf16
   static constexpr int TOTAL = Z + CH * ZLD * 2;
@@ -202,10 +202,30 @@ __global__ void __launch_bounds__(NW * 32, 1) gdn_prefill_kernel(
   }
   store_tile_bf16<S_NT, DKc>(smem + GdnSmem::S, sacc, smt * 16, sng * (S_NT * 8), lane, 1.f);
 
+  // blocks of T above the diagonal stay zero for every chunk
+  for (int e = tid; e < CH * CH; e += NT_) {
+    const int r = e / CH, c = e % CH;
+    if ((c >> 4) > (r >> 4))
+      *reinterpret_cast<__nv_bfloat16*>(smem + GdnSmem::T + sw_elem<CH>(r, c)) = f2bf(0.f);
+  }
+  // raw b, a of the gating for token tid of the chunk, loaded one chunk ahead
+  float g_b = 0.f, g_a = 0.f;
+  if (tid < CH && tid < n) {
+    g_b = bf2f(ba[(int64_t)(t_begin + tid) * ldba + hv]);
+    g_a = bf2f(ba[(int64_t)(t_begin + tid) * ldba + HV + hv]);
+  }
   for (int ch = 0; ch < n_chunks; ++ch) {
     const int tc = t_begin + ch * CH;
     const int nc = min(CH, n - ch * CH);
     const int b = ch & 1;
+    const float cur_b = g_b, cur_a = g_a;
+    if (tid < CH) {
+      g_b = g_a = 0.f;
+      if ((ch + 1) * CH + tid < n) {
+        g_b = bf2f(ba[(int64_t)(tc + CH + tid) * ldba + hv]);
+        g_a = bf2f(ba[(int64_t)(tc + CH + tid) * ldba + HV + hv]);
+      }
+    }
     const uint32_t sQ = s0 + GdnSmem::QKV + b * 3 * GdnSmem::TILE;
     const uint32_t sK = sQ + GdnSmem::TILE, sV = sK + GdnSmem::TILE;
     uint8_t* pK = smem + GdnSmem::QKV + b * 3 * GdnSmem::TILE + GdnSmem::TILE;
@@ -227,11 +247,10 @@ __global__ void __launch_bounds__(NW * 32, 1) gdn_prefill_kernel(
     if (tid < CH) {
       float gg = 0.f, bb = 0.f;
       if (tid < nc) {
-        const int64_t t = tc + tid;
-        const float xa = bf2f(ba[t * ldba + HV + hv]) + dtb;
+        const float xa = cur_a + dtb;
         const float sp = xa <= 20.f ? logf(1.f + expf(xa)) : xa;
         gg = -a_log * sp;
-        bb = bf16_round(1.f / (1.f + expf(-bf2f(ba[t * ldba + hv]))));
+        bb = bf16_round(1.f / (1.f + expf(-cur_b)));
       }
       sBeta[tid] = bb;
       float x = gg;
@@ -278,18 +297,25 @@ __global__ void __launch_bounds__(NW * 32, 1) gdn_prefill_kernel(
       // invert the unit lower-triangular diagonal block b = warp; lane j < 16 owns column j
       const int bb = warp, j = lane;
       float tcol[16];
+      const float* arow = A32 + (bb * 16) * LDA + bb * 16;
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
+        // row i of the block: i broadcast loads issued together, then a predicated dot
+        // product with the column computed so far (T[k][j] = 0 for k < j)
+        float a[16];
+#pragma unroll
+        for (int kx = 0; kx < i; ++kx) a[kx] = arow[i * LDA + kx];
         float acc = 0.f;
 #pragma unroll
-        for (int kx = 0; kx < 16; ++kx) {
-          if (kx < i && j < 16 && kx >= j) acc += A32[(bb * 16 + i) * LDA + bb * 16 + kx] * tcol[kx];
-        }
+        for (int kx = 0; kx < i; ++kx) acc += (kx >= j) ? a[kx] * tcol[kx] : 0.f;
         tcol[i] = (i == j) ? 1.f : (i > j ? -acc : 0.f);
       }
       if (j < 16) {
 #pragma unroll
-        for (int i = 0; i < 16; ++i) T32[(bb * 16 + i) * LDA + bb * 16 + j] = tcol[i];
+        for (int i = 0; i < 16; ++i) {
+          T32[(bb * 16 + i) * LDA + bb * 16 + j] = tcol[i];
+          *reinterpret_cast<__nv_bfloat16*>(smem + GdnSmem::T + sw_elem<CH>(bb * 16 + i, bb * 16 + j)) = f2bf(tcol[i]);
+        }
       }
     } else {
       // meanwhile: b e^G K into KB and b V in place (inputs of W and U)
@@ -309,7 +335,19 @@ __global__ void __launch_bounds__(NW * 32, 1) gdn_prefill_kernel(
       }
     }
     __syncthreads();
-    // off-diagonal blocks by distance d: T_ij = -T_ii * sum_{k=j}^{i-1} A_ik T_kj
+    // below-diagonal blocks: with M_ik = T_ii A_ik, T_ij = -sum_{k=j}^{i-1} M_ik T_kj.
+    // M for the six blocks (1,0) (2,0) (2,1) (3,0) (3,1) (3,2) in one pass, then one pass
+    // per distance i - j; each T_ij goes to T32 (read by later levels) and to bf16 T.
+    for (int e = tid; e < 6 * 256; e += NT_) {
+      const int pi = e >> 8, r = (e >> 4) & 15, c = e & 15;
+      const int i = pi < 1 ? 1 : (pi < 3 ? 2 : 3);
+      const int kk = pi < 1 ? 0 : (pi < 3 ? pi - 1 : pi - 3);
+      float acc = 0.f;
+#pragma unroll
+      for (int x = 0; x < 16; ++x) acc += T32[(i * 16 + r) * LDA + i * 16 + x] * A32[(i * 16 + x) * LDA + kk * 16 + c];
+      X32[pi * 256 + r * 16 + c] = acc;
+    }
+    __syncthreads();
 #pragma unroll 1
     for (int d = 1; d < 4; ++d) {
       const int nb = 4 - d;  // number of blocks at this distance
@@ -318,30 +356,15 @@ __global__ void __launch_bounds__(NW * 32, 1) gdn_prefill_kernel(
         const int j = bi, i = bi + d;
         float acc = 0.f;
         for (int kb = j; kb < i; ++kb) {
-#pragma unroll 4
-          for (int x = 0; x < 16; ++x) acc += A32[(i * 16 + r) * LDA + kb * 16 + x] * T32[(kb * 16 + x) * LDA + j * 16 + c];
+          const int pi = (i == 1) ? 0 : (i == 2 ? 1 + kb : 3 + kb);  // M_{i,kb}
+#pragma unroll
+          for (int x = 0; x < 16; ++x) acc += X32[pi * 256 + r * 16 + x] * T32[(kb * 16 + x) * LDA + j * 16 + c];
         }
-        X32[bi * 256 + r * 16 + c] = acc;
-      }
-      __syncthreads();
-      for (int e = tid; e < nb * 256; e += NT_) {
-        const int bi = e >> 8, r = (e >> 4) & 15, c = e & 15;
-        const int j = bi, i = bi + d;
-        float acc = 0.f;
-#pragma unroll 4
-        for (int x = 0; x < 16; ++x) acc += T32[(i * 16 + r) * LDA + i * 16 + x] * X32[bi * 256 + x * 16 + c];
         T32[(i * 16 + r) * LDA + j * 16 + c] = -acc;
+        *reinterpret_cast<__nv_bfloat16*>(smem + GdnSmem::T + sw_elem<CH>(i * 16 + r, j * 16 + c)) = f2bf(-acc);
       }
       __syncthreads();
     }
-    // T (lower triangle incl. diagonal) -> bf16 [t][s]
-    for (int i = tid; i < CH * CH / 2; i += NT_) {
-      const int r = i / (CH / 2), cc = (i % (CH / 2)) * 2;
-      const float a0 = (cc <= r) ? T32[r * LDA + cc] : 0.f;
-      const float a1 = (cc + 1 <= r) ? T32[r * LDA + cc + 1] : 0.f;
-      *reinterpret_cast<uint32_t*>(smem + GdnSmem::T + sw_elem<CH>(r, cc)) = pack_bf16x2(a0, a1);
-    }
-    __syncthreads();
 
     // ---------------------------------------------------------------- W = T (b e^G K), stored negated
     {
