@@ -105,6 +105,19 @@ int qw_attn_decode(const void* qkv, int64_t ldq, int64_t B, int64_t nq, int64_t 
                    int64_t splits, void* out, int64_t ldo, float scale, void* workspace, size_t ws_bytes,
                    qw_stream_t stream);
 
+/* qw_attn_decode with its split-KV scratch in a library-owned, file-scope device array of
+ * QW_ATTN_DECODE_STATIC_SCRATCH_BYTES instead of a caller workspace: the call allocates
+ * nothing. Returns QW_ERR_WORKSPACE when qw_attn_decode_workspace_bytes(B, nq, d, splits)
+ * exceeds that size. Every call on a device shares the one array, so calls whose kernels
+ * overlap in time race on it; calls ordered on one stream are safe. The first call on each
+ * device looks up the array's address (cudaGetSymbolAddress, with that device current), so
+ * make it before any stream capture. No counterpart in the reference.                        */
+#define QW_ATTN_DECODE_STATIC_SCRATCH_BYTES (8u << 20)
+size_t qw_attn_decode_static_max_bytes(void);
+int qw_attn_decode_static(const void* qkv, int64_t ldq, int64_t B, int64_t nq, int64_t nkv, int64_t d,
+                          const void* k_cache, const void* v_cache, const int32_t* seq_len, const int32_t* kv_base,
+                          int64_t max_len, int64_t splits, void* out, int64_t ldo, float scale, qw_stream_t stream);
+
 /* ---- Gated DeltaNet ------------------------------------------------------------------ */
 /* Prefill causal conv (width 4) + SiLU over the first 2*qk_dim+v_dim columns of x [T, ldx],
  * L2 norm of q/k heads, token-major q,k [T, qk_dim], v [T, v_dim]; conv_state [S, C, 3]
