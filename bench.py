@@ -36,6 +36,24 @@ METRIC = "prefill+decode tok/s at B32/L1024 (27B hybrid, bf16); sum of call medi
 UNIT = "tok/s"
 
 
+EPI_NAMES = {0: "bf16", 1: "f32-of-bf16", 2: "SwiGLU"}
+
+
+def _ncu_traffic(shape):
+    """DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) of the GEMM of
+    this shape, from the ncu summary committed for it (None when there is none)."""
+    M, N, K, kind = shape
+    path = os.path.join(ROOT, "profiles", f"gemm_{EPI_NAMES.get(kind, kind).lower()}_M{M}_N{N}_K{K}.md")
+    try:
+        with open(path) as f:
+            for line in f:
+                if line.startswith("traffic_bytes_per_launch:"):
+                    return int(line.split(":")[1].strip().replace(",", ""))
+    except OSError:
+        pass
+    return None
+
+
 def _peaks():
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
@@ -293,16 +311,32 @@ def run_gpu(args):
     dec_breakdown = {}
     for name, a, b in dec_ops:
         dec_breakdown[name] = dec_breakdown.get(name, 0.0) + a.elapsed_time(b)
-    flops = sum(f for f, _, _ in prof)
-    ms = sum(a.elapsed_time(b) for _, a, b in prof)
     hbm, tf_burst, tf_sust, src = _peaks()
-    achieved = flops / (ms * 1e-3) / 1e12 if ms > 0 else None
-    roof = {"bound": "tensor", "kernel": "gemm_tcgen05_kernel (all prefill projections)",
-            "achieved": round(achieved, 1) if achieved else None, "peak": tf_sust, "unit": "TFLOP/s",
-            "frac": round(achieved / tf_sust, 4) if achieved else None,
+    # GEMM launches grouped by (M, N, K, epilogue); the group with the most device time is
+    # the dominant kernel of the step (the MLP gate_up projection with the SwiGLU epilogue)
+    groups = {}
+    for f, a, b, shape in prof:
+        g = groups.setdefault(shape, [0.0, 0.0, 0])
+        g[0] += f
+        g[1] += a.elapsed_time(b)
+        g[2] += 1
+    all_flops = sum(g[0] for g in groups.values())
+    all_ms = sum(g[1] for g in groups.values())
+    shape, (g_flops, g_ms, g_n) = max(groups.items(), key=lambda kv: kv[1][1])
+    M_, N_, K_, kind = shape
+    per_launch_ms = g_ms / g_n
+    achieved = (g_flops / g_n) / (per_launch_ms * 1e-3) / 1e12
+    traffic = _ncu_traffic(shape)
+    roof = {"bound": "tensor",
+            "kernel": f"gemm_tcgen05_kernel {EPI_NAMES.get(kind, kind)} M={M_} N={N_} K={K_}",
+            "achieved": round(achieved, 1), "peak": tf_sust, "unit": "TFLOP/s",
+            "frac": round(achieved / tf_sust, 4),
             "peak_source": f"{src} bf16_tflops_sustained (kernel timed inside a long step)",
-            "launches": len(prof), "avg_launch_ms": round(ms / max(1, len(prof)), 4),
-            "traffic": None, "gemm_share_of_prefill": round(ms / mp, 4) if mp else None}
+            "flop_per_launch": g_flops / g_n, "launches_per_prefill": g_n, "avg_launch_ms": round(per_launch_ms, 4),
+            "traffic": traffic, "algorithmic_bytes_per_launch": 2 * (M_ * K_ + N_ * K_ + M_ * (N_ // 2 if kind == 2 else N_)),
+            "share_of_prefill": round(g_ms / mp, 4) if mp else None,
+            "all_gemms": {"achieved": round(all_flops / (all_ms * 1e-3) / 1e12, 1), "launches": len(prof),
+                          "share_of_prefill": round(all_ms / mp, 4) if mp else None}}
     out = {"metric": METRIC, "value": round(tokens / (step_ms * 1e-3), 1), "unit": UNIT, "n_gpus": world,
            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_ms, 3), "higher_is_better": True,
            "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
@@ -326,6 +360,100 @@ def run_gpu(args):
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def run_op(args):
+    """One kernel of the step alone, at the step's shape, on random data: the case the ncu
+    captures under profiles/ run (``--op gate_up``: the MLP gate_up GEMM with the SwiGLU
+    epilogue, M = batch*length tokens; ``--op gdn_prefill``: the chunked delta rule with
+    the fused gated RMSNorm over batch requests of length tokens, 27B head geometry)."""
+    import torch
+    from qwen38_inference_b200 import ops
+    from qwen38_inference_b200.config import qwen38_27b
+
+    cfg = qwen38_27b()
+    B, L = args.batch, args.length
+    T = B * L
+    dev = "cuda"
+    g = torch.Generator(device=dev).manual_seed(0)
+    if args.op == "gate_up":
+        x = torch.randn(T, cfg.hidden_size, device=dev, generator=g).bfloat16()
+        w = (torch.randn(2 * cfg.intermediate_size, cfg.hidden_size, device=dev, generator=g) * 0.02).bfloat16()
+        y = torch.empty(T, cfg.intermediate_size, device=dev, dtype=torch.bfloat16)
+        work = 2.0 * T * w.shape[0] * cfg.hidden_size
+        unit = "TFLOP/s"
+
+        def launch():
+            ops.gemm(x, w, y, out_kind=ops.OUT_SWIGLU)
+    elif args.op == "conv_prefill":
+        C = cfg.conv_dim
+        x = torch.randn(T, cfg.qkvz_dim, device=dev, generator=g).bfloat16()
+        w = (torch.randn(C, cfg.linear_conv_kernel_dim, device=dev, generator=g) * 0.5).bfloat16()
+        cs = torch.zeros(B, C, cfg.linear_conv_kernel_dim - 1, device=dev).bfloat16()
+        cu = torch.arange(0, T + 1, L, dtype=torch.int32, device=dev)
+        slots = torch.arange(B, dtype=torch.int32, device=dev)
+        has = torch.zeros(B, dtype=torch.int32, device=dev)
+        qo = torch.empty(T, cfg.gdn_qk_dim, device=dev).bfloat16()
+        ko = torch.empty_like(qo)
+        vo = torch.empty(T, cfg.gdn_v_dim, device=dev).bfloat16()
+        work = 2.0 * T * C * 2  # read the conv channels of x, write q, k, v
+        unit = "GB/s"
+
+        def launch():
+            ops.conv_prefill(x, w, cs, cu, slots, has, B, L, qo, ko, vo, cfg.gdn_qk_dim, cfg.gdn_v_dim,
+                             cfg.linear_key_head_dim)
+    elif args.op == "attn_prefill":
+        from qwen38_inference_b200.model import build_metadata
+        nq, nkv, d = cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim
+        cap = L
+        kc = torch.randn(B * cap + 64, nkv, d, device=dev, generator=g).bfloat16()
+        vc = torch.randn(B * cap + 64, nkv, d, device=dev, generator=g).bfloat16()
+        qkv = torch.randn(T, cfg.qkv_dim, device=dev, generator=g).bfloat16()
+        packed, offs, _ = build_metadata(list(range(B)), [0] * B, [L] * B, cap)
+        md = {k_: torch.from_numpy(packed[o:o + n]).to(dev) for k_, (o, n) in offs.items()}
+        out = torch.empty(T, nq * d, device=dev).bfloat16()
+        work = 2.0 * 2 * B * (L * (L + 1) / 2) * d * nq  # causal QK^T and PV
+        unit = "TFLOP/s"
+
+        def launch():
+            ops.attn_prefill(qkv, nq, nkv, d, kc, vc, md["tiles"], md["cu"], md["prefix"], md["kv_base"], out,
+                             d ** -0.5)
+    else:
+        H, HV, dk, dv = cfg.linear_num_key_heads, cfg.linear_num_value_heads, cfg.linear_key_head_dim, \
+            cfg.linear_value_head_dim
+        nrm = torch.nn.functional.normalize
+        q = nrm(torch.randn(T, H, dk, device=dev, generator=g), dim=-1).bfloat16().view(T, H * dk)
+        k = nrm(torch.randn(T, H, dk, device=dev, generator=g), dim=-1).bfloat16().view(T, H * dk)
+        v = torch.randn(T, HV * dv, device=dev, generator=g).bfloat16()
+        ba = torch.randn(T, 2 * HV, device=dev, generator=g).bfloat16()
+        A_log = torch.zeros(HV, device=dev)
+        dt_bias = torch.zeros(HV, device=dev).bfloat16()
+        cu = torch.arange(0, T + 1, L, dtype=torch.int32, device=dev)
+        slots = torch.arange(B, dtype=torch.int32, device=dev)
+        state = torch.zeros(B, HV, dv, dk, device=dev)
+        z = torch.randn(T, HV * dv, device=dev, generator=g).bfloat16()
+        nw = torch.ones(dv, device=dev).bfloat16()
+        y = torch.empty(T, HV * dv, device=dev, dtype=torch.bfloat16)
+        # algorithmic bytes: q, k, v, z, ba read once, y written once, state read + written
+        work = 2.0 * T * (2 * H * dk + 2 * HV * dv + 2 * HV) + 2.0 * T * HV * dv + 2.0 * B * HV * dv * dk * 4
+        unit = "GB/s"
+
+        def launch():
+            ops.gdn_prefill(q, k, v, ba, A_log, dt_bias, cu, slots, B, state, z, nw, y, H, HV, dk, dv, dk ** -0.5,
+                            cfg.rms_norm_eps)
+    for _ in range(args.warmup):
+        launch()
+    torch.cuda.synchronize()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2 * args.steps)]
+    for i in range(args.steps):
+        ev[2 * i].record()
+        launch()
+        ev[2 * i + 1].record()
+    torch.cuda.synchronize()
+    ms = statistics.median(ev[2 * i].elapsed_time(ev[2 * i + 1]) for i in range(args.steps))
+    rate = work / (ms * 1e-3) / (1e12 if unit == "TFLOP/s" else 1e9)
+    print(json.dumps({"op": args.op, "batch": B, "length": L, "median_ms": round(ms, 4),
+                      "achieved": round(rate, 1), "unit": unit, "work_per_launch": work}), flush=True)
 
 
 def run_reference(args):
@@ -354,10 +482,14 @@ def main():
     ap.add_argument("--batch", type=int, default=32)
     ap.add_argument("--length", type=int, default=1024)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--op", choices=["gate_up", "gdn_prefill", "conv_prefill", "attn_prefill"], default=None,
+                    help="time one kernel of the step alone (the case the ncu captures run)")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         print("note: fewer than 3 warm-up steps", file=sys.stderr)
-    if args.impl == "reference":
+    if args.op:
+        run_op(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_gpu(args)

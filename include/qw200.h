@@ -38,6 +38,7 @@ typedef struct CUstream_st* qw_stream_t;
 /* device error word values */
 #define QW_DEV_ERR_TIMEOUT_GEMM 101
 #define QW_DEV_ERR_INDEX 102
+#define QW_DEV_ERR_TIMEOUT_GDN 103 /* a bounded wait of the chunked delta-rule pipeline gave up */
 
 /* ---- library ----------------------------------------------------------------------- */
 int qw_version(void);
@@ -129,14 +130,16 @@ int qw_conv_prefill(const void* x, int64_t ldx, const void* conv_w, void* conv_s
                     qw_stream_t stream);
 /* Chunked gated delta rule over varlen requests with the gating folded in; state
  * [S, HV, dv, dk] fp32 read and written in place at slots[b]; the output o (rounded to
- * bf16) goes straight through the gated RMSNorm with z [T, ldz] and norm_w [dv]:
+ * bf16) goes straight through the gated RMSNorm with z [T, ldz] and norm_w [dv]; q, k are
+ * [T, H*dk] and v [T, HV*dv] (T = total tokens, read by TMA):
  * y bf16 [T, ldy] = bf16(o * rsqrt(mean o^2 + eps) * w * z * sigmoid(z))
  * (REF:5081-5086: fused_gdn_gating + flashinfer chunk_gated_delta_rule + index_copy_ +
  * rms_norm_gated)                                                                            */
 int qw_gdn_prefill(const void* q, const void* k, const void* v, const void* ba, int64_t ldba, const float* A_log,
-                   const void* dt_bias, const int32_t* cu_seqlens, const int32_t* slots, int64_t B, int64_t n_slots,
-                   float* state, const void* z, int64_t ldz, const void* norm_w, void* y, int64_t ldy, int64_t H,
-                   int64_t HV, int64_t dk, int64_t dv, float scale, float eps, qw_stream_t stream);
+                   const void* dt_bias, const int32_t* cu_seqlens, const int32_t* slots, int64_t B, int64_t T,
+                   int64_t n_slots, float* state, const void* z, int64_t ldz, const void* norm_w, void* y,
+                   int64_t ldy, int64_t H, int64_t HV, int64_t dk, int64_t dv, float scale, float eps,
+                   qw_stream_t stream);
 /* Decode: conv update + L2 norm + gating + one recurrent step + gated RMSNorm, y bf16
  * [B, HV*dv] (REF:5072-5075 fused_qkvzba_causal_conv1d_update + recurrent packed decode,
  * REF:5086 rms_norm_gated)                                                                   */

@@ -35,8 +35,8 @@ SIGNATURES = {
     "qw_attn_decode_static_max_bytes": (SZ, []),
     "qw_attn_decode_static": (I32, [P, I64, I64, I64, I64, I64, P, P, P, P, I64, I64, P, I64, F32, P]),
     "qw_conv_prefill": (I32, [P, I64, P, P, P, P, P, I64, I64, I64, P, P, P, I64, I64, I64, P]),
-    "qw_gdn_prefill": (I32, [P, P, P, P, I64, P, P, P, P, I64, I64, P, P, I64, P, P, I64, I64, I64, I64, I64, F32,
-                             F32, P]),
+    "qw_gdn_prefill": (I32, [P, P, P, P, I64, P, P, P, P, I64, I64, I64, P, P, I64, P, P, I64, I64, I64, I64, I64,
+                             F32, F32, P]),
     "qw_gdn_decode": (I32, [P, I64, P, I64, P, P, P, P, I64, I64, P, P, P, P, I64, I64, I64, I64, I64, F32, P]),
     "qw_kv_grow": (I32, [P, P, P, P, P, I64, I64, I64, I64, P]),
 }

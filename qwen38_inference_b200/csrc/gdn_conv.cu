@@ -2,7 +2,8 @@
 // projection, the split into token-major q, k, v, the L2 norm of q and k, and the conv
 // state update (REF:704-1253 conv, REF:603-699 split, REF:1550-1638 l2norm).
 //
-// Grid (request, chunk of 64 tokens, 128-channel block), 256 threads. The CTA stages the
+// Grid (128-channel block, chunk of 64 tokens, request), 256 threads; the channel block
+// varies fastest so CTAs running together cover whole token rows (DRAM page locality). The CTA stages the
 // 3 history rows + 64 token rows of its 128 channels in shared memory with 16-byte loads
 // (all in flight together), convolves from shared memory, normalizes q/k heads per token
 // (one warp per token) and writes 16-byte-aligned rows. Only chunk 0 of a request reads
@@ -23,7 +24,7 @@ __global__ void __launch_bounds__(256) conv_prefill_kernel(
   constexpr int BT = 64, BC = 128, W = 4, HIST = W - 1;
   __shared__ __align__(16) __nv_bfloat16 sx[BT + HIST][BC];
   __shared__ __align__(16) __nv_bfloat16 sy[BT][BC];  // bf16(silu(conv)), exact
-  const int seq = blockIdx.x, chunk = blockIdx.y, cb = blockIdx.z;
+  const int cb = blockIdx.x, chunk = blockIdx.y, seq = blockIdx.z;
   const int t0 = cu[seq], n = cu[seq + 1] - t0;
   const int tb = chunk * BT;
   if (tb >= n) return;
@@ -136,12 +137,13 @@ extern "C" int qw_conv_prefill(const void* x, int64_t ldx, const void* conv_w, v
                                int64_t qk_dim, int64_t v_dim, int64_t head_dim, qw_stream_t stream) {
   QW_CHECK_ARG(x && conv_w && conv_state && cu_seqlens && slots && has_initial && q_out && k_out && v_out, QW_ERR_ARG);
   QW_CHECK_ARG(B > 0 && max_len > 0 && n_slots > 0, QW_ERR_ARG);
+  QW_CHECK_ARG(B <= 65535 && (max_len + 63) / 64 <= 65535, QW_ERR_UNSUPPORTED);  // grid y/z limits
   QW_CHECK_ARG(qk_dim % 128 == 0 && v_dim % 128 == 0, QW_ERR_UNSUPPORTED);
   QW_CHECK_ARG(((uintptr_t)x % 16) == 0 && (ldx % 8) == 0, QW_ERR_ALIGN);
   QW_CHECK_ARG(((uintptr_t)q_out % 8) == 0 && ((uintptr_t)k_out % 8) == 0 && ((uintptr_t)v_out % 8) == 0, QW_ERR_ALIGN);
   auto* s = reinterpret_cast<cudaStream_t>(stream);
   const int C = (int)(2 * qk_dim + v_dim);
-  dim3 grid((unsigned)B, (unsigned)((max_len + 63) / 64), (unsigned)(C / 128));
+  dim3 grid((unsigned)(C / 128), (unsigned)((max_len + 63) / 64), (unsigned)B);
   const auto* xp = static_cast<const __nv_bfloat16*>(x);
   const auto* wp = static_cast<const __nv_bfloat16*>(conv_w);
   auto* cs = static_cast<__nv_bfloat16*>(conv_state);

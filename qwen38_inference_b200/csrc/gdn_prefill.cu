@@ -1,6 +1,7 @@
 // Chunked gated delta rule for prefill (replaces flashinfer chunk_gated_delta_rule,
-// REF:4852/5084, plus the gating kernel REF:1258-1323 and the state gather/scatter
-// REF:5082-5085: the state is read and written in place at the request's slot).
+// REF:4852/5084, plus the gating kernel REF:1258-1323, the state gather/scatter
+// REF:5082-5085 and the gated RMSNorm REF:5086: the state is read and written in place at
+// the request's slot and the output goes straight through the norm).
 //
 // Recurrence per token t (state S is [dv, dk], fp32):
 //   S_t = a_t S_{t-1} (I - b_t k_t k_t^T) + b_t v_t k_t^T,   o_t = S_t q_t * scale
@@ -8,15 +9,55 @@
 // Chunk form (C = 64 tokens, G = within-chunk cumsum of g, S0 = state before the chunk):
 //   A_ts = b_t e^{G_t - G_s} k_t.k_s (s < t),   T = (I + A)^-1
 //   W = T diag(b e^G) K,   U = T diag(b) V - W S0^T
-//   O = scale (diag(e^G) Q S0^T + [s <= t] e^{G_t - G_s} (Q K^T) U)
+//   O = scale diag(e^G) Q S0^T + ([s <= t] scale e^{G_t - G_s} Q K^T) U
 //   S_C = e^{G_C} S0 + U^T diag(e^{G_C - G}) K
-// The 64 x 64 and 64 x 128 products run on tensor cores (mma.sync m16n8k16, bf16 operands,
-// fp32 accumulation); T is a blocked fp32 forward substitution; S stays in registers as
-// the accumulator of the state update across all chunks of the sequence.
-// One CTA (8 warps) per (sequence, value head).
+//
+// One CTA of 16 warps per (sequence, value head), two warp groups in a software pipeline:
+//  * prep warps 0-7 work one chunk ahead on everything that does not depend on the state:
+//    gating, K K^T and Q K^T (mma.sync), T by a blocked inverse (16 x 16 diagonal blocks by
+//    forward substitution in fp32, off-diagonal blocks on tf32 tensor cores), b e^G K,
+//    W = T (b e^G K), b V and e^{G_C - G} K; the chunk is handed over on an mbarrier;
+//  * state warps 8-15 each own 16 rows (dv) of S in registers (mma accumulator layout for the
+//    whole sequence) and compute their strips of U^T = (bV)^T T^T - S0 W^T,
+//    O^T = scale S0 Q^T diag(e^G) + U^T P^T and S += U^T (e^{G_C-G} K) with S0 and U^T as
+//    register A operands; then the gated RMSNorm y = bf16(o) rstd w silu(z) through a per-warp
+//    staging tile (z in, y out, both 16-byte coalesced).
+// Q, K, V chunks arrive by TMA (128-byte swizzle) into two chunk buffers; the state warps
+// release a buffer and issue the loads of the chunk two ahead. Every mbarrier wait is bounded
+// (QW_DEV_ERR_TIMEOUT_GDN); after a timeout all waits return at once and both groups run
+// their remaining iterations on whatever is in shared memory, so every named barrier is still
+// reached by all its warps and the kernel ends.
 #include "common.cuh"
+#include "tmap.cuh"
 
 namespace qw {
+namespace gdn {
+
+constexpr int CH = 64;  // chunk length
+constexpr int D = 128;  // key / value head dim
+constexpr int TILE = CH * D * 2;      // [64][128] bf16 = two 64-column halves of 8 KB
+constexpr int TILE64 = CH * CH * 2;   // [64][64] bf16
+// one chunk buffer: Q | K (then e^{G_C-G} K) | V (then b V) | b e^G K (then -W) | T | P | vectors
+constexpr int B_Q = 0, B_K = TILE, B_V = 2 * TILE, B_W = 3 * TILE, B_T = 4 * TILE, B_P = B_T + TILE64;
+constexpr int B_VEC = B_P + TILE64;   // e^G [64], e^{G_C}
+constexpr int BUF = B_VEC + 1024;     // multiple of 1024 (TMA swizzle atoms)
+constexpr int BLD = 20;               // row stride (floats) of a compact 16 x 16 fp32 block
+constexpr int BLK = 16 * BLD;         // floats per block
+constexpr int S_BLK = 2 * BUF;        // 20 blocks: [0,6) A_ij then T_ij (i > j), [6,10) A_ii, [10,14) T_ii, [14,20) M_ik
+constexpr int S_IG = S_BLK + 20 * BLK * 4;  // prep vectors: G, beta, e^{G_C-G} (3 x 64 fp32)
+constexpr int S_SS = S_IG + 3 * CH * 4;     // state: [8][64] partial sums of squares, rstd [64]
+constexpr int S_Z = S_SS + 9 * CH * 4;      // state: per-warp z / y staging [64][16] bf16
+constexpr int S_U = S_Z + 8 * CH * 32;      // state: per-warp bf16 U^T strip [16][64]
+constexpr int S_BAR = S_U + 8 * 16 * CH * 2;
+constexpr int SMEM = S_BAR + 64 + 1024;     // + slack to align the base to 1024
+static_assert(BUF % 1024 == 0 && S_Z % 16 == 0, "layout alignment");
+
+QW_DEV int blk_lo(int i, int j) { return i * (i - 1) / 2 + j; }  // i > j
+
+// byte offset of 16-byte chunk c (0..15) of row r (0..63) of a 64-row bf16 tile stored as
+// 64-column halves of 8 KB, each with the TMA 128-byte swizzle (chunk ^= row % 8)
+QW_DEV uint32_t swz(int r, int c) { return (uint32_t)(((c >> 3) << 13) | (r << 7) | (((c & 7) ^ (r & 7)) << 4)); }
+QW_DEV uint32_t swz_elem(int r, int col) { return swz(r, col >> 3) + ((col & 7) << 1); }
 
 QW_DEV void ldsm_x4(uint32_t addr, uint32_t* r) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
@@ -28,6 +69,16 @@ QW_DEV void ldsm_x4_t(uint32_t addr, uint32_t* r) {
                : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
                : "r"(addr));
 }
+QW_DEV void stsm_x4(uint32_t addr, const uint32_t* r) {
+  asm volatile("stmatrix.sync.aligned.m8n8.x4.shared.b16 [%0], {%1,%2,%3,%4};" ::"r"(addr), "r"(r[0]), "r"(r[1]),
+               "r"(r[2]), "r"(r[3])
+               : "memory");
+}
+QW_DEV void stsm_x4_t(uint32_t addr, const uint32_t* r) {
+  asm volatile("stmatrix.sync.aligned.m8n8.x4.trans.shared.b16 [%0], {%1,%2,%3,%4};" ::"r"(addr), "r"(r[0]),
+               "r"(r[1]), "r"(r[2]), "r"(r[3])
+               : "memory");
+}
 QW_DEV void mma16816(float* d, const uint32_t* a, uint32_t b0, uint32_t b1) {
   asm volatile(
       "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
@@ -35,137 +86,141 @@ QW_DEV void mma16816(float* d, const uint32_t* a, uint32_t b0, uint32_t b1) {
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
+QW_DEV uint32_t to_tf32(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return r;
+}
+QW_DEV void mma1688_tf32(float* d, const uint32_t* a, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
 QW_DEV void cpa16(uint32_t dst, const void* src, bool pred) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(pred ? 16 : 0) : "memory");
 }
+// Register split between the warp groups: the CTA is launched with 512 x 128 registers
+// (ptxas is held to 128 by the launch bounds); the prep warpgroups give 40 back and the
+// state warpgroups (64 accumulator registers of S each) take 40 more:
+// 256 x 88 + 256 x 168 = 512 x 128.
+constexpr int PREP_REGS = 88, STATE_REGS = 168;
+static_assert(256 * PREP_REGS + 256 * STATE_REGS == 512 * 128, "register split must equal the launch allocation");
+QW_DEV void named_bar(int id) { asm volatile("bar.sync %0, 256;" ::"r"(id) : "memory"); }
+QW_DEV void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
-// swizzled byte offset of 16-byte chunk c of row r in a tile with RL bf16 per row
-template <int RL>
-QW_DEV uint32_t sw(int r, int c) {
-  return (uint32_t)(r * RL * 2 + ((c ^ (r & 7)) << 4));
+// mma.sync fragments from swizzled 64-row tiles
+QW_DEV void frag_a(uint32_t base, int m0, int k0, int lane, uint32_t* a) {  // tile [M][K]
+  ldsm_x4(base + swz(m0 + (lane & 15), (k0 >> 3) + (lane >> 4)), a);
 }
-template <int RL>
-QW_DEV uint32_t sw_elem(int r, int col) {  // byte offset of element (r, col)
-  return sw<RL>(r, col >> 3) + ((col & 7) << 1);
+QW_DEV void frag_a_t(uint32_t base, int m0, int k0, int lane, uint32_t* a) {  // tile [K][M]
+  ldsm_x4_t(base + swz(k0 + (lane & 7) + ((lane >> 4) << 3), (m0 >> 3) + ((lane >> 3) & 1)), a);
 }
-// A fragment, tile stored [M][K]
-template <int RL>
-QW_DEV void frag_a(uint32_t base, int m0, int k0, int lane, uint32_t* a) {
-  ldsm_x4(base + sw<RL>(m0 + (lane & 15), (k0 >> 3) + (lane >> 4)), a);
+// b[0],b[1]: n-tile n0; b[2],b[3]: n-tile n0+8
+QW_DEV void frag_b(uint32_t base, int n0, int k0, int lane, uint32_t* b) {  // tile [N][K]
+  ldsm_x4(base + swz(n0 + (lane & 7) + ((lane >> 4) << 3), (k0 >> 3) + ((lane >> 3) & 1)), b);
 }
-// A fragment, tile stored [K][M]
-template <int RL>
-QW_DEV void frag_a_t(uint32_t base, int m0, int k0, int lane, uint32_t* a) {
-  ldsm_x4_t(base + sw<RL>(k0 + (lane & 7) + ((lane >> 4) << 3), (m0 >> 3) + ((lane >> 3) & 1)), a);
-}
-// B fragments of n-tiles n0 and n0+8: b[0],b[1] (tile n0), b[2],b[3] (tile n0+8); tile stored [N][K]
-template <int RL>
-QW_DEV void frag_b(uint32_t base, int n0, int k0, int lane, uint32_t* b) {
-  ldsm_x4(base + sw<RL>(n0 + (lane & 7) + ((lane >> 4) << 3), (k0 >> 3) + ((lane >> 3) & 1)), b);
-}
-// same, tile stored [K][N]
-template <int RL>
-QW_DEV void frag_b_t(uint32_t base, int n0, int k0, int lane, uint32_t* b) {
-  ldsm_x4_t(base + sw<RL>(k0 + (lane & 7) + (((lane >> 3) & 1) << 3), (n0 >> 3) + (lane >> 4)), b);
+QW_DEV void frag_b_t(uint32_t base, int n0, int k0, int lane, uint32_t* b) {  // tile [K][N]
+  ldsm_x4_t(base + swz(k0 + (lane & 7) + (((lane >> 3) & 1) << 3), (n0 >> 3) + (lane >> 4)), b);
 }
 // acc[NT][4] += A(16 x 16*KS at rows m0) * B(16*KS x 8*NT at cols n0)
-template <int NT, int KS, int RLA, int RLB, bool AT, bool BT>
+template <int NT, int KS, bool AT, bool BT>
 QW_DEV void mma_tile(float (*acc)[4], uint32_t sa, uint32_t sb, int m0, int n0, int lane) {
 #pragma unroll
   for (int ks = 0; ks < KS; ++ks) {
     uint32_t a[4];
-    if constexpr (AT) frag_a_t<RLA>(sa, m0, ks * 16, lane, a);
-    else frag_a<RLA>(sa, m0, ks * 16, lane, a);
+    if constexpr (AT) frag_a_t(sa, m0, ks * 16, lane, a);
+    else frag_a(sa, m0, ks * 16, lane, a);
 #pragma unroll
     for (int nt = 0; nt < NT; nt += 2) {
       uint32_t b[4];
-      if constexpr (BT) frag_b_t<RLB>(sb, n0 + nt * 8, ks * 16, lane, b);
-      else frag_b<RLB>(sb, n0 + nt * 8, ks * 16, lane, b);
+      if constexpr (BT) frag_b_t(sb, n0 + nt * 8, ks * 16, lane, b);
+      else frag_b(sb, n0 + nt * 8, ks * 16, lane, b);
       mma16816(acc[nt], a, b[0], b[1]);
       mma16816(acc[nt + 1], a, b[2], b[3]);
     }
   }
 }
-// store a 16 x 8*NT accumulator tile as bf16 (times `mul`) into a swizzled [rows][RL] tile
-template <int NT, int RL>
-QW_DEV void store_tile_bf16(uint8_t* smem_base, float (*acc)[4], int m0, int n0, int lane, float mul) {
+template <int NT>
+QW_DEV void store_tile_bf16(uint8_t* tile, float (*acc)[4], int m0, int n0, int lane, float mul) {
   const int g = lane >> 2, c = lane & 3;
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) {
     const int col = n0 + nt * 8 + c * 2;
-    *reinterpret_cast<uint32_t*>(smem_base + sw_elem<RL>(m0 + g, col)) = pack_bf16x2(acc[nt][0] * mul, acc[nt][1] * mul);
-    *reinterpret_cast<uint32_t*>(smem_base + sw_elem<RL>(m0 + g + 8, col)) =
-        pack_bf16x2(acc[nt][2] * mul, acc[nt][3] * mul);
+    *reinterpret_cast<uint32_t*>(tile + swz_elem(m0 + g, col)) = pack_bf16x2(acc[nt][0] * mul, acc[nt][1] * mul);
+    *reinterpret_cast<uint32_t*>(tile + swz_elem(m0 + g + 8, col)) = pack_bf16x2(acc[nt][2] * mul, acc[nt][3] * mul);
   }
 }
-constexpr int CH = 64;   // chunk length
-constexpr int DKc = 128; // key / value head dim
-constexpr int LDA = 65;  // fp32 row stride of the A / T matrices
-
-struct GdnSmem {
-  static constexpr int TILE = CH * DKc * 2;       // 16 KB
-  static constexpr int QKV = 0;                   // [2 buffers][Q | K | V]
-  static constexpr int KB = QKV + 6 * TILE;       // b e^G K, later e^{G_C-G} K
-  static constexpr int R = KB + TILE;             // A32 | T32 during the inverse; then -W | U
-  static constexpr int W = R;
-  static constexpr int U = R + TILE;
-  static constexpr int A32 = R;
-  static constexpr int T32 = R + CH * LDA * 4;
-  static constexpr int R_BYTES = 2 * CH * LDA * 4;  // >= 2 * TILE
-  static constexpr int S = R + R_BYTES;           // S0 bf16 [dv][dk], 32 KB
-  static constexpr int P = S + 2 * TILE;          // [t][s] bf16, 8 KB
-  static constexpr int T = P + CH * CH * 2;
-  static constexpr int X32 = T + CH * CH * 2;     // 6 x 16 x 16 fp32 scratch (T_ii A_ik)
-  static constexpr int VEC = X32 + 6 * 256 * 4;   // G, eG, eGl, beta: 4 x 64 fp32; row sums 4 x 64
-  static constexpr int ZLD = DKc + 8;             // padded row of the z tile (bf16)
-  static constexpr int Z = VEC + 8 * CH * 4;      // z rows of the chunk [64][ZLD] bf16
-  static constexpr int TOTAL = Z + CH * ZLD * 2;
-};
-static_assert(GdnSmem::R_BYTES >= 2 * GdnSmem::TILE, "W and U must fit in the inverse's scratch");
-
-// Issue the loads of chunk `ch` (rows beyond the request are zero-filled) into buffer `b`.
-template <int NTHR>
-QW_DEV void gdn_load_chunk(uint32_t s0, int b, const __nv_bfloat16* q, const __nv_bfloat16* k,
-                           const __nv_bfloat16* v, int64_t tc, int nc, int h, int hv, int H, int HV, int tid) {
-  const uint32_t base = s0 + GdnSmem::QKV + b * 3 * GdnSmem::TILE;
-  for (int i = tid; i < CH * 16; i += NTHR) {
-    const int r = i >> 4, c = i & 15;
-    const bool ok = r < nc;
-    const int64_t t = tc + (ok ? r : 0);
-    cpa16(base + sw<DKc>(r, c), q + (t * H + h) * DKc + c * 8, ok);
-    cpa16(base + GdnSmem::TILE + sw<DKc>(r, c), k + (t * H + h) * DKc + c * 8, ok);
-    cpa16(base + 2 * GdnSmem::TILE + sw<DKc>(r, c), v + (t * HV + hv) * DKc + c * 8, ok);
+// bf16 A-operand fragment of k-step ks from a 16-row accumulator strip held in registers
+QW_DEV void acc_to_a(const float (*s)[4], int ks, uint32_t* a) {
+  a[0] = pack_bf16x2(s[2 * ks][0], s[2 * ks][1]);
+  a[1] = pack_bf16x2(s[2 * ks][2], s[2 * ks][3]);
+  a[2] = pack_bf16x2(s[2 * ks + 1][0], s[2 * ks + 1][1]);
+  a[3] = pack_bf16x2(s[2 * ks + 1][2], s[2 * ks + 1][3]);
+}
+// acc[2][4] += X * Y for compact 16 x 16 fp32 blocks, tf32 tensor cores
+QW_DEV void blk_mma(float (*acc)[4], const float* X, const float* Y, int lane) {
+  const int g = lane >> 2, c = lane & 3;
+#pragma unroll
+  for (int kk = 0; kk < 16; kk += 8) {
+    uint32_t a[4] = {to_tf32(X[g * BLD + kk + c]), to_tf32(X[(g + 8) * BLD + kk + c]),
+                     to_tf32(X[g * BLD + kk + c + 4]), to_tf32(X[(g + 8) * BLD + kk + c + 4])};
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+      mma1688_tf32(acc[nt], a, to_tf32(Y[(kk + c) * BLD + nt * 8 + g]), to_tf32(Y[(kk + c + 4) * BLD + nt * 8 + g]));
   }
-  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+// store mul * acc as a compact fp32 block and, when tile != nullptr, as bf16 at (r0, c0)
+QW_DEV void blk_store(float* out, float (*acc)[4], float mul, uint8_t* tile, int r0, int c0, int lane) {
+  const int g = lane >> 2, c = lane & 3;
+#pragma unroll
+  for (int nt = 0; nt < 2; ++nt) {
+    const int col = nt * 8 + 2 * c;
+    const float v0 = acc[nt][0] * mul, v1 = acc[nt][1] * mul, v2 = acc[nt][2] * mul, v3 = acc[nt][3] * mul;
+    out[g * BLD + col] = v0;
+    out[g * BLD + col + 1] = v1;
+    out[(g + 8) * BLD + col] = v2;
+    out[(g + 8) * BLD + col + 1] = v3;
+    if (tile) {
+      *reinterpret_cast<uint32_t*>(tile + swz_elem(r0 + g, c0 + col)) = pack_bf16x2(v0, v1);
+      *reinterpret_cast<uint32_t*>(tile + swz_elem(r0 + g + 8, c0 + col)) = pack_bf16x2(v2, v3);
+    }
+  }
 }
 
-// NW warps per CTA (8 or 16): the 64-row products are split into 4 m-tiles x NW/4 column
-// groups, the 128 x 128 state into 8 m-tiles x NW/8 column groups.
-template <int NW>
-__global__ void __launch_bounds__(NW * 32, 1) gdn_prefill_kernel(
-    const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k, const __nv_bfloat16* __restrict__ v,
-    const __nv_bfloat16* __restrict__ ba, int64_t ldba, const float* __restrict__ A_log,
-    const __nv_bfloat16* __restrict__ dt_bias, const int32_t* __restrict__ cu, const int32_t* __restrict__ slots,
-    int n_slots, float* __restrict__ state, const __nv_bfloat16* __restrict__ z, int64_t ldz,
-    const __nv_bfloat16* __restrict__ norm_w, __nv_bfloat16* __restrict__ y, int64_t ldy, int H, int HV, float scale,
-    float eps, int* err) {
-  extern __shared__ __align__(128) uint8_t smem[];
+QW_DEV void issue_chunk_loads(uint8_t* buf, uint64_t* bar, const CUtensorMap* tq, const CUtensorMap* tk,
+                              const CUtensorMap* tv, int h, int hv, int row) {
+  mbar_arrive_expect_tx(bar, 3 * TILE);
+#pragma unroll
+  for (int half = 0; half < 2; ++half) {
+    tma_load_2d(buf + B_Q + half * (TILE / 2), tq, bar, h * D + half * 64, row);
+    tma_load_2d(buf + B_K + half * (TILE / 2), tk, bar, h * D + half * 64, row);
+    tma_load_2d(buf + B_V + half * (TILE / 2), tv, bar, hv * D + half * 64, row);
+  }
+}
+
+}  // namespace gdn
+
+using namespace gdn;
+
+__global__ void __launch_bounds__(512, 1) gdn_prefill_kernel(
+    const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+    const __grid_constant__ CUtensorMap tm_v, const __nv_bfloat16* __restrict__ ba, int64_t ldba,
+    const float* __restrict__ A_log, const __nv_bfloat16* __restrict__ dt_bias, const int32_t* __restrict__ cu,
+    const int32_t* __restrict__ slots, int n_slots, float* __restrict__ state, const __nv_bfloat16* __restrict__ z,
+    int64_t ldz, const __nv_bfloat16* __restrict__ norm_w, __nv_bfloat16* __restrict__ y, int64_t ldy, int H, int HV,
+    float scale, float eps, int* err) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t s0 = smem_u32(smem);
-  float* A32 = reinterpret_cast<float*>(smem + GdnSmem::A32);
-  float* T32 = reinterpret_cast<float*>(smem + GdnSmem::T32);
-  float* X32 = reinterpret_cast<float*>(smem + GdnSmem::X32);
-  float* sG = reinterpret_cast<float*>(smem + GdnSmem::VEC);
-  float* sEG = sG + CH;
-  float* sEGl = sEG + CH;
-  float* sBeta = sEGl + CH;
-  float* sSS = sBeta + CH;  // [NW/4][64] partial sums of squares of the output rows
-  constexpr int NT_ = NW * 32;          // threads
-  constexpr int NQ = NW / 4;            // column groups of the 64-row products
-  constexpr int KK_NT = 8 / NQ;         // n-tiles per warp, 64-column outputs
-  constexpr int V_NT = 16 / NQ;         // n-tiles per warp, 128-column outputs
-  constexpr int S_NT = 16 / (NW / 8);   // n-tiles per warp of the state
+  uint64_t* loaded = reinterpret_cast<uint64_t*>(smem + S_BAR);  // [2] chunk tiles landed
+  uint64_t* ready = loaded + 2;                                  // [2] chunk prepared
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(ready + 2);
 
-  const int seq = blockIdx.x, hv = blockIdx.y;
+  // value heads vary fastest: the CTAs resident together read whole token rows of q, k, v, z
+  // (DRAM page locality) and the value heads of one key head share its q, k tiles in L2
+  const int hv = blockIdx.x, seq = blockIdx.y;
   const int h = hv / (HV / H);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g4 = lane >> 2, c4 = lane & 3;
@@ -175,307 +230,451 @@ __global__ void __launch_bounds__(NW * 32, 1) gdn_prefill_kernel(
     if (tid == 0) set_error(err, QW_DEV_ERR_INDEX);
     return;
   }
-  float* Sg = state + ((int64_t)slot * HV + hv) * DKc * DKc;
-  const float a_log = expf(A_log[hv]);
-  const float dtb = bf2f(dt_bias[hv]);
   const int n_chunks = (n + CH - 1) / CH;
-  gdn_load_chunk<NT_>(s0, 0, q, k, v, t_begin, min(CH, n), h, hv, H, HV, tid);
-  const __nv_bfloat16* zrow = z + (int64_t)hv * DKc;
-  const int mt = warp & 3, nh = warp >> 2;  // 64-row products: m-tile and column group
-  uint32_t wpair[V_NT];  // norm weight pairs of this thread's output columns
-#pragma unroll
-  for (int nt = 0; nt < V_NT; ++nt)
-    wpair[nt] = *reinterpret_cast<const uint32_t*>(norm_w + nh * (V_NT * 8) + nt * 8 + c4 * 2);
 
-  // state accumulator: warp w owns dv rows [16 (w % 8), +16) and dk columns of group w / 8
-  const int smt = warp & 7, sng = warp >> 3;
-  float sacc[S_NT][4];
-#pragma unroll
-  for (int nt = 0; nt < S_NT; ++nt) {
-    const int col = sng * (S_NT * 8) + nt * 8 + c4 * 2;
-    const float2 lo = *reinterpret_cast<const float2*>(Sg + (int64_t)(smt * 16 + g4) * DKc + col);
-    const float2 hi = *reinterpret_cast<const float2*>(Sg + (int64_t)(smt * 16 + g4 + 8) * DKc + col);
-    sacc[nt][0] = lo.x;
-    sacc[nt][1] = lo.y;
-    sacc[nt][2] = hi.x;
-    sacc[nt][3] = hi.y;
+  if (tid == 0) {
+    mbar_init(&loaded[0], 1);
+    mbar_init(&loaded[1], 1);
+    mbar_init(&ready[0], 256);
+    mbar_init(&ready[1], 256);
+    *abort_flag = 0;
+    fence_barrier_init();
   }
-  store_tile_bf16<S_NT, DKc>(smem + GdnSmem::S, sacc, smt * 16, sng * (S_NT * 8), lane, 1.f);
+  // blocks of T above the diagonal stay zero in both buffers
+  for (int e = tid; e < 2 * CH * CH; e += 512) {
+    const int bb = e / (CH * CH), r = (e / CH) % CH, cc = e % CH;
+    if ((cc >> 4) > (r >> 4))
+      *reinterpret_cast<__nv_bfloat16*>(smem + bb * BUF + B_T + swz_elem(r, cc)) = f2bf(0.f);
+  }
+  __syncthreads();
+  if (tid == 0) {
+    tma_prefetch_desc(&tm_q);
+    tma_prefetch_desc(&tm_k);
+    tma_prefetch_desc(&tm_v);
+    for (int c = 0; c < 2 && c < n_chunks; ++c)
+      issue_chunk_loads(smem + c * BUF, &loaded[c], &tm_q, &tm_k, &tm_v, h, hv, t_begin + c * CH);
+  }
 
-  // blocks of T above the diagonal stay zero for every chunk
-  for (int e = tid; e < CH * CH; e += NT_) {
-    const int r = e / CH, c = e % CH;
-    if ((c >> 4) > (r >> 4))
-      *reinterpret_cast<__nv_bfloat16*>(smem + GdnSmem::T + sw_elem<CH>(r, c)) = f2bf(0.f);
-  }
-  // raw b, a of the gating for token tid of the chunk, loaded one chunk ahead
-  float g_b = 0.f, g_a = 0.f;
-  if (tid < CH && tid < n) {
-    g_b = bf2f(ba[(int64_t)(t_begin + tid) * ldba + hv]);
-    g_a = bf2f(ba[(int64_t)(t_begin + tid) * ldba + HV + hv]);
-  }
-  for (int ch = 0; ch < n_chunks; ++ch) {
-    const int tc = t_begin + ch * CH;
-    const int nc = min(CH, n - ch * CH);
-    const int b = ch & 1;
-    const float cur_b = g_b, cur_a = g_a;
-    if (tid < CH) {
-      g_b = g_a = 0.f;
-      if ((ch + 1) * CH + tid < n) {
-        g_b = bf2f(ba[(int64_t)(tc + CH + tid) * ldba + hv]);
-        g_a = bf2f(ba[(int64_t)(tc + CH + tid) * ldba + HV + hv]);
-      }
-    }
-    const uint32_t sQ = s0 + GdnSmem::QKV + b * 3 * GdnSmem::TILE;
-    const uint32_t sK = sQ + GdnSmem::TILE, sV = sK + GdnSmem::TILE;
-    uint8_t* pK = smem + GdnSmem::QKV + b * 3 * GdnSmem::TILE + GdnSmem::TILE;
-    uint8_t* pV = pK + GdnSmem::TILE;
-    // z rows of this chunk (consumed by the epilogue), then the next chunk's q/k/v into the
-    // other buffer (its previous contents are dead)
-    for (int i = tid; i < CH * 16; i += NT_) {
-      const int r = i >> 4, c = i & 15;
-      const bool ok = r < nc;
-      cpa16(s0 + GdnSmem::Z + (uint32_t)(r * GdnSmem::ZLD + c * 8) * 2, zrow + (int64_t)(tc + (ok ? r : 0)) * ldz + c * 8, ok);
-    }
-    asm volatile("cp.async.commit_group;" ::: "memory");
-    if (ch + 1 < n_chunks) {
-      gdn_load_chunk<NT_>(s0, b ^ 1, q, k, v, tc + CH, min(CH, n - (ch + 1) * CH), h, hv, H, HV, tid);
-    } else {
-      asm volatile("cp.async.commit_group;" ::: "memory");
-    }
-    // gating (threads 0..63) and the within-chunk cumulative log decay
-    if (tid < CH) {
-      float gg = 0.f, bb = 0.f;
-      if (tid < nc) {
-        const float xa = cur_a + dtb;
-        const float sp = xa <= 20.f ? logf(1.f + expf(xa)) : xa;
-        gg = -a_log * sp;
-        bb = bf16_round(1.f / (1.f + expf(-cur_b)));
-      }
-      sBeta[tid] = bb;
-      float x = gg;
+  if (warp < 8) {
+    // =============================================================== prep warps
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(PREP_REGS));
+    const int mt = warp & 3, nh = warp >> 2;
+    float* sG = reinterpret_cast<float*>(smem + S_IG);
+    float* sBeta = sG + CH;
+    float* sEGl = sBeta + CH;
+    float* blk = reinterpret_cast<float*>(smem + S_BLK);
+    const float a_log = expf(A_log[hv]);
+    const float dtb = bf2f(dt_bias[hv]);
+    // raw b, a of tokens lane and lane + 32 of the next chunk (warps 0 and 1 both hold all 64)
+    float nb[2] = {0.f, 0.f}, na[2] = {0.f, 0.f};
+    if (warp < 2) {
 #pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const float yv = __shfl_up_sync(0xffffffffu, x, o);
-        if (lane >= o) x += yv;
-      }
-      sG[tid] = x;
-    }
-    asm volatile("cp.async.wait_group 2;" ::: "memory");  // this chunk's q/k/v tiles have landed
-    __syncthreads();
-    if (tid >= 32 && tid < CH) sG[tid] += sG[31];
-    __syncthreads();
-    const float G_last = sG[CH - 1];
-    if (tid < CH) {
-      sEG[tid] = expf(sG[tid]);
-      sEGl[tid] = expf(G_last - sG[tid]);
-    }
-    // ---------------------------------------------------------------- K K^T -> A,  Q K^T -> P
-    {
-      float kk[KK_NT][4], qk[KK_NT][4];
-#pragma unroll
-      for (int i = 0; i < KK_NT; ++i) kk[i][0] = kk[i][1] = kk[i][2] = kk[i][3] = qk[i][0] = qk[i][1] = qk[i][2] = qk[i][3] = 0.f;
-      mma_tile<KK_NT, 8, DKc, DKc, false, false>(kk, sK, sK, mt * 16, nh * (KK_NT * 8), lane);
-      mma_tile<KK_NT, 8, DKc, DKc, false, false>(qk, sQ, sK, mt * 16, nh * (KK_NT * 8), lane);
-#pragma unroll
-      for (int nt = 0; nt < KK_NT; ++nt) {
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int t = mt * 16 + g4 + ((e >> 1) << 3);
-          const int s = nh * (KK_NT * 8) + nt * 8 + c4 * 2 + (e & 1);
-          const float dec = (s <= t) ? expf(sG[t] - sG[s]) : 0.f;
-          A32[t * LDA + s] = (s < t) ? sBeta[t] * dec * kk[nt][e] : 0.f;
-          qk[nt][e] = (s <= t) ? scale * dec * qk[nt][e] : 0.f;
+      for (int hf = 0; hf < 2; ++hf) {
+        const int t = lane + 32 * hf;
+        if (t < n) {
+          nb[hf] = bf2f(ba[(int64_t)(t_begin + t) * ldba + hv]);
+          na[hf] = bf2f(ba[(int64_t)(t_begin + t) * ldba + HV + hv]);
         }
       }
-      store_tile_bf16<KK_NT, CH>(smem + GdnSmem::P, qk, mt * 16, nh * (KK_NT * 8), lane, 1.f);
     }
-    __syncthreads();
-
-    // ---------------------------------------------------------------- T = (I + A)^-1, blocked
-    if (warp < 4) {
-      // invert the unit lower-triangular diagonal block b = warp; lane j < 16 owns column j
-      const int bb = warp, j = lane;
-      float tcol[16];
-      const float* arow = A32 + (bb * 16) * LDA + bb * 16;
+    for (int c = 0; c < n_chunks; ++c) {
+      const int b = c & 1;
+      uint8_t* buf = smem + b * BUF;
+      const uint32_t sb = s0 + b * BUF;
+      const int nc = min(CH, n - c * CH);
+      float* vec = reinterpret_cast<float*>(buf + B_VEC);
+      const float cb[2] = {nb[0], nb[1]}, ca[2] = {na[0], na[1]};
+      if (warp < 2) {
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        // row i of the block: i broadcast loads issued together, then a predicated dot
-        // product with the column computed so far (T[k][j] = 0 for k < j)
-        float a[16];
-#pragma unroll
-        for (int kx = 0; kx < i; ++kx) a[kx] = arow[i * LDA + kx];
-        float acc = 0.f;
-#pragma unroll
-        for (int kx = 0; kx < i; ++kx) acc += (kx >= j) ? a[kx] * tcol[kx] : 0.f;
-        tcol[i] = (i == j) ? 1.f : (i > j ? -acc : 0.f);
-      }
-      if (j < 16) {
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          T32[(bb * 16 + i) * LDA + bb * 16 + j] = tcol[i];
-          *reinterpret_cast<__nv_bfloat16*>(smem + GdnSmem::T + sw_elem<CH>(bb * 16 + i, bb * 16 + j)) = f2bf(tcol[i]);
+        for (int hf = 0; hf < 2; ++hf) {
+          const int t = (c + 1) * CH + lane + 32 * hf;
+          nb[hf] = na[hf] = 0.f;
+          if (t < n) {
+            nb[hf] = bf2f(ba[(int64_t)(t_begin + t) * ldba + hv]);
+            na[hf] = bf2f(ba[(int64_t)(t_begin + t) * ldba + HV + hv]);
+          }
         }
       }
-    } else {
-      // meanwhile: b e^G K into KB and b V in place (inputs of W and U)
-      for (int i = tid - 128; i < CH * 16; i += NT_ - 128) {
-        const int r = i >> 4, c = i & 15;
-        float kf[8], vf[8];
-        load_bf16x8(reinterpret_cast<const __nv_bfloat16*>(pK + sw<DKc>(r, c)), kf);
-        load_bf16x8(reinterpret_cast<const __nv_bfloat16*>(pV + sw<DKc>(r, c)), vf);
-        const float fk = sBeta[r] * sEG[r], fv = sBeta[r];
-#pragma unroll
-        for (int jj = 0; jj < 8; ++jj) {
-          kf[jj] *= fk;
-          vf[jj] *= fv;
+      mbar_wait(&loaded[b], (c >> 1) & 1, abort_flag, err, QW_DEV_ERR_TIMEOUT_GDN);
+      if (nc < CH) {
+        // rows past the request hold the next request's tokens (or TMA zero fill): clear them
+        for (int e = tid; e < (CH - nc) * 16 * 3; e += 256) {
+          const int tile = e % 3, rc = e / 3;
+          *reinterpret_cast<uint4*>(buf + tile * TILE + swz(nc + (rc >> 4), rc & 15)) = make_uint4(0, 0, 0, 0);
         }
-        store_bf16x8(reinterpret_cast<__nv_bfloat16*>(smem + GdnSmem::KB + sw<DKc>(r, c)), kf);
-        store_bf16x8(reinterpret_cast<__nv_bfloat16*>(pV + sw<DKc>(r, c)), vf);
       }
-    }
-    __syncthreads();
-    // below-diagonal blocks: with M_ik = T_ii A_ik, T_ij = -sum_{k=j}^{i-1} M_ik T_kj.
-    // M for the six blocks (1,0) (2,0) (2,1) (3,0) (3,1) (3,2) in one pass, then one pass
-    // per distance i - j; each T_ij goes to T32 (read by later levels) and to bf16 T.
-    for (int e = tid; e < 6 * 256; e += NT_) {
-      const int pi = e >> 8, r = (e >> 4) & 15, c = e & 15;
-      const int i = pi < 1 ? 1 : (pi < 3 ? 2 : 3);
-      const int kk = pi < 1 ? 0 : (pi < 3 ? pi - 1 : pi - 3);
-      float acc = 0.f;
+      // ---- gating and the within-chunk cumulative log decay (warps 0, 1)
+      if (warp < 2) {
+        float gg[2], bt[2];
 #pragma unroll
-      for (int x = 0; x < 16; ++x) acc += T32[(i * 16 + r) * LDA + i * 16 + x] * A32[(i * 16 + x) * LDA + kk * 16 + c];
-      X32[pi * 256 + r * 16 + c] = acc;
-    }
-    __syncthreads();
+        for (int hf = 0; hf < 2; ++hf) {
+          gg[hf] = bt[hf] = 0.f;
+          if (lane + 32 * hf < nc) {
+            const float xa = ca[hf] + dtb;
+            const float sp = xa <= 20.f ? logf(1.f + expf(xa)) : xa;
+            gg[hf] = -a_log * sp;
+            bt[hf] = bf16_round(1.f / (1.f + expf(-cb[hf])));
+          }
+        }
+        float x0 = gg[0], x1 = gg[1];
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const float y0 = __shfl_up_sync(0xffffffffu, x0, o), y1 = __shfl_up_sync(0xffffffffu, x1, o);
+          if (lane >= o) {
+            x0 += y0;
+            x1 += y1;
+          }
+        }
+        x1 += __shfl_sync(0xffffffffu, x0, 31);
+        const float G_last = __shfl_sync(0xffffffffu, x1, 31);
+        const int t = lane + 32 * warp;
+        const float G = warp == 0 ? x0 : x1;
+        sG[t] = G;
+        sBeta[t] = warp == 0 ? bt[0] : bt[1];
+        vec[t] = expf(G);
+        sEGl[t] = expf(G_last - G);
+        if (t == 0) vec[CH] = expf(G_last);
+      }
+      named_bar(1);
+      // ---- K K^T -> A (fp32 blocks), Q K^T -> P (bf16)
+      {
+        float kk[4][4], qk[4][4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) kk[i][e] = qk[i][e] = 0.f;
+        if (nh * 32 <= mt * 16 + 15) {  // tiles wholly above the diagonal stay zero
+          mma_tile<4, 8, false, false>(kk, sb + B_K, sb + B_K, mt * 16, nh * 32, lane);
+          mma_tile<4, 8, false, false>(qk, sb + B_Q, sb + B_K, mt * 16, nh * 32, lane);
+        }
+#pragma unroll
+        for (int nt = 0; nt < 4; ++nt) {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int t = mt * 16 + g4 + ((e >> 1) << 3);
+            const int s = nh * 32 + nt * 8 + c4 * 2 + (e & 1);
+            const float dec = (s <= t) ? expf(sG[t] - sG[s]) : 0.f;
+            const int bi = t >> 4, bj = s >> 4;
+            if (bj < bi) blk[blk_lo(bi, bj) * BLK + (t & 15) * BLD + (s & 15)] = sBeta[t] * dec * kk[nt][e];
+            else if (bj == bi) blk[(6 + bi) * BLK + (t & 15) * BLD + (s & 15)] = (s < t) ? sBeta[t] * dec * kk[nt][e] : 0.f;
+            qk[nt][e] = (s <= t) ? scale * dec * qk[nt][e] : 0.f;
+          }
+        }
+        store_tile_bf16<4>(buf + B_P, qk, mt * 16, nh * 32, lane, 1.f);
+      }
+      named_bar(1);
+      // ---- diagonal blocks of T (warps 0-3) || b e^G K, e^{G_C-G} K, b V (warps 4-7)
+      if (warp < 4) {
+        const int i = warp, j = lane;  // lane j < 16 owns column j of T_ii
+        const float* a = blk + (6 + i) * BLK;
+        float tcol[16];
+#pragma unroll
+        for (int r = 0; r < 16; ++r) {
+          float av[16];
+#pragma unroll
+          for (int kx = 0; kx < r; ++kx) av[kx] = a[r * BLD + kx];
+          float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+          for (int kx = 0; kx < r; ++kx) acc[kx & 3] += av[kx] * tcol[kx];  // tcol[kx] = 0 for kx < j
+          const float sum = (acc[0] + acc[1]) + (acc[2] + acc[3]);
+          tcol[r] = (r == j) ? 1.f : (r > j ? -sum : 0.f);
+        }
+        if (j < 16) {
+          float* td = blk + (10 + i) * BLK;
+#pragma unroll
+          for (int r = 0; r < 16; ++r) {
+            td[r * BLD + j] = tcol[r];
+            *reinterpret_cast<__nv_bfloat16*>(buf + B_T + swz_elem(16 * i + r, 16 * i + j)) = f2bf(tcol[r]);
+          }
+        }
+      } else {
+        for (int e = tid - 128; e < CH * 16; e += 128) {
+          const int r = e >> 4;
+          const uint32_t off = swz(r, e & 15);
+          float kf[8], vf[8], kb[8], kd[8];
+          load_bf16x8(reinterpret_cast<const __nv_bfloat16*>(buf + B_K + off), kf);
+          load_bf16x8(reinterpret_cast<const __nv_bfloat16*>(buf + B_V + off), vf);
+          const float fb = sBeta[r], fk = fb * vec[r], fd = sEGl[r];
+#pragma unroll
+          for (int jj = 0; jj < 8; ++jj) {
+            kb[jj] = kf[jj] * fk;
+            kd[jj] = kf[jj] * fd;
+            vf[jj] *= fb;
+          }
+          store_bf16x8(reinterpret_cast<__nv_bfloat16*>(buf + B_W + off), kb);
+          store_bf16x8(reinterpret_cast<__nv_bfloat16*>(buf + B_K + off), kd);
+          store_bf16x8(reinterpret_cast<__nv_bfloat16*>(buf + B_V + off), vf);
+        }
+      }
+      named_bar(1);
+      // ---- M_ik = T_ii A_ik for the six blocks below the diagonal (warps 0-5)
+      if (warp < 6) {
+        const int p = warp, i = p < 1 ? 1 : (p < 3 ? 2 : 3);
+        float acc[2][4] = {};
+        blk_mma(acc, blk + (10 + i) * BLK, blk + p * BLK, lane);
+        blk_store(blk + (14 + p) * BLK, acc, 1.f, nullptr, 0, 0, lane);
+      }
+      named_bar(1);
+      // ---- T_ij = -sum_{k=j}^{i-1} M_ik T_kj, one level of i - j at a time
 #pragma unroll 1
-    for (int d = 1; d < 4; ++d) {
-      const int nb = 4 - d;  // number of blocks at this distance
-      for (int e = tid; e < nb * 256; e += NT_) {
-        const int bi = e >> 8, r = (e >> 4) & 15, c = e & 15;
-        const int j = bi, i = bi + d;
-        float acc = 0.f;
-        for (int kb = j; kb < i; ++kb) {
-          const int pi = (i == 1) ? 0 : (i == 2 ? 1 + kb : 3 + kb);  // M_{i,kb}
-#pragma unroll
-          for (int x = 0; x < 16; ++x) acc += X32[pi * 256 + r * 16 + x] * T32[(kb * 16 + x) * LDA + j * 16 + c];
+      for (int d = 1; d < 4; ++d) {
+        if (warp < 4 - d) {
+          const int j = warp, i = warp + d;
+          float acc[2][4] = {};
+          for (int k = j; k < i; ++k)
+            blk_mma(acc, blk + (14 + blk_lo(i, k)) * BLK, blk + (k == j ? 10 + j : blk_lo(k, j)) * BLK, lane);
+          blk_store(blk + blk_lo(i, j) * BLK, acc, -1.f, buf + B_T, 16 * i, 16 * j, lane);
         }
-        T32[(i * 16 + r) * LDA + j * 16 + c] = -acc;
-        *reinterpret_cast<__nv_bfloat16*>(smem + GdnSmem::T + sw_elem<CH>(i * 16 + r, j * 16 + c)) = f2bf(-acc);
+        named_bar(1);
       }
-      __syncthreads();
-    }
-
-    // ---------------------------------------------------------------- W = T (b e^G K), stored negated
-    {
-      float w[V_NT][4];
+      // ---- W = T (b e^G K), stored negated over b e^G K
+      {
+        float w[8][4];
 #pragma unroll
-      for (int i = 0; i < V_NT; ++i) w[i][0] = w[i][1] = w[i][2] = w[i][3] = 0.f;
-      mma_tile<V_NT, 4, CH, DKc, false, true>(w, s0 + GdnSmem::T, s0 + GdnSmem::KB, mt * 16, nh * (V_NT * 8), lane);
-      store_tile_bf16<V_NT, DKc>(smem + GdnSmem::W, w, mt * 16, nh * (V_NT * 8), lane, -1.f);
-    }
-    __syncthreads();
-    // ---------------------------------------------------------------- U = T (b V) - W S0^T
-    {
-      float u[V_NT][4];
+        for (int i = 0; i < 8; ++i) w[i][0] = w[i][1] = w[i][2] = w[i][3] = 0.f;
+#pragma unroll 1
+        for (int ks = 0; ks <= mt; ++ks) {  // T is lower triangular by 16-row blocks
+          uint32_t a[4];
+          frag_a(sb + B_T, mt * 16, ks * 16, lane, a);
 #pragma unroll
-      for (int i = 0; i < V_NT; ++i) u[i][0] = u[i][1] = u[i][2] = u[i][3] = 0.f;
-      mma_tile<V_NT, 4, CH, DKc, false, true>(u, s0 + GdnSmem::T, sV, mt * 16, nh * (V_NT * 8), lane);
-      mma_tile<V_NT, 8, DKc, DKc, false, false>(u, s0 + GdnSmem::W, s0 + GdnSmem::S, mt * 16, nh * (V_NT * 8), lane);
-      store_tile_bf16<V_NT, DKc>(smem + GdnSmem::U, u, mt * 16, nh * (V_NT * 8), lane, 1.f);
-    }
-    __syncthreads();
-    // ---------------------------------------------------------------- O, gated RMSNorm; e^{G_C - G} K into KB
-    {
-      float o[V_NT][4];
-#pragma unroll
-      for (int i = 0; i < V_NT; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
-      mma_tile<V_NT, 8, DKc, DKc, false, false>(o, sQ, s0 + GdnSmem::S, mt * 16, nh * (V_NT * 8), lane);
-      const float f0 = scale * sEG[mt * 16 + g4], f1 = scale * sEG[mt * 16 + g4 + 8];
-#pragma unroll
-      for (int i = 0; i < V_NT; ++i) {
-        o[i][0] *= f0;
-        o[i][1] *= f0;
-        o[i][2] *= f1;
-        o[i][3] *= f1;
+          for (int nt = 0; nt < 8; nt += 2) {
+            uint32_t bq[4];
+            frag_b_t(sb + B_W, nh * 64 + nt * 8, ks * 16, lane, bq);
+            mma16816(w[nt], a, bq[0], bq[1]);
+            mma16816(w[nt + 1], a, bq[2], bq[3]);
+          }
+        }
+        named_bar(1);
+        store_tile_bf16<8>(buf + B_W, w, mt * 16, nh * 64, lane, -1.f);
       }
-      mma_tile<V_NT, 4, CH, DKc, false, true>(o, s0 + GdnSmem::P, s0 + GdnSmem::U, mt * 16, nh * (V_NT * 8), lane);
-      // o rounds to bf16 (the reference's GDN output dtype), then y = o rstd w z sigmoid(z)
-      float ss[2] = {0.f, 0.f};
+      mbar_arrive(&ready[b]);
+    }
+  } else {
+    // =============================================================== state warps
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(STATE_REGS));
+    const int sw = warp - 8, dv0 = sw * 16, stid = tid - 256;
+    float* sSS = reinterpret_cast<float*>(smem + S_SS);  // [8][64]
+    float* sRstd = sSS + 8 * CH;
+    const uint32_t zb = s0 + S_Z + sw * (CH * 32);
+    const uint32_t ub = s0 + S_U + sw * (16 * CH * 2);  // U^T strip, rows dv, 128-byte swizzled
+    float* Sg = state + ((int64_t)slot * HV + hv) * D * D;
+    float sacc[16][4];
 #pragma unroll
-      for (int i = 0; i < V_NT; ++i) {
+    for (int nt = 0; nt < 16; ++nt) {
+      const int col = nt * 8 + c4 * 2;
+      const float2 lo = *reinterpret_cast<const float2*>(Sg + (int64_t)(dv0 + g4) * D + col);
+      const float2 hi = *reinterpret_cast<const float2*>(Sg + (int64_t)(dv0 + g4 + 8) * D + col);
+      sacc[nt][0] = lo.x;
+      sacc[nt][1] = lo.y;
+      sacc[nt][2] = hi.x;
+      sacc[nt][3] = hi.y;
+    }
+    const float w_lo = bf2f(norm_w[dv0 + g4]), w_hi = bf2f(norm_w[dv0 + g4 + 8]);
+    // staging row t holds dv0..dv0+15 of token t: 32 bytes, 16-byte halves swapped on rows 4-7 mod 8
+    auto z_addr = [&](int t, int half) -> uint32_t { return zb + t * 32 + ((half ^ ((t >> 2) & 1)) << 4); };
+    auto prefetch_z = [&](int c) {
+      const int64_t tz = t_begin + (int64_t)c * CH;
+      const int ncz = min(CH, n - c * CH);
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          o[i][e] = bf16_round(o[i][e]);
-          ss[e >> 1] += o[i][e] * o[i][e];
+      for (int i = 0; i < 4; ++i) {
+        const int q = lane + 32 * i, t = q >> 1, half = q & 1;
+        const bool ok = t < ncz;
+        cpa16(z_addr(t, half), z + (tz + (ok ? t : 0)) * ldz + (int64_t)hv * D + dv0 + half * 8, ok);
+      }
+      asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    if (n_chunks > 0) prefetch_z(0);
+    for (int c = 0; c < n_chunks; ++c) {
+      const int b = c & 1;
+      const uint32_t sb = s0 + b * BUF;
+      const float* vec = reinterpret_cast<const float*>(smem + b * BUF + B_VEC);
+      const int nc = min(CH, n - c * CH);
+      const int64_t tc = t_begin + (int64_t)c * CH;
+      mbar_wait(&ready[b], (c >> 1) & 1, abort_flag, err, QW_DEV_ERR_TIMEOUT_GDN);
+      // ---- U^T = (bV)^T T^T + S0 (-W)^T, rounded to bf16 into the warp's strip
+      {
+        float u[8][4];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) u[i][0] = u[i][1] = u[i][2] = u[i][3] = 0.f;
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks) {
+          uint32_t a[4];
+          frag_a_t(sb + B_V, dv0, ks * 16, lane, a);
+#pragma unroll
+          for (int np = ks; np < 4; ++np) {  // T[t][s] = 0 for s-blocks after the t-block
+            uint32_t bq[4];
+            frag_b(sb + B_T, np * 16, ks * 16, lane, bq);
+            mma16816(u[2 * np], a, bq[0], bq[1]);
+            mma16816(u[2 * np + 1], a, bq[2], bq[3]);
+          }
+        }
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks) {
+          uint32_t a[4];
+          acc_to_a(sacc, ks, a);
+#pragma unroll
+          for (int np = 0; np < 4; ++np) {
+            uint32_t bq[4];
+            frag_b(sb + B_W, np * 16, ks * 16, lane, bq);
+            mma16816(u[2 * np], a, bq[0], bq[1]);
+            mma16816(u[2 * np + 1], a, bq[2], bq[3]);
+          }
+        }
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks) {
+          uint32_t a[4];
+          acc_to_a(u, ks, a);
+          stsm_x4(ub + swz(lane & 15, 2 * ks + (lane >> 4)), a);
+        }
+        __syncwarp();
+      }
+      // ---- O^T = scale S0 Q^T diag(e^G) + U^T P^T
+      float o[8][4];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks) {
+        uint32_t a[4];
+        acc_to_a(sacc, ks, a);
+#pragma unroll
+        for (int np = 0; np < 4; ++np) {
+          uint32_t bq[4];
+          frag_b(sb + B_Q, np * 16, ks * 16, lane, bq);
+          mma16816(o[2 * np], a, bq[0], bq[1]);
+          mma16816(o[2 * np + 1], a, bq[2], bq[3]);
         }
       }
 #pragma unroll
-      for (int rr = 0; rr < 2; ++rr) {
-        ss[rr] += __shfl_xor_sync(0xffffffffu, ss[rr], 1);
-        ss[rr] += __shfl_xor_sync(0xffffffffu, ss[rr], 2);
+      for (int nt = 0; nt < 8; ++nt) {
+        const float2 e2 = *reinterpret_cast<const float2*>(vec + nt * 8 + 2 * c4);
+        o[nt][0] *= scale * e2.x;
+        o[nt][1] *= scale * e2.y;
+        o[nt][2] *= scale * e2.x;
+        o[nt][3] *= scale * e2.y;
       }
-      if (c4 == 0) {
-        sSS[nh * CH + mt * 16 + g4] = ss[0];
-        sSS[nh * CH + mt * 16 + g4 + 8] = ss[1];
-      }
-      for (int i = tid; i < CH * 16; i += NT_) {
-        const int r = i >> 4, c = i & 15;
-        float kf[8];
-        load_bf16x8(reinterpret_cast<const __nv_bfloat16*>(pK + sw<DKc>(r, c)), kf);
-        const float f = sEGl[r];
 #pragma unroll
-        for (int jj = 0; jj < 8; ++jj) kf[jj] *= f;
-        store_bf16x8(reinterpret_cast<__nv_bfloat16*>(smem + GdnSmem::KB + sw<DKc>(r, c)), kf);
-      }
-      asm volatile("cp.async.wait_group 1;" ::: "memory");  // this chunk's z rows
-      __syncthreads();
-      const __nv_bfloat16* sZ = reinterpret_cast<const __nv_bfloat16*>(smem + GdnSmem::Z);
+      for (int ks = 0; ks < 4; ++ks) {
+        uint32_t a[4];
+        frag_a(ub, 0, ks * 16, lane, a);
 #pragma unroll
-      for (int rr = 0; rr < 2; ++rr) {
-        const int t = mt * 16 + g4 + rr * 8;
-        if (t >= nc) continue;
-        float ssum = 0.f;
-#pragma unroll
-        for (int gq = 0; gq < NQ; ++gq) ssum += sSS[gq * CH + t];
-        const float rstd = rsqrtf(ssum / (float)DKc + eps);
-        const int64_t tok = tc + t;
-        const __nv_bfloat16* zr = sZ + t * GdnSmem::ZLD + nh * (V_NT * 8);
-        __nv_bfloat16* dst = y + tok * ldy + (int64_t)hv * DKc + nh * (V_NT * 8);
-#pragma unroll
-        for (int nt = 0; nt < V_NT; ++nt) {
-          const int col = nt * 8 + c4 * 2;
-          float z0, z1, w0, w1;
-          unpack_bf16x2(*reinterpret_cast<const uint32_t*>(zr + col), z0, z1);
-          unpack_bf16x2(wpair[nt], w0, w1);
-          const float y0 = o[nt][rr * 2] * rstd * w0 * (z0 / (1.f + __expf(-z0)));
-          const float y1 = o[nt][rr * 2 + 1] * rstd * w1 * (z1 / (1.f + __expf(-z1)));
-          *reinterpret_cast<uint32_t*>(dst + col) = pack_bf16x2(y0, y1);
+        for (int np = ks; np < 4; ++np) {  // P[t][s] = 0 for s > t
+          uint32_t bq[4];
+          frag_b(sb + B_P, np * 16, ks * 16, lane, bq);
+          mma16816(o[2 * np], a, bq[0], bq[1]);
+          mma16816(o[2 * np + 1], a, bq[2], bq[3]);
         }
       }
-    }
-    // ---------------------------------------------------------------- S <- e^{G_C} S + U^T (e^{G_C-G} K)
-    {
-      const float eC = expf(G_last);
+      // ---- S <- e^{G_C} S + U^T (e^{G_C-G} K)
+      {
+        const float eC = vec[CH];
 #pragma unroll
-      for (int nt = 0; nt < S_NT; ++nt) {
-        sacc[nt][0] *= eC;
-        sacc[nt][1] *= eC;
-        sacc[nt][2] *= eC;
-        sacc[nt][3] *= eC;
+        for (int nt = 0; nt < 16; ++nt) {
+          sacc[nt][0] *= eC;
+          sacc[nt][1] *= eC;
+          sacc[nt][2] *= eC;
+          sacc[nt][3] *= eC;
+        }
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks) {
+          uint32_t a[4];
+          frag_a(ub, 0, ks * 16, lane, a);
+#pragma unroll
+          for (int np = 0; np < 8; ++np) {
+            uint32_t bq[4];
+            frag_b_t(sb + B_K, np * 16, ks * 16, lane, bq);
+            mma16816(sacc[2 * np], a, bq[0], bq[1]);
+            mma16816(sacc[2 * np + 1], a, bq[2], bq[3]);
+          }
+        }
       }
-      mma_tile<S_NT, 4, DKc, DKc, true, true>(sacc, s0 + GdnSmem::U, s0 + GdnSmem::KB, smt * 16, sng * (S_NT * 8), lane);
-      store_tile_bf16<S_NT, DKc>(smem + GdnSmem::S, sacc, smt * 16, sng * (S_NT * 8), lane, 1.f);
+      named_bar(2);  // every state warp is done with chunk buffer b
+      if (stid == 0 && c + 2 < n_chunks && !*abort_flag) {
+        fence_proxy_async_smem();
+        issue_chunk_loads(smem + b * BUF, &loaded[b], &tm_q, &tm_k, &tm_v, h, hv, t_begin + (c + 2) * CH);
+      }
+      // ---- gated RMSNorm of bf16(o) over the 128 values of each token
+      {
+        float ss[8][2];
+#pragma unroll
+        for (int nt = 0; nt < 8; ++nt) {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) o[nt][e] = bf16_round(o[nt][e]);
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            float v = o[nt][j] * o[nt][j] + o[nt][2 + j] * o[nt][2 + j];
+            v += __shfl_xor_sync(0xffffffffu, v, 4);
+            v += __shfl_xor_sync(0xffffffffu, v, 8);
+            v += __shfl_xor_sync(0xffffffffu, v, 16);
+            ss[nt][j] = v;
+          }
+        }
+        if (g4 == 0) {
+#pragma unroll
+          for (int nt = 0; nt < 8; ++nt) {
+            sSS[sw * CH + nt * 8 + 2 * c4] = ss[nt][0];
+            sSS[sw * CH + nt * 8 + 2 * c4 + 1] = ss[nt][1];
+          }
+        }
+      }
+      named_bar(2);
+      if (stid < CH) {
+        float tot = 0.f;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) tot += sSS[w * CH + stid];
+        sRstd[stid] = rsqrtf(tot / (float)D + eps);
+      }
+      named_bar(2);
+      asm volatile("cp.async.wait_group 0;" ::: "memory");  // this chunk's z rows
+      __syncwarp();
+#pragma unroll
+      for (int np = 0; np < 4; ++np) {
+        const int tl = np * 16 + (lane & 7) + ((lane >> 4) << 3), half = (lane >> 3) & 1;
+        uint32_t zr[4], yr[4];
+        ldsm_x4_t(z_addr(tl, half), zr);
+        const float2 ra = *reinterpret_cast<const float2*>(sRstd + np * 16 + 2 * c4);
+        const float2 rb = *reinterpret_cast<const float2*>(sRstd + np * 16 + 8 + 2 * c4);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int nt = 2 * np + (q >> 1), hi = q & 1;
+          const float2 r = (q >> 1) ? rb : ra;
+          float z0, z1;
+          unpack_bf16x2(zr[q], z0, z1);
+          const float wv = hi ? w_hi : w_lo;
+          const float y0 = o[nt][2 * hi] * r.x * wv * __fdividef(z0, 1.f + __expf(-z0));
+          const float y1 = o[nt][2 * hi + 1] * r.y * wv * __fdividef(z1, 1.f + __expf(-z1));
+          yr[q] = pack_bf16x2(y0, y1);
+        }
+        stsm_x4_t(z_addr(tl, half), yr);
+      }
+      __syncwarp();
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int q = lane + 32 * i, t = q >> 1, half = q & 1;
+        if (t < nc) {
+          uint4 v;
+          asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+                       : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                       : "r"(z_addr(t, half)));
+          *reinterpret_cast<uint4*>(y + (tc + t) * ldy + (int64_t)hv * D + dv0 + half * 8) = v;
+        }
+      }
+      __syncwarp();
+      if (c + 1 < n_chunks) prefetch_z(c + 1);
     }
-    __syncthreads();
+    // ---- final state, in place
+#pragma unroll
+    for (int nt = 0; nt < 16; ++nt) {
+      const int col = nt * 8 + c4 * 2;
+      *reinterpret_cast<float2*>(Sg + (int64_t)(dv0 + g4) * D + col) = make_float2(sacc[nt][0], sacc[nt][1]);
+      *reinterpret_cast<float2*>(Sg + (int64_t)(dv0 + g4 + 8) * D + col) = make_float2(sacc[nt][2], sacc[nt][3]);
+    }
   }
-  asm volatile("cp.async.wait_group 0;" ::: "memory");
-  // ---------------------------------------------------------------- final state, in place
-#pragma unroll
-  for (int nt = 0; nt < S_NT; ++nt) {
-    const int col = sng * (S_NT * 8) + nt * 8 + c4 * 2;
-    *reinterpret_cast<float2*>(Sg + (int64_t)(smt * 16 + g4) * DKc + col) = make_float2(sacc[nt][0], sacc[nt][1]);
-    *reinterpret_cast<float2*>(Sg + (int64_t)(smt * 16 + g4 + 8) * DKc + col) = make_float2(sacc[nt][2], sacc[nt][3]);
+  __syncthreads();
+  if (tid == 0 && *abort_flag) {
+    // a wait gave up: leave time for any bulk copy still in flight before the CTA exits
+    const uint64_t t0 = globaltimer();
+    while (globaltimer() - t0 < 200000ull) {
+    }
   }
 }
 
@@ -485,28 +684,31 @@ using namespace qw;
 
 extern "C" int qw_gdn_prefill(const void* q, const void* k, const void* v, const void* ba, int64_t ldba,
                               const float* A_log, const void* dt_bias, const int32_t* cu_seqlens,
-                              const int32_t* slots, int64_t B, int64_t n_slots, float* state, const void* z,
-                              int64_t ldz, const void* norm_w, void* y, int64_t ldy, int64_t H, int64_t HV,
-                              int64_t dk, int64_t dv, float scale, float eps, qw_stream_t stream) {
+                              const int32_t* slots, int64_t B, int64_t T, int64_t n_slots, float* state,
+                              const void* z, int64_t ldz, const void* norm_w, void* y, int64_t ldy, int64_t H,
+                              int64_t HV, int64_t dk, int64_t dv, float scale, float eps, qw_stream_t stream) {
   QW_CHECK_ARG(q && k && v && ba && A_log && dt_bias && cu_seqlens && slots && state && z && norm_w && y, QW_ERR_ARG);
-  QW_CHECK_ARG(B > 0 && H > 0 && HV % H == 0 && n_slots > 0, QW_ERR_ARG);
-  if (dk != 128 || dv != 128) return QW_ERR_UNSUPPORTED;
+  QW_CHECK_ARG(B > 0 && T > 0 && T < (1ll << 31) && H > 0 && HV % H == 0 && n_slots > 0 && B <= 65535, QW_ERR_ARG);
+  if (dk != gdn::D || dv != gdn::D) return QW_ERR_UNSUPPORTED;
   QW_CHECK_ARG(((uintptr_t)q % 16) == 0 && ((uintptr_t)k % 16) == 0 && ((uintptr_t)v % 16) == 0 &&
-                   ((uintptr_t)state % 16) == 0 && ((uintptr_t)y % 4) == 0 &&
-                   ((uintptr_t)z % 16) == 0 && (ldz % 8) == 0 && (ldy % 2) == 0,
+                   ((uintptr_t)state % 16) == 0 && ((uintptr_t)y % 16) == 0 && (ldy % 8) == 0 &&
+                   ((uintptr_t)z % 16) == 0 && (ldz % 8) == 0,
                QW_ERR_ALIGN);
+  CUtensorMap tq, tk, tv;
+  if (!tmap_bf16_2d_sw128(&tq, q, T, H * dk, H * dk, 64, gdn::CH) ||
+      !tmap_bf16_2d_sw128(&tk, k, T, H * dk, H * dk, 64, gdn::CH) ||
+      !tmap_bf16_2d_sw128(&tv, v, T, HV * dv, HV * dv, 64, gdn::CH))
+    return QW_ERR_DRIVER;
   auto* s = reinterpret_cast<cudaStream_t>(stream);
-  constexpr int NW = 16;
   static bool cfg = false;
   if (!cfg) {
-    cudaFuncSetAttribute(gdn_prefill_kernel<NW>, cudaFuncAttributeMaxDynamicSharedMemorySize, GdnSmem::TOTAL);
+    cudaFuncSetAttribute(gdn_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, gdn::SMEM);
     cfg = true;
   }
-  dim3 grid((unsigned)B, (unsigned)HV);
-  gdn_prefill_kernel<NW><<<grid, NW * 32, GdnSmem::TOTAL, s>>>(
-      static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(k), static_cast<const __nv_bfloat16*>(v),
-      static_cast<const __nv_bfloat16*>(ba), ldba, A_log, static_cast<const __nv_bfloat16*>(dt_bias), cu_seqlens,
-      slots, (int)n_slots, state, static_cast<const __nv_bfloat16*>(z), ldz,
+  dim3 grid((unsigned)HV, (unsigned)B);
+  gdn_prefill_kernel<<<grid, 512, gdn::SMEM, s>>>(
+      tq, tk, tv, static_cast<const __nv_bfloat16*>(ba), ldba, A_log, static_cast<const __nv_bfloat16*>(dt_bias),
+      cu_seqlens, slots, (int)n_slots, state, static_cast<const __nv_bfloat16*>(z), ldz,
       static_cast<const __nv_bfloat16*>(norm_w), static_cast<__nv_bfloat16*>(y), ldy, (int)H, (int)HV, scale, eps,
       device_error_ptr());
   QW_LAUNCH_CHECK();

@@ -14,7 +14,8 @@ BF16 = torch.bfloat16
 OUT_BF16, OUT_F32_OF_BF16, OUT_SWIGLU = 0, 1, 2
 
 # Kernels launched through this module (a benchmark's claim of native launches), and an
-# optional list that, when set, receives (flops, start_event, end_event) per GEMM launch.
+# optional list that, when set, receives (flops, start_event, end_event, (M, N, K, out_kind))
+# per GEMM launch.
 LAUNCHES = [0]
 PROFILE = None
 
@@ -80,7 +81,7 @@ def gemm(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None, *, o
               out.stride(0), out_kind, _ptr(wsp), need, _stream())
     if prof is not None:
         e1.record()
-        prof.append((2.0 * M * N * K, e0, e1))
+        prof.append((2.0 * M * N * K, e0, e1, (M, N, K, out_kind)))
     LAUNCHES[0] += 2 if need else 1
     return out
 
@@ -154,9 +155,13 @@ def conv_prefill(x, conv_w, conv_state, cu, slots, has_initial, B, max_len, q_ou
 
 def gdn_prefill(q, k, v, ba, A_log, dt_bias, cu, slots, B, state, z, norm_w, y, H, HV, dk, dv, scale, eps):
     """Chunked delta rule + gated RMSNorm: y = norm(o) * w * silu(z), o never leaves the SM."""
+    T = q.shape[0]
+    if not (q.is_contiguous() and k.is_contiguous() and v.is_contiguous() and k.shape[0] == T and v.shape[0] == T
+            and q.numel() == T * H * dk and v.numel() == T * HV * dv):
+        raise ValueError("gdn_prefill expects contiguous q, k [T, H*dk] and v [T, HV*dv]")
     LAUNCHES[0] += 1
     _lib.call("qw_gdn_prefill", q.data_ptr(), k.data_ptr(), v.data_ptr(), ba.data_ptr(), ba.stride(0),
-              A_log.data_ptr(), dt_bias.data_ptr(), cu.data_ptr(), slots.data_ptr(), B, state.shape[0],
+              A_log.data_ptr(), dt_bias.data_ptr(), cu.data_ptr(), slots.data_ptr(), B, T, state.shape[0],
               state.data_ptr(), z.data_ptr(), z.stride(0), norm_w.data_ptr(), y.data_ptr(), y.stride(0), H, HV, dk,
               dv, scale, eps, _stream())
 

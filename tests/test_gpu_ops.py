@@ -205,7 +205,7 @@ def _gdn_inputs(g, lens, H=2, HV=6, S=None):
     return q, k, v, ba, A_log, dt, state
 
 
-@pytest.mark.parametrize("lens", [[64], [1, 63, 65, 130], [200, 7], [257]])
+@pytest.mark.parametrize("lens", [[64], [1, 63, 65, 130], [200, 7], [257], [0, 129, 3], [600, 1, 64, 448]])
 def test_gdn_prefill_chunked(K, lens):
     g = gen(7)
     H, HV, dk = 2, 6, 128
