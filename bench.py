@@ -34,6 +34,9 @@ sys.path.insert(0, ROOT)
 
 METRIC = "prefill+decode tok/s at B32/L1024 (27B hybrid, bf16); sum of call medians"
 UNIT = "tok/s"
+# The reference GPU path's published number for this exact metric on one B200
+# (results/shapes.csv: 1298.65 ms prefill + 35.26 ms decode at B32/L1024).
+BASELINE_TOK_S = 24589.0
 
 
 EPI_NAMES = {0: "bf16", 1: "f32-of-bf16", 2: "SwiGLU"}
@@ -339,8 +342,8 @@ def run_gpu(args):
                           "share_of_prefill": round(all_ms / mp, 4) if mp else None}}
     out = {"metric": METRIC, "value": round(tokens / (step_ms * 1e-3), 1), "unit": UNIT, "n_gpus": world,
            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_ms, 3), "higher_is_better": True,
-           "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-           "data": "synthetic (random-init N(0,0.02) 27B weights; uniform token ids, reference case seeds 26/27)",
+           "scaling": "weak", "vs_baseline": round(tokens / (step_ms * 1e-3) / BASELINE_TOK_S, 4),
+           "dtype": "bf16", "data": "synthetic (random-init N(0,0.02) 27B weights; uniform token ids, reference case seeds 26/27)",
            "config": {"workload": f"B{B}xL{L} prefill into a fresh cache + B{B} decode at {L} context, 27B hybrid",
                       "model": "Qwen3.8-27B hybrid geometry (48 GDN + 16 gated GQA), random init",
                       "global_batch": world * B, "seq_len": L, "parallelism": f"replicas x{world} (requests sharded)",

@@ -37,20 +37,22 @@ constexpr int CH = 64;  // chunk length
 constexpr int D = 128;  // key / value head dim
 constexpr int TILE = CH * D * 2;      // [64][128] bf16 = two 64-column halves of 8 KB
 constexpr int TILE64 = CH * CH * 2;   // [64][64] bf16
-// one chunk buffer: Q | K (then e^{G_C-G} K) | V (then b V) | b e^G K (then -W) | T | P | vectors
+// one chunk buffer: Q | K (then e^{G_C-G} K) | V (then b V) | b e^G K (then -W) | T | P
 constexpr int B_Q = 0, B_K = TILE, B_V = 2 * TILE, B_W = 3 * TILE, B_T = 4 * TILE, B_P = B_T + TILE64;
-constexpr int B_VEC = B_P + TILE64;   // e^G [64], e^{G_C}
-constexpr int BUF = B_VEC + 1024;     // multiple of 1024 (TMA swizzle atoms)
+constexpr int BUF = B_P + TILE64;     // multiple of 1024 (TMA swizzle atoms)
 constexpr int BLD = 20;               // row stride (floats) of a compact 16 x 16 fp32 block
 constexpr int BLK = 16 * BLD;         // floats per block
 constexpr int S_BLK = 2 * BUF;        // 20 blocks: [0,6) A_ij then T_ij (i > j), [6,10) A_ii, [10,14) T_ii, [14,20) M_ik
-constexpr int S_IG = S_BLK + 20 * BLK * 4;  // prep vectors: G, beta, e^{G_C-G} (3 x 64 fp32)
-constexpr int S_SS = S_IG + 3 * CH * 4;     // state: [8][64] partial sums of squares, rstd [64]
-constexpr int S_Z = S_SS + 9 * CH * 4;      // state: per-warp z / y staging [64][16] bf16
+// gating of a chunk (written by the state warps two chunks ahead, three slots):
+// G * log2(e), beta, e^{G_C - G}, e^G (64 each), e^{G_C}
+constexpr int GB_G2 = 0, GB_BETA = CH, GB_EGL = 2 * CH, GB_EG = 3 * CH, GB_EC = 4 * CH, GB_FLOATS = 4 * CH + 4;
+constexpr int S_GB = S_BLK + 20 * BLK * 4;
+constexpr int S_SS = S_GB + 3 * GB_FLOATS * 4;  // state: [8][64] partial sums of squares, rstd [64]
+constexpr int S_Z = (S_SS + 9 * CH * 4 + 127) / 128 * 128;  // state: per-warp z / y staging [64][16] bf16
 constexpr int S_U = S_Z + 8 * CH * 32;      // state: per-warp bf16 U^T strip [16][64]
 constexpr int S_BAR = S_U + 8 * 16 * CH * 2;
 constexpr int SMEM = S_BAR + 64 + 1024;     // + slack to align the base to 1024
-static_assert(BUF % 1024 == 0 && S_Z % 16 == 0, "layout alignment");
+static_assert(BUF % 1024 == 0 && S_Z % 128 == 0, "layout alignment");
 
 QW_DEV int blk_lo(int i, int j) { return i * (i - 1) / 2 + j; }  // i > j
 
@@ -189,6 +191,58 @@ QW_DEV void blk_store(float* out, float (*acc)[4], float mul, uint8_t* tile, int
   }
 }
 
+// Gating of one chunk by one warp (lane owns tokens lane and lane + 32; nc valid tokens):
+// g = -exp(A_log) softplus(a + dt_bias), beta = bf16(sigmoid(b)), G = inclusive cumsum of g.
+// The exponentials and logarithm use the approximate hardware forms, as the reference's
+// Triton gating kernel does.
+QW_DEV void chunk_gating(float* gb, const float* rb, const float* ra, int nc, float a_log, float dtb, int lane) {
+  float gg[2], bt[2];
+#pragma unroll
+  for (int hf = 0; hf < 2; ++hf) {
+    gg[hf] = bt[hf] = 0.f;
+    if (lane + 32 * hf < nc) {
+      const float xa = ra[hf] + dtb;
+      const float sp = xa <= 20.f ? __logf(1.f + __expf(xa)) : xa;
+      gg[hf] = -a_log * sp;
+      bt[hf] = bf16_round(__fdividef(1.f, 1.f + __expf(-rb[hf])));
+    }
+  }
+  float x0 = gg[0], x1 = gg[1];
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const float y0 = __shfl_up_sync(0xffffffffu, x0, o), y1 = __shfl_up_sync(0xffffffffu, x1, o);
+    if (lane >= o) {
+      x0 += y0;
+      x1 += y1;
+    }
+  }
+  x1 += __shfl_sync(0xffffffffu, x0, 31);
+  const float G_last = __shfl_sync(0xffffffffu, x1, 31);
+#pragma unroll
+  for (int hf = 0; hf < 2; ++hf) {
+    const int t = lane + 32 * hf;
+    const float G = hf ? x1 : x0;
+    gb[GB_G2 + t] = G * 1.4426950408889634f;
+    gb[GB_BETA + t] = bt[hf];
+    gb[GB_EGL + t] = __expf(G_last - G);
+    gb[GB_EG + t] = __expf(G);
+  }
+  if (lane == 0) gb[GB_EC] = __expf(G_last);
+}
+// raw b, a of tokens lane and lane + 32 of chunk c (zero past the request)
+QW_DEV void load_gating_inputs(float* rb, float* ra, const __nv_bfloat16* ba, int64_t ldba, int t_begin, int n, int c,
+                               int hv, int HV, int lane) {
+#pragma unroll
+  for (int hf = 0; hf < 2; ++hf) {
+    const int t = c * CH + lane + 32 * hf;
+    rb[hf] = ra[hf] = 0.f;
+    if (t < n) {
+      rb[hf] = bf2f(ba[(int64_t)(t_begin + t) * ldba + hv]);
+      ra[hf] = bf2f(ba[(int64_t)(t_begin + t) * ldba + HV + hv]);
+    }
+  }
+}
+
 QW_DEV void issue_chunk_loads(uint8_t* buf, uint64_t* bar, const CUtensorMap* tq, const CUtensorMap* tk,
                               const CUtensorMap* tv, int h, int hv, int row) {
   mbar_arrive_expect_tx(bar, 3 * TILE);
@@ -240,6 +294,9 @@ __global__ void __launch_bounds__(512, 1) gdn_prefill_kernel(
     *abort_flag = 0;
     fence_barrier_init();
   }
+  float* gbuf = reinterpret_cast<float*>(smem + S_GB);
+  const float a_log = expf(A_log[hv]);
+  const float dtb = bf2f(dt_bias[hv]);
   // blocks of T above the diagonal stay zero in both buffers
   for (int e = tid; e < 2 * CH * CH; e += 512) {
     const int bb = e / (CH * CH), r = (e / CH) % CH, cc = e % CH;
@@ -247,54 +304,23 @@ __global__ void __launch_bounds__(512, 1) gdn_prefill_kernel(
       *reinterpret_cast<__nv_bfloat16*>(smem + bb * BUF + B_T + swz_elem(r, cc)) = f2bf(0.f);
   }
   __syncthreads();
-  if (tid == 0) {
-    tma_prefetch_desc(&tm_q);
-    tma_prefetch_desc(&tm_k);
-    tma_prefetch_desc(&tm_v);
-    for (int c = 0; c < 2 && c < n_chunks; ++c)
-      issue_chunk_loads(smem + c * BUF, &loaded[c], &tm_q, &tm_k, &tm_v, h, hv, t_begin + c * CH);
-  }
 
   if (warp < 8) {
     // =============================================================== prep warps
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(PREP_REGS));
     const int mt = warp & 3, nh = warp >> 2;
-    float* sG = reinterpret_cast<float*>(smem + S_IG);
-    float* sBeta = sG + CH;
-    float* sEGl = sBeta + CH;
     float* blk = reinterpret_cast<float*>(smem + S_BLK);
-    const float a_log = expf(A_log[hv]);
-    const float dtb = bf2f(dt_bias[hv]);
-    // raw b, a of tokens lane and lane + 32 of the next chunk (warps 0 and 1 both hold all 64)
-    float nb[2] = {0.f, 0.f}, na[2] = {0.f, 0.f};
-    if (warp < 2) {
-#pragma unroll
-      for (int hf = 0; hf < 2; ++hf) {
-        const int t = lane + 32 * hf;
-        if (t < n) {
-          nb[hf] = bf2f(ba[(int64_t)(t_begin + t) * ldba + hv]);
-          na[hf] = bf2f(ba[(int64_t)(t_begin + t) * ldba + HV + hv]);
-        }
-      }
-    }
     for (int c = 0; c < n_chunks; ++c) {
       const int b = c & 1;
       uint8_t* buf = smem + b * BUF;
       const uint32_t sb = s0 + b * BUF;
       const int nc = min(CH, n - c * CH);
-      float* vec = reinterpret_cast<float*>(buf + B_VEC);
-      const float cb[2] = {nb[0], nb[1]}, ca[2] = {na[0], na[1]};
-      if (warp < 2) {
-#pragma unroll
-        for (int hf = 0; hf < 2; ++hf) {
-          const int t = (c + 1) * CH + lane + 32 * hf;
-          nb[hf] = na[hf] = 0.f;
-          if (t < n) {
-            nb[hf] = bf2f(ba[(int64_t)(t_begin + t) * ldba + hv]);
-            na[hf] = bf2f(ba[(int64_t)(t_begin + t) * ldba + HV + hv]);
-          }
-        }
-      }
+      // gating of this chunk (written by the state warps before they issued its loads)
+      const float* gb = gbuf + (c % 3) * GB_FLOATS;
+      const float* sG = gb + GB_G2;
+      const float* sBeta = gb + GB_BETA;
+      const float* sEGl = gb + GB_EGL;
+      const float* sEG = gb + GB_EG;
       mbar_wait(&loaded[b], (c >> 1) & 1, abort_flag, err, QW_DEV_ERR_TIMEOUT_GDN);
       if (nc < CH) {
         // rows past the request hold the next request's tokens (or TMA zero fill): clear them
@@ -302,38 +328,6 @@ __global__ void __launch_bounds__(512, 1) gdn_prefill_kernel(
           const int tile = e % 3, rc = e / 3;
           *reinterpret_cast<uint4*>(buf + tile * TILE + swz(nc + (rc >> 4), rc & 15)) = make_uint4(0, 0, 0, 0);
         }
-      }
-      // ---- gating and the within-chunk cumulative log decay (warps 0, 1)
-      if (warp < 2) {
-        float gg[2], bt[2];
-#pragma unroll
-        for (int hf = 0; hf < 2; ++hf) {
-          gg[hf] = bt[hf] = 0.f;
-          if (lane + 32 * hf < nc) {
-            const float xa = ca[hf] + dtb;
-            const float sp = xa <= 20.f ? logf(1.f + expf(xa)) : xa;
-            gg[hf] = -a_log * sp;
-            bt[hf] = bf16_round(1.f / (1.f + expf(-cb[hf])));
-          }
-        }
-        float x0 = gg[0], x1 = gg[1];
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-          const float y0 = __shfl_up_sync(0xffffffffu, x0, o), y1 = __shfl_up_sync(0xffffffffu, x1, o);
-          if (lane >= o) {
-            x0 += y0;
-            x1 += y1;
-          }
-        }
-        x1 += __shfl_sync(0xffffffffu, x0, 31);
-        const float G_last = __shfl_sync(0xffffffffu, x1, 31);
-        const int t = lane + 32 * warp;
-        const float G = warp == 0 ? x0 : x1;
-        sG[t] = G;
-        sBeta[t] = warp == 0 ? bt[0] : bt[1];
-        vec[t] = expf(G);
-        sEGl[t] = expf(G_last - G);
-        if (t == 0) vec[CH] = expf(G_last);
       }
       named_bar(1);
       // ---- K K^T -> A (fp32 blocks), Q K^T -> P (bf16)
@@ -347,17 +341,25 @@ __global__ void __launch_bounds__(512, 1) gdn_prefill_kernel(
           mma_tile<4, 8, false, false>(kk, sb + B_K, sb + B_K, mt * 16, nh * 32, lane);
           mma_tile<4, 8, false, false>(qk, sb + B_Q, sb + B_K, mt * 16, nh * 32, lane);
         }
+        // rows t = mt*16 + g4 (+8), columns s = s0, s0 + 1 of each n-tile
 #pragma unroll
-        for (int nt = 0; nt < 4; ++nt) {
+        for (int rr = 0; rr < 2; ++rr) {
+          const int t = mt * 16 + g4 + 8 * rr;
+          const float gt = sG[t], bt = sBeta[t];
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int t = mt * 16 + g4 + ((e >> 1) << 3);
-            const int s = nh * 32 + nt * 8 + c4 * 2 + (e & 1);
-            const float dec = (s <= t) ? expf(sG[t] - sG[s]) : 0.f;
-            const int bi = t >> 4, bj = s >> 4;
-            if (bj < bi) blk[blk_lo(bi, bj) * BLK + (t & 15) * BLD + (s & 15)] = sBeta[t] * dec * kk[nt][e];
-            else if (bj == bi) blk[(6 + bi) * BLK + (t & 15) * BLD + (s & 15)] = (s < t) ? sBeta[t] * dec * kk[nt][e] : 0.f;
-            qk[nt][e] = (s <= t) ? scale * dec * qk[nt][e] : 0.f;
+          for (int nt = 0; nt < 4; ++nt) {
+            const int s0 = nh * 32 + nt * 8 + 2 * c4;
+            const int bj = (nh * 32 + nt * 8) >> 4;
+            const float2 gs = *reinterpret_cast<const float2*>(sG + s0);
+            const float d0 = (s0 <= t) ? exp2f(gt - gs.x) : 0.f;
+            const float d1 = (s0 + 1 <= t) ? exp2f(gt - gs.y) : 0.f;
+            const float a0 = (s0 < t) ? bt * d0 * kk[nt][2 * rr] : 0.f;
+            const float a1 = (s0 + 1 < t) ? bt * d1 * kk[nt][2 * rr + 1] : 0.f;
+            qk[nt][2 * rr] = scale * d0 * qk[nt][2 * rr];
+            qk[nt][2 * rr + 1] = scale * d1 * qk[nt][2 * rr + 1];
+            if (bj <= mt)
+              *reinterpret_cast<float2*>(blk + (bj < mt ? blk_lo(mt, bj) : 6 + mt) * BLK + (g4 + 8 * rr) * BLD +
+                                         (s0 & 15)) = make_float2(a0, a1);
           }
         }
         store_tile_bf16<4>(buf + B_P, qk, mt * 16, nh * 32, lane, 1.f);
@@ -394,7 +396,7 @@ __global__ void __launch_bounds__(512, 1) gdn_prefill_kernel(
           float kf[8], vf[8], kb[8], kd[8];
           load_bf16x8(reinterpret_cast<const __nv_bfloat16*>(buf + B_K + off), kf);
           load_bf16x8(reinterpret_cast<const __nv_bfloat16*>(buf + B_V + off), vf);
-          const float fb = sBeta[r], fk = fb * vec[r], fd = sEGl[r];
+          const float fb = sBeta[r], fk = fb * sEG[r], fd = sEGl[r];
 #pragma unroll
           for (int jj = 0; jj < 8; ++jj) {
             kb[jj] = kf[jj] * fk;
@@ -484,12 +486,37 @@ __global__ void __launch_bounds__(512, 1) gdn_prefill_kernel(
       asm volatile("cp.async.commit_group;" ::: "memory");
     };
     if (n_chunks > 0) prefetch_z(0);
+    float rb[2] = {0.f, 0.f}, ra[2] = {0.f, 0.f};  // warp 8: raw gating inputs of chunk c + 2
+    if (sw == 0) {
+      // gating of chunks 0 and 1, then their loads (the load mbarrier publishes the gating
+      // to the prep warps, as for every later chunk)
+      for (int c = 0; c < 2 && c < n_chunks; ++c) {
+        load_gating_inputs(rb, ra, ba, ldba, t_begin, n, c, hv, HV, lane);
+        chunk_gating(gbuf + c * GB_FLOATS, rb, ra, min(CH, n - c * CH), a_log, dtb, lane);
+      }
+      __syncwarp();
+      if (lane == 0) {
+        tma_prefetch_desc(&tm_q);
+        tma_prefetch_desc(&tm_k);
+        tma_prefetch_desc(&tm_v);
+        for (int c = 0; c < 2 && c < n_chunks; ++c)
+          issue_chunk_loads(smem + c * BUF, &loaded[c], &tm_q, &tm_k, &tm_v, h, hv, t_begin + c * CH);
+      }
+      load_gating_inputs(rb, ra, ba, ldba, t_begin, n, 2, hv, HV, lane);
+    }
     for (int c = 0; c < n_chunks; ++c) {
       const int b = c & 1;
       const uint32_t sb = s0 + b * BUF;
-      const float* vec = reinterpret_cast<const float*>(smem + b * BUF + B_VEC);
+      const float* gb = gbuf + (c % 3) * GB_FLOATS;
+      const float* sEG = gb + GB_EG;
       const int nc = min(CH, n - c * CH);
       const int64_t tc = t_begin + (int64_t)c * CH;
+      if (sw == 0 && c + 2 < n_chunks) {
+        // gating of chunk c + 2 into its slot; published to the prep warps by the release
+        // barrier below and the mbarrier of that chunk's loads
+        chunk_gating(gbuf + ((c + 2) % 3) * GB_FLOATS, rb, ra, min(CH, n - (c + 2) * CH), a_log, dtb, lane);
+        load_gating_inputs(rb, ra, ba, ldba, t_begin, n, c + 3, hv, HV, lane);
+      }
       mbar_wait(&ready[b], (c >> 1) & 1, abort_flag, err, QW_DEV_ERR_TIMEOUT_GDN);
       // ---- U^T = (bV)^T T^T + S0 (-W)^T, rounded to bf16 into the warp's strip
       {
@@ -546,7 +573,7 @@ __global__ void __launch_bounds__(512, 1) gdn_prefill_kernel(
       }
 #pragma unroll
       for (int nt = 0; nt < 8; ++nt) {
-        const float2 e2 = *reinterpret_cast<const float2*>(vec + nt * 8 + 2 * c4);
+        const float2 e2 = *reinterpret_cast<const float2*>(sEG + nt * 8 + 2 * c4);
         o[nt][0] *= scale * e2.x;
         o[nt][1] *= scale * e2.y;
         o[nt][2] *= scale * e2.x;
@@ -566,7 +593,7 @@ __global__ void __launch_bounds__(512, 1) gdn_prefill_kernel(
       }
       // ---- S <- e^{G_C} S + U^T (e^{G_C-G} K)
       {
-        const float eC = vec[CH];
+        const float eC = gb[GB_EC];
 #pragma unroll
         for (int nt = 0; nt < 16; ++nt) {
           sacc[nt][0] *= eC;
