@@ -625,18 +625,33 @@ struct SkinnyPlan {
   int bn, b_tiles, a_tiles, splits, kb_per_split, kb_total;
 };
 
+// Split-K plan for weight streaming (M <= 64). Cost of a plan in k-block times of the
+// busiest SM: ceil(units / SMs) * (k-blocks per split + 2), the 2 standing for the unit's
+// partial-tile epilogue, plus the split-K partials written and read back, spread over all
+// SMs. The cheapest split count with at least 8 k-blocks per split wins (ties: fewer splits).
 static SkinnyPlan plan_skinny(int64_t M, int64_t N, int64_t K) {
   SkinnyPlan pl;
   pl.bn = M <= 16 ? 16 : M <= 32 ? 32 : 64;
   pl.b_tiles = 1;
   pl.a_tiles = (int)((N + BM - 1) / BM);
   pl.kb_total = (int)((K + BK - 1) / BK);
-  const int target = 2 * num_sms();
-  int splits = (target + pl.a_tiles - 1) / pl.a_tiles;
-  const int max_splits = pl.kb_total / 4 > 0 ? pl.kb_total / 4 : 1;  // keep >= 4 k-blocks per split
-  if (splits > max_splits) splits = max_splits;
-  if (splits < 1) splits = 1;
-  pl.kb_per_split = (pl.kb_total + splits - 1) / splits;
+  const int64_t sms = num_sms();
+  const int64_t kb_bytes = (int64_t)BM * BK * 2;  // weight bytes of one k-block
+  const int max_splits = pl.kb_total / 8 > 0 ? pl.kb_total / 8 : 1;
+  int64_t best_cost = -1;
+  int best_kbps = pl.kb_total;
+  for (int s = 1; s <= max_splits; ++s) {
+    const int kbps = (pl.kb_total + s - 1) / s;
+    const int64_t splits = (pl.kb_total + kbps - 1) / kbps;
+    const int64_t rounds = (pl.a_tiles * splits + sms - 1) / sms;
+    int64_t cost = rounds * (kbps + 2);
+    if (splits > 1) cost += (splits * M * N * 8 + kb_bytes * sms - 1) / (kb_bytes * sms);
+    if (best_cost < 0 || cost < best_cost) {
+      best_cost = cost;
+      best_kbps = kbps;
+    }
+  }
+  pl.kb_per_split = best_kbps;
   pl.splits = (pl.kb_total + pl.kb_per_split - 1) / pl.kb_per_split;
   return pl;
 }

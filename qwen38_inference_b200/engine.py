@@ -2,16 +2,18 @@
 
 Prefill (any call that is not pure decode, REF:5027) runs per layer:
   norm -> [attention: qkv GEMM, q/k norm + RoPE + KV store, varlen attention (gated), o GEMM]
-       or [GDN: qkvz GEMM, ba GEMM, conv + split + L2 norm, chunked delta rule (gating
+       or [GDN: one qkvz|ba GEMM, conv + split + L2 norm, chunked delta rule (gating
            fused, state in place), gated RMSNorm, out GEMM]
   -> add-norm -> gate_up GEMM with fused SwiGLU -> down GEMM
 then the final add-norm on the selected rows and the lm_head GEMM writing fp32 logits.
 Decode replaces the GDN middle by one fused kernel and attention by split-KV decode, and
-is replayed from a CUDA graph per (batch, cache) once captured.
+is replayed from a CUDA graph per (batch, cache buffer addresses) once captured.
 
 All per-call indices travel in one int32 upload (``build_metadata``).
 """
 from __future__ import annotations
+
+import collections
 
 import numpy as np
 import torch
@@ -29,7 +31,7 @@ class Engine:
         self.dev = model.device
         self.ws = ops.Workspace(self.dev, 1 << 20)
         self.staging = _Staging()
-        self.graphs = {}
+        self.graphs = collections.OrderedDict()
         self.use_graphs = True
 
     # ------------------------------------------------------------------ helpers
@@ -53,57 +55,56 @@ class Engine:
         return self._run(md, T, len(slots), max(lens), cache, is_decode, return_all_logits)
 
     # ------------------------------------------------------------------ decode graphs
-    def _decode_graph(self, arr, offs, T, slots, cache):
-        """Decode through a CUDA graph keyed by (batch, cache buffers).
+    MAX_GRAPHS = 4  # captured decode graphs kept, least recently used evicted first
 
-        The first decode of a key runs eagerly. The second runs eagerly too and then
-        captures the same launch sequence (capture records, it does not execute, and its
-        host cost overlaps the eager step on the GPU). Later calls copy the new indices into
-        the graph's input buffer and replay. A cache that is decoded once (a benchmark
-        repetition) therefore never pays for a capture.
+    def _decode_graph(self, arr, offs, T, slots, cache):
+        """Decode through a CUDA graph keyed by the batch shape and the addresses of every
+        cache buffer. A graph bakes in its pointers, so any cache whose buffers sit at exactly
+        those addresses with the same capacity and slot count replays it correctly, including
+        a fresh cache that the allocator placed where a freed one was.
+
+        The first decode of a key runs eagerly. The second runs eagerly too and then captures
+        the same launch sequence (capture records, it does not execute) with a workspace and
+        an index buffer of its own. Later calls copy the new indices in and replay.
         """
         B = len(slots)
-        key = (B, cache.capacity, len(cache.lengths), tuple(k.data_ptr() for k, _ in cache.kv.values()),
+        key = (B, T, cache.capacity, len(cache.lengths), tuple(k.data_ptr() for k, _ in cache.kv.values()),
                tuple(x.data_ptr() for x in cache.recurrent.values()), tuple(x.data_ptr() for x in cache.conv.values()))
         ent = self.graphs.get(key)
-        # decodes of this shape on this cache object (the allocator may hand a new cache the
-        # addresses of a freed one, so the count lives on the cache, not on the key)
-        seen = getattr(cache, "_decode_counts", None)
-        if seen is None:
-            seen = {}
-            cache._decode_counts = seen
-        n_prev = seen.get(key, 0)
-        seen[key] = n_prev + 1
-        if ent is None or ent.get("graph") is None:
-            if ent is None:
-                for k in [k for k in self.graphs if k[0] == B]:  # built on a grown or freed cache
-                    del self.graphs[k]
-            dev_in = torch.empty(arr.size, dtype=torch.int32, device=self.dev)
-            dev_in.copy_(torch.from_numpy(arr), non_blocking=True)
-            md = self._meta_views(dev_in[T:], offs)
-            md["tokens"] = dev_in[:T]
-            out = self._run(md, T, B, 1, cache, True, False)
-            if n_prev == 0:
-                self.graphs[key] = {"graph": None}
-                return out
+        if ent is not None and ent["graph"] is not None:
+            if ent["offs"] != offs:
+                raise RuntimeError("decode metadata layout changed for a captured shape")
+            self.graphs.move_to_end(key)
+            ent["input"].copy_(torch.from_numpy(arr))
+            ent["graph"].replay()
+            ops.LAUNCHES[0] += ent["launches"]
+            return ent["out"].clone()
+        dev_in = torch.empty(arr.size, dtype=torch.int32, device=self.dev)
+        dev_in.copy_(torch.from_numpy(arr), non_blocking=True)
+        md = self._meta_views(dev_in[T:], offs)
+        md["tokens"] = dev_in[:T]
+        out = self._run(md, T, B, 1, cache, True, False, self.ws)
+        if ent is None:
+            self.graphs[key] = {"graph": None}
+        else:
+            gws = ops.Workspace(self.dev, self.ws.buf.numel())  # sized by the eager run
             g = torch.cuda.CUDAGraph()
             n0 = ops.LAUNCHES[0]
             with torch.cuda.graph(g):
-                g_out = self._run(md, T, B, 1, cache, True, False)
+                g_out = self._run(md, T, B, 1, cache, True, False, gws)
             n_launch = ops.LAUNCHES[0] - n0
             ops.LAUNCHES[0] = n0  # captured launches do not execute
-            self.graphs[key] = {"graph": g, "input": dev_in, "out": g_out, "offs": offs, "launches": n_launch}
-            return out
-        if ent["offs"] != offs:
-            raise RuntimeError("decode metadata layout changed for a captured shape")
-        ent["input"].copy_(torch.from_numpy(arr))
-        ent["graph"].replay()
-        ops.LAUNCHES[0] += ent["launches"]
-        return ent["out"].clone()
+            self.graphs[key] = {"graph": g, "input": dev_in, "out": g_out, "offs": offs, "launches": n_launch,
+                                "ws": gws}
+        self.graphs.move_to_end(key)
+        while len(self.graphs) > self.MAX_GRAPHS:
+            self.graphs.popitem(last=False)
+        return out
 
     # ------------------------------------------------------------------ the layer loop
-    def _run(self, md, T, B, max_len, cache, is_decode, return_all_logits):
-        m, c, dev, ws = self.m, self.c, self.dev, self.ws
+    def _run(self, md, T, B, max_len, cache, is_decode, return_all_logits, ws=None):
+        m, c, dev = self.m, self.c, self.dev
+        ws = self.ws if ws is None else ws
         H = c.hidden_size
         eps = m.eps
         resid = torch.empty(T, H, dtype=BF16, device=dev)
@@ -111,9 +112,8 @@ class Engine:
         ops.embed_rmsnorm(md["tokens"], m.embedding, m.layers[0]["input_norm"], resid, hidden, eps)
         nq, nkv, d = c.num_attention_heads, c.num_key_value_heads, c.head_dim
         Hk, HV, dk, dv = c.linear_num_key_heads, c.linear_num_value_heads, c.linear_key_head_dim, c.linear_value_head_dim
-        big = max(c.qkv_dim, c.qkvz_dim)
+        big = max(c.qkv_dim, c.qkvz_dim + c.ba_dim)
         proj = torch.empty(T, big, dtype=BF16, device=dev)
-        ba = torch.empty(T, c.ba_dim, dtype=BF16, device=dev)
         mix = torch.empty(T, max(c.attn_out_dim, c.gdn_v_dim), dtype=BF16, device=dev)
         act = torch.empty(T, c.intermediate_size, dtype=BF16, device=dev)
         if not is_decode:
@@ -139,9 +139,8 @@ class Engine:
                                      att, d ** -0.5)
                 ops.gemm(att, w["out"], hidden, ws=ws)
             else:
-                qkvz = proj[:, :c.qkvz_dim]
-                ops.gemm(hidden, w["qkvz"], qkvz, ws=ws)
-                ops.gemm(hidden, w["ba"], ba, ws=ws)
+                ops.gemm(hidden, w["qkvzba"], proj[:, :c.qkvz_dim + c.ba_dim], ws=ws)
+                qkvz, ba = proj[:, :c.qkvz_dim], proj[:, c.qkvz_dim:c.qkvz_dim + c.ba_dim]
                 y = mix[:, :c.gdn_v_dim]
                 if is_decode:
                     ops.gdn_decode(qkvz, ba, w["conv"], cache.conv[i], cache.recurrent[i], md["slots"], B, w["A_log"],

@@ -13,9 +13,11 @@ library loads.
 """
 from __future__ import annotations
 
+import collections
 import dataclasses
 import json
 import math
+import weakref
 from pathlib import Path
 
 import numpy as np
@@ -131,6 +133,45 @@ def build_metadata(slots, prefixes, lens, capacity, attn_tile=128):
     return packed, offs, T
 
 
+class _BufferArena:
+    """Device buffers of dead caches, handed to the next cache of the same shape.
+
+    A new cache (or a grown KV pool) then sits at the addresses of the one it replaces, so
+    decode graphs captured on the earlier cache replay on the new one (a graph bakes in
+    buffer addresses). Buffers return when their cache is garbage collected or when growth
+    replaces a KV pool, and are handed out first in, first out, so each layer of the next
+    cache gets the buffer the same layer had before. All use is ordered on one stream: a
+    returned buffer is only touched by work queued after its previous owner's last use.
+    At most ``max_bytes`` (default a quarter of device memory) are held.
+    """
+
+    def __init__(self, device, max_bytes=None):
+        self.device = device
+        if max_bytes is None:
+            max_bytes = (torch.cuda.get_device_properties(device).total_memory // 4
+                         if torch.device(device).type == "cuda" else 1 << 30)
+        self.max_bytes = max_bytes
+        self.held = 0
+        self.free = collections.defaultdict(collections.deque)
+
+    def take(self, shape, dtype, zero):
+        q = self.free.get((tuple(shape), dtype))
+        if q:
+            t = q.popleft()
+            self.held -= t.numel() * t.element_size()
+            if zero:
+                t.zero_()
+            return t
+        return (torch.zeros if zero else torch.empty)(tuple(shape), dtype=dtype, device=self.device)
+
+    def give(self, tensors):
+        for t in tensors:
+            nbytes = t.numel() * t.element_size()
+            if self.held + nbytes <= self.max_bytes:
+                self.free[(tuple(t.shape), t.dtype)].append(t)
+                self.held += nbytes
+
+
 class _Staging:
     """Pinned host buffers for metadata uploads, reused once their copy has completed."""
 
@@ -214,9 +255,17 @@ class Qwen38:
             want = torch.float32 if k.endswith("A_log") else torch.bfloat16
             flat[k] = v.to(device=self.device, dtype=want).contiguous()
         self.layers, g = nested_layers(flat, cfg)
+        for kind, w in zip(self.layer_types, self.layers):
+            if kind != "full_attention":
+                # one projection for [q; k; v; z; b; a]: the small b/a rows ride along with the
+                # big GEMM instead of a launch of their own; qkvz and ba stay as row views
+                fused = torch.cat([w["qkvz"], w["ba"]], 0)
+                w["qkvzba"] = fused
+                w["qkvz"], w["ba"] = fused[:cfg.qkvz_dim], fused[cfg.qkvz_dim:]
         self.embedding, self.final_norm, self.lm_head = g["embedding"], g["final_norm"], g["lm_head"]
         self.rotary_dim = cfg.rotary_dim
         self.rope = rope_table(cfg, self.max_context, self.device)
+        self._arena = _BufferArena(self.device)
         from .engine import Engine
         self._engine = Engine(self)
 
@@ -240,16 +289,21 @@ class Qwen38:
             raise ValueError("Invalid cache capacity/context limit")
         capacity = math.ceil(min(initial_capacity, limit) / PAGE) * PAGE
         kv, conv, recurrent = {}, {}, {}
+        take = self._arena.take
         for i, kind in enumerate(self.layer_types):
             if kind == "full_attention":
                 shape = (batch_size * capacity + PAGE, c.num_key_value_heads, c.head_dim)
-                kv[i] = tuple(torch.zeros(shape, dtype=self.dtype, device=self.device) for _ in range(2))
+                kv[i] = (take(shape, self.dtype, True), take(shape, self.dtype, True))
             else:
-                conv[i] = torch.zeros((batch_size, c.conv_dim, c.linear_conv_kernel_dim - 1), dtype=self.dtype,
-                                      device=self.device)
-                recurrent[i] = torch.zeros((batch_size, c.linear_num_value_heads, c.linear_value_head_dim,
-                                            c.linear_key_head_dim), dtype=torch.float32, device=self.device)
-        return HybridCache(id(self), [0] * batch_size, capacity, limit, kv, conv, recurrent)
+                conv[i] = take((batch_size, c.conv_dim, c.linear_conv_kernel_dim - 1), self.dtype, True)
+                recurrent[i] = take((batch_size, c.linear_num_value_heads, c.linear_value_head_dim,
+                                     c.linear_key_head_dim), torch.float32, True)
+        cache = HybridCache(id(self), [0] * batch_size, capacity, limit, kv, conv, recurrent)
+        # the buffers the cache holds when it dies go back to the arena (growth updates the box)
+        box = [t for pair in kv.values() for t in pair] + list(conv.values()) + list(recurrent.values())
+        cache._arena_box = box
+        weakref.finalize(cache, self._arena.give, box)
+        return cache
 
     def _reserve(self, cache, needed):
         if needed > cache.max_context:
@@ -260,14 +314,21 @@ class Qwen38:
         S = len(cache.lengths)
         lengths = torch.tensor(cache.lengths, dtype=torch.int32).to(self.device, non_blocking=True)
         new_kv = {}
+        box = getattr(cache, "_arena_box", None)
         for i, (k_old, v_old) in cache.kv.items():
             shape = (S * capacity + PAGE,) + tuple(k_old.shape[1:])
-            k_new = torch.empty(shape, dtype=self.dtype, device=self.device)
-            v_new = torch.empty(shape, dtype=self.dtype, device=self.device)
+            k_new = self._arena.take(shape, self.dtype, False)
+            v_new = self._arena.take(shape, self.dtype, False)
             ops.kv_grow(k_old, v_old, k_new, v_new, lengths, S, cache.capacity, capacity)
             new_kv[i] = (k_new, v_new)
+        old = [t for pair in cache.kv.values() for t in pair]
         cache.kv = new_kv
         cache.capacity = capacity
+        if box is not None:
+            # the replaced pools leave the cache's box and return to the arena
+            ids = {id(t) for t in old}
+            box[:] = [t for t in box if id(t) not in ids] + [t for pair in new_kv.values() for t in pair]
+            self._arena.give(old)
 
     # ------------------------------------------------------------------ forward (REF:5004-5099)
     @torch.inference_mode()

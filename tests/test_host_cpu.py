@@ -108,8 +108,34 @@ def host_model(monkeypatch):
     m.max_context, m.layer_types, m.page_size = 1000, cfg.layer_types, 64
     m.eos_token_ids = {cfg.eos_token_id}
     m._engine = _StubEngine(cfg.vocab_size)
+    m._arena = M._BufferArena(m.device)
     monkeypatch.setattr(M.ops, "kv_grow", _cpu_kv_grow)
     return m
+
+
+def test_arena_reuses_buffers_of_dead_caches(host_model):
+    """A fresh cache gets the (zeroed) buffers of a dead one, growth hands the replaced KV
+    pools back, and no buffer is ever owned by two live caches."""
+    import gc
+    m = host_model
+    a = m.new_cache(2, initial_capacity=64)
+    ptrs_a = sorted(t.data_ptr() for t in a._arena_box)
+    with torch.inference_mode():
+        a.recurrent[0].fill_(3.0)
+    a.lengths = [10, 0]
+    m._reserve(a, 100)  # grow: the 64-capacity pools go back to the arena
+    grown = sorted(t.data_ptr() for t in a._arena_box)
+    b = m.new_cache(2, initial_capacity=64)  # takes the pools a gave back
+    ptrs_b = sorted(t.data_ptr() for t in b._arena_box)
+    assert set(ptrs_b) & set(grown) == set()  # a is alive: nothing shared with it
+    assert set(ptrs_b) & set(ptrs_a)  # the returned 64-capacity pools are reused
+    del a
+    gc.collect()
+    c = m.new_cache(2, initial_capacity=64)
+    assert set(t.data_ptr() for t in c._arena_box) & set(grown)  # a's state buffers came back
+    assert float(c.recurrent[0].abs().sum()) == 0.0 and float(c.kv[3][0].abs().sum()) == 0.0
+    live = [t.data_ptr() for t in b._arena_box] + [t.data_ptr() for t in c._arena_box]
+    assert len(live) == len(set(live))
 
 
 def test_new_cache_and_growth_policy(host_model):
