@@ -347,105 +347,173 @@ __global__ void __launch_bounds__(256, 1)
   }
 }
 
-// ============================================================== decode attention (CUDA cores)
-// grid (B * nkv, splits); 4 warps; each warp takes 32 keys at a time, lane = key for the
-// scores, lane = 8-dim slice for the value accumulation.
+// Decode attention (one query token per request) on tensor cores. CTA = (request, kv head,
+// split of the keys), 4 warps; each warp takes a contiguous quarter of the split's keys,
+// 16 at a time: S^T = K Q^T ([16 keys] x [8 query heads of the group], Q held as register B
+// fragments), an online softmax per head in the log2 domain, P^T rounded to bf16 through
+// shared memory, and O^T += V^T P^T ([d] x [heads]). K and V rows stream through a per-warp
+// double buffer of cp.async copies. The warps' (max, sum, O) merge in shared memory into
+// the split's partial; attn_decode_combine_kernel merges the splits and applies the gate.
+template <int D>
+struct DecodeSmem {
+  static constexpr int KB = 16;                   // keys per warp step
+  static constexpr int TK = KB * D * 2;           // one K (or V) step tile
+  static constexpr int WARP = 4 * TK;             // two stages of K and V
+  static constexpr int P = 4 * WARP;              // per-warp P^T tiles [8 heads][16 keys] bf16
+  static constexpr int ML = P + 4 * 8 * KB * 2;   // per-warp max and sum of the 8 head columns
+  static constexpr int TOTAL = ML + 2 * 4 * 8 * 4;
+  static_assert(4 * 8 * D * 4 <= P, "the warps' O^T merge reuses the K/V stages");
+};
+
+QW_DEV void ldmatrix_x2(uint32_t addr, uint32_t& r0, uint32_t& r1) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(addr));
+}
+
 template <int D, int G>
 __global__ void __launch_bounds__(128) attn_decode_kernel(
     const __nv_bfloat16* __restrict__ qkv, int64_t ldq, int nq, int nkv, const __nv_bfloat16* __restrict__ kc,
     const __nv_bfloat16* __restrict__ vc, const int32_t* __restrict__ seq_len, const int32_t* __restrict__ kv_base,
     int keys_per_split, float scale_log2, float* __restrict__ part_o, float* __restrict__ part_ml, int splits) {
-  constexpr int E = D / 32;
-  __shared__ float sq[G][D];
-  __shared__ float s_m[4][G], s_l[4][G];
-  __shared__ float s_o[4][G][D];
-  const int b = blockIdx.x / nkv, kvh = blockIdx.x % nkv;
-  const int split = blockIdx.y;
-  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  static_assert(G <= 8 && D % 16 == 0, "the query heads of a group fill one 8-wide n-tile");
+  using L_ = DecodeSmem<D>;
+  constexpr int KB = L_::KB, TK = L_::TK, NCH = D / 8, MT = D / 16;
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
+  const int b = blockIdx.x / nkv, kvh = blockIdx.x % nkv, split = blockIdx.y;
   const int L = seq_len[b];
   const int64_t base = kv_base[b];
   const int k_begin = split * keys_per_split;
   const int k_end = min(L, k_begin + keys_per_split);
-  for (int i = threadIdx.x; i < G * D; i += blockDim.x) {
-    const int gi = i / D, d = i % D;
-    sq[gi][d] = bf2f(qkv[(int64_t)b * ldq + (int64_t)(kvh * G + gi) * 2 * D + d]);
-  }
-  __syncthreads();
-  float m[G], l[G], acc[G][E];
+  const int span = (keys_per_split + 4 * KB - 1) / (4 * KB) * KB;  // keys per warp, multiple of 16
+  const int w_begin = k_begin + warp * span;
+  const int w_end = min(k_end, w_begin + span);
+  const int steps = w_end > w_begin ? (w_end - w_begin + KB - 1) / KB : 0;
+  const uint32_t ws0 = smem_u32(smem + warp * L_::WARP);
+  __nv_bfloat16* sP = reinterpret_cast<__nv_bfloat16*>(smem + L_::P + warp * 8 * KB * 2);
+
+  // Q of the group as B fragments: b0 = (d = 16 ks + 2c, +1; head g), b1 = (d + 8; head g)
+  uint32_t qf[MT][2];
+  {
+    const bool ok = g < G;
+    const __nv_bfloat16* qr = qkv + (int64_t)b * ldq + (int64_t)(kvh * G + (ok ? g : 0)) * 2 * D;
 #pragma unroll
-  for (int gi = 0; gi < G; ++gi) {
-    m[gi] = -INFINITY;
-    l[gi] = 0.f;
-#pragma unroll
-    for (int e = 0; e < E; ++e) acc[gi][e] = 0.f;
-  }
-  for (int k0 = k_begin + warp * 32; k0 < k_end; k0 += 128) {
-    const int key = k0 + lane;
-    const bool valid = key < k_end;
-    float s[G];
-#pragma unroll
-    for (int gi = 0; gi < G; ++gi) s[gi] = 0.f;
-    if (valid) {
-      const __nv_bfloat16* kr = kc + ((base + key) * nkv + kvh) * D;
-#pragma unroll 4
-      for (int c = 0; c < D; c += 8) {
-        float kf[8];
-        load_bf16x8(kr + c, kf);
-#pragma unroll
-        for (int gi = 0; gi < G; ++gi) {
-#pragma unroll
-          for (int e = 0; e < 8; ++e) s[gi] += sq[gi][c + e] * kf[e];
-        }
-      }
-    }
-    float pw[G];
-#pragma unroll
-    for (int gi = 0; gi < G; ++gi) {
-      const float v = valid ? s[gi] * scale_log2 : -INFINITY;
-      const float mx = fmaxf(m[gi], warp_max(v));
-      const float alpha = (mx == -INFINITY) ? 1.f : exp2f(m[gi] - mx);
-      pw[gi] = valid ? exp2f(v - mx) : 0.f;
-      l[gi] = l[gi] * alpha + warp_sum(pw[gi]);
-      m[gi] = mx;
-#pragma unroll
-      for (int e = 0; e < E; ++e) acc[gi][e] *= alpha;
-    }
-    const int nk = min(32, k_end - k0);
-    for (int jj = 0; jj < nk; ++jj) {
-      const __nv_bfloat16* vr = vc + ((base + k0 + jj) * nkv + kvh) * D + lane * E;
-      float vf[E];
-#pragma unroll
-      for (int e = 0; e < E; ++e) vf[e] = bf2f(vr[e]);
-#pragma unroll
-      for (int gi = 0; gi < G; ++gi) {
-        const float pj = __shfl_sync(0xffffffffu, pw[gi], jj);
-#pragma unroll
-        for (int e = 0; e < E; ++e) acc[gi][e] += pj * vf[e];
-      }
+    for (int ks = 0; ks < MT; ++ks) {
+      qf[ks][0] = ok ? *reinterpret_cast<const uint32_t*>(qr + 16 * ks + 2 * c) : 0u;
+      qf[ks][1] = ok ? *reinterpret_cast<const uint32_t*>(qr + 16 * ks + 8 + 2 * c) : 0u;
     }
   }
-  // combine the 4 warps
-  if (lane == 0) {
+  auto load_step = [&](int st) {
+    const int key0 = w_begin + st * KB;
+    const uint32_t kd = ws0 + (st & 1) * 2 * TK, vd = kd + TK;
+    for (int i = lane; i < KB * NCH; i += 32) {
+      const int r = i / NCH, ch = i % NCH;
+      const bool ok = key0 + r < w_end;
+      const int64_t row = (base + (ok ? key0 + r : 0)) * nkv + kvh;
+      cp_async16(kd + swz<D>(r, ch), kc + row * D + ch * 8, ok);
+      cp_async16(vd + swz<D>(r, ch), vc + row * D + ch * 8, ok);
+    }
+    cp_async_commit();
+  };
+
+  float o[MT][4];
 #pragma unroll
-    for (int gi = 0; gi < G; ++gi) {
-      s_m[warp][gi] = m[gi];
-      s_l[warp][gi] = l[gi];
+  for (int mt = 0; mt < MT; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
+  float m_j[2] = {-INFINITY, -INFINITY}, l_j[2] = {0.f, 0.f};  // heads 2c, 2c+1
+  if (steps > 0) load_step(0);
+  for (int st = 0; st < steps; ++st) {
+    if (st + 1 < steps) {
+      load_step(st + 1);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncwarp();
+    const uint32_t kd = ws0 + (st & 1) * 2 * TK, vd = kd + TK;
+    // ---- S^T = K Q^T
+    float sc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int ks = 0; ks < MT; ++ks) {
+      uint32_t a[4];
+      ldmatrix_x4(kd + swz<D>(lane & 15, 2 * ks + (lane >> 4)), a[0], a[1], a[2], a[3]);
+      mma_bf16_16816(sc, a, qf[ks][0], qf[ks][1]);
+    }
+    // ---- online softmax per head column (keys g and g + 8 of the step)
+    const int key0 = w_begin + st * KB;
+    const bool v0 = key0 + g < w_end, v1 = key0 + g + 8 < w_end;
+    const float x[4] = {v0 ? sc[0] * scale_log2 : -INFINITY, v0 ? sc[1] * scale_log2 : -INFINITY,
+                        v1 ? sc[2] * scale_log2 : -INFINITY, v1 ? sc[3] * scale_log2 : -INFINITY};
+    float pr[4], alpha[2];
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      float mx = fmaxf(x[j], x[2 + j]);
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+      const float mn = fmaxf(m_j[j], mx);  // finite: key0 is always a valid key
+      alpha[j] = exp2f(m_j[j] - mn);
+      pr[j] = exp2f(x[j] - mn);
+      pr[2 + j] = exp2f(x[2 + j] - mn);
+      float ps = pr[j] + pr[2 + j];
+      ps += __shfl_xor_sync(0xffffffffu, ps, 4);
+      ps += __shfl_xor_sync(0xffffffffu, ps, 8);
+      ps += __shfl_xor_sync(0xffffffffu, ps, 16);
+      l_j[j] = l_j[j] * alpha[j] + ps;
+      m_j[j] = mn;
+    }
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt) {
+      o[mt][0] *= alpha[0];
+      o[mt][1] *= alpha[1];
+      o[mt][2] *= alpha[0];
+      o[mt][3] *= alpha[1];
+    }
+    // ---- P^T as [head][key] bf16, read back as the B fragments of V^T P^T
+    sP[(2 * c) * KB + g] = f2bf(pr[0]);
+    sP[(2 * c + 1) * KB + g] = f2bf(pr[1]);
+    sP[(2 * c) * KB + g + 8] = f2bf(pr[2]);
+    sP[(2 * c + 1) * KB + g + 8] = f2bf(pr[3]);
+    __syncwarp();
+    uint32_t pb0, pb1;
+    ldmatrix_x2(smem_u32(sP) + (lane & 7) * (KB * 2) + ((lane >> 3) & 1) * 16, pb0, pb1);
+    // ---- O^T += V^T P^T
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt) {
+      uint32_t a[4];
+      ldmatrix_x4_trans(vd + swz<D>((lane & 7) + ((lane >> 4) << 3), 2 * mt + ((lane >> 3) & 1)), a[0], a[1], a[2],
+                        a[3]);
+      mma_bf16_16816(o[mt], a, pb0, pb1);
+    }
+    __syncwarp();  // this stage and P are refilled next
+  }
+  // ---- merge the 4 warps into the split's partial
+  __syncthreads();  // every warp is done with its K/V stages
+  float* sO = reinterpret_cast<float*>(smem);  // [4 warps][8 heads][D]
+  float* sM = reinterpret_cast<float*>(smem + L_::ML);
+  float* sL = sM + 4 * 8;
+#pragma unroll
+  for (int mt = 0; mt < MT; ++mt) {
+#pragma unroll
+    for (int e = 0; e < 4; ++e) sO[(warp * 8 + 2 * c + (e & 1)) * D + 16 * mt + g + 8 * (e >> 1)] = o[mt][e];
+  }
+  if (g == 0) {
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      sM[warp * 8 + 2 * c + j] = m_j[j];
+      sL[warp * 8 + 2 * c + j] = l_j[j];
     }
   }
-#pragma unroll
-  for (int gi = 0; gi < G; ++gi)
-#pragma unroll
-    for (int e = 0; e < E; ++e) s_o[warp][gi][lane * E + e] = acc[gi][e];
   __syncthreads();
   for (int i = threadIdx.x; i < G * D; i += blockDim.x) {
     const int gi = i / D, d = i % D;
     float mm = -INFINITY;
-    for (int w = 0; w < 4; ++w) mm = fmaxf(mm, s_m[w][gi]);
+#pragma unroll
+    for (int w = 0; w < 4; ++w) mm = fmaxf(mm, sM[w * 8 + gi]);
     float ll = 0.f, oo = 0.f;
+#pragma unroll
     for (int w = 0; w < 4; ++w) {
-      const float f = (s_m[w][gi] == -INFINITY) ? 0.f : exp2f(s_m[w][gi] - mm);
-      ll += s_l[w][gi] * f;
-      oo += s_o[w][gi][d] * f;
+      const float f = (sM[w * 8 + gi] == -INFINITY) ? 0.f : exp2f(sM[w * 8 + gi] - mm);
+      ll += sL[w * 8 + gi] * f;
+      oo += sO[(w * 8 + gi) * D + d] * f;
     }
     const int h = kvh * G + gi;
     const int64_t slot = ((int64_t)b * nq + h) * splits + split;
@@ -567,14 +635,20 @@ extern "C" int qw_attn_decode(const void* qkv, int64_t ldq, int64_t B, int64_t n
   float* part_ml = part_o + B * nq * splits * d;
   const float sl2 = scale * 1.4426950408889634f;
   dim3 grid((unsigned)(B * nkv), (unsigned)splits);
+  static bool configured = false;
+  if (!configured) {
+    cudaFuncSetAttribute(attn_decode_kernel<256, 6>, cudaFuncAttributeMaxDynamicSharedMemorySize, DecodeSmem<256>::TOTAL);
+    cudaFuncSetAttribute(attn_decode_kernel<64, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, DecodeSmem<64>::TOTAL);
+    configured = true;
+  }
   const auto* q = static_cast<const __nv_bfloat16*>(qkv);
   const auto* kc = static_cast<const __nv_bfloat16*>(k_cache);
   const auto* vc = static_cast<const __nv_bfloat16*>(v_cache);
   if (d == 256 && group == 6)
-    attn_decode_kernel<256, 6><<<grid, 128, 0, s>>>(q, ldq, (int)nq, (int)nkv, kc, vc, seq_len, kv_base, kps, sl2,
+    attn_decode_kernel<256, 6><<<grid, 128, DecodeSmem<256>::TOTAL, s>>>(q, ldq, (int)nq, (int)nkv, kc, vc, seq_len, kv_base, kps, sl2,
                                                     part_o, part_ml, (int)splits);
   else if (d == 64 && group == 2)
-    attn_decode_kernel<64, 2><<<grid, 128, 0, s>>>(q, ldq, (int)nq, (int)nkv, kc, vc, seq_len, kv_base, kps, sl2,
+    attn_decode_kernel<64, 2><<<grid, 128, DecodeSmem<64>::TOTAL, s>>>(q, ldq, (int)nq, (int)nkv, kc, vc, seq_len, kv_base, kps, sl2,
                                                    part_o, part_ml, (int)splits);
   else
     return QW_ERR_UNSUPPORTED;

@@ -159,7 +159,8 @@ def test_attn_decode(K, nq, nkv, d, splits):
     q = qkv.float()[:, :2 * nq * d].view(B, nq, 2 * d)
     att = O.paged_attention(q[..., :d], kc, vc, starts, prefixes, lens, d ** -0.5, O.bf16)
     exp = O.sigmoid_mul(att.reshape(B, -1), q[..., d:].reshape(B, -1), O.bf16)
-    close(out, exp, n_ulp=2, atol=1e-4, max_frac=0.2)
+    # P is rounded to bf16 before the PV product (tensor cores), as in prefill
+    close(out, exp, n_ulp=4, atol=2e-3, max_frac=0.5)
 
 
 def test_conv_prefill(K):
