@@ -39,6 +39,7 @@ typedef struct CUstream_st* qw_stream_t;
 #define QW_DEV_ERR_TIMEOUT_GEMM 101
 #define QW_DEV_ERR_INDEX 102
 #define QW_DEV_ERR_TIMEOUT_GDN 103 /* a bounded wait of the chunked delta-rule pipeline gave up */
+#define QW_DEV_ERR_TIMEOUT_ATTN 104 /* a bounded wait of the prefill attention pipeline gave up */
 
 /* ---- library ----------------------------------------------------------------------- */
 int qw_version(void);
@@ -89,14 +90,14 @@ int qw_qk_norm_rope_store(void* qkv, int64_t ldq, int64_t T, int64_t nq, int64_t
                           const int32_t* positions, const int32_t* locations, void* k_cache, void* v_cache,
                           int64_t cache_rows, float eps, qw_stream_t stream);
 /* Causal varlen attention for prefill/extend; tiles = int32 pairs (request, first query)
- * of 128-query tiles; request i owns query rows cu[i]..cu[i+1], has prefix[i] cached tokens
- * and its keys start at cache row kv_base[i]. out bf16 [T, ldo] =
- * bf16(bf16(softmax(q k^T * scale) v) * sigmoid(gate))
+ * of 128-query tiles; request i owns query rows cu[i]..cu[i+1] of the T rows of qkv, has
+ * prefix[i] cached tokens and its keys start at cache row kv_base[i] of the cache_rows rows
+ * of k_cache / v_cache. out bf16 [T, ldo] = bf16(bf16(softmax(q k^T * scale) v) * sigmoid(gate))
  * (REF:5059-5066 trtllm_batch_context_with_kv_cache + fused_sigmoid_mul)                   */
 int qw_attn_prefill(const void* qkv, int64_t ldq, int64_t nq, int64_t nkv, int64_t d, const void* k_cache,
                     const void* v_cache, const void* tiles, int64_t n_tiles, const int32_t* cu_seqlens,
-                    const int32_t* prefix, const int32_t* kv_base, void* out, int64_t ldo, float scale,
-                    qw_stream_t stream);
+                    const int32_t* prefix, const int32_t* kv_base, void* out, int64_t ldo, float scale, int64_t T,
+                    int64_t cache_rows, qw_stream_t stream);
 /* One query per request against seq_len[b] keys from row kv_base[b], split over `splits`
  * CTAs per (request, kv head) and combined (REF:5059-5062 trtllm_batch_decode_with_kv_cache
  * + REF:5066 fused_sigmoid_mul)                                                              */

@@ -13,6 +13,7 @@
 // therefore contiguous from row kv_base = 64 + slot*capacity, which is what the kernels
 // address; the page table of REF:5038-5040 is implied by that layout.
 #include "common.cuh"
+#include "tmap.cuh"
 
 namespace qw {
 
@@ -160,190 +161,288 @@ struct PrefillTile {
   int32_t q0;     // first query (within the request) of this tile
 };
 
-template <int D, int BM, int BN>
-struct AttnSmem {
-  static constexpr int Q = BM * D * 2;
-  static constexpr int KV = BN * D * 2;
-  static constexpr int TOTAL = Q + 4 * KV;  // Q, then double-buffered K and V
+// ============================================================== prefill attention (tcgen05)
+// CTA = (query head, 128-query tile), 6 warps:
+//  * warp 0 issues the TMA loads: the Q tile once, then K and V in blocks of 64 keys, each
+//    double-buffered (SWIZZLE_128B boxes of 64 columns);
+//  * warp 1 issues tcgen05.mma from one lane: S_j = Q K_j^T (M 128, N 64) into one of two TMEM
+//    S buffers, then O += P_{j-1} V_{j-1} (M 128, N = head dim, V as the MN-major operand);
+//  * warps 2-5 own one query row each (TMEM lane = row) and run the online softmax: S row from
+//    TMEM, causal mask, scores in log2 units, P = exp2(s - m) rounded to bf16 into shared
+//    memory (the A operand of P V). The running max m is raised only when a block's max
+//    exceeds it by more than 8, so P < 2^8 and the O row in TMEM is rescaled rarely (after the
+//    previous P V has completed). Epilogue: out = bf16(bf16(O / l) * sigmoid(gate)).
+// Every wait is a bounded mbarrier wait (QW_DEV_ERR_TIMEOUT_ATTN).
+template <int D>
+struct AttnTc {
+  static constexpr int BM = 128, BN = 64, NB = D / 64;  // 64-column boxes per row
+  static constexpr int QB = BM * 128;                   // bytes of one Q box
+  static constexpr int KVB = BN * 128;                  // bytes of one K or V box
+  static constexpr int Q = 0;
+  static constexpr int K0 = Q + NB * QB;                // 2 stages x NB boxes
+  static constexpr int V0 = K0 + 2 * NB * KVB;
+  static constexpr int P0 = V0 + 2 * NB * KVB;          // 2 buffers [128 rows][64 keys] bf16
+  static constexpr int PB = BM * 128;
+  static constexpr int BAR = P0 + 2 * PB;
+  static constexpr int SMEM = BAR + 256 + 1024;         // + slack to align the base to 1024
+  static constexpr int TMEM_O = 2 * BN;                 // S buffers at TMEM columns 0 and 64
+  static constexpr uint32_t TMEM_COLS = (TMEM_O + D <= 256) ? 256 : 512;
 };
 
-// grid: (n_tiles, nq). 8 warps x 16 query rows.
 template <int D>
-__global__ void __launch_bounds__(256, 1)
-    attn_prefill_kernel(const __nv_bfloat16* __restrict__ qkv, int64_t ldq, int nq, int nkv,
-                        const __nv_bfloat16* __restrict__ kc, const __nv_bfloat16* __restrict__ vc,
-                        const PrefillTile* __restrict__ tiles, const int32_t* __restrict__ cu,
-                        const int32_t* __restrict__ prefix, const int32_t* __restrict__ kv_base,
-                        __nv_bfloat16* __restrict__ out, int64_t ldo, float scale_log2) {
-  constexpr int BM = 128, BN = 64, NW = 8;
-  constexpr int CH = D / 8;  // 16-byte chunks per row
-  using L = AttnSmem<D, BM, BN>;
-  extern __shared__ __align__(128) uint8_t smem[];
-  const uint32_t sQ = smem_u32(smem);
-  const uint32_t sK0 = sQ + L::Q;
-  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const PrefillTile tile = tiles[blockIdx.x];
-  const int h = blockIdx.y;
-  const int kvh = h / (nq / nkv);
+__global__ void __launch_bounds__(192, 1) attn_prefill_kernel(
+    const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+    const __grid_constant__ CUtensorMap tmV, const PrefillTile* __restrict__ tiles, const int32_t* __restrict__ cu,
+    const int32_t* __restrict__ prefix, const int32_t* __restrict__ kv_base, const __nv_bfloat16* __restrict__ qkv,
+    int64_t ldq, __nv_bfloat16* __restrict__ out, int64_t ldo, int nq, int nkv, float scale_log2, int* err) {
+  using L = AttnTc<D>;
+  constexpr int CODE = QW_DEV_ERR_TIMEOUT_ATTN;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::BAR);
+  uint64_t* q_full = bars;
+  uint64_t* k_full = bars + 1;
+  uint64_t* k_empty = bars + 3;
+  uint64_t* v_full = bars + 5;
+  uint64_t* v_empty = bars + 7;
+  uint64_t* s_full = bars + 9;
+  uint64_t* s_empty = bars + 11;
+  uint64_t* p_full = bars + 13;
+  uint64_t* p_empty = bars + 15;
+  uint64_t* mma_done = bars + 17;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 18);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int h = blockIdx.x, kvh = h / (nq / nkv);
+  const PrefillTile tile = tiles[blockIdx.y];
   const int t0 = cu[tile.req], n = cu[tile.req + 1] - t0;
-  const int p = prefix[tile.req];
-  const int64_t kb = kv_base[tile.req];
-  const int q_end = min(n, tile.q0 + BM);            // exclusive, within request
-  const int kv_len = p + q_end;                      // keys needed by this tile
-  const int n_kv_tiles = (kv_len + BN - 1) / BN;
+  const int q0 = tile.q0;
+  const int pre = prefix[tile.req];
+  const int kend = min(pre + q0 + L::BM, pre + n);  // keys any valid row of the tile can see
+  const int nblk = (kend + L::BN - 1) / L::BN;
+  const int kvrow = kv_base[tile.req];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
-  // ---- load Q tile (rows beyond the request are zero-filled)
-  for (int i = threadIdx.x; i < BM * CH; i += blockDim.x) {
-    const int r = i / CH, c = i % CH;
-    const int qi = tile.q0 + r;
-    const __nv_bfloat16* src = qkv + (int64_t)(t0 + min(qi, n - 1)) * ldq + (int64_t)h * 2 * D + c * 8;
-    cp_async16(sQ + swz<D>(r, c), src, qi < n);
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_empty[i], 128);
+      mbar_init(&p_full[i], 128);
+      mbar_init(&p_empty[i], 1);
+    }
+    mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
   }
-  auto load_kv = [&](int j, int buf) {
-    const uint32_t sK = sK0 + buf * 2 * L::KV;
-    const uint32_t sV = sK + L::KV;
-    for (int i = threadIdx.x; i < BN * CH; i += blockDim.x) {
-      const int r = i / CH, c = i % CH;
-      const int key = j * BN + r;
-      const int64_t rowi = kb + min(key, kv_len - 1);
-      const bool ok = key < kv_len;
-      cp_async16(sK + swz<D>(r, c), kc + (rowi * nkv + kvh) * D + c * 8, ok);
-      cp_async16(sV + swz<D>(r, c), vc + (rowi * nkv + kvh) * D + c * 8, ok);
-    }
-  };
-  load_kv(0, 0);
-  cp_async_commit();
-
-  float o[D / 8][4];
-#pragma unroll
-  for (int i = 0; i < D / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
-  float m_r[2] = {-INFINITY, -INFINITY}, l_r[2] = {0.f, 0.f};
-  const int g = lane >> 2, cq = lane & 3;
-  const int row0 = warp * 16;  // warp's first row in the tile
-  const int qpos0 = p + tile.q0 + row0 + g;  // absolute position of row g (and +8)
-
-  for (int j = 0; j < n_kv_tiles; ++j) {
-    if (j + 1 < n_kv_tiles) load_kv(j + 1, (j + 1) & 1);
-    cp_async_commit();
-    cp_async_wait<1>();
-    __syncthreads();
-    const uint32_t sK = sK0 + (j & 1) * 2 * L::KV;
-    const uint32_t sV = sK + L::KV;
-    // warps whose rows all precede this key tile skip the math (causal)
-    const bool active = (p + tile.q0 + row0 + 15) >= j * BN;
-    if (active) {
-      // ---- S = Q K^T  (16 x 64 per warp)
-      float s[8][4];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) s[i][0] = s[i][1] = s[i][2] = s[i][3] = 0.f;
-#pragma unroll
-      for (int kk = 0; kk < D / 16; ++kk) {
-        uint32_t a[4];
-        {
-          const int r = row0 + (lane & 15);
-          const int c = kk * 2 + (lane >> 4);
-          ldmatrix_x4(sQ + swz<D>(r, c), a[0], a[1], a[2], a[3]);
-        }
-#pragma unroll
-        for (int nt = 0; nt < 8; nt += 2) {
-          // matrices: keys nt*8..+7 (k lo, k hi), keys (nt+1)*8..+7 (k lo, k hi)
-          const int r = nt * 8 + (lane & 7) + ((lane >> 4) << 3);
-          const int c = kk * 2 + ((lane >> 3) & 1);
-          uint32_t b0, b1, b2, b3;
-          ldmatrix_x4(sK + swz<D>(r, c), b0, b1, b2, b3);
-          mma_bf16_16816(s[nt], a, b0, b1);
-          mma_bf16_16816(s[nt + 1], a, b2, b3);
-        }
-      }
-      // ---- mask + online softmax (rows g and g+8)
-      float mx[2] = {m_r[0], m_r[1]};
-#pragma unroll
-      for (int nt = 0; nt < 8; ++nt) {
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int key = j * BN + nt * 8 + cq * 2 + (e & 1);
-          const int qpos = qpos0 + ((e >> 1) << 3);
-          float v = s[nt][e] * scale_log2;
-          if (key > qpos || key >= kv_len) v = -INFINITY;
-          s[nt][e] = v;
-          mx[e >> 1] = fmaxf(mx[e >> 1], v);
-        }
-      }
-#pragma unroll
-      for (int r = 0; r < 2; ++r) {
-        mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 1));
-        mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 2));
-      }
-      float alpha[2], rs[2] = {0.f, 0.f};
-#pragma unroll
-      for (int r = 0; r < 2; ++r) {
-        alpha[r] = (mx[r] == -INFINITY) ? 1.f : exp2f(m_r[r] - mx[r]);
-        m_r[r] = mx[r];
-      }
-      uint32_t pa[4][4];  // P as A fragments, 4 k-steps of 16 keys
-#pragma unroll
-      for (int nt = 0; nt < 8; ++nt) {
-        float pv[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int r = e >> 1;
-          pv[e] = (m_r[r] == -INFINITY) ? 0.f : exp2f(s[nt][e] - m_r[r]);
-          rs[r] += pv[e];
-        }
-        const int ks = nt >> 1, hi = nt & 1;
-        pa[ks][hi * 2 + 0] = pack_bf16x2(pv[0], pv[1]);
-        pa[ks][hi * 2 + 1] = pack_bf16x2(pv[2], pv[3]);
-      }
-#pragma unroll
-      for (int r = 0; r < 2; ++r) {
-        rs[r] += __shfl_xor_sync(0xffffffffu, rs[r], 1);
-        rs[r] += __shfl_xor_sync(0xffffffffu, rs[r], 2);
-        l_r[r] = l_r[r] * alpha[r] + rs[r];
-      }
-#pragma unroll
-      for (int i = 0; i < D / 8; ++i) {
-        o[i][0] *= alpha[0];
-        o[i][1] *= alpha[0];
-        o[i][2] *= alpha[1];
-        o[i][3] *= alpha[1];
-      }
-      // ---- O += P V
-#pragma unroll
-      for (int ks = 0; ks < 4; ++ks) {
-        uint32_t a[4] = {pa[ks][0], pa[ks][1], pa[ks][2], pa[ks][3]};
-#pragma unroll
-        for (int dt = 0; dt < D / 8; dt += 2) {
-          // matrices (trans): keys ks*16+0..7 / +8..15 for d-tiles dt and dt+1
-          const int r = ks * 16 + (lane & 7) + (((lane >> 3) & 1) << 3);
-          const int c = dt + (lane >> 4);
-          uint32_t b0, b1, b2, b3;
-          ldmatrix_x4_trans(sV + swz<D>(r, c), b0, b1, b2, b3);
-          mma_bf16_16816(o[dt], a, b0, b1);
-          mma_bf16_16816(o[dt + 1], a, b2, b3);
-        }
-      }
-    }
-    __syncthreads();
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, L::TMEM_COLS);
+    tmem_relinquish();
   }
-  cp_async_wait<0>();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
 
-  // ---- epilogue: out = bf16(bf16(O / l) * sigmoid(gate))
-  float inv_l[2] = {l_r[0] > 0.f ? 1.f / l_r[0] : 0.f, l_r[1] > 0.f ? 1.f / l_r[1] : 0.f};
-#pragma unroll
-  for (int r = 0; r < 2; ++r) {
-    const int qi = tile.q0 + row0 + g + r * 8;
-    if (qi >= n) continue;
-    const int64_t t = t0 + qi;
-    const __nv_bfloat16* gate = qkv + t * ldq + (int64_t)h * 2 * D + D;
-    __nv_bfloat16* dst = out + t * ldo + (int64_t)h * D;
-#pragma unroll
-    for (int dt = 0; dt < D / 8; ++dt) {
-      const int c = dt * 8 + cq * 2;
-      const float a0 = bf16_round(o[dt][r * 2 + 0] * inv_l[r]);
-      const float a1 = bf16_round(o[dt][r * 2 + 1] * inv_l[r]);
-      const float g0 = bf2f(gate[c]), g1 = bf2f(gate[c + 1]);
-      *reinterpret_cast<uint32_t*>(dst + c) = pack_bf16x2(a0 / (1.f + expf(-g0)), a1 / (1.f + expf(-g1)));
+  if (warp == 0) {
+    // ---------------------------------------------------------------- TMA producer
+    if (elect_one()) {
+      mbar_arrive_expect_tx(q_full, L::NB * L::QB);
+      for (int i = 0; i < L::NB; ++i)
+        tma_load_2d(smem + L::Q + i * L::QB, &tmQ, q_full, h * 2 * D + i * 64, t0 + q0);
+      for (int j = 0; j < nblk; ++j) {
+        const int s = j & 1;
+        const uint32_t ph = (j >> 1) & 1;
+        if (!mbar_wait(&k_empty[s], ph ^ 1, abort_flag, err, CODE)) break;
+        mbar_arrive_expect_tx(&k_full[s], L::NB * L::KVB);
+        for (int i = 0; i < L::NB; ++i)
+          tma_load_2d(smem + L::K0 + (s * L::NB + i) * L::KVB, &tmK, &k_full[s], kvh * D + i * 64, kvrow + j * L::BN);
+        if (!mbar_wait(&v_empty[s], ph ^ 1, abort_flag, err, CODE)) break;
+        mbar_arrive_expect_tx(&v_full[s], L::NB * L::KVB);
+        for (int i = 0; i < L::NB; ++i)
+          tma_load_2d(smem + L::V0 + (s * L::NB + i) * L::KVB, &tmV, &v_full[s], kvh * D + i * 64, kvrow + j * L::BN);
+      }
     }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (elect_one()) {
+      constexpr uint32_t IDESC_S = umma_idesc_bf16(128, L::BN);
+      constexpr uint32_t IDESC_O = umma_idesc_bf16(128, D) | (1u << 16);  // B (V) MN-major
+      bool ok = mbar_wait(q_full, 0, abort_flag, err, CODE);
+      for (int j = 0; ok && j <= nblk; ++j) {
+        if (j < nblk) {
+          // S_j = Q K_j^T
+          const int s = j & 1;
+          const uint32_t ph = (j >> 1) & 1;
+          if (!mbar_wait(&k_full[s], ph, abort_flag, err, CODE) ||
+              !mbar_wait(&s_empty[s], ph ^ 1, abort_flag, err, CODE)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint64_t ad = umma_sdesc_sw128(smem_u32(smem + L::Q + (kk >> 2) * L::QB) + (kk & 3) * 32);
+            const uint64_t bd =
+                umma_sdesc_sw128(smem_u32(smem + L::K0 + (s * L::NB + (kk >> 2)) * L::KVB) + (kk & 3) * 32);
+            umma_bf16(tmem + s * L::BN, ad, bd, IDESC_S, kk > 0 ? 1u : 0u);
+          }
+          umma_commit(&s_full[s]);
+          umma_commit(&k_empty[s]);
+        }
+        if (j >= 1) {
+          // O += P_{j-1} V_{j-1}
+          const int jp = j - 1, s = jp & 1;
+          const uint32_t ph = (jp >> 1) & 1;
+          if (!mbar_wait(&v_full[s], ph, abort_flag, err, CODE) || !mbar_wait(&p_full[s], ph, abort_flag, err, CODE)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+#pragma unroll
+          for (int ks = 0; ks < L::BN / 16; ++ks) {
+            const uint64_t ad = umma_sdesc_sw128(smem_u32(smem + L::P0 + s * L::PB) + ks * 32);
+            const uint64_t bd = umma_sdesc_mn_sw128(smem_u32(smem + L::V0 + s * L::NB * L::KVB) + ks * 2048, L::KVB);
+            umma_bf16(tmem + L::TMEM_O, ad, bd, IDESC_O, (jp > 0 || ks > 0) ? 1u : 0u);
+          }
+          umma_commit(&p_empty[s]);
+          umma_commit(&v_empty[s]);
+        }
+      }
+      umma_commit(mma_done);
+      mbar_wait(mma_done, 0, nullptr, err, CODE);  // every MMA of this CTA has completed
+    }
+    __syncwarp();
+  } else {
+    // ---------------------------------------------------------------- softmax + epilogue (warps 2-5)
+    // tcgen05.ld/st are warp-collective: every decision that guards them is made per warp
+    // (__any_sync / __all_sync), so the 32 lanes always execute them together.
+    const int row = 32 * (warp & 3) + lane;  // TMEM lane = query row of the tile
+    const uint32_t trow = tmem + ((uint32_t)(32 * (warp & 3)) << 16);
+    const int qpos = pre + q0 + row;  // keys at positions <= qpos are visible
+    float m_used = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nblk; ++j) {
+      const int s = j & 1;
+      const uint32_t ph = (j >> 1) & 1;
+      if (!__all_sync(0xffffffffu, mbar_wait(&s_full[s], ph, abort_flag, err, CODE))) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      uint32_t sr[64];
+      tmem_ld_32x32b_x32(trow + s * L::BN, sr);
+      tmem_ld_32x32b_x32(trow + s * L::BN + 32, sr + 32);
+      tmem_ld_wait();
+      tc_fence_before();
+      mbar_arrive(&s_empty[s]);
+      const int key0 = j * L::BN;
+      float mx = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < 64; ++i) {
+        const float v = (key0 + i <= qpos) ? __uint_as_float(sr[i]) * scale_log2 : -INFINITY;
+        sr[i] = __float_as_uint(v);
+        mx = fmaxf(mx, v);
+      }
+      // the running max of a row is raised only when the block's max exceeds it by more
+      // than 8; rows of O are rescaled in TMEM by the whole warp (factor 1 on rows whose
+      // max stayed), once P V_{j-1} has completed
+      const bool grow = mx > m_used + 8.f;
+      const float m_new = grow ? mx : m_used;
+      if (__any_sync(0xffffffffu, grow && j > 0)) {
+        const int jp = j - 1;
+        if (!__all_sync(0xffffffffu, mbar_wait(&p_empty[jp & 1], (jp >> 1) & 1, abort_flag, err, CODE))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const float alpha = (grow && j > 0) ? exp2f(m_used - m_new) : 1.f;
+#pragma unroll 1
+        for (int c0 = 0; c0 < D; c0 += 32) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(trow + L::TMEM_O + c0, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+          tmem_st_32x32b_x32(trow + L::TMEM_O + c0, r);
+        }
+        tmem_st_wait();
+        l *= alpha;
+      }
+      m_used = m_new;
+      const float mu = (m_used == -INFINITY) ? 0.f : m_used;
+      // the P buffer is free once P V_{j-2} has completed
+      if (!__all_sync(0xffffffffu, mbar_wait(&p_empty[s], ph ^ 1, abort_flag, err, CODE))) {
+        ok = false;
+        break;
+      }
+      uint8_t* prow = smem + L::P0 + s * L::PB + row * 128;
+      float ps = 0.f;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        float pv[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          pv[e] = exp2f(__uint_as_float(sr[c * 8 + e]) - mu);
+          ps += pv[e];
+        }
+        uint4 u;
+        u.x = pack_bf16x2(pv[0], pv[1]);
+        u.y = pack_bf16x2(pv[2], pv[3]);
+        u.z = pack_bf16x2(pv[4], pv[5]);
+        u.w = pack_bf16x2(pv[6], pv[7]);
+        *reinterpret_cast<uint4*>(prow + ((c ^ (row & 7)) << 4)) = u;
+      }
+      l += ps;
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // P is read by the tensor core
+      tc_fence_before();                                             // after any O rescale
+      mbar_arrive(&p_full[s]);
+    }
+    // ---- epilogue once the last P V has completed
+    if (ok && nblk > 0) {
+      const int jp = nblk - 1;
+      ok = __all_sync(0xffffffffu, mbar_wait(&p_empty[jp & 1], (jp >> 1) & 1, abort_flag, err, CODE));
+    }
+    __syncwarp();
+    tc_fence_after();
+    const bool valid = ok && q0 + row < n;
+    const float inv_l = l > 0.f ? 1.f / l : 0.f;
+    const int64_t t = t0 + q0 + row;
+#pragma unroll 1
+    for (int c0 = 0; c0 < D; c0 += 32) {
+      uint32_t r[32];
+      tmem_ld_32x32b_x32(trow + L::TMEM_O + c0, r);
+      tmem_ld_wait();
+      if (valid) {
+        const __nv_bfloat16* gate = qkv + t * ldq + (int64_t)h * 2 * D + D + c0;
+        __nv_bfloat16* dst = out + t * ldo + (int64_t)h * D + c0;
+#pragma unroll
+        for (int v = 0; v < 4; ++v) {
+          float g[8], y[8];
+          load_bf16x8(gate + v * 8, g);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const float a = bf16_round(__uint_as_float(r[v * 8 + e]) * inv_l);
+            y[e] = a / (1.f + expf(-g[e]));
+          }
+          store_bf16x8(dst + v * 8, y);
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, L::TMEM_COLS);
   }
 }
 
@@ -588,30 +687,38 @@ extern "C" int qw_qk_norm_rope_store(void* qkv, int64_t ldq, int64_t T, int64_t 
 extern "C" int qw_attn_prefill(const void* qkv, int64_t ldq, int64_t nq, int64_t nkv, int64_t d, const void* k_cache,
                                const void* v_cache, const void* tiles, int64_t n_tiles, const int32_t* cu_seqlens,
                                const int32_t* prefix, const int32_t* kv_base, void* out, int64_t ldo, float scale,
-                               qw_stream_t stream) {
+                               int64_t T, int64_t cache_rows, qw_stream_t stream) {
   QW_CHECK_ARG(qkv && k_cache && v_cache && tiles && cu_seqlens && prefix && kv_base && out, QW_ERR_ARG);
-  QW_CHECK_ARG(n_tiles > 0 && nq > 0 && nkv > 0 && nq % nkv == 0, QW_ERR_ARG);
-  QW_CHECK_ARG(((uintptr_t)qkv % 16) == 0 && (ldq % 8) == 0, QW_ERR_ALIGN);
+  QW_CHECK_ARG(n_tiles > 0 && n_tiles <= 65535 && nq > 0 && nkv > 0 && nq % nkv == 0, QW_ERR_ARG);
+  QW_CHECK_ARG(T > 0 && T < (1ll << 31) && cache_rows > 0 && cache_rows < (1ll << 31) && ldq >= 2 * nq * d, QW_ERR_ARG);
+  QW_CHECK_ARG(((uintptr_t)qkv % 16) == 0 && (ldq % 8) == 0 && ((uintptr_t)out % 16) == 0 && (ldo % 8) == 0 &&
+                   ((uintptr_t)k_cache % 16) == 0 && ((uintptr_t)v_cache % 16) == 0,
+               QW_ERR_ALIGN);
+  if (d != 64 && d != 128 && d != 256) return QW_ERR_UNSUPPORTED;
+  CUtensorMap tq, tk, tv;
+  if (!tmap_bf16_2d_sw128(&tq, qkv, T, ldq, ldq, 64, 128) ||
+      !tmap_bf16_2d_sw128(&tk, k_cache, cache_rows, nkv * d, nkv * d, 64, 64) ||
+      !tmap_bf16_2d_sw128(&tv, v_cache, cache_rows, nkv * d, nkv * d, 64, 64))
+    return QW_ERR_DRIVER;
   auto* s = reinterpret_cast<cudaStream_t>(stream);
   const float sl2 = scale * 1.4426950408889634f;
-  dim3 grid((unsigned)n_tiles, (unsigned)nq);
-#define QW_ATTN_LAUNCH(DD)                                                                                          \
-  do {                                                                                                              \
-    constexpr int smem = AttnSmem<DD, 128, 64>::TOTAL;                                                              \
-    static bool cfg = false;                                                                                        \
-    if (!cfg) {                                                                                                     \
-      cudaFuncSetAttribute(attn_prefill_kernel<DD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);             \
-      cfg = true;                                                                                                   \
-    }                                                                                                               \
-    attn_prefill_kernel<DD><<<grid, 256, smem, s>>>(                                                                \
-        static_cast<const __nv_bfloat16*>(qkv), ldq, (int)nq, (int)nkv, static_cast<const __nv_bfloat16*>(k_cache), \
-        static_cast<const __nv_bfloat16*>(v_cache), static_cast<const PrefillTile*>(tiles), cu_seqlens, prefix,     \
-        kv_base, static_cast<__nv_bfloat16*>(out), ldo, sl2);                                                       \
+  dim3 grid((unsigned)nq, (unsigned)n_tiles);  // heads fastest: a kv group's heads share K/V in L2
+#define QW_ATTN_LAUNCH(DD)                                                                                        \
+  do {                                                                                                            \
+    static bool cfg = false;                                                                                      \
+    if (!cfg) {                                                                                                   \
+      cudaFuncSetAttribute(attn_prefill_kernel<DD>, cudaFuncAttributeMaxDynamicSharedMemorySize,                 \
+                           AttnTc<DD>::SMEM);                                                                     \
+      cfg = true;                                                                                                 \
+    }                                                                                                             \
+    attn_prefill_kernel<DD><<<grid, 192, AttnTc<DD>::SMEM, s>>>(                                                  \
+        tq, tk, tv, static_cast<const PrefillTile*>(tiles), cu_seqlens, prefix, kv_base,                         \
+        static_cast<const __nv_bfloat16*>(qkv), ldq, static_cast<__nv_bfloat16*>(out), ldo, (int)nq, (int)nkv,   \
+        sl2, device_error_ptr());                                                                                 \
   } while (0)
   if (d == 256) QW_ATTN_LAUNCH(256);
   else if (d == 128) QW_ATTN_LAUNCH(128);
-  else if (d == 64) QW_ATTN_LAUNCH(64);
-  else return QW_ERR_UNSUPPORTED;
+  else QW_ATTN_LAUNCH(64);
 #undef QW_ATTN_LAUNCH
   QW_LAUNCH_CHECK();
   return QW_OK;

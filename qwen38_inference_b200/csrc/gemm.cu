@@ -206,7 +206,8 @@ __global__ void __launch_bounds__(gemm_threads<MT>(), 1)
       int at, bt, split;
       decode_unit(p, u, at, bt, split);
       const int buf = tcount % NBUF;
-      if (!mbar_wait(&tfull[buf], (tcount / NBUF) & 1, abort_flag, p.err, QW_DEV_ERR_TIMEOUT_GEMM)) break;
+      // warp-uniform: the tcgen05.ld below are warp-collective
+      if (!__all_sync(0xffffffffu, mbar_wait(&tfull[buf], (tcount / NBUF) & 1, abort_flag, p.err, QW_DEV_ERR_TIMEOUT_GEMM))) break;
       tc_fence_after();
       const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + buf * ACC + msub * BN;
       const int a_row = at * (BM * MT) + row_in_tile;
@@ -431,7 +432,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
       int at, bt, split;
       decode_unit(p, u, at, bt, split);
       const int buf = tcount & 1;
-      if (!mbar_wait(&tfull[buf], (tcount >> 1) & 1, abort_flag, p.err, QW_DEV_ERR_TIMEOUT_GEMM)) break;
+      // warp-uniform: the tcgen05.ld below are warp-collective
+      if (!__all_sync(0xffffffffu, mbar_wait(&tfull[buf], (tcount >> 1) & 1, abort_flag, p.err, QW_DEV_ERR_TIMEOUT_GEMM))) break;
       tc_fence_after();
       const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + buf * P_BN;
       const int a_row = at * 256 + row_in_tile;

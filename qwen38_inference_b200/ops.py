@@ -125,10 +125,13 @@ def qk_norm_rope_store(qkv, nq, nkv, d, q_w, k_w, rope, positions, locations, kc
 
 
 def attn_prefill(qkv, nq, nkv, d, kc, vc, tiles, cu, prefix, kv_base, out, scale):
+    """Causal varlen attention over the cache; qkv [T, ldq] rows, kc/vc [cache_rows, nkv, d]."""
+    if not (kc.is_contiguous() and vc.is_contiguous() and kc.shape == vc.shape and qkv.stride(1) == 1):
+        raise ValueError("attn_prefill expects contiguous K/V caches of one shape and unit-stride qkv rows")
     LAUNCHES[0] += 1
     _lib.call("qw_attn_prefill", qkv.data_ptr(), qkv.stride(0), nq, nkv, d, kc.data_ptr(), vc.data_ptr(),
               tiles.data_ptr(), tiles.numel() // 2, cu.data_ptr(), prefix.data_ptr(), kv_base.data_ptr(),
-              out.data_ptr(), out.stride(0), scale, _stream())
+              out.data_ptr(), out.stride(0), scale, qkv.shape[0], kc.shape[0], _stream())
 
 
 def attn_decode_workspace_bytes(B, nq, d, splits):

@@ -124,13 +124,24 @@ def _attn_case(g, nq, nkv, d, prefixes, lens, cap=512):
     return kc, vc, qkv, starts
 
 
-@pytest.mark.parametrize("nq,nkv,d", [(24, 4, 256), (6, 1, 256), (4, 2, 64)])
-def test_attn_prefill(K, nq, nkv, d):
+@pytest.mark.parametrize("nq,nkv,d,case", [(24, 4, 256, "mixed"), (6, 1, 256, "mixed"), (4, 2, 64, "mixed"),
+                                           (24, 4, 256, "long"), (4, 2, 64, "long")])
+def test_attn_prefill(K, nq, nkv, d, case):
+    """Causal varlen attention: ragged requests with cached prefixes; "long" has several
+    query tiles and key blocks with growing score magnitudes (the running max rises
+    across blocks, so rows of O are rescaled in TMEM)."""
     from qwen38_inference_b200.model import build_metadata
     g = gen(4)
-    prefixes, lens = [0, 37, 130, 0], [200, 1, 77, 129]
-    kc, vc, qkv, starts = _attn_case(g, nq, nkv, d, prefixes, lens)
-    packed, offs, T = build_metadata(list(range(len(lens))), prefixes, lens, 512)
+    if case == "mixed":
+        prefixes, lens = [0, 37, 130, 0], [200, 1, 77, 129]
+    else:
+        prefixes, lens = [0, 300], [700, 260]
+    kc, vc, qkv, starts = _attn_case(g, nq, nkv, d, prefixes, lens, cap=1024)
+    if case == "long":
+        # keys grow in magnitude with their position: later blocks raise the row max
+        pos = torch.arange(kc.shape[0], dtype=torch.float32).view(-1, 1, 1)
+        kc = bf(kc.float() * (1.0 + pos / 256.0))
+    packed, offs, T = build_metadata(list(range(len(lens))), prefixes, lens, 1024)
     md = {k: torch.from_numpy(packed[o:o + n]).to(DEV) for k, (o, n) in offs.items()}
     out = torch.empty(T, nq * d, dtype=torch.bfloat16, device=DEV)
     K.attn_prefill(qkv.to(DEV), nq, nkv, d, kc.to(DEV), vc.to(DEV), md["tiles"], md["cu"], md["prefix"],
@@ -138,8 +149,10 @@ def test_attn_prefill(K, nq, nkv, d):
     q = qkv.float()[:, :2 * nq * d].view(T, nq, 2 * d)
     att = O.paged_attention(q[..., :d], kc, vc, starts, prefixes, lens, d ** -0.5, O.bf16)
     exp = O.sigmoid_mul(att.reshape(T, -1), q[..., d:].reshape(T, -1), O.bf16)
-    # P is rounded to bf16 before the PV product (tensor cores): allow a few ulps
-    close(out, exp, n_ulp=4, atol=2e-3, max_frac=0.5)
+    # P is rounded to bf16 before the PV product (tensor cores): allow a few ulps. With the
+    # peaked rows of the "long" case (a few keys carry almost all the weight) that rounding
+    # reaches ~2^-7 of |v| on isolated outputs.
+    close(out, exp, n_ulp=4, atol=2e-3 if case == "mixed" else 1.6e-2, max_frac=0.5)
 
 
 @pytest.mark.parametrize("nq,nkv,d", [(24, 4, 256), (4, 2, 64)])
