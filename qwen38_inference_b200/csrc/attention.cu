@@ -162,14 +162,16 @@ struct PrefillTile {
 };
 
 // ============================================================== prefill attention (tcgen05)
-// CTA = (query head, 128-query tile), 6 warps:
-//  * warp 0 issues the TMA loads: the Q tile once, then K and V in blocks of 64 keys, each
-//    double-buffered (SWIZZLE_128B boxes of 64 columns);
+// CTA = (query head, 128-query tile), 7 warps:
+//  * warp 0 issues the TMA loads of the Q tile, then K in blocks of 64 keys (three stages,
+//    SWIZZLE_128B boxes of 64 columns), and after the last S MMA the gate tile into the Q
+//    buffer; warp 6 loads V (two stages, its own stream, so K never waits behind V);
 //  * warp 1 issues tcgen05.mma from one lane: S_j = Q K_j^T (M 128, N 64) into one of two TMEM
-//    S buffers, then O += P_{j-1} V_{j-1} (M 128, N = head dim, V as the MN-major operand);
+//    S buffers, then O += P_{j-1} V_{j-1} (M 128, N = head dim) with P read from TMEM and V as
+//    the MN-major shared-memory operand;
 //  * warps 2-5 own one query row each (TMEM lane = row) and run the online softmax: S row from
-//    TMEM, causal mask, scores in log2 units, P = exp2(s - m) rounded to bf16 into shared
-//    memory (the A operand of P V). The running max m is raised only when a block's max
+//    TMEM, causal mask, scores in log2 units, P = exp2(s - m) rounded to bf16 pairs into one
+//    of two TMEM P buffers (the A operand of P V). The running max m is raised only when a block's max
 //    exceeds it by more than 8, so P < 2^8 and the O row in TMEM is rescaled rarely (after the
 //    previous P V has completed). Epilogue: out = bf16(bf16(O / l) * sigmoid(gate)).
 // Every wait is a bounded mbarrier wait (QW_DEV_ERR_TIMEOUT_ATTN).
@@ -179,18 +181,19 @@ struct AttnTc {
   static constexpr int QB = BM * 128;                   // bytes of one Q box
   static constexpr int KVB = BN * 128;                  // bytes of one K or V box
   static constexpr int Q = 0;
-  static constexpr int K0 = Q + NB * QB;                // 2 stages x NB boxes
-  static constexpr int V0 = K0 + 2 * NB * KVB;
-  static constexpr int P0 = V0 + 2 * NB * KVB;          // 2 buffers [128 rows][64 keys] bf16
-  static constexpr int PB = BM * 128;
-  static constexpr int BAR = P0 + 2 * PB;
+  static constexpr int KST = 3;                         // K stages
+  static constexpr int K0 = Q + NB * QB;                // KST stages x NB boxes
+  static constexpr int V0 = K0 + KST * NB * KVB;        // 2 stages x NB boxes
+  static constexpr int BAR = V0 + 2 * NB * KVB;
   static constexpr int SMEM = BAR + 256 + 1024;         // + slack to align the base to 1024
+  static constexpr int THREADS = 224;
   static constexpr int TMEM_O = 2 * BN;                 // S buffers at TMEM columns 0 and 64
-  static constexpr uint32_t TMEM_COLS = (TMEM_O + D <= 256) ? 256 : 512;
+  static constexpr int TMEM_P = TMEM_O + D;             // P buffers: 32 columns (64 bf16) each
+  static constexpr uint32_t TMEM_COLS = (TMEM_P + BN <= 256) ? 256 : 512;
 };
 
 template <int D>
-__global__ void __launch_bounds__(192, 1) attn_prefill_kernel(
+__global__ void __launch_bounds__(224, 1) attn_prefill_kernel(
     const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
     const __grid_constant__ CUtensorMap tmV, const PrefillTile* __restrict__ tiles, const int32_t* __restrict__ cu,
     const int32_t* __restrict__ prefix, const int32_t* __restrict__ kv_base, const __nv_bfloat16* __restrict__ qkv,
@@ -201,16 +204,18 @@ __global__ void __launch_bounds__(192, 1) attn_prefill_kernel(
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::BAR);
   uint64_t* q_full = bars;
-  uint64_t* k_full = bars + 1;
-  uint64_t* k_empty = bars + 3;
-  uint64_t* v_full = bars + 5;
-  uint64_t* v_empty = bars + 7;
-  uint64_t* s_full = bars + 9;
-  uint64_t* s_empty = bars + 11;
-  uint64_t* p_full = bars + 13;
-  uint64_t* p_empty = bars + 15;
-  uint64_t* mma_done = bars + 17;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 18);
+  uint64_t* k_full = bars + 1;   // [3]
+  uint64_t* k_empty = bars + 4;  // [3]
+  uint64_t* v_full = bars + 7;
+  uint64_t* v_empty = bars + 9;
+  uint64_t* s_full = bars + 11;
+  uint64_t* s_empty = bars + 13;
+  uint64_t* p_full = bars + 15;
+  uint64_t* p_empty = bars + 17;
+  uint64_t* mma_done = bars + 19;
+  uint64_t* q_free = bars + 20;  // the last S MMA has read Q
+  uint64_t* g_full = bars + 21;  // gate tile landed in the Q buffer
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 22);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int h = blockIdx.x, kvh = h / (nq / nkv);
@@ -225,9 +230,11 @@ __global__ void __launch_bounds__(192, 1) attn_prefill_kernel(
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < L::KST; ++i) {
       mbar_init(&k_full[i], 1);
       mbar_init(&k_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
       mbar_init(&v_full[i], 1);
       mbar_init(&v_empty[i], 1);
       mbar_init(&s_full[i], 1);
@@ -236,6 +243,8 @@ __global__ void __launch_bounds__(192, 1) attn_prefill_kernel(
       mbar_init(&p_empty[i], 1);
     }
     mbar_init(mma_done, 1);
+    mbar_init(q_free, 1);
+    mbar_init(g_full, 1);
     *abort_flag = 0;
     fence_barrier_init();
     tma_prefetch_desc(&tmQ);
@@ -252,18 +261,36 @@ __global__ void __launch_bounds__(192, 1) attn_prefill_kernel(
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
-    // ---------------------------------------------------------------- TMA producer
+    // ---------------------------------------------------------------- TMA: Q, K, then the gate
     if (elect_one()) {
       mbar_arrive_expect_tx(q_full, L::NB * L::QB);
       for (int i = 0; i < L::NB; ++i)
         tma_load_2d(smem + L::Q + i * L::QB, &tmQ, q_full, h * 2 * D + i * 64, t0 + q0);
+      bool okp = true;
       for (int j = 0; j < nblk; ++j) {
-        const int s = j & 1;
-        const uint32_t ph = (j >> 1) & 1;
-        if (!mbar_wait(&k_empty[s], ph ^ 1, abort_flag, err, CODE)) break;
+        const int s = j % L::KST;
+        const uint32_t ph = (j / L::KST) & 1;
+        if (!mbar_wait(&k_empty[s], ph ^ 1, abort_flag, err, CODE)) {
+          okp = false;
+          break;
+        }
         mbar_arrive_expect_tx(&k_full[s], L::NB * L::KVB);
         for (int i = 0; i < L::NB; ++i)
           tma_load_2d(smem + L::K0 + (s * L::NB + i) * L::KVB, &tmK, &k_full[s], kvh * D + i * 64, kvrow + j * L::BN);
+      }
+      // the output gate of the tile goes where Q was, once the last S MMA has read Q
+      if (okp && mbar_wait(q_free, 0, abort_flag, err, CODE)) {
+        mbar_arrive_expect_tx(g_full, L::NB * L::QB);
+        for (int i = 0; i < L::NB; ++i)
+          tma_load_2d(smem + L::Q + i * L::QB, &tmQ, g_full, h * 2 * D + D + i * 64, t0 + q0);
+      }
+    }
+  } else if (warp == 6) {
+    // ---------------------------------------------------------------- TMA: V
+    if (elect_one()) {
+      for (int j = 0; j < nblk; ++j) {
+        const int s = j & 1;
+        const uint32_t ph = (j >> 1) & 1;
         if (!mbar_wait(&v_empty[s], ph ^ 1, abort_flag, err, CODE)) break;
         mbar_arrive_expect_tx(&v_full[s], L::NB * L::KVB);
         for (int i = 0; i < L::NB; ++i)
@@ -279,9 +306,9 @@ __global__ void __launch_bounds__(192, 1) attn_prefill_kernel(
       for (int j = 0; ok && j <= nblk; ++j) {
         if (j < nblk) {
           // S_j = Q K_j^T
-          const int s = j & 1;
+          const int s = j & 1, ks3 = j % L::KST;
           const uint32_t ph = (j >> 1) & 1;
-          if (!mbar_wait(&k_full[s], ph, abort_flag, err, CODE) ||
+          if (!mbar_wait(&k_full[ks3], (j / L::KST) & 1, abort_flag, err, CODE) ||
               !mbar_wait(&s_empty[s], ph ^ 1, abort_flag, err, CODE)) {
             ok = false;
             break;
@@ -291,11 +318,12 @@ __global__ void __launch_bounds__(192, 1) attn_prefill_kernel(
           for (int kk = 0; kk < D / 16; ++kk) {
             const uint64_t ad = umma_sdesc_sw128(smem_u32(smem + L::Q + (kk >> 2) * L::QB) + (kk & 3) * 32);
             const uint64_t bd =
-                umma_sdesc_sw128(smem_u32(smem + L::K0 + (s * L::NB + (kk >> 2)) * L::KVB) + (kk & 3) * 32);
+                umma_sdesc_sw128(smem_u32(smem + L::K0 + (ks3 * L::NB + (kk >> 2)) * L::KVB) + (kk & 3) * 32);
             umma_bf16(tmem + s * L::BN, ad, bd, IDESC_S, kk > 0 ? 1u : 0u);
           }
           umma_commit(&s_full[s]);
-          umma_commit(&k_empty[s]);
+          umma_commit(&k_empty[ks3]);
+          if (j == nblk - 1) umma_commit(q_free);
         }
         if (j >= 1) {
           // O += P_{j-1} V_{j-1}
@@ -308,9 +336,9 @@ __global__ void __launch_bounds__(192, 1) attn_prefill_kernel(
           tc_fence_after();
 #pragma unroll
           for (int ks = 0; ks < L::BN / 16; ++ks) {
-            const uint64_t ad = umma_sdesc_sw128(smem_u32(smem + L::P0 + s * L::PB) + ks * 32);
             const uint64_t bd = umma_sdesc_mn_sw128(smem_u32(smem + L::V0 + s * L::NB * L::KVB) + ks * 2048, L::KVB);
-            umma_bf16(tmem + L::TMEM_O, ad, bd, IDESC_O, (jp > 0 || ks > 0) ? 1u : 0u);
+            umma_bf16_ts(tmem + L::TMEM_O, tmem + L::TMEM_P + s * (L::BN / 2) + ks * 8, bd, IDESC_O,
+                         (jp > 0 || ks > 0) ? 1u : 0u);
           }
           umma_commit(&p_empty[s]);
           umma_commit(&v_empty[s]);
@@ -344,13 +372,17 @@ __global__ void __launch_bounds__(192, 1) attn_prefill_kernel(
       tc_fence_before();
       mbar_arrive(&s_empty[s]);
       const int key0 = j * L::BN;
-      float mx = -INFINITY;
+      float mx8[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) mx8[e] = -INFINITY;
 #pragma unroll
       for (int i = 0; i < 64; ++i) {
         const float v = (key0 + i <= qpos) ? __uint_as_float(sr[i]) * scale_log2 : -INFINITY;
         sr[i] = __float_as_uint(v);
-        mx = fmaxf(mx, v);
+        mx8[i & 7] = fmaxf(mx8[i & 7], v);
       }
+      const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                             fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
       // the running max of a row is raised only when the block's max exceeds it by more
       // than 8; rows of O are rescaled in TMEM by the whole warp (factor 1 on rows whose
       // max stayed), once P V_{j-1} has completed
@@ -383,26 +415,19 @@ __global__ void __launch_bounds__(192, 1) attn_prefill_kernel(
         ok = false;
         break;
       }
-      uint8_t* prow = smem + L::P0 + s * L::PB + row * 128;
-      float ps = 0.f;
+      float ps8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      uint32_t pk[32];  // bf16 pairs (keys 2c, 2c + 1) of this row
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        float pv[8];
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          pv[e] = exp2f(__uint_as_float(sr[c * 8 + e]) - mu);
-          ps += pv[e];
-        }
-        uint4 u;
-        u.x = pack_bf16x2(pv[0], pv[1]);
-        u.y = pack_bf16x2(pv[2], pv[3]);
-        u.z = pack_bf16x2(pv[4], pv[5]);
-        u.w = pack_bf16x2(pv[6], pv[7]);
-        *reinterpret_cast<uint4*>(prow + ((c ^ (row & 7)) << 4)) = u;
+      for (int c = 0; c < 32; ++c) {
+        const float p0 = exp2f(__uint_as_float(sr[2 * c]) - mu), p1 = exp2f(__uint_as_float(sr[2 * c + 1]) - mu);
+        ps8[(2 * c) & 7] += p0;
+        ps8[(2 * c + 1) & 7] += p1;
+        pk[c] = pack_bf16x2(p0, p1);
       }
-      l += ps;
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // P is read by the tensor core
-      tc_fence_before();                                             // after any O rescale
+      tmem_st_32x32b_x32(trow + L::TMEM_P + s * (L::BN / 2), pk);
+      tmem_st_wait();
+      l += ((ps8[0] + ps8[1]) + (ps8[2] + ps8[3])) + ((ps8[4] + ps8[5]) + (ps8[6] + ps8[7]));
+      tc_fence_before();  // P (and any O rescale) in TMEM before the P V issue
       mbar_arrive(&p_full[s]);
     }
     // ---- epilogue once the last P V has completed
@@ -410,6 +435,7 @@ __global__ void __launch_bounds__(192, 1) attn_prefill_kernel(
       const int jp = nblk - 1;
       ok = __all_sync(0xffffffffu, mbar_wait(&p_empty[jp & 1], (jp >> 1) & 1, abort_flag, err, CODE));
     }
+    if (ok) ok = __all_sync(0xffffffffu, mbar_wait(g_full, 0, abort_flag, err, CODE));
     __syncwarp();
     tc_fence_after();
     const bool valid = ok && q0 + row < n;
@@ -421,16 +447,18 @@ __global__ void __launch_bounds__(192, 1) attn_prefill_kernel(
       tmem_ld_32x32b_x32(trow + L::TMEM_O + c0, r);
       tmem_ld_wait();
       if (valid) {
-        const __nv_bfloat16* gate = qkv + t * ldq + (int64_t)h * 2 * D + D + c0;
+        // gate row from the swizzled [128][64] boxes in the Q buffer
+        const uint8_t* grow = smem + L::Q + (c0 >> 6) * L::QB + row * 128;
         __nv_bfloat16* dst = out + t * ldo + (int64_t)h * D + c0;
 #pragma unroll
         for (int v = 0; v < 4; ++v) {
           float g[8], y[8];
-          load_bf16x8(gate + v * 8, g);
+          const int chunk = ((c0 & 63) >> 3) + v;
+          load_bf16x8(reinterpret_cast<const __nv_bfloat16*>(grow + ((chunk ^ (row & 7)) << 4)), g);
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
             const float a = bf16_round(__uint_as_float(r[v * 8 + e]) * inv_l);
-            y[e] = a / (1.f + expf(-g[e]));
+            y[e] = __fdividef(a, 1.f + __expf(-g[e]));
           }
           store_bf16x8(dst + v * 8, y);
         }
@@ -711,7 +739,7 @@ extern "C" int qw_attn_prefill(const void* qkv, int64_t ldq, int64_t nq, int64_t
                            AttnTc<DD>::SMEM);                                                                     \
       cfg = true;                                                                                                 \
     }                                                                                                             \
-    attn_prefill_kernel<DD><<<grid, 192, AttnTc<DD>::SMEM, s>>>(                                                  \
+    attn_prefill_kernel<DD><<<grid, AttnTc<DD>::THREADS, AttnTc<DD>::SMEM, s>>>(                                                  \
         tq, tk, tv, static_cast<const PrefillTile*>(tiles), cu_seqlens, prefix, kv_base,                         \
         static_cast<const __nv_bfloat16*>(qkv), ldq, static_cast<__nv_bfloat16*>(out), ldo, (int)nq, (int)nkv,   \
         sl2, device_error_ptr());                                                                                 \
