@@ -123,6 +123,19 @@ def make_inputs(V, B, L, rank):
     return prefill, decode
 
 
+def reduce_step_times(rec, world, device):
+    """This rank's median per-call times, then the maximum over ranks (a weak-scaling job
+    is as slow as its slowest replica). Returns (step_ms, e2e_ms, prefill_ms, decode_ms)."""
+    import torch
+    import torch.distributed as dist
+    med_p, med_d = statistics.median(rec["p"]), statistics.median(rec["d"])
+    med_pw, med_dw = statistics.median(rec["p_wall"]), statistics.median(rec["d_wall"])
+    t = torch.tensor([med_p + med_d, med_pw + med_dw, med_p, med_d], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return tuple(t.tolist())
+
+
 # ------------------------------------------------------------------------- CPU baseline
 def cpu_baseline(B=32, L=1024, sample_tokens=512, decode_ctx=128):
     """CPU restatement (oracle/) of the 27B step on a bounded sample: one GDN layer, one
@@ -287,12 +300,7 @@ def run_gpu(args):
         barrier()
     launches = ops.LAUNCHES[0] // max(1, args.steps)
     clocks = clk.summary()
-    med_p, med_d = statistics.median(rec["p"]), statistics.median(rec["d"])
-    med_pw, med_dw = statistics.median(rec["p_wall"]), statistics.median(rec["d_wall"])
-    t = torch.tensor([med_p + med_d, med_pw + med_dw, med_p, med_d], dtype=torch.float64, device="cuda")
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    step_ms, e2e_ms, mp, md = t.tolist()
+    step_ms, e2e_ms, mp, md = reduce_step_times(rec, world, "cuda")
     tokens = world * (B * L + B)
 
     # ---- roofline of the dominant kernel (the tcgen05 GEMM): one instrumented prefill
