@@ -316,8 +316,10 @@ def run_gpu(args):
         breakdown[name] = breakdown.get(name, 0.0) + a.elapsed_time(b)
     dec_ops = []
     _lib.PROFILE = dec_ops
+    model._engine.use_graphs = False  # per-op events need the eager launch sequence
     model.forward_step(decode, cache)
     torch.cuda.synchronize()
+    model._engine.use_graphs = True
     _lib.PROFILE = None
     dec_breakdown = {}
     for name, a, b in dec_ops:

@@ -62,6 +62,16 @@ size_t qw_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K, int out_kind);
 int qw_gemm_bf16(const void* x, const void* w, void* y, int64_t M, int64_t N, int64_t K, int64_t ldx,
                  int64_t ldw, int64_t ldy, int out_kind, void* workspace, size_t ws_bytes, qw_stream_t stream);
 
+/* Decode (M <= 64) projection fused with the residual add-norm that follows it:
+ * x = bf16(x_in . w^T) [M, N]; v = x + resid (fp32); resid = bf16(v);
+ * hidden = bf16(v * rsqrt(mean v^2 + eps) * (1 + norm_w)); resid and hidden are [M, N]
+ * contiguous. The split-K partials ([splits, M, N] fp32) live in the workspace
+ * (REF:5087-5088 / 5092 + 5052: F.linear then gemma_fused_add_rmsnorm)                      */
+size_t qw_gemm_add_rmsnorm_workspace_bytes(int64_t M, int64_t N, int64_t K);
+int qw_gemm_add_rmsnorm(const void* x, const void* w, int64_t M, int64_t N, int64_t K, int64_t ldx, int64_t ldw,
+                        void* resid, const void* norm_w, void* hidden, float eps, void* workspace, size_t ws_bytes,
+                        qw_stream_t stream);
+
 /* ---- hidden-state norms ------------------------------------------------------------ */
 /* residual = table[tokens] (bf16 [T,H]); hidden = bf16(r * rsqrt(mean r^2 + eps) * (1 + w))
  * (REF:5045 F.embedding + REF:5049-5050 sgl_kernel gemma_rmsnorm)                          */

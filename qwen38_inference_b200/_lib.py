@@ -24,6 +24,8 @@ SIGNATURES = {
     "qw_take_device_error": (I32, [C.POINTER(I32)]),
     "qw_gemm_workspace_bytes": (SZ, [I64, I64, I64, I32]),
     "qw_gemm_bf16": (I32, [P, P, P, I64, I64, I64, I64, I64, I64, I32, P, SZ, P]),
+    "qw_gemm_add_rmsnorm_workspace_bytes": (SZ, [I64, I64, I64]),
+    "qw_gemm_add_rmsnorm": (I32, [P, P, I64, I64, I64, I64, I64, P, P, P, F32, P, SZ, P]),
     "qw_embed_rmsnorm": (I32, [P, I64, P, I64, I64, P, P, P, F32, P]),
     "qw_add_rmsnorm": (I32, [P, P, P, I64, I64, F32, P]),
     "qw_add_rmsnorm_rows": (I32, [P, P, P, I64, I64, I64, P, P, F32, P]),

@@ -475,7 +475,8 @@ __global__ void __launch_bounds__(224, 1) attn_prefill_kernel(
 }
 
 // Decode attention (one query token per request) on tensor cores. CTA = (request, kv head,
-// split of the keys), 4 warps; each warp takes a contiguous quarter of the split's keys,
+// split of the keys), 2 warps (64 KB of shared memory at d = 256, three CTAs per SM); each
+// warp takes a contiguous half of the split's keys,
 // 16 at a time: S^T = K Q^T ([16 keys] x [8 query heads of the group], Q held as register B
 // fragments), an online softmax per head in the log2 domain, P^T rounded to bf16 through
 // shared memory, and O^T += V^T P^T ([d] x [heads]). K and V rows stream through a per-warp
@@ -483,13 +484,14 @@ __global__ void __launch_bounds__(224, 1) attn_prefill_kernel(
 // the split's partial; attn_decode_combine_kernel merges the splits and applies the gate.
 template <int D>
 struct DecodeSmem {
+  static constexpr int NW = 2;                    // warps per CTA
   static constexpr int KB = 16;                   // keys per warp step
   static constexpr int TK = KB * D * 2;           // one K (or V) step tile
   static constexpr int WARP = 4 * TK;             // two stages of K and V
-  static constexpr int P = 4 * WARP;              // per-warp P^T tiles [8 heads][16 keys] bf16
-  static constexpr int ML = P + 4 * 8 * KB * 2;   // per-warp max and sum of the 8 head columns
-  static constexpr int TOTAL = ML + 2 * 4 * 8 * 4;
-  static_assert(4 * 8 * D * 4 <= P, "the warps' O^T merge reuses the K/V stages");
+  static constexpr int P = NW * WARP;             // per-warp P^T tiles [8 heads][16 keys] bf16
+  static constexpr int ML = P + NW * 8 * KB * 2;  // per-warp max and sum of the 8 head columns
+  static constexpr int TOTAL = ML + 2 * NW * 8 * 4;
+  static_assert(NW * 8 * D * 4 <= P, "the warps' O^T merge reuses the K/V stages");
 };
 
 QW_DEV void ldmatrix_x2(uint32_t addr, uint32_t& r0, uint32_t& r1) {
@@ -497,13 +499,13 @@ QW_DEV void ldmatrix_x2(uint32_t addr, uint32_t& r0, uint32_t& r1) {
 }
 
 template <int D, int G>
-__global__ void __launch_bounds__(128) attn_decode_kernel(
+__global__ void __launch_bounds__(64) attn_decode_kernel(
     const __nv_bfloat16* __restrict__ qkv, int64_t ldq, int nq, int nkv, const __nv_bfloat16* __restrict__ kc,
     const __nv_bfloat16* __restrict__ vc, const int32_t* __restrict__ seq_len, const int32_t* __restrict__ kv_base,
     int keys_per_split, float scale_log2, float* __restrict__ part_o, float* __restrict__ part_ml, int splits) {
   static_assert(G <= 8 && D % 16 == 0, "the query heads of a group fill one 8-wide n-tile");
   using L_ = DecodeSmem<D>;
-  constexpr int KB = L_::KB, TK = L_::TK, NCH = D / 8, MT = D / 16;
+  constexpr int KB = L_::KB, TK = L_::TK, NCH = D / 8, MT = D / 16, NW = L_::NW;
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
   const int b = blockIdx.x / nkv, kvh = blockIdx.x % nkv, split = blockIdx.y;
@@ -511,7 +513,7 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(
   const int64_t base = kv_base[b];
   const int k_begin = split * keys_per_split;
   const int k_end = min(L, k_begin + keys_per_split);
-  const int span = (keys_per_split + 4 * KB - 1) / (4 * KB) * KB;  // keys per warp, multiple of 16
+  const int span = (keys_per_split + NW * KB - 1) / (NW * KB) * KB;  // keys per warp, multiple of 16
   const int w_begin = k_begin + warp * span;
   const int w_end = min(k_end, w_begin + span);
   const int steps = w_end > w_begin ? (w_end - w_begin + KB - 1) / KB : 0;
@@ -612,11 +614,11 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(
     }
     __syncwarp();  // this stage and P are refilled next
   }
-  // ---- merge the 4 warps into the split's partial
+  // ---- merge the warps into the split's partial
   __syncthreads();  // every warp is done with its K/V stages
-  float* sO = reinterpret_cast<float*>(smem);  // [4 warps][8 heads][D]
+  float* sO = reinterpret_cast<float*>(smem);  // [NW warps][8 heads][D]
   float* sM = reinterpret_cast<float*>(smem + L_::ML);
-  float* sL = sM + 4 * 8;
+  float* sL = sM + NW * 8;
 #pragma unroll
   for (int mt = 0; mt < MT; ++mt) {
 #pragma unroll
@@ -634,10 +636,10 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(
     const int gi = i / D, d = i % D;
     float mm = -INFINITY;
 #pragma unroll
-    for (int w = 0; w < 4; ++w) mm = fmaxf(mm, sM[w * 8 + gi]);
+    for (int w = 0; w < NW; ++w) mm = fmaxf(mm, sM[w * 8 + gi]);
     float ll = 0.f, oo = 0.f;
 #pragma unroll
-    for (int w = 0; w < 4; ++w) {
+    for (int w = 0; w < NW; ++w) {
       const float f = (sM[w * 8 + gi] == -INFINITY) ? 0.f : exp2f(sM[w * 8 + gi] - mm);
       ll += sL[w * 8 + gi] * f;
       oo += sO[(w * 8 + gi) * D + d] * f;
@@ -780,10 +782,10 @@ extern "C" int qw_attn_decode(const void* qkv, int64_t ldq, int64_t B, int64_t n
   const auto* kc = static_cast<const __nv_bfloat16*>(k_cache);
   const auto* vc = static_cast<const __nv_bfloat16*>(v_cache);
   if (d == 256 && group == 6)
-    attn_decode_kernel<256, 6><<<grid, 128, DecodeSmem<256>::TOTAL, s>>>(q, ldq, (int)nq, (int)nkv, kc, vc, seq_len, kv_base, kps, sl2,
+    attn_decode_kernel<256, 6><<<grid, 32 * DecodeSmem<256>::NW, DecodeSmem<256>::TOTAL, s>>>(q, ldq, (int)nq, (int)nkv, kc, vc, seq_len, kv_base, kps, sl2,
                                                     part_o, part_ml, (int)splits);
   else if (d == 64 && group == 2)
-    attn_decode_kernel<64, 2><<<grid, 128, DecodeSmem<64>::TOTAL, s>>>(q, ldq, (int)nq, (int)nkv, kc, vc, seq_len, kv_base, kps, sl2,
+    attn_decode_kernel<64, 2><<<grid, 32 * DecodeSmem<64>::NW, DecodeSmem<64>::TOTAL, s>>>(q, ldq, (int)nq, (int)nkv, kc, vc, seq_len, kv_base, kps, sl2,
                                                    part_o, part_ml, (int)splits);
   else
     return QW_ERR_UNSUPPORTED;

@@ -537,6 +537,55 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ ws, void* out, in
   }
 }
 
+// Decode projection followed by the residual add-norm: row m of the output is
+// x = bf16(sum_s ws[s][m][:]) (splits in order, as splitk_reduce_kernel), then
+// v = x + resid (fp32), resid = bf16(v), hidden = bf16(v * rsqrt(mean v^2 + eps) * (1 + w)).
+// One CTA per row, one thread per 8 columns (all split partials of a thread in flight at once).
+constexpr int kAddNormMaxThreads = 1024;
+__global__ void __launch_bounds__(kAddNormMaxThreads) splitk_add_rmsnorm_kernel(
+    const float* __restrict__ ws, int splits, int64_t part_stride, int N, __nv_bfloat16* __restrict__ resid,
+    const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ hidden, float eps) {
+  __shared__ float red[32];
+  const int m = blockIdx.x;
+  const int c = threadIdx.x * 8;
+  const bool on = c < N;
+  float v[8];
+  float ss = 0.f;
+  if (on) {
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    const float* src = ws + (int64_t)m * N + c;
+#pragma unroll 4
+    for (int sp = 0; sp < splits; ++sp) {
+      const float4 a = reinterpret_cast<const float4*>(src + sp * part_stride)[0];
+      const float4 b = reinterpret_cast<const float4*>(src + sp * part_stride)[1];
+      acc[0] += a.x; acc[1] += a.y; acc[2] += a.z; acc[3] += a.w;
+      acc[4] += b.x; acc[5] += b.y; acc[6] += b.z; acc[7] += b.w;
+    }
+    float r[8];
+    load_bf16x8(resid + (int64_t)m * N + c, r);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      v[j] = bf16_round(acc[j]) + r[j];
+      ss += v[j] * v[j];
+    }
+    store_bf16x8(resid + (int64_t)m * N + c, v);
+  }
+  ss = warp_sum(ss);
+  const int nwarp = blockDim.x >> 5;
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
+  for (int i = 0; i < nwarp; ++i) tot += red[i];
+  const float rstd = rsqrtf(tot / (float)N + eps);
+  if (on) {
+    float wf[8], o[8];
+    load_bf16x8(w + c, wf);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[j] = v[j] * rstd * (1.0f + wf[j]);
+    store_bf16x8(hidden + (int64_t)m * N + c, o);
+  }
+}
+
 // ------------------------------------------------------------------ host side
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -803,6 +852,58 @@ extern "C" int qw_gemm_bf16(const void* x, const void* w, void* y, int64_t M, in
     splitk_reduce_kernel<EPI_F32><<<blocks, threads, 0, s>>>(ws, y, (int)M, (int)n_out, ldy, pl.splits, p.part_stride, N, 0);
   else
     splitk_reduce_kernel<EPI_BF16><<<blocks, threads, 0, s>>>(ws, y, (int)M, (int)n_out, ldy, pl.splits, p.part_stride, N, 0);
+  QW_LAUNCH_CHECK();
+  return QW_OK;
+}
+
+extern "C" size_t qw_gemm_add_rmsnorm_workspace_bytes(int64_t M, int64_t N, int64_t K) {
+  if (!use_skinny(M)) return 0;
+  const SkinnyPlan pl = plan_skinny(M, N, K);
+  return (size_t)pl.splits * (size_t)M * (size_t)N * sizeof(float);
+}
+
+extern "C" int qw_gemm_add_rmsnorm(const void* x, const void* w, int64_t M, int64_t N, int64_t K, int64_t ldx,
+                                   int64_t ldw, void* resid, const void* norm_w, void* hidden, float eps,
+                                   void* workspace, size_t ws_bytes, qw_stream_t stream) {
+  QW_CHECK_ARG(x && w && resid && norm_w && hidden && M > 0 && N > 0 && K > 0 && ldx >= K && ldw >= K, QW_ERR_ARG);
+  QW_CHECK_ARG(use_skinny(M) && N % 8 == 0 && N <= kAddNormMaxThreads * 8, QW_ERR_UNSUPPORTED);
+  QW_CHECK_ARG(((uintptr_t)x % 16) == 0 && ((uintptr_t)w % 16) == 0 && (ldx % 8) == 0 && (ldw % 8) == 0 &&
+                   ((uintptr_t)resid % 16) == 0 && ((uintptr_t)hidden % 16) == 0 && ((uintptr_t)norm_w % 16) == 0,
+               QW_ERR_ALIGN);
+  const SkinnyPlan pl = plan_skinny(M, N, K);
+  const size_t need = (size_t)pl.splits * (size_t)M * (size_t)N * sizeof(float);
+  QW_CHECK_ARG(workspace != nullptr && ws_bytes >= need, QW_ERR_WORKSPACE);
+  QW_CHECK_ARG(((uintptr_t)workspace % 16) == 0, QW_ERR_ALIGN);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  CUtensorMap ta, tb;
+  int rc;
+  if ((rc = make_tmap(&ta, w, N, K, ldw, BM)) != QW_OK) return rc;
+  if ((rc = make_tmap(&tb, x, M, K, ldx, pl.bn)) != QW_OK) return rc;
+  GemmParams p{};
+  p.err = device_error_ptr();
+  p.K = (int)K;
+  p.kb_total = pl.kb_total;
+  p.group = 1;
+  p.a_rows = (int)N;
+  p.b_rows = (int)M;
+  p.a_tiles = pl.a_tiles;
+  p.b_tiles = 1;
+  p.k_splits = pl.splits;
+  p.kb_per_split = pl.kb_per_split;
+  p.swap = 1;
+  p.out = workspace;
+  p.ldo = N;
+  p.part_stride = (int64_t)M * N;
+  switch (pl.bn) {
+    case 16: rc = launch_gemm<16, 8, EPI_PARTIAL>(ta, tb, p, s); break;
+    case 32: rc = launch_gemm<32, 8, EPI_PARTIAL>(ta, tb, p, s); break;
+    default: rc = launch_gemm<64, 8, EPI_PARTIAL>(ta, tb, p, s); break;
+  }
+  if (rc != QW_OK) return rc;
+  const int threads = (int)((N / 8 + 31) / 32 * 32);
+  splitk_add_rmsnorm_kernel<<<(unsigned)M, threads, 0, s>>>(
+      static_cast<const float*>(workspace), pl.splits, p.part_stride, (int)N, static_cast<__nv_bfloat16*>(resid),
+      static_cast<const __nv_bfloat16*>(norm_w), static_cast<__nv_bfloat16*>(hidden), eps);
   QW_LAUNCH_CHECK();
   return QW_OK;
 }

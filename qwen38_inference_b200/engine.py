@@ -36,7 +36,8 @@ class Engine:
 
     # ------------------------------------------------------------------ helpers
     def _decode_splits(self, capacity):
-        return int(min(64, max(1, (capacity + 255) // 256)))
+        # key splits of decode attention: one per 128 slots of capacity (CTAs of 2 warps)
+        return int(min(128, max(1, (capacity + 127) // 128)))
 
     def _meta_views(self, dev, offs):
         return {k: dev[o:o + n] for k, (o, n) in offs.items()}
@@ -121,9 +122,18 @@ class Engine:
             kb = torch.empty(T, c.gdn_qk_dim, dtype=BF16, device=dev)
             vb = torch.empty(T, c.gdn_v_dim, dtype=BF16, device=dev)
         splits = self._decode_splits(cache.capacity)
+        fused = is_decode and T <= 64  # weight-streaming projections: split-K sum + add-norm in one kernel
+
+        def proj_add_norm(x, wt, norm_w):
+            """hidden = x . wt^T, then resid += hidden, hidden = norm(resid)."""
+            if fused:
+                ops.gemm_add_rmsnorm(x, wt, resid, norm_w, hidden, eps, ws)
+            else:
+                ops.gemm(x, wt, hidden, ws=ws)
+                ops.add_rmsnorm(hidden, resid, norm_w, eps)
+
+        n_layers = len(m.layers)
         for i, (kind, w) in enumerate(zip(m.layer_types, m.layers)):
-            if i > 0:
-                ops.add_rmsnorm(hidden, resid, w["input_norm"], eps)
             if kind == "full_attention":
                 qkv = proj[:, :c.qkv_dim]
                 ops.gemm(hidden, w["qkv"], qkv, ws=ws)
@@ -137,7 +147,7 @@ class Engine:
                 else:
                     ops.attn_prefill(qkv, nq, nkv, d, kc, vc, md["tiles"], md["cu"], md["prefix"], md["kv_base"],
                                      att, d ** -0.5)
-                ops.gemm(att, w["out"], hidden, ws=ws)
+                proj_add_norm(att, w["out"], w["post_norm"])
             else:
                 ops.gemm(hidden, w["qkvzba"], proj[:, :c.qkvz_dim + c.ba_dim], ws=ws)
                 qkvz, ba = proj[:, :c.qkvz_dim], proj[:, c.qkvz_dim:c.qkvz_dim + c.ba_dim]
@@ -151,10 +161,12 @@ class Engine:
                     ops.gdn_prefill(qb, kb, vb, ba, w["A_log"], w["dt_bias"], md["cu"], md["slots"], B,
                                     cache.recurrent[i], qkvz[:, c.conv_dim:], w["norm"], y, Hk, HV, dk, dv,
                                     dk ** -0.5, eps)
-                ops.gemm(y, w["out"], hidden, ws=ws)
-            ops.add_rmsnorm(hidden, resid, w["post_norm"], eps)
+                proj_add_norm(y, w["out"], w["post_norm"])
             ops.gemm(hidden, w["gate_up"], act, out_kind=ops.OUT_SWIGLU, ws=ws)
-            ops.gemm(act, w["down"], hidden, ws=ws)
+            if i + 1 < n_layers:
+                proj_add_norm(act, w["down"], m.layers[i + 1]["input_norm"])  # the next layer's input norm
+            else:
+                ops.gemm(act, w["down"], hidden, ws=ws)
         rows = None if return_all_logits else md["last_rows"]
         R = T if return_all_logits else B
         fin = torch.empty(R, H, dtype=BF16, device=dev)

@@ -87,6 +87,22 @@ def gemm(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None, *, o
 
 
 # ----------------------------------------------------------------------------- norms
+def gemm_add_rmsnorm(x, w, resid, norm_w, hidden, eps, ws: Workspace):
+    """Decode projection (M <= 64) fused with the add-norm after it: resid += bf16(x . w^T),
+    hidden = GemmaRMSNorm(resid) (the split-K partials are summed by the norm kernel)."""
+    _req(x, BF16, "x")
+    _req(w, BF16, "w")
+    M, K = x.shape
+    N = w.shape[0]
+    if not (resid.is_contiguous() and hidden.is_contiguous() and resid.shape == (M, N) and hidden.shape == (M, N)):
+        raise ValueError("gemm_add_rmsnorm expects contiguous resid and hidden [M, N]")
+    need = int(_lib.load().qw_gemm_add_rmsnorm_workspace_bytes(M, N, K))
+    buf = ws.get(need)
+    LAUNCHES[0] += 2
+    _lib.call("qw_gemm_add_rmsnorm", x.data_ptr(), w.data_ptr(), M, N, K, x.stride(0), w.stride(0), resid.data_ptr(),
+              norm_w.data_ptr(), hidden.data_ptr(), eps, buf.data_ptr(), need, _stream())
+
+
 def embed_rmsnorm(tokens, table, w, resid_out, hidden_out, eps):
     T = tokens.numel()
     LAUNCHES[0] += 1

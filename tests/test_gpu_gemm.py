@@ -101,3 +101,27 @@ def test_gemm_strided_input(ops):
     w = (torch.randn(640, 512, device="cuda", generator=g) * 0.05).to(torch.bfloat16)
     y = ops.gemm(x, w)
     check_bf16(y, x, w)
+
+
+@pytest.mark.parametrize("M,N,K", [(32, 5120, 6144), (32, 5120, 17408), (5, 1024, 512), (64, 768, 2048)])
+def test_gemm_add_rmsnorm_matches_unfused(ops, M, N, K):
+    """The decode projection fused with the add-norm after it matches the projection
+    followed by the add-norm kernel: the residual bit for bit (same split-K order), the
+    normalized output within one bf16 ulp (the sum of squares is reduced in another order)."""
+    g = torch.Generator(device="cuda").manual_seed(11)
+    x = torch.randn(M, K, device="cuda", generator=g).to(torch.bfloat16)
+    w = (torch.randn(N, K, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+    resid0 = torch.randn(M, N, device="cuda", generator=g).to(torch.bfloat16)
+    nw = (torch.randn(N, device="cuda", generator=g) * 0.1).to(torch.bfloat16)
+    ws = ops.Workspace("cuda")
+    r_a, h_a = resid0.clone(), torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    ops.gemm_add_rmsnorm(x, w, r_a, nw, h_a, 1e-6, ws)
+    r_b = resid0.clone()
+    h_b = ops.gemm(x, w, ws=ws)
+    check_bf16(h_b, x, w)
+    ops.add_rmsnorm(h_b, r_b, nw, 1e-6)
+    torch.cuda.synchronize()
+    assert torch.equal(r_a, r_b)
+    d = (h_a.float() - h_b.float()).abs()
+    ulp = torch.exp2(torch.floor(torch.log2(h_b.float().abs().clamp_min(2.0 ** -126))) - 7)
+    assert bool((d <= ulp).all()) and (d > 0).float().mean().item() < 0.01
