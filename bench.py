@@ -375,6 +375,143 @@ def run_gpu(args):
         dist.destroy_process_group()
 
 
+def _rank_weight_bytes(model):
+    """Bytes of this rank's weights that a decode step streams (every linear layer and the
+    lm_head; the embedding is a row gather)."""
+    seen, total = set(), 0
+    for w in model.layers:
+        for k, t in w.items():
+            if k in ("qkvz", "ba"):  # views into qkvzba
+                continue
+            if t.data_ptr() not in seen:
+                seen.add(t.data_ptr())
+                total += t.numel() * t.element_size()
+    return total + model.final_norm.numel() * 2 + model.lm_head.numel() * 2
+
+
+def run_long(args):
+    """One long request with head-wise tensor parallelism over the N GPUs (torchrun): a
+    B1 prompt of ``--long-tokens`` tokens fed in ``--chunk``-token forward_step calls into a
+    fresh cache, then decode steps at that context (the reference configuration "B1 prefill
+    of 131071 tokens in 512-token chunks, then decode"). One step = the whole chunked prefill
+    plus ``--decode-steps`` decodes (the first two set up the decode graph and are untimed).
+    Warm-up steps run the first 8 chunks only. Times are per-call CUDA events summed over the
+    chunks, max over ranks (strong scaling: the same request whatever N)."""
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=torch.device("cuda", local))
+    from qwen38_inference_b200 import Qwen38, ops
+    from qwen38_inference_b200.config import qwen38_27b
+
+    cfg = qwen38_27b()
+    n_tok, chunk = args.long_tokens, args.chunk
+    n_dec = max(3, args.decode_steps)
+    model = Qwen38(config=cfg, seed=0, device=f"cuda:{local}", max_context=n_tok + n_dec + 64,
+                   tensor_parallel=True if world > 1 else None)
+    g = torch.Generator().manual_seed(26)
+    prompt = torch.randint(cfg.vocab_size, (n_tok,), generator=g).tolist()  # same tokens on every rank
+    g = torch.Generator().manual_seed(27)
+    dec_tokens = torch.randint(cfg.vocab_size, (n_dec,), generator=g).tolist()
+    chunks = [prompt[i:i + chunk] for i in range(0, n_tok, chunk)]
+    stream = torch.cuda.current_stream()
+
+    def one_step(n_chunks, rec):
+        cache = model.new_cache(1, initial_capacity=64)
+        pf, pw, dd, dw = [], [], [], []
+        h2d = d2h = 0
+        torch.cuda.synchronize()
+        for c in chunks[:n_chunks]:
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            t0 = time.perf_counter()
+            e0.record(stream)
+            lg = model.forward_step([c], cache)
+            e1.record(stream)
+            h2d += model._engine.last_h2d_bytes
+            host = lg.cpu()
+            pw.append((time.perf_counter() - t0) * 1e3)
+            d2h += host.numel() * 4
+            pf.append((e0, e1))
+        for i, t in enumerate(dec_tokens):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            t0 = time.perf_counter()
+            e0.record(stream)
+            lg = model.forward_step([[t]], cache)
+            e1.record(stream)
+            host = lg.cpu()
+            if i >= 2:  # graph set-up calls are untimed
+                dw.append((time.perf_counter() - t0) * 1e3)
+                dd.append((e0, e1))
+        torch.cuda.synchronize()
+        if rec is not None:
+            rec["p"].append(sum(a.elapsed_time(b) for a, b in pf))
+            rec["p_wall"].append(sum(pw))
+            rec["d"].append(statistics.median(a.elapsed_time(b) for a, b in dd))
+            rec["d_wall"].append(statistics.median(dw))
+            rec["io"] = (h2d, d2h)
+        return cache
+
+    for _ in range(args.warmup):
+        one_step(min(8, len(chunks)), None)
+    rec = {"p": [], "d": [], "p_wall": [], "d_wall": []}
+    ops.LAUNCHES[0] = 0
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    with ClockSampler(local) as clk:
+        for _ in range(args.steps):
+            cache = one_step(len(chunks), rec)
+        torch.cuda.synchronize()
+    launches = ops.LAUNCHES[0] // max(1, args.steps)
+    step_ms, e2e_ms, mp, md = reduce_step_times(rec, world, "cuda")
+    # decode roofline (HBM): this rank's weights + its KV heads over the context + its GDN
+    # states (read and written), per decode step
+    c = model.cfg
+    ctx = n_tok + n_dec
+    kv_bytes = sum(1 for k in model.layer_types if k == "full_attention") * 2 * c.num_key_value_heads * c.head_dim * 2 * ctx
+    st_bytes = sum(1 for k in model.layer_types if k != "full_attention") * c.linear_num_value_heads * \
+        c.linear_value_head_dim * c.linear_key_head_dim * 4 * 2
+    dec_bytes = _rank_weight_bytes(model) + kv_bytes + st_bytes
+    hbm, _, _, src = _peaks()
+    achieved = dec_bytes / (md * 1e-3) / 1e9
+    h2d, d2h = rec["io"]
+    out = {"metric": f"B1 long-context chunked prefill tok/s ({n_tok} tokens in {chunk}-token calls), 27B hybrid, "
+                     f"head-wise tensor parallel", "value": round(n_tok / (mp * 1e-3), 1), "unit": UNIT,
+           "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_ms, 3),
+           "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+           "data": "synthetic (random-init N(0,0.02) 27B weights; uniform token ids, seeds 26/27)",
+           "config": {"workload": f"B1 x {n_tok} tokens in {chunk}-token chunks into a fresh cache, then decode at "
+                                  f"{n_tok} context", "global_batch": 1, "seq_len": n_tok,
+                      "parallelism": f"tp{world} (head-wise; fp32 NCCL all-reduce after each row-parallel projection)"
+                      if world > 1 else "single GPU",
+                      "warmup_steps": "first 8 chunks + decodes", "l2": "inputs larger than L2 (weights streamed per call)"},
+           "median_ms": {"prefill_total": round(mp, 2), "decode": round(md, 3)},
+           "reference_published": {"prefill_ms_one_131072_token_call": 7753.7, "decode_ms_at_131k": 15.79},
+           "e2e": {"value": round(n_tok / (statistics.median(rec["p_wall"]) * 1e-3), 1), "unit": UNIT,
+                   "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                   "decode_ms": round(statistics.median(rec["d_wall"]), 3)},
+           "gpu_launches": launches, "clocks": clk.summary(),
+           "roofline": {"bound": "hbm", "kernel": "decode step at the long context (all kernels of one step)",
+                        "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s", "frac": round(achieved / hbm, 4),
+                        "peak_source": f"{src} hbm_gbs", "bytes_per_rank_step": dec_bytes, "traffic": None}}
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+    del cache
+    model._engine.graphs.clear()  # graphs holding NCCL calls go before the process group
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def run_op(args):
     """One kernel of the step alone, at the step's shape, on random data: the case the ncu
     captures under profiles/ run (``--op gate_up``: the MLP gate_up GEMM with the SwiGLU
@@ -495,6 +632,12 @@ def main():
     ap.add_argument("--batch", type=int, default=32)
     ap.add_argument("--length", type=int, default=1024)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", choices=["step", "long"], default="step",
+                    help="step: the headline B32/L1024 prefill+decode (replicas over N GPUs); long: one long "
+                         "request with head-wise tensor parallelism over N GPUs")
+    ap.add_argument("--long-tokens", type=int, default=131071)
+    ap.add_argument("--chunk", type=int, default=512)
+    ap.add_argument("--decode-steps", type=int, default=10)
     ap.add_argument("--op", choices=["gate_up", "gdn_prefill", "conv_prefill", "attn_prefill"], default=None,
                     help="time one kernel of the step alone (the case the ncu captures run)")
     args = ap.parse_args()
@@ -504,6 +647,8 @@ def main():
         run_op(args)
     elif args.impl == "reference":
         run_reference(args)
+    elif args.workload == "long":
+        run_long(args)
     else:
         run_gpu(args)
 

@@ -52,12 +52,15 @@ int qw_take_device_error(int* code);
  *   out_kind QW_OUT_F32_OF_BF16: y f32  [M, ldy] = float(bf16(acc))     (F.linear().float(), REF:5096)
  *   out_kind QW_OUT_SWIGLU:      w = [gate; up] with N = 2*I rows, y bf16 [M, ldy] with I
  *                                columns = bf16(silu(bf16(g)) * bf16(u)) (REF:5089-5091 + REF:2238-2281)
+ *   out_kind QW_OUT_F32:         y f32  [M, ldy] = acc, unrounded: the partial sum of one tensor-
+ *                                parallel rank, rounded once after the all-reduce (qw_add_rmsnorm_f32)
  * Small M (decode) runs weight-streaming split-K tiles and needs a workspace of
  * qw_gemm_workspace_bytes(M, N, K) bytes (0 for large M).
  */
 #define QW_OUT_BF16 0
 #define QW_OUT_F32_OF_BF16 1
 #define QW_OUT_SWIGLU 2
+#define QW_OUT_F32 3
 size_t qw_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K, int out_kind);
 int qw_gemm_bf16(const void* x, const void* w, void* y, int64_t M, int64_t N, int64_t K, int64_t ldx,
                  int64_t ldw, int64_t ldy, int out_kind, void* workspace, size_t ws_bytes, qw_stream_t stream);
@@ -71,6 +74,14 @@ size_t qw_gemm_add_rmsnorm_workspace_bytes(int64_t M, int64_t N, int64_t K);
 int qw_gemm_add_rmsnorm(const void* x, const void* w, int64_t M, int64_t N, int64_t K, int64_t ldx, int64_t ldw,
                         void* resid, const void* norm_w, void* hidden, float eps, void* workspace, size_t ws_bytes,
                         qw_stream_t stream);
+
+/* The residual add-norm of REF:5052/5088 (gemma_fused_add_rmsnorm) with the projection
+ * output given as fp32 partial sums: x = bf16(sum_p parts[p]) over n_parts slices
+ * part_stride floats apart (each [T, H] contiguous, summed in order p = 0, 1, ...);
+ * v = x + resid (fp32); resid = bf16(v); hidden = bf16(v * rsqrt(mean v^2 + eps) * (1 + w)).
+ * Tensor parallelism feeds it the all-reduced row-parallel projection (n_parts = 1).      */
+int qw_add_rmsnorm_f32(const float* parts, int64_t n_parts, int64_t part_stride, int64_t T, int64_t H,
+                       void* resid, const void* norm_w, void* hidden, float eps, qw_stream_t stream);
 
 /* ---- hidden-state norms ------------------------------------------------------------ */
 /* residual = table[tokens] (bf16 [T,H]); hidden = bf16(r * rsqrt(mean r^2 + eps) * (1 + w))
@@ -108,6 +119,17 @@ int qw_attn_prefill(const void* qkv, int64_t ldq, int64_t nq, int64_t nkv, int64
                     const void* v_cache, const void* tiles, int64_t n_tiles, const int32_t* cu_seqlens,
                     const int32_t* prefix, const int32_t* kv_base, void* out, int64_t ldo, float scale, int64_t T,
                     int64_t cache_rows, qw_stream_t stream);
+/* qw_attn_prefill with the keys of every tile split over `splits` CTAs (long prefixes, e.g.
+ * chunked prefill of a 128k-token request, where heads x tiles alone leave SMs idle). Each
+ * CTA writes an unnormalized partial (O, running max, sum) per query row to the workspace;
+ * a merge kernel combines the splits and applies the gate. Same output as qw_attn_prefill up
+ * to fp32 summation order. splits == 1 is qw_attn_prefill (no workspace needed).          */
+size_t qw_attn_prefill_split_workspace_bytes(int64_t T, int64_t nq, int64_t d, int64_t splits);
+int qw_attn_prefill_split(const void* qkv, int64_t ldq, int64_t nq, int64_t nkv, int64_t d, const void* k_cache,
+                          const void* v_cache, const void* tiles, int64_t n_tiles, const int32_t* cu_seqlens,
+                          const int32_t* prefix, const int32_t* kv_base, void* out, int64_t ldo, float scale,
+                          int64_t T, int64_t cache_rows, int64_t splits, void* workspace, size_t ws_bytes,
+                          qw_stream_t stream);
 /* One query per request against seq_len[b] keys from row kv_base[b], split over `splits`
  * CTAs per (request, kv head) and combined (REF:5059-5062 trtllm_batch_decode_with_kv_cache
  * + REF:5066 fused_sigmoid_mul)                                                              */
@@ -165,6 +187,16 @@ int qw_gdn_decode(const void* qkvz, int64_t ldx, const void* ba, int64_t ldba, c
  * row zero. Applied to K and V together (REF:4985-5001 _reserve; solution/cache_growth.py) */
 int qw_kv_grow(const void* src_k, const void* src_v, void* dst_k, void* dst_v, const int32_t* lengths, int64_t S,
                int64_t old_cap, int64_t new_cap, int64_t row_elems, qw_stream_t stream);
+
+/* ---- head-wise tensor parallelism (new: the reference runs one GPU) ------------------ *
+ * The collectives themselves are NCCL all-reduce / all-gather calls made by the host; these
+ * move the data on either side of them.
+ * y bf16 [n] = bf16(x fp32 [n]): the all-reduced row-parallel down projection of the last
+ * layer becomes the bf16 F.linear output that the final norm reads (REF:5092-5093).        */
+int qw_round_f32_bf16(const float* x, void* y, int64_t n, qw_stream_t stream);
+/* dst fp32 [R, G*Vs] = src fp32 [G, R, Vs] with dst[r][g*Vs + v] = src[g][r][v]: the logits
+ * of G vocabulary shards, all-gathered rank-major, in vocabulary order (REF:5096 lm_head). */
+int qw_gather_vocab_shards(const float* src, int64_t G, int64_t R, int64_t Vs, float* dst, qw_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -53,7 +53,8 @@ def _names(cfg: HybridConfig):
     return out
 
 
-def load_weights(path, cfg: HybridConfig, device) -> dict:
+def load_weights(path, cfg: HybridConfig, device, shard=None) -> dict:
+    """``shard(name, tensor) -> tensor`` keeps a tensor-parallel rank's slice of each tensor."""
     from safetensors import safe_open
     path = Path(path)
     index = json.loads((path / "model.safetensors.index.json").read_text())["weight_map"]
@@ -81,7 +82,8 @@ def load_weights(path, cfg: HybridConfig, device) -> dict:
         t = torch.cat(ts) if len(ts) > 1 else ts[0]
         if name.endswith(".conv"):
             t = t.reshape(t.shape[0], -1)
-        flat[name] = t.to(device=device, dtype=torch.float32 if name.endswith("A_log") else torch.bfloat16)
+        t = t.to(device=device, dtype=torch.float32 if name.endswith("A_log") else torch.bfloat16)
+        flat[name] = shard(name, t) if shard is not None else t
     return flat
 
 

@@ -183,13 +183,16 @@ def weight_shapes(cfg: HybridConfig) -> dict:
 
 
 def random_weights(cfg: HybridConfig, seed: int = 0, *, dtype=torch.bfloat16, device="cpu",
-                   std: float = 0.02, norm_mode: str = "random") -> dict:
+                   std: float = 0.02, norm_mode: str = "random", shard=None) -> dict:
     """Every tensor i.i.d. N(0, std) from ``seed`` (one generator stream per tensor, so a
     tensor's values do not depend on the device or on the other tensors).
 
     ``norm_mode="unit"`` sets every Gemma norm weight to 0 (gain 1) and the plain gated
     norm weight to 1, the sensitivity variant of the synthetic-input plan.
     Returns a flat dict ``name -> tensor`` (see :func:`weight_shapes`). ``A_log`` is fp32.
+    ``shard(name, tensor) -> tensor``, when given, is applied to each full tensor right after
+    it is drawn (tensor parallelism keeps only its rank's slice, so at most one full tensor
+    is alive at a time and every rank's slices agree with the unsharded weights).
     """
     device = torch.device(device)
     out = {}
@@ -202,7 +205,8 @@ def random_weights(cfg: HybridConfig, seed: int = 0, *, dtype=torch.bfloat16, de
                 t.zero_()
             elif name.endswith(".norm"):
                 t.fill_(1.0)
-        out[name] = t if kind == "f32" else t.to(dtype)
+        t = t if kind == "f32" else t.to(dtype)
+        out[name] = shard(name, t) if shard is not None else t
     return out
 
 

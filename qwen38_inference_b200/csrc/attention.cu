@@ -197,7 +197,8 @@ __global__ void __launch_bounds__(224, 1) attn_prefill_kernel(
     const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
     const __grid_constant__ CUtensorMap tmV, const PrefillTile* __restrict__ tiles, const int32_t* __restrict__ cu,
     const int32_t* __restrict__ prefix, const int32_t* __restrict__ kv_base, const __nv_bfloat16* __restrict__ qkv,
-    int64_t ldq, __nv_bfloat16* __restrict__ out, int64_t ldo, int nq, int nkv, float scale_log2, int* err) {
+    int64_t ldq, __nv_bfloat16* __restrict__ out, int64_t ldo, int nq, int nkv, float scale_log2,
+    float* __restrict__ part_o, float* __restrict__ part_ml, int* err) {
   using L = AttnTc<D>;
   constexpr int CODE = QW_DEV_ERR_TIMEOUT_ATTN;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -224,7 +225,16 @@ __global__ void __launch_bounds__(224, 1) attn_prefill_kernel(
   const int q0 = tile.q0;
   const int pre = prefix[tile.req];
   const int kend = min(pre + q0 + L::BM, pre + n);  // keys any valid row of the tile can see
-  const int nblk = (kend + L::BN - 1) / L::BN;
+  const int nblk_all = (kend + L::BN - 1) / L::BN;
+  // split-KV (gridDim.z > 1): this CTA takes key blocks [jb, jb + nblk) of the tile and writes
+  // an unnormalized partial (O, running max, sum) per row; the gate is applied at the merge
+  const int nsplit = gridDim.z, split = blockIdx.z;
+  int jb = 0, nblk = nblk_all;
+  if (nsplit > 1) {
+    const int per = (nblk_all + nsplit - 1) / nsplit;
+    jb = min(nblk_all, split * per);
+    nblk = min(nblk_all, jb + per) - jb;
+  }
   const int kvrow = kv_base[tile.req];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -276,10 +286,11 @@ __global__ void __launch_bounds__(224, 1) attn_prefill_kernel(
         }
         mbar_arrive_expect_tx(&k_full[s], L::NB * L::KVB);
         for (int i = 0; i < L::NB; ++i)
-          tma_load_2d(smem + L::K0 + (s * L::NB + i) * L::KVB, &tmK, &k_full[s], kvh * D + i * 64, kvrow + j * L::BN);
+          tma_load_2d(smem + L::K0 + (s * L::NB + i) * L::KVB, &tmK, &k_full[s], kvh * D + i * 64,
+                      kvrow + (jb + j) * L::BN);
       }
       // the output gate of the tile goes where Q was, once the last S MMA has read Q
-      if (okp && mbar_wait(q_free, 0, abort_flag, err, CODE)) {
+      if (okp && nsplit == 1 && mbar_wait(q_free, 0, abort_flag, err, CODE)) {
         mbar_arrive_expect_tx(g_full, L::NB * L::QB);
         for (int i = 0; i < L::NB; ++i)
           tma_load_2d(smem + L::Q + i * L::QB, &tmQ, g_full, h * 2 * D + D + i * 64, t0 + q0);
@@ -294,7 +305,8 @@ __global__ void __launch_bounds__(224, 1) attn_prefill_kernel(
         if (!mbar_wait(&v_empty[s], ph ^ 1, abort_flag, err, CODE)) break;
         mbar_arrive_expect_tx(&v_full[s], L::NB * L::KVB);
         for (int i = 0; i < L::NB; ++i)
-          tma_load_2d(smem + L::V0 + (s * L::NB + i) * L::KVB, &tmV, &v_full[s], kvh * D + i * 64, kvrow + j * L::BN);
+          tma_load_2d(smem + L::V0 + (s * L::NB + i) * L::KVB, &tmV, &v_full[s], kvh * D + i * 64,
+                      kvrow + (jb + j) * L::BN);
       }
     }
   } else if (warp == 1) {
@@ -371,7 +383,7 @@ __global__ void __launch_bounds__(224, 1) attn_prefill_kernel(
       tmem_ld_wait();
       tc_fence_before();
       mbar_arrive(&s_empty[s]);
-      const int key0 = j * L::BN;
+      const int key0 = (jb + j) * L::BN;
       float mx8[8];
 #pragma unroll
       for (int e = 0; e < 8; ++e) mx8[e] = -INFINITY;
@@ -435,14 +447,42 @@ __global__ void __launch_bounds__(224, 1) attn_prefill_kernel(
       const int jp = nblk - 1;
       ok = __all_sync(0xffffffffu, mbar_wait(&p_empty[jp & 1], (jp >> 1) & 1, abort_flag, err, CODE));
     }
-    if (ok) ok = __all_sync(0xffffffffu, mbar_wait(g_full, 0, abort_flag, err, CODE));
+    if (ok && nsplit == 1) ok = __all_sync(0xffffffffu, mbar_wait(g_full, 0, abort_flag, err, CODE));
     __syncwarp();
     tc_fence_after();
     const bool valid = ok && q0 + row < n;
     const float inv_l = l > 0.f ? 1.f / l : 0.f;
     const int64_t t = t0 + q0 + row;
+    if (nsplit > 1) {
+      // partial of this split in the layout of the decode merge: slot (t * nq + h) * nsplit + split;
+      // O is in TMEM only if a P V ran (nblk > 0, uniform over the CTA); rows that saw no key
+      // have m = -inf and l = 0 and are ignored by the merge
+      const int64_t slot = ((int64_t)t * nq + h) * nsplit + split;
 #pragma unroll 1
-    for (int c0 = 0; c0 < D; c0 += 32) {
+      for (int c0 = 0; c0 < D; c0 += 32) {
+        uint32_t r[32];
+        if (nblk > 0) {
+          tmem_ld_32x32b_x32(trow + L::TMEM_O + c0, r);
+          tmem_ld_wait();
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) r[i] = 0u;
+        }
+        if (valid) {
+          float4* dst = reinterpret_cast<float4*>(part_o + slot * D + c0);
+#pragma unroll
+          for (int v = 0; v < 8; ++v)
+            dst[v] = make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]),
+                                 __uint_as_float(r[4 * v + 2]), __uint_as_float(r[4 * v + 3]));
+        }
+      }
+      if (valid) {
+        part_ml[slot * 2 + 0] = nblk > 0 ? m_used : -INFINITY;
+        part_ml[slot * 2 + 1] = nblk > 0 ? l : 0.f;
+      }
+    }
+#pragma unroll 1
+    for (int c0 = 0; c0 < D && nsplit == 1; c0 += 32) {
       uint32_t r[32];
       tmem_ld_32x32b_x32(trow + L::TMEM_O + c0, r);
       tmem_ld_wait();
@@ -714,13 +754,15 @@ extern "C" int qw_qk_norm_rope_store(void* qkv, int64_t ldq, int64_t T, int64_t 
   return QW_OK;
 }
 
-extern "C" int qw_attn_prefill(const void* qkv, int64_t ldq, int64_t nq, int64_t nkv, int64_t d, const void* k_cache,
+static int attn_prefill_launch(const void* qkv, int64_t ldq, int64_t nq, int64_t nkv, int64_t d, const void* k_cache,
                                const void* v_cache, const void* tiles, int64_t n_tiles, const int32_t* cu_seqlens,
                                const int32_t* prefix, const int32_t* kv_base, void* out, int64_t ldo, float scale,
-                               int64_t T, int64_t cache_rows, qw_stream_t stream) {
+                               int64_t T, int64_t cache_rows, int64_t splits, float* part_o, float* part_ml,
+                               qw_stream_t stream) {
   QW_CHECK_ARG(qkv && k_cache && v_cache && tiles && cu_seqlens && prefix && kv_base && out, QW_ERR_ARG);
   QW_CHECK_ARG(n_tiles > 0 && n_tiles <= 65535 && nq > 0 && nkv > 0 && nq % nkv == 0, QW_ERR_ARG);
   QW_CHECK_ARG(T > 0 && T < (1ll << 31) && cache_rows > 0 && cache_rows < (1ll << 31) && ldq >= 2 * nq * d, QW_ERR_ARG);
+  QW_CHECK_ARG(splits >= 1 && splits <= 65535, QW_ERR_ARG);
   QW_CHECK_ARG(((uintptr_t)qkv % 16) == 0 && (ldq % 8) == 0 && ((uintptr_t)out % 16) == 0 && (ldo % 8) == 0 &&
                    ((uintptr_t)k_cache % 16) == 0 && ((uintptr_t)v_cache % 16) == 0,
                QW_ERR_ALIGN);
@@ -732,7 +774,8 @@ extern "C" int qw_attn_prefill(const void* qkv, int64_t ldq, int64_t nq, int64_t
     return QW_ERR_DRIVER;
   auto* s = reinterpret_cast<cudaStream_t>(stream);
   const float sl2 = scale * 1.4426950408889634f;
-  dim3 grid((unsigned)nq, (unsigned)n_tiles);  // heads fastest: a kv group's heads share K/V in L2
+  // heads fastest: a kv group's heads share K/V in L2; key splits slowest
+  dim3 grid((unsigned)nq, (unsigned)n_tiles, (unsigned)splits);
 #define QW_ATTN_LAUNCH(DD)                                                                                        \
   do {                                                                                                            \
     static bool cfg = false;                                                                                      \
@@ -741,17 +784,56 @@ extern "C" int qw_attn_prefill(const void* qkv, int64_t ldq, int64_t nq, int64_t
                            AttnTc<DD>::SMEM);                                                                     \
       cfg = true;                                                                                                 \
     }                                                                                                             \
-    attn_prefill_kernel<DD><<<grid, AttnTc<DD>::THREADS, AttnTc<DD>::SMEM, s>>>(                                                  \
+    attn_prefill_kernel<DD><<<grid, AttnTc<DD>::THREADS, AttnTc<DD>::SMEM, s>>>(                                  \
         tq, tk, tv, static_cast<const PrefillTile*>(tiles), cu_seqlens, prefix, kv_base,                         \
         static_cast<const __nv_bfloat16*>(qkv), ldq, static_cast<__nv_bfloat16*>(out), ldo, (int)nq, (int)nkv,   \
-        sl2, device_error_ptr());                                                                                 \
+        sl2, part_o, part_ml, device_error_ptr());                                                                \
   } while (0)
   if (d == 256) QW_ATTN_LAUNCH(256);
   else if (d == 128) QW_ATTN_LAUNCH(128);
   else QW_ATTN_LAUNCH(64);
 #undef QW_ATTN_LAUNCH
   QW_LAUNCH_CHECK();
+  if (splits == 1) return QW_OK;
+  const auto* q = static_cast<const __nv_bfloat16*>(qkv);
+  auto* o = static_cast<__nv_bfloat16*>(out);
+  if (d == 256)
+    attn_decode_combine_kernel<256><<<(unsigned)(T * nq), 128, 0, s>>>(part_o, part_ml, (int)splits, q, ldq, (int)nq, o, ldo);
+  else if (d == 128)
+    attn_decode_combine_kernel<128><<<(unsigned)(T * nq), 128, 0, s>>>(part_o, part_ml, (int)splits, q, ldq, (int)nq, o, ldo);
+  else
+    attn_decode_combine_kernel<64><<<(unsigned)(T * nq), 64, 0, s>>>(part_o, part_ml, (int)splits, q, ldq, (int)nq, o, ldo);
+  QW_LAUNCH_CHECK();
   return QW_OK;
+}
+
+extern "C" int qw_attn_prefill(const void* qkv, int64_t ldq, int64_t nq, int64_t nkv, int64_t d, const void* k_cache,
+                               const void* v_cache, const void* tiles, int64_t n_tiles, const int32_t* cu_seqlens,
+                               const int32_t* prefix, const int32_t* kv_base, void* out, int64_t ldo, float scale,
+                               int64_t T, int64_t cache_rows, qw_stream_t stream) {
+  return attn_prefill_launch(qkv, ldq, nq, nkv, d, k_cache, v_cache, tiles, n_tiles, cu_seqlens, prefix, kv_base, out,
+                             ldo, scale, T, cache_rows, 1, nullptr, nullptr, stream);
+}
+
+extern "C" size_t qw_attn_prefill_split_workspace_bytes(int64_t T, int64_t nq, int64_t d, int64_t splits) {
+  return (size_t)(T * nq * splits) * (size_t)(d + 2) * sizeof(float) + 256;
+}
+
+extern "C" int qw_attn_prefill_split(const void* qkv, int64_t ldq, int64_t nq, int64_t nkv, int64_t d,
+                                     const void* k_cache, const void* v_cache, const void* tiles, int64_t n_tiles,
+                                     const int32_t* cu_seqlens, const int32_t* prefix, const int32_t* kv_base,
+                                     void* out, int64_t ldo, float scale, int64_t T, int64_t cache_rows,
+                                     int64_t splits, void* workspace, size_t ws_bytes, qw_stream_t stream) {
+  QW_CHECK_ARG(splits >= 1 && T > 0 && nq > 0, QW_ERR_ARG);
+  if (splits == 1)
+    return attn_prefill_launch(qkv, ldq, nq, nkv, d, k_cache, v_cache, tiles, n_tiles, cu_seqlens, prefix, kv_base,
+                               out, ldo, scale, T, cache_rows, 1, nullptr, nullptr, stream);
+  QW_CHECK_ARG(workspace && ws_bytes >= qw_attn_prefill_split_workspace_bytes(T, nq, d, splits), QW_ERR_WORKSPACE);
+  QW_CHECK_ARG(((uintptr_t)workspace % 16) == 0, QW_ERR_ALIGN);
+  float* part_o = static_cast<float*>(workspace);
+  float* part_ml = part_o + T * nq * splits * d;
+  return attn_prefill_launch(qkv, ldq, nq, nkv, d, k_cache, v_cache, tiles, n_tiles, cu_seqlens, prefix, kv_base, out,
+                             ldo, scale, T, cache_rows, splits, part_o, part_ml, stream);
 }
 
 extern "C" size_t qw_attn_decode_workspace_bytes(int64_t B, int64_t nq, int64_t d, int64_t splits) {
@@ -775,6 +857,7 @@ extern "C" int qw_attn_decode(const void* qkv, int64_t ldq, int64_t B, int64_t n
   static bool configured = false;
   if (!configured) {
     cudaFuncSetAttribute(attn_decode_kernel<256, 6>, cudaFuncAttributeMaxDynamicSharedMemorySize, DecodeSmem<256>::TOTAL);
+    cudaFuncSetAttribute(attn_decode_kernel<256, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize, DecodeSmem<256>::TOTAL);
     cudaFuncSetAttribute(attn_decode_kernel<64, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, DecodeSmem<64>::TOTAL);
     configured = true;
   }
@@ -783,6 +866,9 @@ extern "C" int qw_attn_decode(const void* qkv, int64_t ldq, int64_t B, int64_t n
   const auto* vc = static_cast<const __nv_bfloat16*>(v_cache);
   if (d == 256 && group == 6)
     attn_decode_kernel<256, 6><<<grid, 32 * DecodeSmem<256>::NW, DecodeSmem<256>::TOTAL, s>>>(q, ldq, (int)nq, (int)nkv, kc, vc, seq_len, kv_base, kps, sl2,
+                                                    part_o, part_ml, (int)splits);
+  else if (d == 256 && group == 3)  // 8-way tensor parallel: 3 query heads per replicated KV head
+    attn_decode_kernel<256, 3><<<grid, 32 * DecodeSmem<256>::NW, DecodeSmem<256>::TOTAL, s>>>(q, ldq, (int)nq, (int)nkv, kc, vc, seq_len, kv_base, kps, sl2,
                                                     part_o, part_ml, (int)splits);
   else if (d == 64 && group == 2)
     attn_decode_kernel<64, 2><<<grid, 32 * DecodeSmem<64>::NW, DecodeSmem<64>::TOTAL, s>>>(q, ldq, (int)nq, (int)nkv, kc, vc, seq_len, kv_base, kps, sl2,

@@ -36,7 +36,14 @@ int* device_error_ptr() {
   return ptrs[dev];
 }
 
-enum Epi : int { EPI_BF16 = 0, EPI_F32 = 1, EPI_SWIGLU = 2, EPI_PARTIAL = 3 };
+enum Epi : int { EPI_BF16 = 0, EPI_F32 = 1, EPI_SWIGLU = 2, EPI_PARTIAL = 3, EPI_F32RAW = 4 };
+
+// fp32 outputs: EPI_F32 stores float(bf16(acc)) (F.linear().float()), EPI_F32RAW the accumulator itself
+template <int EPI>
+QW_DEV float f32_out(float acc) {
+  if constexpr (EPI == EPI_F32) return bf16_round(acc);
+  else return acc;
+}
 
 struct GemmParams {
   int a_rows, b_rows, K;
@@ -266,17 +273,17 @@ __global__ void __launch_bounds__(gemm_threads<MT>(), 1)
               } else {
                 for (int j = 0; j < nb; ++j) dst[j] = f2bf(f[j]);
               }
-            } else if constexpr (EPI == EPI_F32) {
+            } else if constexpr (EPI == EPI_F32 || EPI == EPI_F32RAW) {
               float* dst = reinterpret_cast<float*>(p.out) + (int64_t)a_row * p.ldo + b0;
               if (nb == 32 && p.vec_ok) {
 #pragma unroll
                 for (int j = 0; j < 32; j += 4) {
-                  float4 v4 = make_float4(bf16_round(__uint_as_float(r[j])), bf16_round(__uint_as_float(r[j + 1])),
-                                          bf16_round(__uint_as_float(r[j + 2])), bf16_round(__uint_as_float(r[j + 3])));
+                  float4 v4 = make_float4(f32_out<EPI>(__uint_as_float(r[j])), f32_out<EPI>(__uint_as_float(r[j + 1])),
+                                          f32_out<EPI>(__uint_as_float(r[j + 2])), f32_out<EPI>(__uint_as_float(r[j + 3])));
                   *reinterpret_cast<float4*>(dst + j) = v4;
                 }
               } else {
-                for (int j = 0; j < nb; ++j) dst[j] = bf16_round(__uint_as_float(r[j]));
+                for (int j = 0; j < nb; ++j) dst[j] = f32_out<EPI>(__uint_as_float(r[j]));
               }
             }
           } else {
@@ -284,9 +291,9 @@ __global__ void __launch_bounds__(gemm_threads<MT>(), 1)
             if constexpr (EPI == EPI_BF16) {
               __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.out) + a_row;
               for (int j = 0; j < nb; ++j) dst[(int64_t)(b0 + j) * p.ldo] = f2bf(__uint_as_float(r[j]));
-            } else if constexpr (EPI == EPI_F32) {
+            } else if constexpr (EPI == EPI_F32 || EPI == EPI_F32RAW) {
               float* dst = reinterpret_cast<float*>(p.out) + a_row;
-              for (int j = 0; j < nb; ++j) dst[(int64_t)(b0 + j) * p.ldo] = bf16_round(__uint_as_float(r[j]));
+              for (int j = 0; j < nb; ++j) dst[(int64_t)(b0 + j) * p.ldo] = f32_out<EPI>(__uint_as_float(r[j]));
             } else if constexpr (EPI == EPI_PARTIAL) {
               float* dst = reinterpret_cast<float*>(p.out) + (int64_t)split * p.part_stride + a_row;
               for (int j = 0; j < nb; ++j) dst[(int64_t)(b0 + j) * p.ldo] = __uint_as_float(r[j]);
@@ -492,10 +499,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
 #pragma unroll
               for (int j = 0; j < 32; j += 4)
                 *reinterpret_cast<float4*>(dst + j) =
-                    make_float4(bf16_round(__uint_as_float(r[j])), bf16_round(__uint_as_float(r[j + 1])),
-                                bf16_round(__uint_as_float(r[j + 2])), bf16_round(__uint_as_float(r[j + 3])));
+                    make_float4(f32_out<EPI>(__uint_as_float(r[j])), f32_out<EPI>(__uint_as_float(r[j + 1])),
+                                f32_out<EPI>(__uint_as_float(r[j + 2])), f32_out<EPI>(__uint_as_float(r[j + 3])));
             } else {
-              for (int j = 0; j < nb; ++j) dst[j] = bf16_round(__uint_as_float(r[j]));
+              for (int j = 0; j < nb; ++j) dst[j] = f32_out<EPI>(__uint_as_float(r[j]));
             }
           }
         }
@@ -530,8 +537,8 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ ws, void* out, in
     for (int s = 0; s < splits; ++s) up += ws[s * part_stride + (int64_t)m * ldw + up_offset + n];
     const float g = bf16_round(acc), u = bf16_round(up);
     reinterpret_cast<__nv_bfloat16*>(out)[(int64_t)m * ldo + n] = f2bf(g / (1.0f + expf(-g)) * u);
-  } else if constexpr (EPI == EPI_F32) {
-    reinterpret_cast<float*>(out)[(int64_t)m * ldo + n] = bf16_round(acc);
+  } else if constexpr (EPI == EPI_F32 || EPI == EPI_F32RAW) {
+    reinterpret_cast<float*>(out)[(int64_t)m * ldo + n] = f32_out<EPI>(acc);
   } else {
     reinterpret_cast<__nv_bfloat16*>(out)[(int64_t)m * ldo + n] = f2bf(acc);
   }
@@ -727,7 +734,7 @@ using namespace qw;
 extern "C" size_t qw_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K, int out_kind) {
   if (!use_skinny(M)) return 0;
   SkinnyPlan pl = plan_skinny(M, N, K);
-  if (pl.splits == 1 && out_kind != QW_OUT_SWIGLU) return 0;
+  if (pl.splits == 1 && out_kind != QW_OUT_SWIGLU && out_kind != QW_OUT_F32) return 0;
   return (size_t)pl.splits * (size_t)M * (size_t)N * sizeof(float);
 }
 
@@ -736,7 +743,7 @@ extern "C" int qw_gemm_bf16(const void* x, const void* w, void* y, int64_t M, in
                             qw_stream_t stream) {
   QW_CHECK_ARG(x && w && y && M > 0 && N > 0 && K > 0, QW_ERR_ARG);
   QW_CHECK_ARG(ldx >= K && ldw >= K, QW_ERR_ARG);
-  QW_CHECK_ARG(out_kind >= QW_OUT_BF16 && out_kind <= QW_OUT_SWIGLU, QW_ERR_ARG);
+  QW_CHECK_ARG(out_kind >= QW_OUT_BF16 && out_kind <= QW_OUT_F32, QW_ERR_ARG);
   QW_CHECK_ARG(M < (1 << 30) && N < (1 << 30), QW_ERR_ARG);
   QW_CHECK_ARG(((uintptr_t)x % 16) == 0 && ((uintptr_t)w % 16) == 0 && (ldx % 8) == 0 && (ldw % 8) == 0, QW_ERR_ALIGN);
   const int64_t n_out = out_kind == QW_OUT_SWIGLU ? N / 2 : N;
@@ -754,7 +761,7 @@ extern "C" int qw_gemm_bf16(const void* x, const void* w, void* y, int64_t M, in
   if (!use_skinny(M)) {
     // A = activations [M, K], B = weights [N, K]; out[m][n]
     const bool swiglu = out_kind == QW_OUT_SWIGLU;
-    const int per16 = out_kind == QW_OUT_F32_OF_BF16 ? 4 : 8;  // elements per 16 bytes
+    const int per16 = (out_kind == QW_OUT_F32_OF_BF16 || out_kind == QW_OUT_F32) ? 4 : 8;  // elements per 16 B
     p.vec_ok = ((uintptr_t)y % 16) == 0 && (ldy % per16) == 0;
     constexpr int BN = 256;
     // Kernel choice per shape, from sustained (power-capped) runs of a whole prefill's
@@ -777,6 +784,7 @@ extern "C" int qw_gemm_bf16(const void* x, const void* w, void* y, int64_t M, in
       p.ldo = ldy;
       if (swiglu) return launch_pair<EPI_SWIGLU>(ta, tb, p, s);
       if (out_kind == QW_OUT_F32_OF_BF16) return launch_pair<EPI_F32>(ta, tb, p, s);
+      if (out_kind == QW_OUT_F32) return launch_pair<EPI_F32RAW>(ta, tb, p, s);
       return launch_pair<EPI_BF16>(ta, tb, p, s);
     }
     // 256-row tiles win when the main loop is long enough to hide their single-buffered
@@ -800,10 +808,12 @@ extern "C" int qw_gemm_bf16(const void* x, const void* w, void* y, int64_t M, in
       p.group = 8;
       if (swiglu) return launch_gemm<BN, 3, EPI_SWIGLU, 2>(ta, tb, p, s);
       if (out_kind == QW_OUT_F32_OF_BF16) return launch_gemm<BN, 3, EPI_F32, 2>(ta, tb, p, s);
+      if (out_kind == QW_OUT_F32) return launch_gemm<BN, 3, EPI_F32RAW, 2>(ta, tb, p, s);
       return launch_gemm<BN, 3, EPI_BF16, 2>(ta, tb, p, s);
     }
     if (swiglu) return launch_gemm<BN, 4, EPI_SWIGLU>(ta, tb, p, s);
     if (out_kind == QW_OUT_F32_OF_BF16) return launch_gemm<BN, 4, EPI_F32>(ta, tb, p, s);
+    if (out_kind == QW_OUT_F32) return launch_gemm<BN, 4, EPI_F32RAW>(ta, tb, p, s);
     return launch_gemm<BN, 4, EPI_BF16>(ta, tb, p, s);
   }
 
@@ -819,7 +829,8 @@ extern "C" int qw_gemm_bf16(const void* x, const void* w, void* y, int64_t M, in
   p.kb_per_split = pl.kb_per_split;
   p.swap = 1;
   p.group = 1;
-  const bool partial = pl.splits > 1 || out_kind == QW_OUT_SWIGLU;
+  // raw fp32 outputs always take the partial + reduce route (one instantiation fewer per tile width)
+  const bool partial = pl.splits > 1 || out_kind == QW_OUT_SWIGLU || out_kind == QW_OUT_F32;
   if (!partial) {
     p.out = y;
     p.ldo = ldy;
@@ -850,6 +861,8 @@ extern "C" int qw_gemm_bf16(const void* x, const void* w, void* y, int64_t M, in
     splitk_reduce_kernel<EPI_SWIGLU><<<blocks, threads, 0, s>>>(ws, y, (int)M, (int)n_out, ldy, pl.splits, p.part_stride, N, (int)n_out);
   else if (out_kind == QW_OUT_F32_OF_BF16)
     splitk_reduce_kernel<EPI_F32><<<blocks, threads, 0, s>>>(ws, y, (int)M, (int)n_out, ldy, pl.splits, p.part_stride, N, 0);
+  else if (out_kind == QW_OUT_F32)
+    splitk_reduce_kernel<EPI_F32RAW><<<blocks, threads, 0, s>>>(ws, y, (int)M, (int)n_out, ldy, pl.splits, p.part_stride, N, 0);
   else
     splitk_reduce_kernel<EPI_BF16><<<blocks, threads, 0, s>>>(ws, y, (int)M, (int)n_out, ldy, pl.splits, p.part_stride, N, 0);
   QW_LAUNCH_CHECK();
@@ -904,6 +917,24 @@ extern "C" int qw_gemm_add_rmsnorm(const void* x, const void* w, int64_t M, int6
   splitk_add_rmsnorm_kernel<<<(unsigned)M, threads, 0, s>>>(
       static_cast<const float*>(workspace), pl.splits, p.part_stride, (int)N, static_cast<__nv_bfloat16*>(resid),
       static_cast<const __nv_bfloat16*>(norm_w), static_cast<__nv_bfloat16*>(hidden), eps);
+  QW_LAUNCH_CHECK();
+  return QW_OK;
+}
+
+extern "C" int qw_add_rmsnorm_f32(const float* x, int64_t n_parts, int64_t part_stride, int64_t T, int64_t H,
+                                  void* resid, const void* norm_w, void* hidden, float eps, qw_stream_t stream) {
+  QW_CHECK_ARG(x && resid && norm_w && hidden && T > 0 && n_parts >= 1 && part_stride >= 0, QW_ERR_ARG);
+  QW_CHECK_ARG(n_parts == 1 || part_stride >= T * H, QW_ERR_ARG);
+  QW_CHECK_ARG(H % 8 == 0 && H <= kAddNormMaxThreads * 8 && T <= 0x7fffffff, QW_ERR_UNSUPPORTED);
+  QW_CHECK_ARG(((uintptr_t)x % 16) == 0 && (part_stride % 4) == 0 && ((uintptr_t)resid % 16) == 0 &&
+                   ((uintptr_t)hidden % 16) == 0 && ((uintptr_t)norm_w % 16) == 0,
+               QW_ERR_ALIGN);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const int threads = (int)((H / 8 + 31) / 32 * 32);
+  splitk_add_rmsnorm_kernel<<<(unsigned)T, threads, 0, s>>>(x, (int)n_parts, part_stride, (int)H,
+                                                            static_cast<__nv_bfloat16*>(resid),
+                                                            static_cast<const __nv_bfloat16*>(norm_w),
+                                                            static_cast<__nv_bfloat16*>(hidden), eps);
   QW_LAUNCH_CHECK();
   return QW_OK;
 }

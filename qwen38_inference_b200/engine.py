@@ -53,7 +53,8 @@ class Engine:
         dev = self.staging.upload(arr, self.dev)
         md = self._meta_views(dev[T:], offs)
         md["tokens"] = dev[:T]
-        return self._run(md, T, len(slots), max(lens), cache, is_decode, return_all_logits)
+        max_keys = max(p + n for p, n in zip(prefixes, lens))
+        return self._run(md, T, len(slots), max(lens), cache, is_decode, return_all_logits, max_keys=max_keys)
 
     # ------------------------------------------------------------------ decode graphs
     MAX_GRAPHS = 4  # captured decode graphs kept, least recently used evicted first
@@ -103,8 +104,9 @@ class Engine:
         return out
 
     # ------------------------------------------------------------------ the layer loop
-    def _run(self, md, T, B, max_len, cache, is_decode, return_all_logits, ws=None):
+    def _run(self, md, T, B, max_len, cache, is_decode, return_all_logits, ws=None, max_keys=0):
         m, c, dev = self.m, self.c, self.dev
+        tp = m.tp
         ws = self.ws if ws is None else ws
         H = c.hidden_size
         eps = m.eps
@@ -122,11 +124,19 @@ class Engine:
             kb = torch.empty(T, c.gdn_qk_dim, dtype=BF16, device=dev)
             vb = torch.empty(T, c.gdn_v_dim, dtype=BF16, device=dev)
         splits = self._decode_splits(cache.capacity)
+        n_tiles = 0 if is_decode else md["tiles"].numel() // 2
+        pf_splits = 1 if is_decode else ops.prefill_attn_splits(nq, n_tiles, max_keys)
         fused = is_decode and T <= 64  # weight-streaming projections: split-K sum + add-norm in one kernel
+        # tensor parallel: row-parallel projections produce fp32 partial sums, all-reduced in place
+        part = torch.empty(T, H, dtype=torch.float32, device=dev) if tp is not None else None
 
         def proj_add_norm(x, wt, norm_w):
             """hidden = x . wt^T, then resid += hidden, hidden = norm(resid)."""
-            if fused:
+            if tp is not None:
+                ops.gemm(x, wt, part, out_kind=ops.OUT_F32, ws=ws)
+                tp.all_reduce_(part)
+                ops.add_rmsnorm_f32(part, resid, norm_w, hidden, eps)
+            elif fused:
                 ops.gemm_add_rmsnorm(x, wt, resid, norm_w, hidden, eps, ws)
             else:
                 ops.gemm(x, wt, hidden, ws=ws)
@@ -146,7 +156,7 @@ class Engine:
                                     att, d ** -0.5, ws)
                 else:
                     ops.attn_prefill(qkv, nq, nkv, d, kc, vc, md["tiles"], md["cu"], md["prefix"], md["kv_base"],
-                                     att, d ** -0.5)
+                                     att, d ** -0.5, splits=pf_splits, ws=ws)
                 proj_add_norm(att, w["out"], w["post_norm"])
             else:
                 ops.gemm(hidden, w["qkvzba"], proj[:, :c.qkvz_dim + c.ba_dim], ws=ws)
@@ -165,6 +175,10 @@ class Engine:
             ops.gemm(hidden, w["gate_up"], act, out_kind=ops.OUT_SWIGLU, ws=ws)
             if i + 1 < n_layers:
                 proj_add_norm(act, w["down"], m.layers[i + 1]["input_norm"])  # the next layer's input norm
+            elif tp is not None:
+                ops.gemm(act, w["down"], part, out_kind=ops.OUT_F32, ws=ws)
+                tp.all_reduce_(part)
+                ops.round_f32_bf16(part, hidden)
             else:
                 ops.gemm(act, w["down"], hidden, ws=ws)
         rows = None if return_all_logits else md["last_rows"]
@@ -172,5 +186,14 @@ class Engine:
         fin = torch.empty(R, H, dtype=BF16, device=dev)
         ops.add_rmsnorm_rows(hidden, resid, m.final_norm, fin, eps, rows)
         logits = torch.empty(R, c.vocab_size, dtype=torch.float32, device=dev)
-        ops.gemm(fin, m.lm_head, logits, out_kind=ops.OUT_F32_OF_BF16, ws=ws)
+        if tp is None:
+            ops.gemm(fin, m.lm_head, logits, out_kind=ops.OUT_F32_OF_BF16, ws=ws)
+            return logits
+        # vocab-parallel lm_head: each rank's rows, all-gathered rank-major, then reordered
+        Vs = m.lm_head.shape[0]
+        local = torch.empty(R, Vs, dtype=torch.float32, device=dev)
+        ops.gemm(fin, m.lm_head, local, out_kind=ops.OUT_F32_OF_BF16, ws=ws)
+        gathered = torch.empty(tp.world * R, Vs, dtype=torch.float32, device=dev)
+        tp.all_gather_rows(local, gathered)
+        ops.gather_vocab_shards(gathered.view(tp.world, R, Vs), logits)
         return logits

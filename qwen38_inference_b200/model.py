@@ -224,7 +224,7 @@ class Qwen38:
 
     @torch.inference_mode()
     def __init__(self, model_path=None, device="cuda:0", max_context=None, *, config: HybridConfig | None = None,
-                 seed: int = 0, weights: dict | None = None, norm_mode: str = "random"):
+                 seed: int = 0, weights: dict | None = None, norm_mode: str = "random", tensor_parallel=None):
         self.device = _check_device(device)
         torch.cuda.set_device(self.device)
         _lib.load()  # fail loudly if the native library is missing
@@ -233,8 +233,17 @@ class Qwen38:
             cfg = load_checkpoint_config(self.path)
         else:
             cfg = config or qwen38_27b()
-        self.cfg = cfg
-        self._validate_geometry(cfg)
+        # head-wise tensor parallelism (a torch.distributed process group, or True for the
+        # default group): this process holds one rank's heads; see tensor_parallel.py
+        self.tp = None
+        shard = None
+        if tensor_parallel is not None and tensor_parallel is not False:
+            from .tensor_parallel import TensorParallel
+            self.tp = TensorParallel(None if tensor_parallel is True else tensor_parallel, cfg)
+            shard = self.tp.shard
+        self.full_cfg = cfg
+        self.cfg = self.tp.local_cfg if self.tp is not None else cfg
+        self._validate_geometry(self.cfg)
         self.config = cfg.text_config()
         self.dtype = torch.bfloat16
         self.eps = cfg.rms_norm_eps
@@ -246,11 +255,11 @@ class Qwen38:
         self.page_size = PAGE
         if self.path is not None:
             from .checkpoint import load_weights
-            flat = load_weights(self.path, cfg, self.device)
+            flat = load_weights(self.path, cfg, self.device, shard=shard)
         elif weights is not None:
-            flat = {k: v.to(self.device) for k, v in weights.items()}
+            flat = {k: (shard(k, v.to(self.device)) if shard else v.to(self.device)) for k, v in weights.items()}
         else:
-            flat = random_weights(cfg, seed, device=self.device, norm_mode=norm_mode)
+            flat = random_weights(cfg, seed, device=self.device, norm_mode=norm_mode, shard=shard)
         for k, v in flat.items():
             want = torch.float32 if k.endswith("A_log") else torch.bfloat16
             flat[k] = v.to(device=self.device, dtype=want).contiguous()
@@ -261,7 +270,7 @@ class Qwen38:
                 # big GEMM instead of a launch of their own; qkvz and ba stay as row views
                 fused = torch.cat([w["qkvz"], w["ba"]], 0)
                 w["qkvzba"] = fused
-                w["qkvz"], w["ba"] = fused[:cfg.qkvz_dim], fused[cfg.qkvz_dim:]
+                w["qkvz"], w["ba"] = fused[:self.cfg.qkvz_dim], fused[self.cfg.qkvz_dim:]
         self.embedding, self.final_norm, self.lm_head = g["embedding"], g["final_norm"], g["lm_head"]
         self.rotary_dim = cfg.rotary_dim
         self.rope = rope_table(cfg, self.max_context, self.device)

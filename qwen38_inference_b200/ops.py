@@ -11,7 +11,7 @@ import torch
 from . import _lib
 
 BF16 = torch.bfloat16
-OUT_BF16, OUT_F32_OF_BF16, OUT_SWIGLU = 0, 1, 2
+OUT_BF16, OUT_F32_OF_BF16, OUT_SWIGLU, OUT_F32 = 0, 1, 2, 3
 
 # Kernels launched through this module (a benchmark's claim of native launches), and an
 # optional list that, when set, receives (flops, start_event, end_event, (M, N, K, out_kind))
@@ -62,7 +62,7 @@ def gemm(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None, *, o
     M, K = x.shape
     N = w.shape[0]
     n_out = N // 2 if out_kind == OUT_SWIGLU else N
-    odt = torch.float32 if out_kind == OUT_F32_OF_BF16 else BF16
+    odt = torch.float32 if out_kind in (OUT_F32_OF_BF16, OUT_F32) else BF16
     if out is None:
         out = torch.empty(M, n_out, dtype=odt, device=x.device)
     if out.dtype != odt or out.shape != (M, n_out) or out.stride(1) != 1:
@@ -103,6 +103,37 @@ def gemm_add_rmsnorm(x, w, resid, norm_w, hidden, eps, ws: Workspace):
               norm_w.data_ptr(), hidden.data_ptr(), eps, buf.data_ptr(), need, _stream())
 
 
+def add_rmsnorm_f32(x, resid, norm_w, hidden, eps):
+    """resid += bf16(x), hidden = GemmaRMSNorm(resid) with x fp32 [T, H] (an all-reduced
+    row-parallel projection), resid and hidden bf16 [T, H] contiguous."""
+    T, H = resid.shape
+    if not (x.dtype == torch.float32 and x.is_contiguous() and x.shape == (T, H) and resid.is_contiguous()
+            and hidden.is_contiguous() and hidden.shape == (T, H)):
+        raise ValueError("add_rmsnorm_f32 expects x fp32 [T, H] and contiguous resid/hidden [T, H]")
+    LAUNCHES[0] += 1
+    _lib.call("qw_add_rmsnorm_f32", x.data_ptr(), 1, 0, T, H, resid.data_ptr(), norm_w.data_ptr(), hidden.data_ptr(),
+              eps, _stream())
+
+
+def round_f32_bf16(x, y):
+    """y (bf16) = bf16(x (fp32)), both contiguous with the same number of elements."""
+    if not (x.dtype == torch.float32 and y.dtype == BF16 and x.is_contiguous() and y.is_contiguous()
+            and x.numel() == y.numel()):
+        raise ValueError("round_f32_bf16 expects contiguous fp32 x and bf16 y of one size")
+    LAUNCHES[0] += 1
+    _lib.call("qw_round_f32_bf16", x.data_ptr(), y.data_ptr(), x.numel(), _stream())
+
+
+def gather_vocab_shards(src, dst):
+    """dst [R, G*Vs] = src [G, R, Vs] reordered so that shard g fills columns g*Vs.."""
+    G, R, Vs = src.shape
+    if not (src.is_contiguous() and dst.is_contiguous() and dst.shape == (R, G * Vs)
+            and src.dtype == torch.float32 and dst.dtype == torch.float32):
+        raise ValueError("gather_vocab_shards expects fp32 src [G, R, Vs] and dst [R, G*Vs]")
+    LAUNCHES[0] += 1
+    _lib.call("qw_gather_vocab_shards", src.data_ptr(), G, R, Vs, dst.data_ptr(), _stream())
+
+
 def embed_rmsnorm(tokens, table, w, resid_out, hidden_out, eps):
     T = tokens.numel()
     LAUNCHES[0] += 1
@@ -140,14 +171,42 @@ def qk_norm_rope_store(qkv, nq, nkv, d, q_w, k_w, rope, positions, locations, kc
               kc.data_ptr(), vc.data_ptr(), kc.shape[0], eps, _stream())
 
 
-def attn_prefill(qkv, nq, nkv, d, kc, vc, tiles, cu, prefix, kv_base, out, scale):
-    """Causal varlen attention over the cache; qkv [T, ldq] rows, kc/vc [cache_rows, nkv, d]."""
+def attn_prefill(qkv, nq, nkv, d, kc, vc, tiles, cu, prefix, kv_base, out, scale, splits=1, ws=None):
+    """Causal varlen attention over the cache; qkv [T, ldq] rows, kc/vc [cache_rows, nkv, d].
+    ``splits > 1`` divides every tile's keys over that many CTAs (long prefixes) and merges
+    the partials, which needs a workspace."""
     if not (kc.is_contiguous() and vc.is_contiguous() and kc.shape == vc.shape and qkv.stride(1) == 1):
         raise ValueError("attn_prefill expects contiguous K/V caches of one shape and unit-stride qkv rows")
-    LAUNCHES[0] += 1
-    _lib.call("qw_attn_prefill", qkv.data_ptr(), qkv.stride(0), nq, nkv, d, kc.data_ptr(), vc.data_ptr(),
+    T = qkv.shape[0]
+    if splits == 1:
+        LAUNCHES[0] += 1
+        _lib.call("qw_attn_prefill", qkv.data_ptr(), qkv.stride(0), nq, nkv, d, kc.data_ptr(), vc.data_ptr(),
+                  tiles.data_ptr(), tiles.numel() // 2, cu.data_ptr(), prefix.data_ptr(), kv_base.data_ptr(),
+                  out.data_ptr(), out.stride(0), scale, T, kc.shape[0], _stream())
+        return
+    need = int(_lib.load().qw_attn_prefill_split_workspace_bytes(T, nq, d, splits))
+    buf = ws.get(need)
+    LAUNCHES[0] += 2
+    _lib.call("qw_attn_prefill_split", qkv.data_ptr(), qkv.stride(0), nq, nkv, d, kc.data_ptr(), vc.data_ptr(),
               tiles.data_ptr(), tiles.numel() // 2, cu.data_ptr(), prefix.data_ptr(), kv_base.data_ptr(),
-              out.data_ptr(), out.stride(0), scale, qkv.shape[0], kc.shape[0], _stream())
+              out.data_ptr(), out.stride(0), scale, T, kc.shape[0], splits, buf.data_ptr(), need, _stream())
+
+
+def prefill_attn_splits(nq, n_tiles, max_keys, sms=148):
+    """Key splits for prefill attention: 1 unless heads x tiles leave SMs idle on a long key
+    range. Cost model (one 230 KB CTA per SM): waves x (key blocks per split + 4 blocks of
+    prologue/merge), minimized over splits with at least 8 key blocks each."""
+    units = nq * n_tiles
+    blocks = (max_keys + 63) // 64
+    if units >= sms or blocks < 32:
+        return 1
+    best, best_cost = 1, None
+    for s in range(1, max(1, blocks // 8) + 1):
+        per = -(-blocks // s)
+        cost = -(-units * s // sms) * (per + 4)
+        if best_cost is None or cost < best_cost:
+            best, best_cost = s, cost
+    return best
 
 
 def attn_decode_workspace_bytes(B, nq, d, splits):

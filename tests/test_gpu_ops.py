@@ -155,6 +155,38 @@ def test_attn_prefill(K, nq, nkv, d, case):
     close(out, exp, n_ulp=4, atol=2e-3 if case == "mixed" else 1.6e-2, max_frac=0.5)
 
 
+@pytest.mark.parametrize("nq,nkv,d", [(24, 4, 256), (3, 1, 256), (4, 2, 64)])
+@pytest.mark.parametrize("splits", [4, 0])
+def test_attn_prefill_split_kv(K, nq, nkv, d, splits):
+    """Prefill attention with every tile's keys split over CTAs (long cached prefixes, as in
+    chunked prefill of one long request; nq = 3, nkv = 1 is an 8-way tensor-parallel rank),
+    against the oracle and against the unsplit kernel. splits = 0 takes the engine's choice.
+    A split whose key range lies beyond a row's causal limit contributes nothing to it."""
+    from qwen38_inference_b200.model import build_metadata
+    g = gen(6)
+    prefixes, lens = [3000, 0, 5000], [512, 130, 64]
+    cap = 8192
+    kc, vc, qkv, starts = _attn_case(g, nq, nkv, d, prefixes, lens, cap=cap)
+    packed, offs, T = build_metadata(list(range(len(lens))), prefixes, lens, cap)
+    md = {k: torch.from_numpy(packed[o:o + n]).to(DEV) for k, (o, n) in offs.items()}
+    n_tiles = md["tiles"].numel() // 2
+    if splits == 0:
+        splits = K.prefill_attn_splits(nq, n_tiles, max(p + n for p, n in zip(prefixes, lens)))
+        assert (splits > 1) == (nq * n_tiles < 148)  # 24 heads x 7 tiles already fill the SMs
+    args = (qkv.to(DEV), nq, nkv, d, kc.to(DEV), vc.to(DEV), md["tiles"], md["cu"], md["prefix"], md["kv_base"])
+    whole = torch.empty(T, nq * d, dtype=torch.bfloat16, device=DEV)
+    K.attn_prefill(*args, whole, d ** -0.5)
+    out = torch.full((T, nq * d), float("nan"), dtype=torch.bfloat16, device=DEV)
+    K.attn_prefill(*args, out, d ** -0.5, splits=splits, ws=K.Workspace(DEV))
+    q = qkv.float()[:, :2 * nq * d].view(T, nq, 2 * d)
+    att = O.paged_attention(q[..., :d], kc, vc, starts, prefixes, lens, d ** -0.5, O.bf16)
+    exp = O.sigmoid_mul(att.reshape(T, -1), q[..., d:].reshape(T, -1), O.bf16)
+    close(out, exp, n_ulp=4, atol=2e-3, max_frac=0.5)
+    # each split keeps its own lazily raised running max, so P is rounded to bf16 at other
+    # scales than in the unsplit kernel: many outputs move by an ulp, none by more than two
+    close(out, whole, n_ulp=2, atol=1e-3, max_frac=0.6)
+
+
 @pytest.mark.parametrize("nq,nkv,d", [(24, 4, 256), (4, 2, 64)])
 @pytest.mark.parametrize("splits", [1, 3])
 def test_attn_decode(K, nq, nkv, d, splits):

@@ -1,0 +1,107 @@
+"""Head-wise tensor parallelism on two GPUs against the one-GPU model on the same seeded
+weights (``mini`` geometry: 2 ranks hold 3 query heads each around one replicated KV head,
+1 QK head and 3 value heads of every GDN layer, half the MLP and half the vocabulary).
+
+Call pattern: a ragged two-request prefill, three decode steps (eager, eager + capture, graph
+replay: the NCCL collectives run inside the captured graph), then one request prefilled in
+512-token chunks up to 2600 tokens (long enough that prefill attention splits the keys).
+
+The row-parallel projections sum fp32 partials across ranks and round once, so the logits
+differ from the one-GPU run only through fp32 summation order; bf16 rounding flips spread
+through the layers, hence the same tolerance as the oracle comparison (0.03 + 0.03 |x|).
+Needs two GPUs; skipped otherwise.
+"""
+import os
+import socket
+import sys
+from datetime import timedelta
+from pathlib import Path
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+ROOT = Path(__file__).resolve().parents[1]
+ATOL = RTOL = 0.03
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _calls(vocab):
+    g = torch.Generator().manual_seed(5)
+    ids = lambda n: torch.randint(vocab, (n,), generator=g).tolist()  # noqa: E731
+    calls = [("new", 2), ("step", [ids(300), ids(77)])]
+    calls += [("step", [ids(1), ids(1)]) for _ in range(3)]
+    calls += [("new", 1)] + [("step", [ids(512)]) for _ in range(5)] + [("step", [ids(40)]), ("step", [ids(1)])]
+    return calls
+
+
+def _run(model, calls):
+    out, cache = [], None
+    for kind, arg in calls:
+        if kind == "new":
+            cache = model.new_cache(arg, initial_capacity=64)
+        else:
+            out.append(model.forward_step(arg, cache).cpu())
+    return out
+
+
+def _rank_main(rank, world, port, res):
+    sys.path.insert(0, str(ROOT))
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    import torch.distributed as dist
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120),
+                            device_id=torch.device("cuda", rank))
+    model = None
+    try:
+        from qwen38_inference_b200 import Qwen38, _lib, ops
+        from qwen38_inference_b200.config import mini
+        cfg = mini(num_layers=4, vocab=2048)
+        calls = _calls(cfg.vocab_size)
+        ref = None
+        if rank == 0:
+            one = Qwen38(config=cfg, seed=21, device="cuda:0", max_context=8192)
+            ref = _run(one, calls)
+            del one
+        dist.barrier()
+        model = Qwen38(config=cfg, seed=21, device=f"cuda:{rank}", max_context=8192, tensor_parallel=True)
+        n0 = ops.LAUNCHES[0]
+        got = _run(model, calls)
+        launches = ops.LAUNCHES[0] - n0
+        code = _lib.take_device_error()
+        if rank == 0:
+            stats = []
+            for a, b in zip(got, ref):
+                d = (a - b).abs()
+                stats.append((float(d.max()), float((d <= ATOL + RTOL * b.abs()).float().mean()),
+                              float((d <= 1e-3 + 1e-3 * b.abs()).float().mean()), tuple(a.shape), tuple(b.shape)))
+            res["stats"] = stats
+        res[f"err{rank}"] = code
+        res[f"launches{rank}"] = launches
+        res[f"graphs{rank}"] = sum(1 for e in model._engine.graphs.values() if e.get("graph") is not None)
+    finally:
+        if model is not None:
+            model._engine.graphs.clear()  # graphs holding NCCL calls go before the process group
+        torch.cuda.synchronize()
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_two_rank_tensor_parallel_matches_one_gpu():
+    import torch.multiprocessing as mp
+    world = 2
+    with mp.Manager() as mgr:
+        res = mgr.dict()
+        mp.spawn(_rank_main, args=(world, _free_port(), res), nprocs=world, join=True)
+        res = dict(res)
+    assert res["err0"] == 0 and res["err1"] == 0
+    assert res["launches0"] > 0 and res["launches0"] == res["launches1"]
+    assert res["graphs0"] >= 1 and res["graphs1"] >= 1  # decode replayed from a captured graph
+    for i, (mx, frac_tol, frac_strict, sa, sb) in enumerate(res["stats"]):
+        assert sa == sb, i
+        assert frac_tol == 1.0, f"call {i}: max |d| {mx}, {frac_tol} within tolerance"
