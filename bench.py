@@ -415,7 +415,7 @@ def run_long(args):
     cfg = qwen38_27b()
     n_tok, chunk = args.long_tokens, args.chunk
     n_dec = max(3, args.decode_steps)
-    model = Qwen38(config=cfg, seed=0, device=f"cuda:{local}", max_context=n_tok + n_dec + 64,
+    model = Qwen38(config=cfg, seed=0, device=f"cuda:{local}", max_context=n_tok + n_dec + 2 * chunk + 64,
                    tensor_parallel=True if world > 1 else None)
     g = torch.Generator().manual_seed(26)
     prompt = torch.randint(cfg.vocab_size, (n_tok,), generator=g).tolist()  # same tokens on every rank
@@ -472,6 +472,21 @@ def run_long(args):
         torch.cuda.synchronize()
     launches = ops.LAUNCHES[0] // max(1, args.steps)
     step_ms, e2e_ms, mp, md = reduce_step_times(rec, world, "cuda")
+    # per-op device time of one more chunk and one more decode at the full context, eager
+    from qwen38_inference_b200 import _lib
+    op_ms = {}
+    model._engine.use_graphs = False
+    for name, toks in (("chunk", [chunks[0]]), ("decode", [[dec_tokens[0]]])):
+        prof = []
+        _lib.PROFILE = prof
+        model.forward_step(toks, cache)
+        torch.cuda.synchronize()
+        _lib.PROFILE = None
+        agg = {}
+        for n, a, b in prof:
+            agg[n[3:]] = agg.get(n[3:], 0.0) + a.elapsed_time(b)
+        op_ms[name] = {k: round(v, 3) for k, v in sorted(agg.items(), key=lambda kv: -kv[1])}
+    model._engine.use_graphs = True
     # decode roofline (HBM): this rank's weights + its KV heads over the context + its GDN
     # states (read and written), per decode step
     c = model.cfg
@@ -498,7 +513,7 @@ def run_long(args):
            "e2e": {"value": round(n_tok / (statistics.median(rec["p_wall"]) * 1e-3), 1), "unit": UNIT,
                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                    "decode_ms": round(statistics.median(rec["d_wall"]), 3)},
-           "gpu_launches": launches, "clocks": clk.summary(),
+           "gpu_launches": launches, "clocks": clk.summary(), "op_ms_at_full_context": op_ms,
            "roofline": {"bound": "hbm", "kernel": "decode step at the long context (all kernels of one step)",
                         "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s", "frac": round(achieved / hbm, 4),
                         "peak_source": f"{src} hbm_gbs", "bytes_per_rank_step": dec_bytes, "traffic": None}}

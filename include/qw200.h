@@ -54,8 +54,9 @@ int qw_take_device_error(int* code);
  *                                columns = bf16(silu(bf16(g)) * bf16(u)) (REF:5089-5091 + REF:2238-2281)
  *   out_kind QW_OUT_F32:         y f32  [M, ldy] = acc, unrounded: the partial sum of one tensor-
  *                                parallel rank, rounded once after the all-reduce (qw_add_rmsnorm_f32)
- * Small M (decode) runs weight-streaming split-K tiles and needs a workspace of
- * qw_gemm_workspace_bytes(M, N, K) bytes (0 for large M).
+ * Small M (decode) runs weight-streaming split-K tiles, and a large M whose 128 x 256 tiles
+ * leave SMs idle splits K too (bf16 and fp32 outputs); both need a workspace of
+ * qw_gemm_workspace_bytes(M, N, K, out_kind) bytes (0 when no split is taken).
  */
 #define QW_OUT_BF16 0
 #define QW_OUT_F32_OF_BF16 1
@@ -65,11 +66,14 @@ size_t qw_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K, int out_kind);
 int qw_gemm_bf16(const void* x, const void* w, void* y, int64_t M, int64_t N, int64_t K, int64_t ldx,
                  int64_t ldw, int64_t ldy, int out_kind, void* workspace, size_t ws_bytes, qw_stream_t stream);
 
-/* Decode (M <= 64) projection fused with the residual add-norm that follows it:
+/* Projection fused with the residual add-norm that follows it:
  * x = bf16(x_in . w^T) [M, N]; v = x + resid (fp32); resid = bf16(v);
  * hidden = bf16(v * rsqrt(mean v^2 + eps) * (1 + norm_w)); resid and hidden are [M, N]
- * contiguous. The split-K partials ([splits, M, N] fp32) live in the workspace
- * (REF:5087-5088 / 5092 + 5052: F.linear then gemma_fused_add_rmsnorm)                      */
+ * contiguous. Decode (M <= 64) streams the weights split over K; a large M whose tiles
+ * leave SMs idle (a 512-token chunk) splits K as well. The split-K partials ([splits, M, N]
+ * fp32, workspace of qw_gemm_add_rmsnorm_workspace_bytes) are summed in k order by the
+ * norm kernel. When that size is 0 for a large M, the call is a bf16 GEMM into hidden and
+ * then qw_add_rmsnorm (REF:5087-5088 / 5092 + 5052: F.linear then gemma_fused_add_rmsnorm) */
 size_t qw_gemm_add_rmsnorm_workspace_bytes(int64_t M, int64_t N, int64_t K);
 int qw_gemm_add_rmsnorm(const void* x, const void* w, int64_t M, int64_t N, int64_t K, int64_t ldx, int64_t ldw,
                         void* resid, const void* norm_w, void* hidden, float eps, void* workspace, size_t ws_bytes,

@@ -273,8 +273,10 @@ __global__ void __launch_bounds__(gemm_threads<MT>(), 1)
               } else {
                 for (int j = 0; j < nb; ++j) dst[j] = f2bf(f[j]);
               }
-            } else if constexpr (EPI == EPI_F32 || EPI == EPI_F32RAW) {
-              float* dst = reinterpret_cast<float*>(p.out) + (int64_t)a_row * p.ldo + b0;
+            } else if constexpr (EPI == EPI_F32 || EPI == EPI_F32RAW || EPI == EPI_PARTIAL) {
+              // EPI_PARTIAL: this split's fp32 slice of a split-K product, [M, ldo] per split
+              float* dst = reinterpret_cast<float*>(p.out) + (EPI == EPI_PARTIAL ? (int64_t)split * p.part_stride : 0) +
+                           (int64_t)a_row * p.ldo + b0;
               if (nb == 32 && p.vec_ok) {
 #pragma unroll
                 for (int j = 0; j < 32; j += 4) {
@@ -716,6 +718,60 @@ static SkinnyPlan plan_skinny(int64_t M, int64_t N, int64_t K) {
 
 static bool use_skinny(int64_t M) { return M <= 64; }
 
+// Split-K for large-M products whose 128 x 256 tiles leave SMs idle (e.g. a 512-token chunk
+// times the 5120-wide down or output projection: 80 tiles for 148 SMs). Cost in k-block
+// times of the busiest SM, as plan_skinny: ceil(units / SMs) * (k-blocks per split + 2), plus
+// the fp32 partials written and read back (one k-block time moves ~3 MB from HBM over all
+// SMs). Returns 1 (no split) when the tiles fill the SMs twice over.
+static int plan_wide_splits(int64_t M, int64_t N, int64_t K) {
+  const int64_t tiles = ((M + BM - 1) / BM) * ((N + 255) / 256);
+  const int64_t sms = num_sms();
+  if (tiles >= 2 * sms) return 1;
+  const int kb = (int)((K + BK - 1) / BK);
+  const int max_splits = kb / 8 > 0 ? kb / 8 : 1;
+  const int64_t kblock_bytes = 3 << 20;
+  int64_t best_cost = -1;
+  int best = 1;
+  for (int s = 1; s <= max_splits && s <= 16; ++s) {
+    const int kbps = (kb + s - 1) / s;
+    const int64_t splits = (kb + kbps - 1) / kbps;
+    int64_t cost = ((tiles * splits + sms - 1) / sms) * (kbps + 2);
+    if (splits > 1) cost += (splits * M * N * 8 + kblock_bytes - 1) / kblock_bytes;
+    if (best_cost < 0 || cost < best_cost) {
+      best_cost = cost;
+      best = (int)splits;
+    }
+  }
+  return best;
+}
+
+// The split-K partial GEMM of a large-M product: x [M, K] . w [N, K]^T as `splits` fp32
+// slices [M, N] in ws (ldo N, slice stride M * N). 128 x 256 tiles, one CTA each.
+static int launch_wide_partials(const void* x, const void* w, int64_t M, int64_t N, int64_t K, int64_t ldx,
+                                int64_t ldw, int splits, void* ws, cudaStream_t s) {
+  CUtensorMap ta, tb;
+  int rc;
+  if ((rc = make_tmap(&ta, x, M, K, ldx, BM)) != QW_OK) return rc;
+  if ((rc = make_tmap(&tb, w, N, K, ldw, 256)) != QW_OK) return rc;
+  GemmParams p{};
+  p.err = device_error_ptr();
+  p.K = (int)K;
+  p.kb_total = (int)((K + BK - 1) / BK);
+  p.a_rows = (int)M;
+  p.b_rows = (int)N;
+  p.a_tiles = (int)((M + BM - 1) / BM);
+  p.b_tiles = (int)((N + 255) / 256);
+  p.kb_per_split = (p.kb_total + splits - 1) / splits;
+  p.k_splits = (p.kb_total + p.kb_per_split - 1) / p.kb_per_split;
+  p.swap = 0;
+  p.group = 16;
+  p.out = ws;
+  p.ldo = N;
+  p.part_stride = M * N;
+  p.vec_ok = ((uintptr_t)ws % 16) == 0 && (N % 4) == 0;
+  return launch_gemm<256, 4, EPI_PARTIAL>(ta, tb, p, s);
+}
+
 // Rows of A per CTA for large-M GEMMs: 256 (two accumulators share each B tile) unless the
 // environment variable QW_GEMM_TILE_ROWS=128 selects the double-buffered 128-row tile.
 static int gemm_tile_rows() {
@@ -732,7 +788,11 @@ static int gemm_tile_rows() {
 using namespace qw;
 
 extern "C" size_t qw_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K, int out_kind) {
-  if (!use_skinny(M)) return 0;
+  if (!use_skinny(M)) {
+    if (out_kind != QW_OUT_BF16 && out_kind != QW_OUT_F32) return 0;
+    const int s = plan_wide_splits(M, N, K);
+    return s > 1 ? (size_t)s * (size_t)M * (size_t)N * sizeof(float) : 0;
+  }
   SkinnyPlan pl = plan_skinny(M, N, K);
   if (pl.splits == 1 && out_kind != QW_OUT_SWIGLU && out_kind != QW_OUT_F32) return 0;
   return (size_t)pl.splits * (size_t)M * (size_t)N * sizeof(float);
@@ -758,6 +818,26 @@ extern "C" int qw_gemm_bf16(const void* x, const void* w, void* y, int64_t M, in
   p.kb_total = (int)((K + BK - 1) / BK);
   p.group = 16;
 
+  if (!use_skinny(M) && (out_kind == QW_OUT_BF16 || out_kind == QW_OUT_F32)) {
+    const int splits = plan_wide_splits(M, N, K);
+    if (splits > 1) {
+      // too few tiles for the SMs: split-K partials, then their sum in k order
+      const size_t need = (size_t)splits * (size_t)M * (size_t)N * sizeof(float);
+      QW_CHECK_ARG(workspace != nullptr && ws_bytes >= need, QW_ERR_WORKSPACE);
+      QW_CHECK_ARG(((uintptr_t)workspace % 16) == 0, QW_ERR_ALIGN);
+      if ((rc = launch_wide_partials(x, w, M, N, K, ldx, ldw, splits, workspace, s)) != QW_OK) return rc;
+      const int64_t total = M * N;
+      const int threads = 256;
+      const int blocks = (int)((total + threads - 1) / threads);
+      const float* wsp = reinterpret_cast<const float*>(workspace);
+      if (out_kind == QW_OUT_F32)
+        splitk_reduce_kernel<EPI_F32RAW><<<blocks, threads, 0, s>>>(wsp, y, (int)M, (int)N, ldy, splits, M * N, N, 0);
+      else
+        splitk_reduce_kernel<EPI_BF16><<<blocks, threads, 0, s>>>(wsp, y, (int)M, (int)N, ldy, splits, M * N, N, 0);
+      QW_LAUNCH_CHECK();
+      return QW_OK;
+    }
+  }
   if (!use_skinny(M)) {
     // A = activations [M, K], B = weights [N, K]; out[m][n]
     const bool swiglu = out_kind == QW_OUT_SWIGLU;
@@ -869,8 +949,14 @@ extern "C" int qw_gemm_bf16(const void* x, const void* w, void* y, int64_t M, in
   return QW_OK;
 }
 
+extern "C" int qw_add_rmsnorm(void* x, void* resid, const void* w, int64_t T, int64_t H, float eps,
+                              qw_stream_t stream);  // norm.cu
+
 extern "C" size_t qw_gemm_add_rmsnorm_workspace_bytes(int64_t M, int64_t N, int64_t K) {
-  if (!use_skinny(M)) return 0;
+  if (!use_skinny(M)) {
+    const int s = plan_wide_splits(M, N, K);
+    return s > 1 ? (size_t)s * (size_t)M * (size_t)N * sizeof(float) : 0;
+  }
   const SkinnyPlan pl = plan_skinny(M, N, K);
   return (size_t)pl.splits * (size_t)M * (size_t)N * sizeof(float);
 }
@@ -879,17 +965,36 @@ extern "C" int qw_gemm_add_rmsnorm(const void* x, const void* w, int64_t M, int6
                                    int64_t ldw, void* resid, const void* norm_w, void* hidden, float eps,
                                    void* workspace, size_t ws_bytes, qw_stream_t stream) {
   QW_CHECK_ARG(x && w && resid && norm_w && hidden && M > 0 && N > 0 && K > 0 && ldx >= K && ldw >= K, QW_ERR_ARG);
-  QW_CHECK_ARG(use_skinny(M) && N % 8 == 0 && N <= kAddNormMaxThreads * 8, QW_ERR_UNSUPPORTED);
+  QW_CHECK_ARG(N % 8 == 0 && N <= kAddNormMaxThreads * 8 && M <= 0x7fffffff, QW_ERR_UNSUPPORTED);
   QW_CHECK_ARG(((uintptr_t)x % 16) == 0 && ((uintptr_t)w % 16) == 0 && (ldx % 8) == 0 && (ldw % 8) == 0 &&
                    ((uintptr_t)resid % 16) == 0 && ((uintptr_t)hidden % 16) == 0 && ((uintptr_t)norm_w % 16) == 0,
                QW_ERR_ALIGN);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  int rc;
+  if (!use_skinny(M)) {
+    const int splits = plan_wide_splits(M, N, K);
+    if (splits == 1) {
+      // enough tiles: bf16 product into hidden, then the in-place add-norm
+      if ((rc = qw_gemm_bf16(x, w, hidden, M, N, K, ldx, ldw, N, QW_OUT_BF16, nullptr, 0, stream)) != QW_OK)
+        return rc;
+      return qw_add_rmsnorm(hidden, resid, norm_w, M, N, eps, stream);
+    }
+    const size_t need = (size_t)splits * (size_t)M * (size_t)N * sizeof(float);
+    QW_CHECK_ARG(workspace != nullptr && ws_bytes >= need, QW_ERR_WORKSPACE);
+    QW_CHECK_ARG(((uintptr_t)workspace % 16) == 0, QW_ERR_ALIGN);
+    if ((rc = launch_wide_partials(x, w, M, N, K, ldx, ldw, splits, workspace, s)) != QW_OK) return rc;
+    const int threads = (int)((N / 8 + 31) / 32 * 32);
+    splitk_add_rmsnorm_kernel<<<(unsigned)M, threads, 0, s>>>(
+        static_cast<const float*>(workspace), splits, M * N, (int)N, static_cast<__nv_bfloat16*>(resid),
+        static_cast<const __nv_bfloat16*>(norm_w), static_cast<__nv_bfloat16*>(hidden), eps);
+    QW_LAUNCH_CHECK();
+    return QW_OK;
+  }
   const SkinnyPlan pl = plan_skinny(M, N, K);
   const size_t need = (size_t)pl.splits * (size_t)M * (size_t)N * sizeof(float);
   QW_CHECK_ARG(workspace != nullptr && ws_bytes >= need, QW_ERR_WORKSPACE);
   QW_CHECK_ARG(((uintptr_t)workspace % 16) == 0, QW_ERR_ALIGN);
-  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   CUtensorMap ta, tb;
-  int rc;
   if ((rc = make_tmap(&ta, w, N, K, ldw, BM)) != QW_OK) return rc;
   if ((rc = make_tmap(&tb, x, M, K, ldx, pl.bn)) != QW_OK) return rc;
   GemmParams p{};

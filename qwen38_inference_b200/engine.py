@@ -6,8 +6,9 @@ Prefill (any call that is not pure decode, REF:5027) runs per layer:
            fused, state in place), gated RMSNorm, out GEMM]
   -> add-norm -> gate_up GEMM with fused SwiGLU -> down GEMM
 then the final add-norm on the selected rows and the lm_head GEMM writing fp32 logits.
-Decode replaces the GDN middle by one fused kernel and attention by split-KV decode, and
-is replayed from a CUDA graph per (batch, cache buffer addresses) once captured.
+Decode replaces the GDN middle by one fused kernel and attention by split-KV decode. Decode
+calls and prefill calls of up to 2048 tokens are replayed from a CUDA graph per (launch
+shape, cache buffer addresses) once captured.
 
 All per-call indices travel in one int32 upload (``build_metadata``).
 """
@@ -33,6 +34,7 @@ class Engine:
         self.staging = _Staging()
         self.graphs = collections.OrderedDict()
         self.use_graphs = True
+        self.replays = 0  # calls served by a captured graph
 
     # ------------------------------------------------------------------ helpers
     def _decode_splits(self, capacity):
@@ -48,44 +50,57 @@ class Engine:
         tokens = np.asarray(flat, dtype=np.int32)
         arr = np.concatenate([tokens, packed])
         self.last_h2d_bytes = int(arr.nbytes)
-        if is_decode and not return_all_logits and self.use_graphs:
-            return self._decode_graph(arr, offs, T, slots, cache)
+        B = len(slots)
+        c = self.c
+        pf_splits = 1
+        if not is_decode:
+            max_keys = max(p + n for p, n in zip(prefixes, lens))
+            pf_splits = ops.prefill_attn_splits(c.num_attention_heads, offs["tiles"][1] // 2, max_keys)
+        if self.use_graphs and not return_all_logits and (is_decode or T <= self.GRAPH_MAX_PREFILL_T):
+            shape = ("decode", B, T) if is_decode else ("prefill", B, T, tuple(lens), pf_splits)
+            return self._graph_call(shape, arr, offs, T, B, max(lens), cache, is_decode, pf_splits)
         dev = self.staging.upload(arr, self.dev)
         md = self._meta_views(dev[T:], offs)
         md["tokens"] = dev[:T]
-        max_keys = max(p + n for p, n in zip(prefixes, lens))
-        return self._run(md, T, len(slots), max(lens), cache, is_decode, return_all_logits, max_keys=max_keys)
+        return self._run(md, T, B, max(lens), cache, is_decode, return_all_logits, pf_splits=pf_splits)
 
-    # ------------------------------------------------------------------ decode graphs
-    MAX_GRAPHS = 4  # captured decode graphs kept, least recently used evicted first
+    # ------------------------------------------------------------------ CUDA graphs
+    MAX_GRAPHS = 4  # captured graphs kept, least recently used evicted first
+    # prefill calls up to this many tokens also run from graphs: their launch sequence costs
+    # more host time than the GPU spends (chunked prefill of one long request, 512 tokens a call)
+    GRAPH_MAX_PREFILL_T = 2048
 
-    def _decode_graph(self, arr, offs, T, slots, cache):
-        """Decode through a CUDA graph keyed by the batch shape and the addresses of every
-        cache buffer. A graph bakes in its pointers, so any cache whose buffers sit at exactly
-        those addresses with the same capacity and slot count replays it correctly, including
-        a fresh cache that the allocator placed where a freed one was.
+    def _graph_call(self, shape, arr, offs, T, B, max_len, cache, is_decode, pf_splits):
+        """Run through a CUDA graph keyed by the call's launch shape and the addresses of every
+        cache buffer. A graph bakes in its pointers and grid sizes, so any call with that shape
+        on a cache whose buffers sit at exactly those addresses with the same capacity and slot
+        count replays it correctly (the per-call indices are device data copied in first),
+        including a fresh cache that the allocator placed where a freed one was.
 
-        The first decode of a key runs eagerly. The second runs eagerly too and then captures
+        The first call of a key runs eagerly. The second runs eagerly too and then captures
         the same launch sequence (capture records, it does not execute) with a workspace and
-        an index buffer of its own. Later calls copy the new indices in and replay.
+        an index buffer of its own. Later calls copy the new indices in and replay. Under
+        tensor parallelism every rank executes the collectives of exactly one forward per call
+        whichever of the three paths it takes, so ranks whose keys differ stay in step.
         """
-        B = len(slots)
-        key = (B, T, cache.capacity, len(cache.lengths), tuple(k.data_ptr() for k, _ in cache.kv.values()),
-               tuple(x.data_ptr() for x in cache.recurrent.values()), tuple(x.data_ptr() for x in cache.conv.values()))
+        key = shape + (cache.capacity, len(cache.lengths), tuple(k.data_ptr() for k, _ in cache.kv.values()),
+                       tuple(x.data_ptr() for x in cache.recurrent.values()),
+                       tuple(x.data_ptr() for x in cache.conv.values()))
         ent = self.graphs.get(key)
         if ent is not None and ent["graph"] is not None:
             if ent["offs"] != offs:
-                raise RuntimeError("decode metadata layout changed for a captured shape")
+                raise RuntimeError("metadata layout changed for a captured shape")
             self.graphs.move_to_end(key)
             ent["input"].copy_(torch.from_numpy(arr))
             ent["graph"].replay()
+            self.replays += 1
             ops.LAUNCHES[0] += ent["launches"]
             return ent["out"].clone()
         dev_in = torch.empty(arr.size, dtype=torch.int32, device=self.dev)
         dev_in.copy_(torch.from_numpy(arr), non_blocking=True)
         md = self._meta_views(dev_in[T:], offs)
         md["tokens"] = dev_in[:T]
-        out = self._run(md, T, B, 1, cache, True, False, self.ws)
+        out = self._run(md, T, B, max_len, cache, is_decode, False, self.ws, pf_splits=pf_splits)
         if ent is None:
             self.graphs[key] = {"graph": None}
         else:
@@ -93,7 +108,7 @@ class Engine:
             g = torch.cuda.CUDAGraph()
             n0 = ops.LAUNCHES[0]
             with torch.cuda.graph(g):
-                g_out = self._run(md, T, B, 1, cache, True, False, gws)
+                g_out = self._run(md, T, B, max_len, cache, is_decode, False, gws, pf_splits=pf_splits)
             n_launch = ops.LAUNCHES[0] - n0
             ops.LAUNCHES[0] = n0  # captured launches do not execute
             self.graphs[key] = {"graph": g, "input": dev_in, "out": g_out, "offs": offs, "launches": n_launch,
@@ -104,7 +119,7 @@ class Engine:
         return out
 
     # ------------------------------------------------------------------ the layer loop
-    def _run(self, md, T, B, max_len, cache, is_decode, return_all_logits, ws=None, max_keys=0):
+    def _run(self, md, T, B, max_len, cache, is_decode, return_all_logits, ws=None, pf_splits=1):
         m, c, dev = self.m, self.c, self.dev
         tp = m.tp
         ws = self.ws if ws is None else ws
@@ -124,8 +139,6 @@ class Engine:
             kb = torch.empty(T, c.gdn_qk_dim, dtype=BF16, device=dev)
             vb = torch.empty(T, c.gdn_v_dim, dtype=BF16, device=dev)
         splits = self._decode_splits(cache.capacity)
-        n_tiles = 0 if is_decode else md["tiles"].numel() // 2
-        pf_splits = 1 if is_decode else ops.prefill_attn_splits(nq, n_tiles, max_keys)
         fused = is_decode and T <= 64  # weight-streaming projections: split-K sum + add-norm in one kernel
         # tensor parallel: row-parallel projections produce fp32 partial sums, all-reduced in place
         part = torch.empty(T, H, dtype=torch.float32, device=dev) if tp is not None else None
@@ -136,7 +149,9 @@ class Engine:
                 ops.gemm(x, wt, part, out_kind=ops.OUT_F32, ws=ws)
                 tp.all_reduce_(part)
                 ops.add_rmsnorm_f32(part, resid, norm_w, hidden, eps)
-            elif fused:
+            elif fused or ops.gemm_add_rmsnorm_workspace_bytes(T, wt.shape[0], wt.shape[1]):
+                # weight streaming (decode) or too few tiles (a chunk): split-K partials summed
+                # by the add-norm kernel
                 ops.gemm_add_rmsnorm(x, wt, resid, norm_w, hidden, eps, ws)
             else:
                 ops.gemm(x, wt, hidden, ws=ws)

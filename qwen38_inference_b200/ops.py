@@ -87,9 +87,14 @@ def gemm(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None, *, o
 
 
 # ----------------------------------------------------------------------------- norms
+def gemm_add_rmsnorm_workspace_bytes(M, N, K) -> int:
+    return int(_lib.load().qw_gemm_add_rmsnorm_workspace_bytes(M, N, K))
+
+
 def gemm_add_rmsnorm(x, w, resid, norm_w, hidden, eps, ws: Workspace):
-    """Decode projection (M <= 64) fused with the add-norm after it: resid += bf16(x . w^T),
-    hidden = GemmaRMSNorm(resid) (the split-K partials are summed by the norm kernel)."""
+    """Projection fused with the add-norm after it: resid += bf16(x . w^T), hidden =
+    GemmaRMSNorm(resid) (split-K partials, when the shape takes them, are summed by the
+    norm kernel)."""
     _req(x, BF16, "x")
     _req(w, BF16, "w")
     M, K = x.shape

@@ -183,14 +183,27 @@ class TensorParallel:
     def shard(self, name, t):
         return shard_tensor(name, t, self.spec)
 
+    def _timed(self, name, fn):
+        from . import _lib
+        prof = _lib.PROFILE
+        if prof is None:
+            fn()
+            return
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        fn()
+        e1.record()
+        prof.append((name, e0, e1))
+
     def all_reduce_(self, t: torch.Tensor) -> None:
-        """In-place sum over the ranks (NCCL on the current stream's order)."""
+        """In-place sum over the ranks (NCCL, ordered with the current stream)."""
         if self.world > 1:
-            self.dist.all_reduce(t, group=self.group)
+            self._timed("qw_nccl_all_reduce", lambda: self.dist.all_reduce(t, group=self.group))
 
     def all_gather_rows(self, local: torch.Tensor, out: torch.Tensor) -> None:
         """out [G * R, ...] = the ranks' ``local`` [R, ...] tensors, rank-major."""
         if self.world > 1:
-            self.dist.all_gather_into_tensor(out, local, group=self.group)
+            self._timed("qw_nccl_all_gather",
+                        lambda: self.dist.all_gather_into_tensor(out, local, group=self.group))
         else:
             out.copy_(local)

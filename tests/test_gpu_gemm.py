@@ -50,6 +50,8 @@ SHAPES = [
     (5, 5120, 6144),      # skinny split-K
     (64, 4096, 17408),
     (17, 248, 512),
+    (512, 5120, 17408),   # a 512-token chunk through the down projection: split-K (80 tiles)
+    (300, 5120, 6144),    # ragged M, split-K
 ]
 
 
@@ -103,11 +105,29 @@ def test_gemm_strided_input(ops):
     check_bf16(y, x, w)
 
 
-@pytest.mark.parametrize("M,N,K", [(32, 5120, 6144), (32, 5120, 17408), (5, 1024, 512), (64, 768, 2048)])
+def test_gemm_f32_raw_split(ops):
+    """Unrounded fp32 output (a tensor-parallel rank's partial product), through the wide
+    split-K path and the skinny path, within fp32 summation-order error of float64."""
+    from qwen38_inference_b200 import _lib
+    for M, N, K in ((512, 5120, 8704), (1, 5120, 3072), (2048, 5120, 1536)):
+        g = torch.Generator(device="cuda").manual_seed(M + K)
+        x = torch.randn(M, K, device="cuda", generator=g).to(torch.bfloat16)
+        w = (torch.randn(N, K, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+        y = ops.gemm(x, w, out_kind=ops.OUT_F32, ws=ops.Workspace("cuda"))
+        torch.cuda.synchronize()
+        ref = x.double() @ w.double().t()
+        assert y.dtype == torch.float32
+        assert bool(((y.double() - ref).abs() <= fp32_sum_bound(x, w) + 1e-30).all()), (M, N, K)
+    assert _lib.take_device_error() == 0
+
+
+@pytest.mark.parametrize("M,N,K", [(32, 5120, 6144), (32, 5120, 17408), (5, 1024, 512), (64, 768, 2048),
+                                   (512, 5120, 17408), (512, 5120, 6144), (300, 5120, 3072)])
 def test_gemm_add_rmsnorm_matches_unfused(ops, M, N, K):
-    """The decode projection fused with the add-norm after it matches the projection
-    followed by the add-norm kernel: the residual bit for bit (same split-K order), the
-    normalized output within one bf16 ulp (the sum of squares is reduced in another order)."""
+    """A projection fused with the add-norm after it (decode: weight streaming; a 512-token
+    chunk: split-K over idle SMs) matches the projection followed by the add-norm kernel: the
+    residual bit for bit (the same partials summed in the same order), the normalized output
+    within one bf16 ulp (the sum of squares is reduced in another order)."""
     g = torch.Generator(device="cuda").manual_seed(11)
     x = torch.randn(M, K, device="cuda", generator=g).to(torch.bfloat16)
     w = (torch.randn(N, K, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
