@@ -139,15 +139,6 @@ QW_DEV void mma_bf16_16816(float* d, const uint32_t* a, uint32_t b0, uint32_t b1
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
-QW_DEV void cp_async16(uint32_t dst, const void* src, bool pred) {
-  const int n = pred ? 16 : 0;
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(n) : "memory");
-}
-QW_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-QW_DEV void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
 
 // byte offset of 16-byte chunk `c` of row `r` in a tile whose rows are D bf16 long,
 // with the chunk index XOR-swizzled by (r % 8) so ldmatrix reads are conflict free

@@ -42,6 +42,20 @@ QW_DEV uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);
 }
+// barrier `id` (1..15) among `n` threads (a multiple of 32) of the CTA
+QW_DEV void named_bar_sync(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
+
+// approximate reciprocal (rcp.approx.ftz.f32: relative error below 2^-23; 1/inf = 0)
+QW_DEV float rcp_approx(float x) {
+  float r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+
+// the two bf16 of a packed pair as floats (low half first): exact bit shifts
+QW_DEV float2 bf16x2_to_float2(uint32_t u) {
+  return make_float2(__uint_as_float(u << 16), __uint_as_float(u & 0xffff0000u));
+}
 QW_DEV void unpack_bf16x2(uint32_t u, float& lo, float& hi) {
   __nv_bfloat162 v = *reinterpret_cast<__nv_bfloat162*>(&u);
   lo = __low2float(v);
@@ -121,6 +135,18 @@ QW_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort, int* 
       }
     }
   }
+}
+
+// ------------------------------------------------------------------ cp.async (16-byte, L2 only)
+// pred false copies nothing and zero-fills the 16 destination bytes
+QW_DEV void cp_async16(uint32_t dst, const void* src, bool pred) {
+  const int n = pred ? 16 : 0;
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(n) : "memory");
+}
+QW_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+QW_DEV void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
 // ------------------------------------------------------------------ TMA (no multicast anywhere)

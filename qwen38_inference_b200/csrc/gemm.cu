@@ -36,7 +36,7 @@ int* device_error_ptr() {
   return ptrs[dev];
 }
 
-enum Epi : int { EPI_BF16 = 0, EPI_F32 = 1, EPI_SWIGLU = 2, EPI_PARTIAL = 3, EPI_F32RAW = 4 };
+enum Epi : int { EPI_BF16 = 0, EPI_F32 = 1, EPI_SWIGLU = 2, EPI_PARTIAL = 3, EPI_F32RAW = 4, EPI_SWIGLU_SWAP = 5 };
 
 // fp32 outputs: EPI_F32 stores float(bf16(acc)) (F.linear().float()), EPI_F32RAW the accumulator itself
 template <int EPI>
@@ -74,6 +74,10 @@ struct GemmSmem {
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int BAR_OFFSET = STAGES * STAGE_BYTES;
   static constexpr int TOTAL = BAR_OFFSET + 256 + 1024;  // barriers + alignment slack
+  // EPI_SWIGLU_SWAP: the up half of a tile handed from its TMEM lanes to the gate lanes,
+  // [64 rows][33] fp32 (padded against bank conflicts), after the barriers
+  static constexpr int XCH = BAR_OFFSET + 256;
+  static constexpr int XCH_BYTES = 64 * 33 * 4;
 };
 
 QW_DEV void decode_unit(const GemmParams& p, int unit, int& at, int& bt, int& split) {
@@ -149,7 +153,13 @@ __global__ void __launch_bounds__(gemm_threads<MT>(), 1)
           uint8_t* sa = smem + stage * L::STAGE_BYTES;
           uint8_t* sb = sa + L::A_BYTES;
           mbar_arrive_expect_tx(&full[stage], L::STAGE_BYTES);
-          tma_load_2d(sa, &tmA, &full[stage], kb * BK, at * (BM * MT));
+          if constexpr (EPI == EPI_SWIGLU_SWAP) {
+            // 64 gate rows, then the 64 up rows of the same output columns (64-row boxes)
+            tma_load_2d(sa, &tmA, &full[stage], kb * BK, at * 64);
+            tma_load_2d(sa + 64 * BK * 2, &tmA, &full[stage], kb * BK, p.b_up_offset + at * 64);
+          } else {
+            tma_load_2d(sa, &tmA, &full[stage], kb * BK, at * (BM * MT));
+          }
           if constexpr (EPI == EPI_SWIGLU) {
             tma_load_2d(sb, &tmB, &full[stage], kb * BK, bt * (BN / 2));
             tma_load_2d(sb + (BN / 2) * BK * 2, &tmB, &full[stage], kb * BK, p.b_up_offset + bt * (BN / 2));
@@ -219,7 +229,43 @@ __global__ void __launch_bounds__(gemm_threads<MT>(), 1)
       const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + buf * ACC + msub * BN;
       const int a_row = at * (BM * MT) + row_in_tile;
       const bool a_ok = a_row < p.a_rows;
-      if constexpr (EPI == EPI_SWIGLU) {
+      if constexpr (EPI == EPI_SWIGLU_SWAP) {
+        // weight-streaming SwiGLU: TMEM lanes 0-63 hold gate rows at*64 + lane (warps with
+        // q = 0, 1), lanes 64-127 the matching up rows (q = 2, 3). The up warps hand their
+        // bf16-rounded values over in shared memory; the gate warps write
+        // act[m][n] = bf16(silu(g) * u) (swap: n is the weight row, m the activation row).
+        float* xch = reinterpret_cast<float*>(smem + L::XCH);
+        const int n = at * 64 + (q & 1) * 32 + lane;  // output column of this lane's row pair
+        __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.out);
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+          constexpr int CW = BN < 32 ? BN : 32;
+          uint32_t r[32];
+          if constexpr (BN >= 32) {
+            tmem_ld_32x32b_x32(t_row + c, r);
+          } else {
+            tmem_ld_32x32b_x16(t_row + c, r);
+          }
+          tmem_ld_wait();
+          if (q >= 2) {
+#pragma unroll
+            for (int j = 0; j < CW; ++j) xch[((q - 2) * 32 + lane) * 33 + j] = bf16_round(__uint_as_float(r[j]));
+          }
+          named_bar_sync(1, 128);
+          if (q < 2 && n < p.a_rows) {
+#pragma unroll
+            for (int j = 0; j < CW; ++j) {
+              const int m = bt * BN + c + j;
+              if (m < p.b_rows) {
+                const float gg = bf16_round(__uint_as_float(r[j]));
+                const float uu = xch[(q * 32 + lane) * 33 + j];
+                out[(int64_t)m * p.ldo + n] = f2bf(gg / (1.0f + expf(-gg)) * uu);
+              }
+            }
+          }
+          named_bar_sync(1, 128);  // the exchange buffer is rewritten by the next chunk
+        }
+      } else if constexpr (EPI == EPI_SWIGLU) {
         // columns [0, BN/2) = gate, [BN/2, BN) = up of output columns bt*BN/2 ...
         __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.out);
 #pragma unroll 1
@@ -641,7 +687,7 @@ static int num_sms() {
 template <int BN, int STAGES, int EPI, int MT = 1>
 static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, cudaStream_t s) {
   auto kern = gemm_tcgen05_kernel<BN, STAGES, EPI, MT>;
-  const int smem = GemmSmem<BN, STAGES, MT>::TOTAL;
+  const int smem = GemmSmem<BN, STAGES, MT>::TOTAL + (EPI == EPI_SWIGLU_SWAP ? GemmSmem<BN, STAGES, MT>::XCH_BYTES : 0);
   static bool configured = false;  // one flag per instantiation
   if (!configured) {
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
@@ -794,7 +840,7 @@ extern "C" size_t qw_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K, int o
     return s > 1 ? (size_t)s * (size_t)M * (size_t)N * sizeof(float) : 0;
   }
   SkinnyPlan pl = plan_skinny(M, N, K);
-  if (pl.splits == 1 && out_kind != QW_OUT_SWIGLU && out_kind != QW_OUT_F32) return 0;
+  if (pl.splits == 1 && out_kind != QW_OUT_F32) return 0;  // SwiGLU without a split: in the epilogue
   return (size_t)pl.splits * (size_t)M * (size_t)N * sizeof(float);
 }
 
@@ -909,6 +955,20 @@ extern "C" int qw_gemm_bf16(const void* x, const void* w, void* y, int64_t M, in
   p.kb_per_split = pl.kb_per_split;
   p.swap = 1;
   p.group = 1;
+  if (out_kind == QW_OUT_SWIGLU && pl.splits == 1) {
+    // gate and up rows of the same output columns in one tile: SwiGLU in the epilogue
+    if ((rc = make_tmap(&ta, w, N, K, ldw, 64)) != QW_OK) return rc;
+    p.a_rows = (int)n_out;
+    p.a_tiles = (int)((n_out + 63) / 64);
+    p.b_up_offset = (int)n_out;
+    p.out = y;
+    p.ldo = ldy;
+    switch (pl.bn) {
+      case 16: return launch_gemm<16, 8, EPI_SWIGLU_SWAP>(ta, tb, p, s);
+      case 32: return launch_gemm<32, 8, EPI_SWIGLU_SWAP>(ta, tb, p, s);
+      default: return launch_gemm<64, 8, EPI_SWIGLU_SWAP>(ta, tb, p, s);
+    }
+  }
   // raw fp32 outputs always take the partial + reduce route (one instantiation fewer per tile width)
   const bool partial = pl.splits > 1 || out_kind == QW_OUT_SWIGLU || out_kind == QW_OUT_F32;
   if (!partial) {

@@ -78,8 +78,13 @@ def test_gemm_f32_logits(ops, M, N, K):
     check_bf16(y, x, w)
 
 
-@pytest.mark.parametrize("M,I,K", [(300, 384, 512), (128, 1024, 256), (32, 512, 1024), (3, 256, 512)])
+@pytest.mark.parametrize("M,I,K", [(300, 384, 512), (128, 1024, 256), (32, 512, 1024), (3, 256, 512),
+                                   (32, 17408, 5120), (7, 200, 256), (64, 2304, 512)])
 def test_gemm_swiglu(ops, M, I, K):
+    """SwiGLU in the epilogue: large M pairs gate and up columns in one B tile; decode
+    (M <= 64) pairs 64 gate rows with their 64 up rows in one weight tile when the product
+    is not split over K (17408 x 5120: the model's gate_up; I = 200: a partial last tile),
+    else sums split-K partials first."""
     g = torch.Generator(device="cuda").manual_seed(9)
     x = torch.randn(M, K, device="cuda", generator=g).to(torch.bfloat16)
     w = (torch.randn(2 * I, K, device="cuda", generator=g) * 0.05).to(torch.bfloat16)
