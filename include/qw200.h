@@ -75,6 +75,9 @@ int qw_gemm_bf16(const void* x, const void* w, void* y, int64_t M, int64_t N, in
  * norm kernel. When that size is 0 for a large M, the call is a bf16 GEMM into hidden and
  * then qw_add_rmsnorm (REF:5087-5088 / 5092 + 5052: F.linear then gemma_fused_add_rmsnorm) */
 size_t qw_gemm_add_rmsnorm_workspace_bytes(int64_t M, int64_t N, int64_t K);
+/* Kernels one qw_gemm_add_rmsnorm call of this shape launches: 1 when the add-norm runs
+ * inside the weight-streaming GEMM (its last M CTAs to finish each take one row), else 2. */
+int qw_gemm_add_rmsnorm_kernels(int64_t M, int64_t N, int64_t K);
 int qw_gemm_add_rmsnorm(const void* x, const void* w, int64_t M, int64_t N, int64_t K, int64_t ldx, int64_t ldw,
                         void* resid, const void* norm_w, void* hidden, float eps, void* workspace, size_t ws_bytes,
                         qw_stream_t stream);

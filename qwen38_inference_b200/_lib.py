@@ -25,6 +25,7 @@ SIGNATURES = {
     "qw_gemm_workspace_bytes": (SZ, [I64, I64, I64, I32]),
     "qw_gemm_bf16": (I32, [P, P, P, I64, I64, I64, I64, I64, I64, I32, P, SZ, P]),
     "qw_gemm_add_rmsnorm_workspace_bytes": (SZ, [I64, I64, I64]),
+    "qw_gemm_add_rmsnorm_kernels": (I32, [I64, I64, I64]),
     "qw_gemm_add_rmsnorm": (I32, [P, P, I64, I64, I64, I64, I64, P, P, P, F32, P, SZ, P]),
     "qw_add_rmsnorm_f32": (I32, [P, I64, I64, I64, I64, P, P, P, F32, P]),
     "qw_round_f32_bf16": (I32, [P, P, I64, P]),

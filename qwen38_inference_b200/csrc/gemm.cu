@@ -56,7 +56,136 @@ struct GemmParams {
   int64_t part_stride; // EPI_PARTIAL: elements between split slices
   int* err;            // device error word
   int vec_ok;          // output rows 16-byte aligned: vector stores allowed
+  // EPI_PARTIAL (weight streaming) with norm_rows > 0: the residual add-norm of the output
+  // rows after the split-K product, by the last norm_rows CTAs to finish (partial_norm_finish)
+  int norm_rows;
+  int* norm_counter;  // [2], zero between launches
+  __nv_bfloat16* resid;
+  const __nv_bfloat16* norm_w;
+  __nv_bfloat16* hidden;
+  float eps;
 };
+
+// Ticket counters of partial_norm_finish, one pair per device (launches on one stream only).
+__device__ int g_norm_counter[2];
+
+static int* norm_counter_ptr() {
+  static int* ptrs[64] = {nullptr};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return nullptr;
+  if (!ptrs[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_norm_counter) == cudaSuccess) ptrs[dev] = static_cast<int*>(p);
+  }
+  return ptrs[dev];
+}
+
+QW_DEV int ld_acquire_gpu(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// The add-norm after a weight-streaming split-K product, inside the GEMM kernel. Every CTA,
+// once its partial stores are issued, fences them and draws a ticket. The last norm_rows
+// ticket holders wait (bounded) until every CTA of the grid holds a ticket, so all partials
+// are in memory, then each takes one output row m:
+//   x = bf16(sum_s partial[s][m][:]) (splits in order), v = x + resid (fp32),
+//   resid = bf16(v), hidden = bf16(v * rsqrt(mean v^2 + eps) * (1 + w)).
+// The waiters only wait for CTAs that are already running: the grid is at most one CTA per
+// SM, and a CTA that has not drawn its ticket is either running or about to be placed on
+// an SM that a finished CTA of this grid or of an earlier kernel gives back. The last waiter
+// to finish resets both counters for the next launch.
+template <int NT>
+QW_DEV void partial_norm_finish(const GemmParams& p) {
+  constexpr int MAXC = 6;  // 8-column chunks per thread: N <= 48 * NT
+  __shared__ int s_ticket, s_ok;
+  __shared__ float s_red[NT / 32];
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) s_ticket = atomicAdd(p.norm_counter, 1);
+  __syncthreads();
+  const int first = (int)gridDim.x - p.norm_rows;
+  const int t = s_ticket;
+  if (t < first) return;
+  if (threadIdx.x == 0) {
+    int ok = 1;
+    const uint64_t t0 = globaltimer();
+    while (ld_acquire_gpu(p.norm_counter) < (int)gridDim.x) {
+      if (globaltimer() - t0 > kWaitLimitNs) {
+        set_error(p.err, QW_DEV_ERR_TIMEOUT_GEMM);
+        ok = 0;
+        break;
+      }
+    }
+    s_ok = ok;
+  }
+  __syncthreads();
+  if (!s_ok) return;
+  const int m = t - first;
+  const int N = p.a_rows;
+  const float* ws = reinterpret_cast<const float*>(p.out) + (int64_t)m * p.ldo;
+  float v[MAXC][8];
+#pragma unroll
+  for (int i = 0; i < MAXC; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[i][j] = 0.f;
+  // splits in order; every chunk's loads of one split are independent, so they are in
+  // flight together
+  for (int sp = 0; sp < p.k_splits; ++sp) {
+    const float* src = ws + sp * p.part_stride;
+#pragma unroll
+    for (int i = 0; i < MAXC; ++i) {
+      const int c = (threadIdx.x + i * NT) * 8;
+      if (c < N) {
+        const float4 a = __ldcg(reinterpret_cast<const float4*>(src + c));
+        const float4 b = __ldcg(reinterpret_cast<const float4*>(src + c + 4));
+        v[i][0] += a.x; v[i][1] += a.y; v[i][2] += a.z; v[i][3] += a.w;
+        v[i][4] += b.x; v[i][5] += b.y; v[i][6] += b.z; v[i][7] += b.w;
+      }
+    }
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < MAXC; ++i) {
+    const int c = (threadIdx.x + i * NT) * 8;
+    if (c < N) {
+      float r[8];
+      load_bf16x8(p.resid + (int64_t)m * N + c, r);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        v[i][j] = bf16_round(v[i][j]) + r[j];
+        ss += v[i][j] * v[i][j];
+      }
+      store_bf16x8(p.resid + (int64_t)m * N + c, v[i]);
+    }
+  }
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) s_red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
+#pragma unroll
+  for (int i = 0; i < NT / 32; ++i) tot += s_red[i];
+  const float rstd = rsqrtf(tot / (float)N + p.eps);
+#pragma unroll
+  for (int i = 0; i < MAXC; ++i) {
+    const int c = (threadIdx.x + i * NT) * 8;
+    if (c < N) {
+      float wf[8], o[8];
+      load_bf16x8(p.norm_w + c, wf);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o[j] = v[i][j] * rstd * (1.0f + wf[j]);
+      store_bf16x8(p.hidden + (int64_t)m * N + c, o);
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0 && atomicAdd(p.norm_counter + 1, 1) == p.norm_rows - 1) {
+    p.norm_counter[0] = 0;  // every waiter is past its wait: reset for the next launch
+    p.norm_counter[1] = 0;
+    __threadfence();
+  }
+}
 
 constexpr int BM = 128;  // rows of one MMA (one TMEM accumulator)
 constexpr int BK = 64;   // 64 bf16 = 128 bytes = one SWIZZLE_128B row
@@ -360,6 +489,9 @@ __global__ void __launch_bounds__(gemm_threads<MT>(), 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+  if constexpr (EPI == EPI_PARTIAL) {
+    if (p.norm_rows > 0) partial_norm_finish<64 + 128 * MT>(p);  // gemm_threads<MT>()
   }
 }
 
@@ -1021,6 +1153,14 @@ extern "C" size_t qw_gemm_add_rmsnorm_workspace_bytes(int64_t M, int64_t N, int6
   return (size_t)pl.splits * (size_t)M * (size_t)N * sizeof(float);
 }
 
+extern "C" int qw_gemm_add_rmsnorm_kernels(int64_t M, int64_t N, int64_t K) {
+  if (!use_skinny(M)) return 2;
+  const SkinnyPlan pl = plan_skinny(M, N, K);
+  const int units = pl.a_tiles * pl.splits;
+  const int grid = units < num_sms() ? units : num_sms();
+  return (grid >= M && N <= 48 * gemm_threads<1>()) ? 1 : 2;
+}
+
 extern "C" int qw_gemm_add_rmsnorm(const void* x, const void* w, int64_t M, int64_t N, int64_t K, int64_t ldx,
                                    int64_t ldw, void* resid, const void* norm_w, void* hidden, float eps,
                                    void* workspace, size_t ws_bytes, qw_stream_t stream) {
@@ -1072,12 +1212,24 @@ extern "C" int qw_gemm_add_rmsnorm(const void* x, const void* w, int64_t M, int6
   p.out = workspace;
   p.ldo = N;
   p.part_stride = (int64_t)M * N;
+  // the add-norm inside the GEMM when the grid has a CTA for every row (partial_norm_finish)
+  const int units = p.a_tiles * p.b_tiles * p.k_splits;
+  const int grid = units < num_sms() ? units : num_sms();
+  int* counter = norm_counter_ptr();
+  if (grid >= M && N <= 48 * gemm_threads<1>() && counter != nullptr) {
+    p.norm_rows = (int)M;
+    p.norm_counter = counter;
+    p.resid = static_cast<__nv_bfloat16*>(resid);
+    p.norm_w = static_cast<const __nv_bfloat16*>(norm_w);
+    p.hidden = static_cast<__nv_bfloat16*>(hidden);
+    p.eps = eps;
+  }
   switch (pl.bn) {
     case 16: rc = launch_gemm<16, 8, EPI_PARTIAL>(ta, tb, p, s); break;
     case 32: rc = launch_gemm<32, 8, EPI_PARTIAL>(ta, tb, p, s); break;
     default: rc = launch_gemm<64, 8, EPI_PARTIAL>(ta, tb, p, s); break;
   }
-  if (rc != QW_OK) return rc;
+  if (rc != QW_OK || p.norm_rows > 0) return rc;
   const int threads = (int)((N / 8 + 31) / 32 * 32);
   splitk_add_rmsnorm_kernel<<<(unsigned)M, threads, 0, s>>>(
       static_cast<const float*>(workspace), pl.splits, p.part_stride, (int)N, static_cast<__nv_bfloat16*>(resid),

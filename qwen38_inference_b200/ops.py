@@ -103,7 +103,7 @@ def gemm_add_rmsnorm(x, w, resid, norm_w, hidden, eps, ws: Workspace):
         raise ValueError("gemm_add_rmsnorm expects contiguous resid and hidden [M, N]")
     need = int(_lib.load().qw_gemm_add_rmsnorm_workspace_bytes(M, N, K))
     buf = ws.get(need)
-    LAUNCHES[0] += 2
+    LAUNCHES[0] += int(_lib.load().qw_gemm_add_rmsnorm_kernels(M, N, K))
     _lib.call("qw_gemm_add_rmsnorm", x.data_ptr(), w.data_ptr(), M, N, K, x.stride(0), w.stride(0), resid.data_ptr(),
               norm_w.data_ptr(), hidden.data_ptr(), eps, buf.data_ptr(), need, _stream())
 
