@@ -417,6 +417,8 @@ def run_long(args):
     n_dec = max(3, args.decode_steps)
     model = Qwen38(config=cfg, seed=0, device=f"cuda:{local}", max_context=n_tok + n_dec + 2 * chunk + 64,
                    tensor_parallel=True if world > 1 else None)
+    if world > 1 and args.tp_allreduce == "peer":
+        model.enable_peer_allreduce()
     g = torch.Generator().manual_seed(26)
     prompt = torch.randint(cfg.vocab_size, (n_tok,), generator=g).tolist()  # same tokens on every rank
     g = torch.Generator().manual_seed(27)
@@ -505,8 +507,9 @@ def run_long(args):
            "data": "synthetic (random-init N(0,0.02) 27B weights; uniform token ids, seeds 26/27)",
            "config": {"workload": f"B1 x {n_tok} tokens in {chunk}-token chunks into a fresh cache, then decode at "
                                   f"{n_tok} context", "global_batch": 1, "seq_len": n_tok,
-                      "parallelism": f"tp{world} (head-wise; fp32 NCCL all-reduce after each row-parallel projection)"
-                      if world > 1 else "single GPU",
+                      "parallelism": (f"tp{world} (head-wise; fp32 all-reduce after each row-parallel projection: "
+                                      + ("NCCL in prefill, in the projection kernel over peer memory in decode)"
+                                         if args.tp_allreduce == "peer" else "NCCL)")) if world > 1 else "single GPU",
                       "warmup_steps": "first 8 chunks + decodes", "l2": "inputs larger than L2 (weights streamed per call)"},
            "median_ms": {"prefill_total": round(mp, 2), "decode": round(md, 3)},
            "reference_published": {"prefill_ms_one_131072_token_call": 7753.7, "decode_ms_at_131k": 15.79},
@@ -520,7 +523,7 @@ def run_long(args):
     if rank == 0:
         print(json.dumps(out), flush=True)
     del cache
-    model._engine.graphs.clear()  # graphs holding NCCL calls go before the process group
+    model.close()  # graphs holding NCCL calls and the peer buffers go before the process group
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
@@ -653,6 +656,8 @@ def main():
     ap.add_argument("--long-tokens", type=int, default=131071)
     ap.add_argument("--chunk", type=int, default=512)
     ap.add_argument("--decode-steps", type=int, default=10)
+    ap.add_argument("--tp-allreduce", choices=["peer", "nccl"], default="peer",
+                    help="long workload, N > 1: decode all-reduce inside the projection kernels (peer) or NCCL")
     ap.add_argument("--op", choices=["gate_up", "gdn_prefill", "conv_prefill", "attn_prefill"], default=None,
                     help="time one kernel of the step alone (the case the ncu captures run)")
     args = ap.parse_args()

@@ -40,6 +40,7 @@ typedef struct CUstream_st* qw_stream_t;
 #define QW_DEV_ERR_INDEX 102
 #define QW_DEV_ERR_TIMEOUT_GDN 103 /* a bounded wait of the chunked delta-rule pipeline gave up */
 #define QW_DEV_ERR_TIMEOUT_ATTN 104 /* a bounded wait of the prefill attention pipeline gave up */
+#define QW_DEV_ERR_TIMEOUT_TP 105 /* a peer rank's row did not arrive in the one-shot all-reduce */
 
 /* ---- library ----------------------------------------------------------------------- */
 int qw_version(void);
@@ -196,8 +197,39 @@ int qw_kv_grow(const void* src_k, const void* src_v, void* dst_k, void* dst_v, c
                int64_t old_cap, int64_t new_cap, int64_t row_elems, qw_stream_t stream);
 
 /* ---- head-wise tensor parallelism (new: the reference runs one GPU) ------------------ *
- * The collectives themselves are NCCL all-reduce / all-gather calls made by the host; these
- * move the data on either side of them.
+ * Peer buffers of the one-shot all-reduce fused into the decode projections
+ * (qw_gemm_add_rmsnorm_tp). Each rank allocates one buffer of qw_tp_buffer_bytes(H) with
+ * qw_ipc_alloc (the one allocation the library makes; zero-filled), publishes the
+ * QW_IPC_HANDLE_BYTES handle to the other ranks of the node, and maps theirs with
+ * qw_ipc_open. Layout: per-row arrival flags [QW_TP_MAX_ROWS][QW_TP_MAX_WORLD] u32 written
+ * by the peers, then the row epochs of this rank, then (at QW_TP_HEADER_BYTES) three slots
+ * of [QW_TP_MAX_ROWS, H] fp32 partial sums.                                                 */
+#define QW_IPC_HANDLE_BYTES 64
+#define QW_TP_MAX_WORLD 8
+#define QW_TP_MAX_ROWS 64
+#define QW_TP_HEADER_BYTES 65536
+size_t qw_tp_buffer_bytes(int64_t H);
+int qw_ipc_alloc(size_t bytes, void** dptr, void* handle);
+int qw_ipc_open(const void* handle, void** dptr);
+int qw_ipc_close(void* dptr);
+int qw_ipc_free(void* dptr);
+/* Decode (M <= QW_TP_MAX_ROWS) row-parallel projection of one tensor-parallel rank fused with
+ * the all-reduce over the `world` ranks and the residual add-norm, in ONE kernel: the GEMM's
+ * last M CTAs each sum one row's split-K partials, publish it in this rank's peer buffer
+ * (slot `slot`), raise the row's flag in every rank's buffer, wait (bounded, else
+ * QW_DEV_ERR_TIMEOUT_TP) for every rank's flag, sum the ranks' rows in rank order and apply
+ * the add-norm of qw_gemm_add_rmsnorm (round_only: hidden = bf16(sum), resid untouched).
+ * peer_bases: device array of the `world` buffer bases, this rank's own at index `rank`.
+ * Every rank must make the same calls in the same order, and a rank must not reuse a slot
+ * in two consecutive calls (alternate 0 and 1; 2 for an odd one out).
+ * (REF:5087-5088 / 5092 + 5052 on one GPU; the all-reduce has no counterpart there)          */
+int qw_gemm_add_rmsnorm_tp(const void* x, const void* w, int64_t M, int64_t N, int64_t K, int64_t ldx, int64_t ldw,
+                           void* resid, const void* norm_w, void* hidden, float eps, void* workspace,
+                           size_t ws_bytes, const void* peer_bases, int64_t world, int64_t rank, int64_t slot,
+                           int64_t round_only, qw_stream_t stream);
+
+/* Prefill (and any call of more than QW_TP_MAX_ROWS rows) uses NCCL all-reduce / all-gather
+ * calls made by the host; these move the data on either side of them.
  * y bf16 [n] = bf16(x fp32 [n]): the all-reduced row-parallel down projection of the last
  * layer becomes the bf16 F.linear output that the final norm reads (REF:5092-5093).        */
 int qw_round_f32_bf16(const float* x, void* y, int64_t n, qw_stream_t stream);

@@ -30,6 +30,12 @@ SIGNATURES = {
     "qw_add_rmsnorm_f32": (I32, [P, I64, I64, I64, I64, P, P, P, F32, P]),
     "qw_round_f32_bf16": (I32, [P, P, I64, P]),
     "qw_gather_vocab_shards": (I32, [P, I64, I64, I64, P, P]),
+    "qw_tp_buffer_bytes": (SZ, [I64]),
+    "qw_ipc_alloc": (I32, [SZ, C.POINTER(C.c_void_p), P]),
+    "qw_ipc_open": (I32, [P, C.POINTER(C.c_void_p)]),
+    "qw_ipc_close": (I32, [P]),
+    "qw_ipc_free": (I32, [P]),
+    "qw_gemm_add_rmsnorm_tp": (I32, [P, P, I64, I64, I64, I64, I64, P, P, P, F32, P, SZ, P, I64, I64, I64, I64, P]),
     "qw_embed_rmsnorm": (I32, [P, I64, P, I64, I64, P, P, P, F32, P]),
     "qw_add_rmsnorm": (I32, [P, P, P, I64, I64, F32, P]),
     "qw_add_rmsnorm_rows": (I32, [P, P, P, I64, I64, I64, P, P, F32, P]),

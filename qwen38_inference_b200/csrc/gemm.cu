@@ -64,6 +64,12 @@ struct GemmParams {
   const __nv_bfloat16* norm_w;
   __nv_bfloat16* hidden;
   float eps;
+  // tensor parallelism (norm_rows > 0, tp_world > 1): each row's local split sum is
+  // exchanged through the ranks' peer buffers before the add-norm (partial_norm_finish)
+  int tp_world, tp_rank;
+  int tp_round_only;                    // 1: hidden = bf16(sum over ranks), no add-norm
+  const unsigned long long* tp_bases;   // device array [tp_world]: every rank's buffer base
+  int64_t tp_slot_off;                  // byte offset of this call's slot in every buffer
 };
 
 // Ticket counters of partial_norm_finish, one pair per device (launches on one stream only).
@@ -84,6 +90,22 @@ static int* norm_counter_ptr() {
 QW_DEV int ld_acquire_gpu(const int* p) {
   int v;
   asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+QW_DEV unsigned ld_acquire_sys(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+QW_DEV void st_release_sys(unsigned* p, unsigned v) {
+  asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+QW_DEV float4 ld_volatile_f4(const float* p) {
+  float4 v;
+  asm volatile("ld.volatile.global.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "l"(p)
+               : "memory");
   return v;
 }
 
@@ -144,6 +166,79 @@ QW_DEV void partial_norm_finish(const GemmParams& p) {
         v[i][0] += a.x; v[i][1] += a.y; v[i][2] += a.z; v[i][3] += a.w;
         v[i][4] += b.x; v[i][5] += b.y; v[i][6] += b.z; v[i][7] += b.w;
       }
+    }
+  }
+  if (p.tp_world > 1) {
+    // one-shot all-reduce of row m over the ranks: publish this rank's row in its own
+    // buffer, raise this row's flag in every rank's buffer, wait (bounded) for every rank's
+    // flag in this buffer, then sum the ranks' rows in rank order (the same bits on every
+    // rank). The slot a call uses alternates with the caller's layer position, so a rank
+    // writes a slot again only after every rank has passed the call that read it.
+    uint8_t* mine = reinterpret_cast<uint8_t*>(p.tp_bases[p.tp_rank]);
+    float* my_row = reinterpret_cast<float*>(mine + p.tp_slot_off) + (int64_t)m * N;
+#pragma unroll
+    for (int i = 0; i < MAXC; ++i) {
+      const int c = (threadIdx.x + i * NT) * 8;
+      if (c < N) {
+        reinterpret_cast<float4*>(my_row + c)[0] = make_float4(v[i][0], v[i][1], v[i][2], v[i][3]);
+        reinterpret_cast<float4*>(my_row + c)[1] = make_float4(v[i][4], v[i][5], v[i][6], v[i][7]);
+      }
+    }
+    __threadfence_system();
+    __syncthreads();
+    unsigned* my_flags = reinterpret_cast<unsigned*>(mine) + m * QW_TP_MAX_WORLD;
+    unsigned* my_epoch = reinterpret_cast<unsigned*>(mine + 4096) + m;
+    __shared__ unsigned s_ep;
+    if (threadIdx.x == 0) s_ep = *my_epoch + 1;  // only this CTA touches row m's epoch in this launch
+    __syncthreads();
+    const unsigned ep = s_ep;
+    if ((int)threadIdx.x < p.tp_world)
+      st_release_sys(reinterpret_cast<unsigned*>(p.tp_bases[threadIdx.x]) + m * QW_TP_MAX_WORLD + p.tp_rank, ep);
+    if (threadIdx.x == 0) {
+      int ok = 1;
+      const uint64_t t0 = globaltimer();
+      for (int q = 0; q < p.tp_world && ok; ++q) {
+        while (ld_acquire_sys(my_flags + q) < ep) {
+          if (globaltimer() - t0 > kWaitLimitNs) {
+            set_error(p.err, QW_DEV_ERR_TIMEOUT_TP);
+            ok = 0;
+            break;
+          }
+        }
+      }
+      *my_epoch = ep;
+      s_ok = ok;
+    }
+    __syncthreads();
+    if (!s_ok) return;
+#pragma unroll
+    for (int i = 0; i < MAXC; ++i) {
+      const int c = (threadIdx.x + i * NT) * 8;
+      if (c < N) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[i][j] = 0.f;
+        for (int q = 0; q < p.tp_world; ++q) {
+          const float* row = reinterpret_cast<const float*>(reinterpret_cast<const uint8_t*>(p.tp_bases[q]) +
+                                                            p.tp_slot_off) + (int64_t)m * N + c;
+          const float4 a = ld_volatile_f4(row), b = ld_volatile_f4(row + 4);
+          v[i][0] += a.x; v[i][1] += a.y; v[i][2] += a.z; v[i][3] += a.w;
+          v[i][4] += b.x; v[i][5] += b.y; v[i][6] += b.z; v[i][7] += b.w;
+        }
+      }
+    }
+    if (p.tp_round_only) {
+#pragma unroll
+      for (int i = 0; i < MAXC; ++i) {
+        const int c = (threadIdx.x + i * NT) * 8;
+        if (c < N) store_bf16x8(p.hidden + (int64_t)m * N + c, v[i]);
+      }
+      __syncthreads();
+      if (threadIdx.x == 0 && atomicAdd(p.norm_counter + 1, 1) == p.norm_rows - 1) {
+        p.norm_counter[0] = 0;
+        p.norm_counter[1] = 0;
+        __threadfence();
+      }
+      return;
     }
   }
   float ss = 0.f;
@@ -1236,6 +1331,64 @@ extern "C" int qw_gemm_add_rmsnorm(const void* x, const void* w, int64_t M, int6
       static_cast<const __nv_bfloat16*>(norm_w), static_cast<__nv_bfloat16*>(hidden), eps);
   QW_LAUNCH_CHECK();
   return QW_OK;
+}
+
+extern "C" int qw_gemm_add_rmsnorm_tp(const void* x, const void* w, int64_t M, int64_t N, int64_t K, int64_t ldx,
+                                      int64_t ldw, void* resid, const void* norm_w, void* hidden, float eps,
+                                      void* workspace, size_t ws_bytes, const void* peer_bases, int64_t world,
+                                      int64_t rank, int64_t slot, int64_t round_only, qw_stream_t stream) {
+  QW_CHECK_ARG(x && w && hidden && peer_bases && M > 0 && N > 0 && K > 0 && ldx >= K && ldw >= K, QW_ERR_ARG);
+  QW_CHECK_ARG(round_only || (resid && norm_w), QW_ERR_ARG);
+  QW_CHECK_ARG(world >= 2 && world <= QW_TP_MAX_WORLD && rank >= 0 && rank < world && slot >= 0 && slot < 3,
+               QW_ERR_ARG);
+  QW_CHECK_ARG(use_skinny(M) && M <= QW_TP_MAX_ROWS && N % 8 == 0 && N <= 48 * gemm_threads<1>(), QW_ERR_UNSUPPORTED);
+  QW_CHECK_ARG(((uintptr_t)x % 16) == 0 && ((uintptr_t)w % 16) == 0 && (ldx % 8) == 0 && (ldw % 8) == 0 &&
+                   ((uintptr_t)hidden % 16) == 0 && ((uintptr_t)resid % 16) == 0 && ((uintptr_t)norm_w % 16) == 0,
+               QW_ERR_ALIGN);
+  const SkinnyPlan pl = plan_skinny(M, N, K);
+  const int units = pl.a_tiles * pl.splits;
+  const int grid = units < num_sms() ? units : num_sms();
+  int* counter = norm_counter_ptr();
+  QW_CHECK_ARG(grid >= M && counter != nullptr, QW_ERR_UNSUPPORTED);
+  const size_t need = (size_t)pl.splits * (size_t)M * (size_t)N * sizeof(float);
+  QW_CHECK_ARG(workspace != nullptr && ws_bytes >= need, QW_ERR_WORKSPACE);
+  QW_CHECK_ARG(((uintptr_t)workspace % 16) == 0, QW_ERR_ALIGN);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  int rc;
+  CUtensorMap ta, tb;
+  if ((rc = make_tmap(&ta, w, N, K, ldw, BM)) != QW_OK) return rc;
+  if ((rc = make_tmap(&tb, x, M, K, ldx, pl.bn)) != QW_OK) return rc;
+  GemmParams p{};
+  p.err = device_error_ptr();
+  p.K = (int)K;
+  p.kb_total = pl.kb_total;
+  p.group = 1;
+  p.a_rows = (int)N;
+  p.b_rows = (int)M;
+  p.a_tiles = pl.a_tiles;
+  p.b_tiles = 1;
+  p.k_splits = pl.splits;
+  p.kb_per_split = pl.kb_per_split;
+  p.swap = 1;
+  p.out = workspace;
+  p.ldo = N;
+  p.part_stride = (int64_t)M * N;
+  p.norm_rows = (int)M;
+  p.norm_counter = counter;
+  p.resid = static_cast<__nv_bfloat16*>(resid);
+  p.norm_w = static_cast<const __nv_bfloat16*>(norm_w);
+  p.hidden = static_cast<__nv_bfloat16*>(hidden);
+  p.eps = eps;
+  p.tp_world = (int)world;
+  p.tp_rank = (int)rank;
+  p.tp_round_only = round_only ? 1 : 0;
+  p.tp_bases = static_cast<const unsigned long long*>(peer_bases);
+  p.tp_slot_off = (int64_t)QW_TP_HEADER_BYTES + slot * (int64_t)QW_TP_MAX_ROWS * N * (int64_t)sizeof(float);
+  switch (pl.bn) {
+    case 16: return launch_gemm<16, 8, EPI_PARTIAL>(ta, tb, p, s);
+    case 32: return launch_gemm<32, 8, EPI_PARTIAL>(ta, tb, p, s);
+    default: return launch_gemm<64, 8, EPI_PARTIAL>(ta, tb, p, s);
+  }
 }
 
 extern "C" int qw_add_rmsnorm_f32(const float* x, int64_t n_parts, int64_t part_stride, int64_t T, int64_t H,

@@ -4,6 +4,11 @@
 //   qw_gather_vocab_shards  [G, R, Vs] fp32 logits of G vocab shards (the rank-major result of
 //                           an all-gather) -> [R, G * Vs] in vocabulary order (REF:5096)
 // Both are plain HBM streams: 8-byte (bf16 x4) / 16-byte vector accesses, grid-stride loops.
+// Also the peer buffers of the one-shot all-reduce fused into the decode projections
+// (gemm.cu, partial_norm_finish): allocated here and shared between the ranks' processes
+// with CUDA IPC handles.
+#include <cstring>
+
 #include "common.cuh"
 
 namespace qw {
@@ -47,6 +52,53 @@ static unsigned stream_blocks(int64_t work, int threads) {
 }  // namespace qw
 
 using namespace qw;
+
+// ---- peer buffers (CUDA IPC): the one allocation the library makes, on request
+static_assert(sizeof(cudaIpcMemHandle_t) == QW_IPC_HANDLE_BYTES, "IPC handle size");
+
+extern "C" size_t qw_tp_buffer_bytes(int64_t H) {
+  if (H <= 0) return 0;
+  return (size_t)QW_TP_HEADER_BYTES + 3 * (size_t)QW_TP_MAX_ROWS * (size_t)H * sizeof(float);
+}
+
+extern "C" int qw_ipc_alloc(size_t bytes, void** dptr, void* handle) {
+  QW_CHECK_ARG(bytes > 0 && dptr && handle, QW_ERR_ARG);
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, bytes);
+  if (e != cudaSuccess) return QW_ERR_CUDA_BASE + (int)e;
+  e = cudaMemset(p, 0, bytes);  // flags and epochs start at zero
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(static_cast<cudaIpcMemHandle_t*>(handle), p);
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return QW_ERR_CUDA_BASE + (int)e;
+  }
+  *dptr = p;
+  return QW_OK;
+}
+
+extern "C" int qw_ipc_open(const void* handle, void** dptr) {
+  QW_CHECK_ARG(handle && dptr, QW_ERR_ARG);
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  void* p = nullptr;
+  const cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return QW_ERR_CUDA_BASE + (int)e;
+  *dptr = p;
+  return QW_OK;
+}
+
+extern "C" int qw_ipc_close(void* dptr) {
+  QW_CHECK_ARG(dptr, QW_ERR_ARG);
+  const cudaError_t e = cudaIpcCloseMemHandle(dptr);
+  return e == cudaSuccess ? QW_OK : QW_ERR_CUDA_BASE + (int)e;
+}
+
+extern "C" int qw_ipc_free(void* dptr) {
+  QW_CHECK_ARG(dptr, QW_ERR_ARG);
+  const cudaError_t e = cudaFree(dptr);
+  return e == cudaSuccess ? QW_OK : QW_ERR_CUDA_BASE + (int)e;
+}
 
 extern "C" int qw_round_f32_bf16(const float* x, void* y, int64_t n, qw_stream_t stream) {
   QW_CHECK_ARG(x && y && n > 0, QW_ERR_ARG);

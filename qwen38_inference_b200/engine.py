@@ -141,11 +141,23 @@ class Engine:
         splits = self._decode_splits(cache.capacity)
         fused = is_decode and T <= 64  # weight-streaming projections: split-K sum + add-norm in one kernel
         # tensor parallel: row-parallel projections produce fp32 partial sums, all-reduced in place
+        # (decode: inside the projection's kernel through the ranks' peer buffers)
         part = torch.empty(T, H, dtype=torch.float32, device=dev) if tp is not None else None
+        peer = tp is not None and tp.peer_bases is not None and fused and all(
+            ops.gemm_add_rmsnorm_kernels(T, H, K) == 1 for K in {c.attn_out_dim, c.gdn_v_dim, c.intermediate_size})
+        use = [0]  # row-parallel projections so far in this call: the peer slot alternates
+
+        def peer_slot(last=False):
+            slot = 2 if last else use[0] % 2
+            use[0] += 1
+            return slot
 
         def proj_add_norm(x, wt, norm_w):
             """hidden = x . wt^T, then resid += hidden, hidden = norm(resid)."""
-            if tp is not None:
+            if peer:
+                ops.gemm_add_rmsnorm_tp(x, wt, resid, norm_w, hidden, eps, ws, tp.peer_bases, tp.world, tp.rank,
+                                        peer_slot())
+            elif tp is not None:
                 ops.gemm(x, wt, part, out_kind=ops.OUT_F32, ws=ws)
                 tp.all_reduce_(part)
                 ops.add_rmsnorm_f32(part, resid, norm_w, hidden, eps)
@@ -190,6 +202,9 @@ class Engine:
             ops.gemm(hidden, w["gate_up"], act, out_kind=ops.OUT_SWIGLU, ws=ws)
             if i + 1 < n_layers:
                 proj_add_norm(act, w["down"], m.layers[i + 1]["input_norm"])  # the next layer's input norm
+            elif peer:
+                ops.gemm_add_rmsnorm_tp(act, w["down"], None, None, hidden, eps, ws, tp.peer_bases, tp.world, tp.rank,
+                                        peer_slot(last=True), round_only=True)
             elif tp is not None:
                 ops.gemm(act, w["down"], part, out_kind=ops.OUT_F32, ws=ws)
                 tp.all_reduce_(part)

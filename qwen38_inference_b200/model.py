@@ -278,6 +278,21 @@ class Qwen38:
         from .engine import Engine
         self._engine = Engine(self)
 
+    def enable_peer_allreduce(self):
+        """Tensor parallelism only: decode projections all-reduce through the ranks' peer
+        buffers inside their GEMM kernel instead of NCCL (collective: every rank calls it)."""
+        if self.tp is None:
+            raise ValueError("enable_peer_allreduce needs a tensor-parallel model")
+        self.tp.enable_peer_buffers(self.cfg.hidden_size, self.device)
+        self._engine.graphs.clear()  # graphs captured on the NCCL path
+
+    def close(self):
+        """Release what outlives a call: captured graphs (they may hold NCCL calls) and the
+        peer buffers of tensor parallelism. Collective under tensor parallelism."""
+        self._engine.graphs.clear()
+        if self.tp is not None:
+            self.tp.close_peer_buffers()
+
     @staticmethod
     def _validate_geometry(c: HybridConfig):
         ok = (c.linear_key_head_dim == 128 and c.linear_value_head_dim == 128 and c.linear_conv_kernel_dim == 4

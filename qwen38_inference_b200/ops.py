@@ -87,6 +87,12 @@ def gemm(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None, *, o
 
 
 # ----------------------------------------------------------------------------- norms
+def gemm_add_rmsnorm_kernels(M, N, K) -> int:
+    """1 when the add-norm of this shape runs inside the GEMM kernel (the condition of the
+    tensor-parallel fused path too), else 2."""
+    return int(_lib.load().qw_gemm_add_rmsnorm_kernels(M, N, K))
+
+
 def gemm_add_rmsnorm_workspace_bytes(M, N, K) -> int:
     return int(_lib.load().qw_gemm_add_rmsnorm_workspace_bytes(M, N, K))
 
@@ -103,9 +109,28 @@ def gemm_add_rmsnorm(x, w, resid, norm_w, hidden, eps, ws: Workspace):
         raise ValueError("gemm_add_rmsnorm expects contiguous resid and hidden [M, N]")
     need = int(_lib.load().qw_gemm_add_rmsnorm_workspace_bytes(M, N, K))
     buf = ws.get(need)
-    LAUNCHES[0] += int(_lib.load().qw_gemm_add_rmsnorm_kernels(M, N, K))
+    LAUNCHES[0] += gemm_add_rmsnorm_kernels(M, N, K)
     _lib.call("qw_gemm_add_rmsnorm", x.data_ptr(), w.data_ptr(), M, N, K, x.stride(0), w.stride(0), resid.data_ptr(),
               norm_w.data_ptr(), hidden.data_ptr(), eps, buf.data_ptr(), need, _stream())
+
+
+def gemm_add_rmsnorm_tp(x, w, resid, norm_w, hidden, eps, ws: Workspace, peer_bases, world, rank, slot,
+                        round_only=False):
+    """A tensor-parallel rank's decode row-parallel projection, the all-reduce over the ranks
+    through their peer buffers and the residual add-norm (or, ``round_only``, hidden =
+    bf16(sum)) in one kernel. ``peer_bases``: int64 device tensor of the ranks' buffer bases."""
+    _req(x, BF16, "x")
+    _req(w, BF16, "w")
+    M, K = x.shape
+    N = w.shape[0]
+    if not (hidden.is_contiguous() and hidden.shape == (M, N)):
+        raise ValueError("gemm_add_rmsnorm_tp expects contiguous hidden [M, N]")
+    need = int(_lib.load().qw_gemm_add_rmsnorm_workspace_bytes(M, N, K))
+    buf = ws.get(need)
+    LAUNCHES[0] += 1
+    _lib.call("qw_gemm_add_rmsnorm_tp", x.data_ptr(), w.data_ptr(), M, N, K, x.stride(0), w.stride(0),
+              _ptr(resid), _ptr(norm_w), hidden.data_ptr(), eps, buf.data_ptr(), need, peer_bases.data_ptr(), world,
+              rank, slot, 1 if round_only else 0, _stream())
 
 
 def add_rmsnorm_f32(x, resid, norm_w, hidden, eps):

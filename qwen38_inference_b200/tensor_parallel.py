@@ -15,8 +15,11 @@ GPU, with NCCL over NVLink for the exchanges:
   - ``lm_head``: vocabulary rows ``[r*V/G, ...)``.
 * row-parallel (each rank holds a column slice, and the outputs are summed):
   attention ``o_proj``, GDN ``out_proj`` and MLP ``down``. Each rank computes an fp32 partial
-  product; NCCL all-reduces the ``[T, hidden]`` fp32 sum, which is rounded to bf16 once, so
-  the result equals the one-GPU projection up to fp32 summation order.
+  product and the ``[T, hidden]`` fp32 sum is rounded to bf16 once, so the result equals the
+  one-GPU projection up to fp32 summation order. Prefill sums with an NCCL all-reduce;
+  decode (up to 64 rows), once ``enable_peer_buffers`` has run, sums inside the projection's
+  own kernel: its last CTAs read the other ranks' rows from their buffers over NVLink
+  (CUDA IPC) and apply the residual add-norm.
 * replicated: the embedding, every RMSNorm weight, the residual stream and the hidden state.
 
 The conv state, recurrent state and KV cache of each rank hold only its own heads. The
@@ -182,6 +185,51 @@ class TensorParallel:
 
     def shard(self, name, t):
         return shard_tensor(name, t, self.spec)
+
+    # ------------------------------------------------------------------ peer buffers
+    peer_bases = None  # int64 device tensor of every rank's peer buffer (decode all-reduce)
+
+    def enable_peer_buffers(self, hidden_size: int, device) -> None:
+        """Allocate this rank's peer buffer (CUDA IPC), exchange handles with the group and
+        map the other ranks' buffers, so that decode projections all-reduce inside their
+        GEMM kernel (``ops.gemm_add_rmsnorm_tp``) instead of through NCCL. Collective: every
+        rank calls it."""
+        import ctypes as C
+        from . import _lib
+        L = _lib.load()
+        nbytes = int(L.qw_tp_buffer_bytes(hidden_size))
+        own = C.c_void_p()
+        handle = C.create_string_buffer(64)
+        _lib.check(L.qw_ipc_alloc(nbytes, C.byref(own), handle), "qw_ipc_alloc")
+        handles = [None] * self.world
+        self.dist.all_gather_object(handles, handle.raw, group=self.group)
+        bases, opened = [], []
+        for r, h in enumerate(handles):
+            if r == self.rank:
+                bases.append(own.value)
+                continue
+            p = C.c_void_p()
+            _lib.check(L.qw_ipc_open(C.create_string_buffer(h, 64), C.byref(p)), "qw_ipc_open")
+            bases.append(p.value)
+            opened.append(p.value)
+        self._own_buffer, self._opened = own.value, opened
+        self.peer_bases = torch.tensor(bases, dtype=torch.int64, device=device)
+        self.dist.barrier(group=self.group)  # every rank maps every buffer before first use
+
+    def close_peer_buffers(self) -> None:
+        """Unmap the other ranks' buffers and free this rank's. Collective; call it when no
+        kernel of any rank can still use them (after a synchronize), before the group ends."""
+        if self.peer_bases is None:
+            return
+        from . import _lib
+        L = _lib.load()
+        torch.cuda.synchronize()
+        self.dist.barrier(group=self.group)
+        for p in self._opened:
+            _lib.check(L.qw_ipc_close(p), "qw_ipc_close")
+        self.dist.barrier(group=self.group)  # nobody maps this rank's buffer any more
+        _lib.check(L.qw_ipc_free(self._own_buffer), "qw_ipc_free")
+        self.peer_bases = None
 
     def _timed(self, name, fn):
         from . import _lib

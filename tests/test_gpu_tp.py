@@ -3,8 +3,10 @@ weights (``mini`` geometry: 2 ranks hold 3 query heads each around one replicate
 1 QK head and 3 value heads of every GDN layer, half the MLP and half the vocabulary).
 
 Call pattern: a ragged two-request prefill, three decode steps (eager, eager + capture, graph
-replay: the NCCL collectives run inside the captured graph), then one request prefilled in
+replay: the collectives run inside the captured graph), then one request prefilled in
 512-token chunks up to 2600 tokens (long enough that prefill attention splits the keys).
+The pattern runs twice on the same tensor-parallel model: with NCCL all-reduces, then with
+the decode all-reduce fused into the projection kernels through the ranks' peer buffers.
 
 The row-parallel projections sum fp32 partials across ranks and round once, so the logits
 differ from the one-GPU run only through fp32 summation order; bf16 rounding flips spread
@@ -70,23 +72,25 @@ def _rank_main(rank, world, port, res):
             del one
         dist.barrier()
         model = Qwen38(config=cfg, seed=21, device=f"cuda:{rank}", max_context=8192, tensor_parallel=True)
-        n0 = ops.LAUNCHES[0]
-        got = _run(model, calls)
-        launches = ops.LAUNCHES[0] - n0
-        code = _lib.take_device_error()
-        if rank == 0:
-            stats = []
-            for a, b in zip(got, ref):
-                d = (a - b).abs()
-                stats.append((float(d.max()), float((d <= ATOL + RTOL * b.abs()).float().mean()),
-                              float((d <= 1e-3 + 1e-3 * b.abs()).float().mean()), tuple(a.shape), tuple(b.shape)))
-            res["stats"] = stats
-        res[f"err{rank}"] = code
-        res[f"launches{rank}"] = launches
-        res[f"replays{rank}"] = model._engine.replays
+        for path in ("nccl", "peer"):
+            if path == "peer":
+                model.enable_peer_allreduce()
+            n0, r0 = ops.LAUNCHES[0], model._engine.replays
+            got = _run(model, calls)
+            res[f"launches_{path}{rank}"] = ops.LAUNCHES[0] - n0
+            res[f"replays_{path}{rank}"] = model._engine.replays - r0
+            res[f"err_{path}{rank}"] = _lib.take_device_error()
+            if rank == 0:
+                stats = []
+                for a, b in zip(got, ref):
+                    d = (a - b).abs()
+                    stats.append((float(d.max()), float((d <= ATOL + RTOL * b.abs()).float().mean()),
+                                  float((d <= 1e-3 + 1e-3 * b.abs()).float().mean()), tuple(a.shape), tuple(b.shape)))
+                res[f"stats_{path}"] = stats
+                res[f"logits_{path}"] = [g[:, :64].clone() for g in got]
     finally:
         if model is not None:
-            model._engine.graphs.clear()  # graphs holding NCCL calls go before the process group
+            model.close()  # graphs (NCCL inside) and peer buffers go before the process group
         torch.cuda.synchronize()
         dist.destroy_process_group()
 
@@ -99,9 +103,15 @@ def test_two_rank_tensor_parallel_matches_one_gpu():
         res = mgr.dict()
         mp.spawn(_rank_main, args=(world, _free_port(), res), nprocs=world, join=True)
         res = dict(res)
-    assert res["err0"] == 0 and res["err1"] == 0
-    assert res["launches0"] > 0 and res["launches0"] == res["launches1"]
-    assert res["replays0"] >= 1 and res["replays0"] == res["replays1"]  # the third decode replays a graph
-    for i, (mx, frac_tol, frac_strict, sa, sb) in enumerate(res["stats"]):
-        assert sa == sb, i
-        assert frac_tol == 1.0, f"call {i}: max |d| {mx}, {frac_tol} within tolerance"
+    for path in ("nccl", "peer"):
+        assert res[f"err_{path}0"] == 0 and res[f"err_{path}1"] == 0, path
+        assert res[f"launches_{path}0"] > 0 and res[f"launches_{path}0"] == res[f"launches_{path}1"], path
+        # the third decode replays a graph (NCCL calls or peer all-reduce kernels inside)
+        assert res[f"replays_{path}0"] >= 1 and res[f"replays_{path}0"] == res[f"replays_{path}1"], path
+        for i, (mx, frac_tol, frac_strict, sa, sb) in enumerate(res[f"stats_{path}"]):
+            assert sa == sb, (path, i)
+            assert frac_tol == 1.0, f"{path} call {i}: max |d| {mx}, {frac_tol} within tolerance"
+    # prefill calls take the same NCCL path either way: bit-identical logits
+    assert torch.equal(res["logits_nccl"][0], res["logits_peer"][0])
+    # the peer path launches fewer kernels (no NCCL calls or add-norm kernels in decode)
+    assert res["launches_peer0"] < res["launches_nccl0"]
