@@ -56,7 +56,10 @@ class Engine:
         if not is_decode:
             max_keys = max(p + n for p, n in zip(prefixes, lens))
             pf_splits = ops.prefill_attn_splits(c.num_attention_heads, offs["tiles"][1] // 2, max_keys)
-        if self.use_graphs and not return_all_logits and (is_decode or T <= self.GRAPH_MAX_PREFILL_T):
+        # prefill graphs only on one GPU: capturing a chunk's NCCL calls costs more than its
+        # launch sequence, and a chunked prompt changes key at every capacity doubling
+        small_prefill = T <= self.GRAPH_MAX_PREFILL_T and self.m.tp is None
+        if self.use_graphs and not return_all_logits and (is_decode or small_prefill):
             shape = ("decode", B, T) if is_decode else ("prefill", B, T, tuple(lens), pf_splits)
             return self._graph_call(shape, arr, offs, T, B, max(lens), cache, is_decode, pf_splits)
         dev = self.staging.upload(arr, self.dev)
