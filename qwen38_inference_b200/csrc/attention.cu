@@ -691,10 +691,13 @@ __global__ void attn_decode_combine_kernel(const float* __restrict__ part_o, con
                                            __nv_bfloat16* __restrict__ out, int64_t ldo) {
   const int bh = blockIdx.x;  // b * nq + h
   const int b = bh / nq, h = bh % nq;
+  // the loops over splits are unrolled so that their independent loads are in flight together
   float mm = -INFINITY;
+#pragma unroll 8
   for (int s = 0; s < splits; ++s) mm = fmaxf(mm, part_ml[((int64_t)bh * splits + s) * 2]);
   for (int d = threadIdx.x; d < D; d += blockDim.x) {
     float ll = 0.f, oo = 0.f;
+#pragma unroll 8
     for (int s = 0; s < splits; ++s) {
       const int64_t slot = (int64_t)bh * splits + s;
       const float ms = part_ml[slot * 2];

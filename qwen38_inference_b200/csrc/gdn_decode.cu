@@ -11,8 +11,38 @@
 
 namespace qw {
 
+// v[i] = this lane's part of row i's sum (16 rows over a warp's 32 lanes). Halving exchange:
+// at each step a lane keeps half of its rows and adds its partner's copy of them. Lanes
+// 2i and 2i+1 return row i's full sum, summed in a fixed order on every lane.
+QW_DEV float rows16_sum(const float (&v)[16], int lane) {
+  float a[8];
+  const bool h16 = lane & 16;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float send = h16 ? v[i] : v[i + 8], keep = h16 ? v[i + 8] : v[i];
+    a[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+  }
+  float c[4];
+  const bool h8 = lane & 8;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float send = h8 ? a[i] : a[i + 4], keep = h8 ? a[i + 4] : a[i];
+    c[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+  }
+  float d[2];
+  const bool h4 = lane & 4;
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const float send = h4 ? c[i] : c[i + 2], keep = h4 ? c[i + 2] : c[i];
+    d[i] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+  }
+  const bool h2 = lane & 2;
+  const float e = (h2 ? d[1] : d[0]) + __shfl_xor_sync(0xffffffffu, h2 ? d[0] : d[1], 2);
+  return e + __shfl_xor_sync(0xffffffffu, e, 1);
+}
+
 template <int DK, int DV, int RATIO>
-__global__ void __launch_bounds__(256) gdn_decode_kernel(
+__global__ void __launch_bounds__(256, 2) gdn_decode_kernel(
     const __nv_bfloat16* __restrict__ qkvz, int64_t ldx, const __nv_bfloat16* __restrict__ ba, int64_t ldba,
     const __nv_bfloat16* __restrict__ conv_w, __nv_bfloat16* __restrict__ conv_state, float* __restrict__ state,
     const int32_t* __restrict__ slots, int n_slots, const float* __restrict__ A_log,
@@ -29,6 +59,17 @@ __global__ void __launch_bounds__(256) gdn_decode_kernel(
   const int slot = slots[b];
   const bool valid = slot >= 0 && slot < n_slots;
   const __nv_bfloat16* xrow = qkvz + (int64_t)b * ldx;
+  // warp w owns value rows [w*ROWS, (w+1)*ROWS) of every head, lane the dims 4*lane..+3;
+  // the first head's rows are requested before the conv so their latency overlaps it
+  constexpr int ROWS = DV / 8;
+  static_assert(ROWS == 16 && DK == 128, "lane layout assumes dk = dv = 128, 8 warps");
+  float* S0 = state + (((int64_t)(valid ? slot : 0) * HV + h * RATIO) * DV) * DK;
+  float4 sv[ROWS];
+  if (valid) {
+#pragma unroll
+    for (int i = 0; i < ROWS; ++i)
+      sv[i] = *reinterpret_cast<const float4*>(S0 + (int64_t)(warp * ROWS + i) * DK + lane * 4);
+  }
 
   // ---- conv update of this CTA's channels
   for (int i = tid; i < NCH; i += blockDim.x) {
@@ -63,7 +104,6 @@ __global__ void __launch_bounds__(256) gdn_decode_kernel(
     return;
   }
   // ---- L2 norms of q and k (fp32, unrounded), lane owns 4 consecutive dims
-  static_assert(DK == 128, "decode kernel lane layout assumes dk = 128");
   float qv[4], kv[4];
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
@@ -89,10 +129,18 @@ __global__ void __launch_bounds__(256) gdn_decode_kernel(
   for (int j = 0; j < 4; ++j) kq += kv[j] * qv[j];
   kq = warp_sum(kq);
 
-  // ---- per value head: state update; warp w owns value rows [w*DV/8, (w+1)*DV/8)
-  constexpr int ROWS = DV / 8;
+  // ---- per value head: state update. All 16 rows of a warp are requested before any is used
+  // (16 loads in flight per thread). Row sums over the 32 lanes use a halving exchange:
+  // after it, lanes 2i and 2i+1 hold row i's sum (16 shuffles for the warp's 16 rows
+  // instead of 5 per row).
+#pragma unroll
   for (int r = 0; r < RATIO; ++r) {
     const int hv = h * RATIO + r;
+    if (r > 0) {
+#pragma unroll
+      for (int i = 0; i < ROWS; ++i)
+        sv[i] = *reinterpret_cast<const float4*>(S0 + ((int64_t)r * DV + warp * ROWS + i) * DK + lane * 4);
+    }
     const float a = bf2f(ba[(int64_t)b * ldba + HV + hv]);
     const float bb = bf2f(ba[(int64_t)b * ldba + hv]);
     const float xg = a + bf2f(dt_bias[hv]);
@@ -100,53 +148,45 @@ __global__ void __launch_bounds__(256) gdn_decode_kernel(
     const float g = -expf(A_log[hv]) * sp;
     const float alpha = expf(g);
     const float beta = bf16_round(1.f / (1.f + expf(-bb)));
-    float* S = state + (((int64_t)slot * HV + hv) * DV) * DK;
-    float4 sv[ROWS];
-#pragma unroll
-    for (int i = 0; i < ROWS; ++i)
-      sv[i] = *reinterpret_cast<const float4*>(S + (int64_t)(warp * ROWS + i) * DK + lane * 4);
-    float ov[ROWS];
+    float* S = S0 + (int64_t)r * DV * DK;
+    float pk[ROWS], pq[ROWS];
 #pragma unroll
     for (int i = 0; i < ROWS; ++i) {
       const float4 s4 = sv[i];
-      float sk = s4.x * kv[0] + s4.y * kv[1] + s4.z * kv[2] + s4.w * kv[3];
-      float sq = s4.x * qv[0] + s4.y * qv[1] + s4.z * qv[2] + s4.w * qv[3];
-      sk = warp_sum(sk);
-      sq = warp_sum(sq);
-      const int row = warp * ROWS + i;
-      const float vrow = s_x[2 * DK + r * DV + row];
-      const float vp = beta * (vrow - alpha * sk);
-      ov[i] = alpha * sq + vp * kq;
+      pk[i] = s4.x * kv[0] + s4.y * kv[1] + s4.z * kv[2] + s4.w * kv[3];
+      pq[i] = s4.x * qv[0] + s4.y * qv[1] + s4.z * qv[2] + s4.w * qv[3];
+    }
+    const float sk = rows16_sum(pk, lane), sq = rows16_sum(pq, lane);
+    const int my_row = lane >> 1;  // the row whose sums this lane now holds
+    const float vrow = s_x[2 * DK + r * DV + warp * ROWS + my_row];
+    const float vp_mine = beta * (vrow - alpha * sk);
+    const float o_mine = alpha * sq + vp_mine * kq;
+#pragma unroll
+    for (int i = 0; i < ROWS; ++i) {
+      const float vp = __shfl_sync(0xffffffffu, vp_mine, 2 * i);
+      const float4 s4 = sv[i];
       float4 n4;
       n4.x = alpha * s4.x + vp * kv[0];
       n4.y = alpha * s4.y + vp * kv[1];
       n4.z = alpha * s4.z + vp * kv[2];
       n4.w = alpha * s4.w + vp * kv[3];
-      *reinterpret_cast<float4*>(S + (int64_t)row * DK + lane * 4) = n4;
+      *reinterpret_cast<float4*>(S + (int64_t)(warp * ROWS + i) * DK + lane * 4) = n4;
     }
     // ---- gated RMSNorm over the DV outputs of this head (o rounded to bf16 first)
-    float ss = 0.f;
-#pragma unroll
-    for (int i = 0; i < ROWS; ++i) {
-      ov[i] = bf16_round(ov[i]);
-      ss += ov[i] * ov[i];
-    }
+    const float o_r = bf16_round(o_mine);
+    float ss = (lane & 1) ? 0.f : o_r * o_r;  // each row once (even lanes)
+    ss = warp_sum(ss);
     if (lane == 0) s_red[warp][r][0] = ss;
     __syncthreads();
     float tot = 0.f;
 #pragma unroll
     for (int w = 0; w < 8; ++w) tot += s_red[w][r][0];
     const float rstd = rsqrtf(tot / (float)DV + eps);
-    if (lane < ROWS) {
-      // lane i of the warp writes row warp*ROWS + i
-      float o_l = 0.f;
-#pragma unroll
-      for (int i = 0; i < ROWS; ++i)
-        if (i == lane) o_l = ov[i];
-      const int row = warp * ROWS + lane;
+    if ((lane & 1) == 0) {
+      const int row = warp * ROWS + my_row;
       const float z = bf2f(xrow[C + hv * DV + row]);
       const float gz = z / (1.f + __expf(-z));
-      y[(int64_t)b * ldy + (int64_t)hv * DV + row] = f2bf(o_l * rstd * bf2f(norm_w[row]) * gz);
+      y[(int64_t)b * ldy + (int64_t)hv * DV + row] = f2bf(o_r * rstd * bf2f(norm_w[row]) * gz);
     }
   }
 }

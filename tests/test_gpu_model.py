@@ -82,6 +82,35 @@ def test_forward_step_parity(pair, name, batch, steps):
     print(name, "fraction within 1e-3:", [round(s[0], 4) for s in stats], "max diff:", [round(s[1], 4) for s in stats])
 
 
+def test_continuous_batching_pattern(pair):
+    """BASELINE configs[2] at small scale: 6 requests with prompt lengths uniform in [20, 60)
+    prefilled in one ragged call, then 12 steps of one token each; every 4 steps two
+    requests are reset and refilled with a new prompt in the same call as the others' decode
+    tokens (a mixed call, which the reference runs as prefill, REF:5027). Exercises slot
+    reuse after reset (stale KV rows past the new length stay in the cache, REF:4809-4818),
+    cache growth and the decode graphs between the mixed calls."""
+    ref, gpu, cfg = pair
+    g = torch.Generator().manual_seed(2024)
+    B, V = 6, cfg.vocab_size
+    rc, gc = ref.new_cache(B, initial_capacity=64), gpu.new_cache(B, initial_capacity=64)
+    rows = [ids(g, int(n), V) for n in torch.randint(20, 60, (B,), generator=g)]
+    stats = []
+    compare(gpu.forward_step([list(r) for r in rows], gc), ref.forward_step([list(r) for r in rows], rc), stats)
+    for step in range(12):
+        refill = [step % B, (step + 3) % B] if step % 4 == 3 else []
+        if refill:
+            rc.reset(refill)
+            gc.reset(refill)
+        inputs = [ids(g, int(torch.randint(20, 60, (1,), generator=g)), V) if s in refill else ids(g, 1, V)
+                  for s in range(B)]
+        compare(gpu.forward_step([list(r) for r in inputs], gc), ref.forward_step([list(r) for r in inputs], rc),
+                stats)
+        assert gc.lengths == rc.lengths and gc.capacity == rc.capacity
+    for i in gc.recurrent:
+        assert gc.recurrent[i].shape == rc.recurrent[i].shape
+    print("continuous batching: fraction within 1e-3:", [round(x[0], 4) for x in stats])
+
+
 def test_decode_graph_replay_matches_eager(pair):
     """A decode replayed from the captured CUDA graph equals an eager decode bit for bit."""
     _, gpu, cfg = pair
