@@ -530,6 +530,39 @@ def run_long(args):
         dist.destroy_process_group()
 
 
+def run_decode_step(args):
+    """The B32 decode step at 1024 tokens of context alone, for a launch list: three rounds of
+    prefill + decode on fresh caches (which the buffer arena places at the same addresses,
+    so the decodes run eagerly, then capture, then replay the decode graph), a fourth
+    prefill, and its decode from the graph bracketed by the CUDA profiler API, so that
+    ``ncu --profile-from-start off`` captures exactly that call's kernels."""
+    import torch
+    from qwen38_inference_b200 import Qwen38
+    from qwen38_inference_b200.config import qwen38_27b
+
+    cfg = qwen38_27b()
+    B, L = args.batch, args.length
+    model = Qwen38(config=cfg, seed=0, device="cuda:0", max_context=max(8192, 2 * L))
+    prefill, decode = make_inputs(cfg.vocab_size, B, L, 0)
+    for _ in range(3):
+        cache = model.new_cache(B, initial_capacity=64)
+        model.forward_step(prefill, cache)
+        model.forward_step(decode, cache)
+        del cache
+    cache = model.new_cache(B, initial_capacity=64)
+    model.forward_step(prefill, cache)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.cudart().cudaProfilerStart()
+    e0.record()
+    model.forward_step(decode, cache)
+    e1.record()
+    torch.cuda.synchronize()
+    torch.cuda.cudart().cudaProfilerStop()
+    print(json.dumps({"op": "decode_step", "batch": B, "context": L, "ms": round(e0.elapsed_time(e1), 3),
+                      "graph_replays": model._engine.replays}), flush=True)
+
+
 def run_op(args):
     """One kernel of the step alone, at the step's shape, on random data: the case the ncu
     captures under profiles/ run (``--op gate_up``: the MLP gate_up GEMM with the SwiGLU
@@ -658,12 +691,15 @@ def main():
     ap.add_argument("--decode-steps", type=int, default=10)
     ap.add_argument("--tp-allreduce", choices=["peer", "nccl"], default="peer",
                     help="long workload, N > 1: decode all-reduce inside the projection kernels (peer) or NCCL")
-    ap.add_argument("--op", choices=["gate_up", "gdn_prefill", "conv_prefill", "attn_prefill"], default=None,
+    ap.add_argument("--op", choices=["gate_up", "gdn_prefill", "conv_prefill", "attn_prefill", "decode_step"],
+                    default=None,
                     help="time one kernel of the step alone (the case the ncu captures run)")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         print("note: fewer than 3 warm-up steps", file=sys.stderr)
-    if args.op:
+    if args.op == "decode_step":
+        run_decode_step(args)
+    elif args.op:
         run_op(args)
     elif args.impl == "reference":
         run_reference(args)

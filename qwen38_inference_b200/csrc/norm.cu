@@ -36,7 +36,9 @@ QW_DEV float block_sum(float v, float* red) {
 
 // mode 0: embedding (src = table row), writes residual copy + normalized
 // mode 1: in-place add-norm (x += r)
-template <int MODE>
+// VEC = 8-column vectors per thread (ceil(H / (8 * kNormThreads))): the row stays in VEC * 8
+// registers, so a narrow row does not pay for the widest one in occupancy
+template <int MODE, int VEC>
 __global__ void __launch_bounds__(kNormThreads) rmsnorm_rows_kernel(
     const __nv_bfloat16* __restrict__ src, int64_t ld_src, const int32_t* __restrict__ rows, int64_t n_table,
     __nv_bfloat16* x, __nv_bfloat16* resid, const __nv_bfloat16* __restrict__ w, __nv_bfloat16* out, int H,
@@ -44,7 +46,7 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_rows_kernel(
   __shared__ float red[33];
   const int row = blockIdx.x;
   const int nvec = H / 8;
-  float v[kMaxVec][8];
+  float v[VEC][8];
   float ss = 0.f;
   const __nv_bfloat16* in_row;
   if constexpr (MODE == 0) {
@@ -56,7 +58,7 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_rows_kernel(
     in_row = src + tok * ld_src;
   }
 #pragma unroll
-  for (int i = 0; i < kMaxVec; ++i) {
+  for (int i = 0; i < VEC; ++i) {
     const int c = (threadIdx.x + i * kNormThreads) * 8;
     if (c < H) {
       if constexpr (MODE == 0) {
@@ -78,7 +80,7 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_rows_kernel(
   const float tot = block_sum(ss, red);
   const float rstd = rsqrtf(tot / (float)H + eps);
 #pragma unroll
-  for (int i = 0; i < kMaxVec; ++i) {
+  for (int i = 0; i < VEC; ++i) {
     const int c = (threadIdx.x + i * kNormThreads) * 8;
     if (c < H) {
       float wf[8], o[8];
@@ -170,9 +172,15 @@ extern "C" int qw_embed_rmsnorm(const int32_t* tokens, int64_t T, const void* ta
   QW_CHECK_ARG(tokens && table && w && resid_out && hidden_out && T > 0 && vocab > 0, QW_ERR_ARG);
   QW_CHECK_ARG(H % 8 == 0 && H <= kNormThreads * kMaxVec * 8, QW_ERR_UNSUPPORTED);
   auto* s = reinterpret_cast<cudaStream_t>(stream);
-  rmsnorm_rows_kernel<0><<<(unsigned)T, kNormThreads, 0, s>>>(
-      static_cast<const __nv_bfloat16*>(table), H, tokens, vocab, nullptr, static_cast<__nv_bfloat16*>(resid_out),
-      static_cast<const __nv_bfloat16*>(w), static_cast<__nv_bfloat16*>(hidden_out), (int)H, eps, device_error_ptr());
+  const int vec = (int)((H + 8 * kNormThreads - 1) / (8 * kNormThreads));
+#define QW_EMBED(V)                                                                                               \
+  rmsnorm_rows_kernel<0, V><<<(unsigned)T, kNormThreads, 0, s>>>(                                               \
+      static_cast<const __nv_bfloat16*>(table), H, tokens, vocab, nullptr, static_cast<__nv_bfloat16*>(resid_out), \
+      static_cast<const __nv_bfloat16*>(w), static_cast<__nv_bfloat16*>(hidden_out), (int)H, eps, device_error_ptr())
+  if (vec <= 1) QW_EMBED(1);
+  else if (vec <= 5) QW_EMBED(5);
+  else QW_EMBED(kMaxVec);
+#undef QW_EMBED
   QW_LAUNCH_CHECK();
   return QW_OK;
 }
@@ -182,9 +190,15 @@ extern "C" int qw_add_rmsnorm(void* x, void* resid, const void* w, int64_t T, in
   QW_CHECK_ARG(x && resid && w && T > 0, QW_ERR_ARG);
   QW_CHECK_ARG(H % 8 == 0 && H <= kNormThreads * kMaxVec * 8, QW_ERR_UNSUPPORTED);
   auto* s = reinterpret_cast<cudaStream_t>(stream);
-  rmsnorm_rows_kernel<1><<<(unsigned)T, kNormThreads, 0, s>>>(
-      nullptr, 0, nullptr, 0, static_cast<__nv_bfloat16*>(x), static_cast<__nv_bfloat16*>(resid),
-      static_cast<const __nv_bfloat16*>(w), nullptr, (int)H, eps, nullptr);
+  const int vec = (int)((H + 8 * kNormThreads - 1) / (8 * kNormThreads));
+#define QW_ADDN(V)                                                                                                \
+  rmsnorm_rows_kernel<1, V><<<(unsigned)T, kNormThreads, 0, s>>>(                                               \
+      nullptr, 0, nullptr, 0, static_cast<__nv_bfloat16*>(x), static_cast<__nv_bfloat16*>(resid),                \
+      static_cast<const __nv_bfloat16*>(w), nullptr, (int)H, eps, nullptr)
+  if (vec <= 1) QW_ADDN(1);
+  else if (vec <= 5) QW_ADDN(5);
+  else QW_ADDN(kMaxVec);
+#undef QW_ADDN
   QW_LAUNCH_CHECK();
   return QW_OK;
 }
