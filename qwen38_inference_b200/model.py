@@ -180,7 +180,9 @@ class _Staging:
         self.events = [None, None]
         self.i = 0
 
-    def upload(self, arr: np.ndarray, device) -> torch.Tensor:
+    def upload(self, arr: np.ndarray, device, dst: torch.Tensor | None = None) -> torch.Tensor:
+        """Copy ``arr`` (int32) to the device without blocking the host: into ``dst`` when
+        given (contiguous int32 of arr.size elements), else into a new device tensor."""
         self.i ^= 1
         k = self.i
         if self.events[k] is not None:
@@ -189,7 +191,7 @@ class _Staging:
             self.bufs[k] = torch.empty(max(arr.size, 4096) * 2, dtype=torch.int32, pin_memory=True)
         host = self.bufs[k][:arr.size]
         host.numpy()[:] = arr
-        dev = torch.empty(arr.size, dtype=torch.int32, device=device)
+        dev = torch.empty(arr.size, dtype=torch.int32, device=device) if dst is None else dst
         dev.copy_(host, non_blocking=True)
         ev = torch.cuda.Event()
         ev.record()
@@ -336,7 +338,10 @@ class Qwen38:
             return
         capacity = math.ceil(min(cache.max_context, max(needed, cache.capacity * 2)) / PAGE) * PAGE
         S = len(cache.lengths)
-        lengths = torch.tensor(cache.lengths, dtype=torch.int32).to(self.device, non_blocking=True)
+        # pinned staging: the host does not wait for earlier work before queuing the growth
+        arr = np.asarray(cache.lengths, dtype=np.int32)
+        staging = getattr(self._engine, "staging", None)
+        lengths = staging.upload(arr, self.device) if staging is not None else torch.from_numpy(arr).to(self.device)
         new_kv = {}
         box = getattr(cache, "_arena_box", None)
         for i, (k_old, v_old) in cache.kv.items():
