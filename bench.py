@@ -586,6 +586,19 @@ def run_op(args):
 
         def launch():
             ops.gemm(x, w, y, out_kind=ops.OUT_SWIGLU)
+    elif args.op in ("qkvz_proj", "down_proj"):
+        # the GDN input projection (CTA-pair kernel) and the MLP down projection (256-row
+        # tiles) of the prefill, bf16 output
+        N, K = (cfg.qkvz_dim + cfg.ba_dim, cfg.hidden_size) if args.op == "qkvz_proj" else \
+            (cfg.hidden_size, cfg.intermediate_size)
+        x = torch.randn(T, K, device=dev, generator=g).bfloat16()
+        w = (torch.randn(N, K, device=dev, generator=g) * 0.02).bfloat16()
+        y = torch.empty(T, N, device=dev, dtype=torch.bfloat16)
+        work = 2.0 * T * N * K
+        unit = "TFLOP/s"
+
+        def launch():
+            ops.gemm(x, w, y)
     elif args.op == "conv_prefill":
         C = cfg.conv_dim
         x = torch.randn(T, cfg.qkvz_dim, device=dev, generator=g).bfloat16()
@@ -691,7 +704,8 @@ def main():
     ap.add_argument("--decode-steps", type=int, default=10)
     ap.add_argument("--tp-allreduce", choices=["peer", "nccl"], default="peer",
                     help="long workload, N > 1: decode all-reduce inside the projection kernels (peer) or NCCL")
-    ap.add_argument("--op", choices=["gate_up", "gdn_prefill", "conv_prefill", "attn_prefill", "decode_step"],
+    ap.add_argument("--op", choices=["gate_up", "qkvz_proj", "down_proj", "gdn_prefill", "conv_prefill",
+                                     "attn_prefill", "decode_step"],
                     default=None,
                     help="time one kernel of the step alone (the case the ncu captures run)")
     args = ap.parse_args()

@@ -378,14 +378,21 @@ __global__ void __launch_bounds__(224, 1) attn_prefill_kernel(
       float mx8[8];
 #pragma unroll
       for (int e = 0; e < 8; ++e) mx8[e] = -INFINITY;
+      // scores stay unscaled (the scale is positive, so the max commutes with it); a block
+      // below the diagonal for every row of the tile needs no mask (CTA-uniform test)
+      if (key0 + L::BN - 1 <= pre + q0) {
 #pragma unroll
-      for (int i = 0; i < 64; ++i) {
-        const float v = (key0 + i <= qpos) ? __uint_as_float(sr[i]) * scale_log2 : -INFINITY;
-        sr[i] = __float_as_uint(v);
-        mx8[i & 7] = fmaxf(mx8[i & 7], v);
+        for (int i = 0; i < 64; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], __uint_as_float(sr[i]));
+      } else {
+#pragma unroll
+        for (int i = 0; i < 64; ++i) {
+          const float v = (key0 + i <= qpos) ? __uint_as_float(sr[i]) : -INFINITY;
+          sr[i] = __float_as_uint(v);
+          mx8[i & 7] = fmaxf(mx8[i & 7], v);
+        }
       }
-      const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
-                             fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+      const float mx = scale_log2 * fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                                          fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
       // the running max of a row is raised only when the block's max exceeds it by more
       // than 8; rows of O are rescaled in TMEM by the whole warp (factor 1 on rows whose
       // max stayed), once P V_{j-1} has completed
@@ -422,7 +429,8 @@ __global__ void __launch_bounds__(224, 1) attn_prefill_kernel(
       uint32_t pk[32];  // bf16 pairs (keys 2c, 2c + 1) of this row
 #pragma unroll
       for (int c = 0; c < 32; ++c) {
-        const float p0 = exp2f(__uint_as_float(sr[2 * c]) - mu), p1 = exp2f(__uint_as_float(sr[2 * c + 1]) - mu);
+        const float p0 = ex2_ftz(fmaf(__uint_as_float(sr[2 * c]), scale_log2, -mu));
+        const float p1 = ex2_ftz(fmaf(__uint_as_float(sr[2 * c + 1]), scale_log2, -mu));
         ps8[(2 * c) & 7] += p0;
         ps8[(2 * c + 1) & 7] += p1;
         pk[c] = pack_bf16x2(p0, p1);
@@ -610,9 +618,9 @@ __global__ void __launch_bounds__(64) attn_decode_kernel(
       mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
       mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
       const float mn = fmaxf(m_j[j], mx);  // finite: key0 is always a valid key
-      alpha[j] = exp2f(m_j[j] - mn);
-      pr[j] = exp2f(x[j] - mn);
-      pr[2 + j] = exp2f(x[2 + j] - mn);
+      alpha[j] = ex2_ftz(m_j[j] - mn);
+      pr[j] = ex2_ftz(x[j] - mn);
+      pr[2 + j] = ex2_ftz(x[2 + j] - mn);
       float ps = pr[j] + pr[2 + j];
       ps += __shfl_xor_sync(0xffffffffu, ps, 4);
       ps += __shfl_xor_sync(0xffffffffu, ps, 8);

@@ -45,6 +45,14 @@ QW_DEV uint32_t pack_bf16x2(float lo, float hi) {
 // barrier `id` (1..15) among `n` threads (a multiple of 32) of the CTA
 QW_DEV void named_bar_sync(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
 
+// 2^x with the approximate hardware exponential, subnormal results flushed to zero
+// (ex2.approx.ftz.f32; 2^-inf = 0): softmax weights in the log2 domain
+QW_DEV float ex2_ftz(float x) {
+  float r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+
 // approximate reciprocal (rcp.approx.ftz.f32: relative error below 2^-23; 1/inf = 0)
 QW_DEV float rcp_approx(float x) {
   float r;
