@@ -172,19 +172,23 @@ struct AttnTc {
   static constexpr int QB = BM * 128;                   // bytes of one Q box
   static constexpr int KVB = BN * 128;                  // bytes of one K or V box
   static constexpr int Q = 0;
-  static constexpr int KST = 3;                         // K stages
+  static constexpr int KST = 2;                         // K stages
   static constexpr int K0 = Q + NB * QB;                // KST stages x NB boxes
   static constexpr int V0 = K0 + KST * NB * KVB;        // 2 stages x NB boxes
   static constexpr int BAR = V0 + 2 * NB * KVB;
-  static constexpr int SMEM = BAR + 256 + 1024;         // + slack to align the base to 1024
-  static constexpr int THREADS = 224;
+  // exchange of the two softmax halves: block maxima [2 parities][2 halves][BM], then the
+  // row sums [2 halves][BM] at the end
+  static constexpr int XMAX = BAR + 256;
+  static constexpr int XSUM = XMAX + 2 * 2 * BM * 4;
+  static constexpr int SMEM = XSUM + 2 * BM * 4 + 1024;  // + slack to align the base to 1024
+  static constexpr int THREADS = 352;
   static constexpr int TMEM_O = 2 * BN;                 // S buffers at TMEM columns 0 and 64
   static constexpr int TMEM_P = TMEM_O + D;             // P buffers: 32 columns (64 bf16) each
   static constexpr uint32_t TMEM_COLS = (TMEM_P + BN <= 256) ? 256 : 512;
 };
 
 template <int D>
-__global__ void __launch_bounds__(224, 1) attn_prefill_kernel(
+__global__ void __launch_bounds__(352, 1) attn_prefill_kernel(
     const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
     const __grid_constant__ CUtensorMap tmV, const PrefillTile* __restrict__ tiles, const int32_t* __restrict__ cu,
     const int32_t* __restrict__ prefix, const int32_t* __restrict__ kv_base, const __nv_bfloat16* __restrict__ qkv,
@@ -207,7 +211,8 @@ __global__ void __launch_bounds__(224, 1) attn_prefill_kernel(
   uint64_t* mma_done = bars + 19;
   uint64_t* q_free = bars + 20;  // the last S MMA has read Q
   uint64_t* g_full = bars + 21;  // gate tile landed in the Q buffer
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 22);
+  uint64_t* x_full = bars + 22;  // [2] both softmax halves have published a block's maxima
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 24);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int h = blockIdx.x, kvh = h / (nq / nkv);
@@ -239,9 +244,10 @@ __global__ void __launch_bounds__(224, 1) attn_prefill_kernel(
       mbar_init(&v_full[i], 1);
       mbar_init(&v_empty[i], 1);
       mbar_init(&s_full[i], 1);
-      mbar_init(&s_empty[i], 128);
-      mbar_init(&p_full[i], 128);
+      mbar_init(&s_empty[i], 256);
+      mbar_init(&p_full[i], 256);
       mbar_init(&p_empty[i], 1);
+      mbar_init(&x_full[i], 256);
     }
     mbar_init(mma_done, 1);
     mbar_init(q_free, 1);
@@ -352,12 +358,20 @@ __global__ void __launch_bounds__(224, 1) attn_prefill_kernel(
     }
     __syncwarp();
   } else {
-    // ---------------------------------------------------------------- softmax + epilogue (warps 2-5)
-    // tcgen05.ld/st are warp-collective: every decision that guards them is made per warp
-    // (__any_sync / __all_sync), so the 32 lanes always execute them together.
+    // ---------------------------------------------------------------- softmax + epilogue (warps 2-5, 7-10)
+    // Two warps per TMEM lane quarter: warps 2-5 own the first 32 keys of every S block and
+    // the first half of O's columns, warps 7-10 the rest. A row's block maximum is the max of
+    // both halves (published in shared memory behind the x_full mbarrier), so both keep the
+    // same running max and rescale decisions; each keeps the sum of its half of P, and the
+    // two sums are added in the epilogue. tcgen05.ld/st are warp-collective: every decision
+    // that guards them is made per warp (__any_sync / __all_sync).
+    const int hf = warp >= 7 ? 1 : 0;
     const int row = 32 * (warp & 3) + lane;  // TMEM lane = query row of the tile
     const uint32_t trow = tmem + ((uint32_t)(32 * (warp & 3)) << 16);
     const int qpos = pre + q0 + row;  // keys at positions <= qpos are visible
+    float* xmax = reinterpret_cast<float*>(smem + L::XMAX);
+    float* xsum = reinterpret_cast<float*>(smem + L::XSUM);
+    constexpr int OC = D / 2;  // O columns of a half
     float m_used = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < nblk; ++j) {
@@ -368,31 +382,37 @@ __global__ void __launch_bounds__(224, 1) attn_prefill_kernel(
         break;
       }
       tc_fence_after();
-      uint32_t sr[64];
-      tmem_ld_32x32b_x32(trow + s * L::BN, sr);
-      tmem_ld_32x32b_x32(trow + s * L::BN + 32, sr + 32);
+      uint32_t sr[32];
+      tmem_ld_32x32b_x32(trow + s * L::BN + hf * 32, sr);
       tmem_ld_wait();
       tc_fence_before();
       mbar_arrive(&s_empty[s]);
-      const int key0 = (jb + j) * L::BN;
+      const int key0 = (jb + j) * L::BN + hf * 32;
       float mx8[8];
 #pragma unroll
       for (int e = 0; e < 8; ++e) mx8[e] = -INFINITY;
       // scores stay unscaled (the scale is positive, so the max commutes with it); a block
       // below the diagonal for every row of the tile needs no mask (CTA-uniform test)
-      if (key0 + L::BN - 1 <= pre + q0) {
+      if ((jb + j) * L::BN + L::BN - 1 <= pre + q0) {
 #pragma unroll
-        for (int i = 0; i < 64; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], __uint_as_float(sr[i]));
+        for (int i = 0; i < 32; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], __uint_as_float(sr[i]));
       } else {
 #pragma unroll
-        for (int i = 0; i < 64; ++i) {
+        for (int i = 0; i < 32; ++i) {
           const float v = (key0 + i <= qpos) ? __uint_as_float(sr[i]) : -INFINITY;
           sr[i] = __float_as_uint(v);
           mx8[i & 7] = fmaxf(mx8[i & 7], v);
         }
       }
-      const float mx = scale_log2 * fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
-                                          fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+      const float mine = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                               fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+      xmax[(s * 2 + hf) * L::BM + row] = mine;
+      mbar_arrive(&x_full[s]);
+      if (!__all_sync(0xffffffffu, mbar_wait(&x_full[s], ph, abort_flag, err, CODE))) {
+        ok = false;
+        break;
+      }
+      const float mx = scale_log2 * fmaxf(mine, xmax[(s * 2 + (hf ^ 1)) * L::BM + row]);
       // the running max of a row is raised only when the block's max exceeds it by more
       // than 8; rows of O are rescaled in TMEM by the whole warp (factor 1 on rows whose
       // max stayed), once P V_{j-1} has completed
@@ -407,7 +427,7 @@ __global__ void __launch_bounds__(224, 1) attn_prefill_kernel(
         tc_fence_after();
         const float alpha = (grow && j > 0) ? exp2f(m_used - m_new) : 1.f;
 #pragma unroll 1
-        for (int c0 = 0; c0 < D; c0 += 32) {
+        for (int c0 = hf * OC; c0 < (hf + 1) * OC; c0 += 32) {
           uint32_t r[32];
           tmem_ld_32x32b_x32(trow + L::TMEM_O + c0, r);
           tmem_ld_wait();
@@ -426,16 +446,16 @@ __global__ void __launch_bounds__(224, 1) attn_prefill_kernel(
         break;
       }
       float ps8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      uint32_t pk[32];  // bf16 pairs (keys 2c, 2c + 1) of this row
+      uint32_t pk[16];  // bf16 pairs (keys 2c, 2c + 1) of this half of the row
 #pragma unroll
-      for (int c = 0; c < 32; ++c) {
+      for (int c = 0; c < 16; ++c) {
         const float p0 = ex2_ftz(fmaf(__uint_as_float(sr[2 * c]), scale_log2, -mu));
         const float p1 = ex2_ftz(fmaf(__uint_as_float(sr[2 * c + 1]), scale_log2, -mu));
         ps8[(2 * c) & 7] += p0;
         ps8[(2 * c + 1) & 7] += p1;
         pk[c] = pack_bf16x2(p0, p1);
       }
-      tmem_st_32x32b_x32(trow + L::TMEM_P + s * (L::BN / 2), pk);
+      tmem_st_32x32b_x16(trow + L::TMEM_P + s * (L::BN / 2) + hf * 16, pk);
       tmem_st_wait();
       l += ((ps8[0] + ps8[1]) + (ps8[2] + ps8[3])) + ((ps8[4] + ps8[5]) + (ps8[6] + ps8[7]));
       tc_fence_before();  // P (and any O rescale) in TMEM before the P V issue
@@ -447,6 +467,10 @@ __global__ void __launch_bounds__(224, 1) attn_prefill_kernel(
       ok = __all_sync(0xffffffffu, mbar_wait(&p_empty[jp & 1], (jp >> 1) & 1, abort_flag, err, CODE));
     }
     if (ok && nsplit == 1) ok = __all_sync(0xffffffffu, mbar_wait(g_full, 0, abort_flag, err, CODE));
+    // the row's sum over both halves (every softmax warp reaches this barrier once)
+    xsum[hf * L::BM + row] = l;
+    named_bar_sync(2, 256);
+    l = xsum[row] + xsum[L::BM + row];
     __syncwarp();
     tc_fence_after();
     const bool valid = ok && q0 + row < n;
@@ -458,7 +482,7 @@ __global__ void __launch_bounds__(224, 1) attn_prefill_kernel(
       // have m = -inf and l = 0 and are ignored by the merge
       const int64_t slot = ((int64_t)t * nq + h) * nsplit + split;
 #pragma unroll 1
-      for (int c0 = 0; c0 < D; c0 += 32) {
+      for (int c0 = hf * OC; c0 < (hf + 1) * OC; c0 += 32) {
         uint32_t r[32];
         if (nblk > 0) {
           tmem_ld_32x32b_x32(trow + L::TMEM_O + c0, r);
@@ -475,13 +499,13 @@ __global__ void __launch_bounds__(224, 1) attn_prefill_kernel(
                                  __uint_as_float(r[4 * v + 2]), __uint_as_float(r[4 * v + 3]));
         }
       }
-      if (valid) {
+      if (valid && hf == 0) {
         part_ml[slot * 2 + 0] = nblk > 0 ? m_used : -INFINITY;
         part_ml[slot * 2 + 1] = nblk > 0 ? l : 0.f;
       }
     }
 #pragma unroll 1
-    for (int c0 = 0; c0 < D && nsplit == 1; c0 += 32) {
+    for (int c0 = hf * OC; c0 < (hf + 1) * OC && nsplit == 1; c0 += 32) {
       uint32_t r[32];
       tmem_ld_32x32b_x32(trow + L::TMEM_O + c0, r);
       tmem_ld_wait();
