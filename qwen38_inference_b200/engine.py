@@ -134,7 +134,10 @@ class Engine:
         ops.embed_rmsnorm(md["tokens"], m.embedding, m.layers[0]["input_norm"], resid, hidden, eps)
         nq, nkv, d = c.num_attention_heads, c.num_key_value_heads, c.head_dim
         Hk, HV, dk, dv = c.linear_num_key_heads, c.linear_num_value_heads, c.linear_key_head_dim, c.linear_value_head_dim
-        big = max(c.qkv_dim, c.qkvz_dim + c.ba_dim)
+        # row stride of the projection buffer: a multiple of 8 elements (16 bytes) for the
+        # vector and TMA reads of the kernels that take its column blocks (an 8-way tensor-
+        # parallel rank's qkvz|ba is 2060 wide)
+        big = -(-max(c.qkv_dim, c.qkvz_dim + c.ba_dim) // 8) * 8
         proj = torch.empty(T, big, dtype=BF16, device=dev)
         mix = torch.empty(T, max(c.attn_out_dim, c.gdn_v_dim), dtype=BF16, device=dev)
         act = torch.empty(T, c.intermediate_size, dtype=BF16, device=dev)
