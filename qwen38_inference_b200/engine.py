@@ -25,6 +25,14 @@ from .model import _Staging, build_metadata
 BF16 = torch.bfloat16
 
 
+def proj_stride(c) -> int:
+    """Row stride (elements) of the buffer that holds a layer's input projection (attention
+    qkv or GDN qkvz|ba): the wider of the two, rounded up to 8 elements (16 bytes) for the
+    vector and TMA reads of the kernels that take its column blocks (an 8-way tensor-parallel
+    rank's qkvz|ba is 2060 wide)."""
+    return -(-max(c.qkv_dim, c.qkvz_dim + c.ba_dim) // 8) * 8
+
+
 class Engine:
     def __init__(self, model):
         self.m = model
@@ -134,10 +142,7 @@ class Engine:
         ops.embed_rmsnorm(md["tokens"], m.embedding, m.layers[0]["input_norm"], resid, hidden, eps)
         nq, nkv, d = c.num_attention_heads, c.num_key_value_heads, c.head_dim
         Hk, HV, dk, dv = c.linear_num_key_heads, c.linear_num_value_heads, c.linear_key_head_dim, c.linear_value_head_dim
-        # row stride of the projection buffer: a multiple of 8 elements (16 bytes) for the
-        # vector and TMA reads of the kernels that take its column blocks (an 8-way tensor-
-        # parallel rank's qkvz|ba is 2060 wide)
-        big = -(-max(c.qkv_dim, c.qkvz_dim + c.ba_dim) // 8) * 8
+        big = proj_stride(c)
         proj = torch.empty(T, big, dtype=BF16, device=dev)
         mix = torch.empty(T, max(c.attn_out_dim, c.gdn_v_dim), dtype=BF16, device=dev)
         act = torch.empty(T, c.intermediate_size, dtype=BF16, device=dev)

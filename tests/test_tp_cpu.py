@@ -40,6 +40,23 @@ def test_27b_shard_geometry():
             check_shardable(c, bad)
 
 
+def test_per_rank_leading_dimensions_are_16_byte_multiples():
+    """Every buffer the engine hands to a kernel as rows of a wider matrix has a row stride
+    of a multiple of 8 bf16 elements at 1, 2, 4 and 8 ranks (the conv, GDN and attention
+    kernels read column blocks of the projection buffer with 16-byte and TMA loads)."""
+    from qwen38_inference_b200.engine import proj_stride
+    c = qwen38_27b()
+    for world in (1, 2, 4, 8):
+        lc = shard_config(c, world)
+        stride = proj_stride(lc)
+        assert stride % 8 == 0 and stride >= lc.qkv_dim and stride >= lc.qkvz_dim + lc.ba_dim
+        for width in (lc.attn_out_dim, lc.gdn_v_dim, lc.intermediate_size, lc.gdn_qk_dim, lc.conv_dim,
+                      lc.hidden_size, c.vocab_size // world):
+            assert width % 8 == 0, (world, width)
+    assert proj_stride(shard_config(c, 8)) == 2064  # 2048 qkvz + 12 ba, rounded up
+    assert proj_stride(c) == 16480  # one GPU: unchanged
+
+
 def _shards(cfg, world, seed=3):
     full = random_weights(cfg, seed, dtype=torch.float32)
     per_rank = [{k: shard_tensor(k, v, ShardSpec(r, world, cfg)) for k, v in full.items()} for r in range(world)]
