@@ -60,6 +60,28 @@ QW_DEV float rcp_approx(float x) {
   return r;
 }
 
+// fp32 pairs in one 64-bit register (low float first) and the sm_100 packed arithmetic on
+// them: one instruction for both lanes, each rounded as the scalar operation
+QW_DEV unsigned long long f2_pack(float lo, float hi) {
+  return ((unsigned long long)__float_as_uint(hi) << 32) | __float_as_uint(lo);
+}
+QW_DEV float f2_lo(unsigned long long v) { return __uint_as_float((uint32_t)v); }
+QW_DEV float f2_hi(unsigned long long v) { return __uint_as_float((uint32_t)(v >> 32)); }
+QW_DEV unsigned long long f2_add(unsigned long long a, unsigned long long b) {
+  unsigned long long d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+QW_DEV unsigned long long f2_mul(unsigned long long a, unsigned long long b) {
+  unsigned long long d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+// a bf16 pair (packed) as an fp32 pair: exact bit shifts
+QW_DEV unsigned long long bf16x2_to_f2(uint32_t u) {
+  return ((unsigned long long)(u & 0xffff0000u) << 32) | (u << 16);
+}
+
 // the two bf16 of a packed pair as floats (low half first): exact bit shifts
 QW_DEV float2 bf16x2_to_float2(uint32_t u) {
   return make_float2(__uint_as_float(u << 16), __uint_as_float(u & 0xffff0000u));

@@ -120,21 +120,24 @@ __global__ void __launch_bounds__(256) conv_prefill_kernel(
       __nv_bfloat162 h0 = *reinterpret_cast<const __nv_bfloat162*>(&sx[j0][c]);
       __nv_bfloat162 h1 = *reinterpret_cast<const __nv_bfloat162*>(&sx[j0 + 1][c]);
       __nv_bfloat162 h2 = *reinterpret_cast<const __nv_bfloat162*>(&sx[j0 + 2][c]);
+      // the channel pair's sums and silu run on fp32 pairs (sm_100 f32x2 arithmetic, each
+      // lane rounded as its scalar operation); exp(-a) = 2^(-a log2 e)
+      const unsigned long long neg_log2e = f2_pack(-1.4426950408889634f, -1.4426950408889634f);
+      const unsigned long long one = f2_pack(1.0f, 1.0f);
 #pragma unroll
       for (int jj = 0; jj < BT / 4; ++jj) {
         const int j = j0 + jj;
         const __nv_bfloat162 xv = *reinterpret_cast<const __nv_bfloat162*>(&sx[j + HIST][c]);
-        const float2 p0 = __bfloat1622float2(__hmul2(h0, wv[0]));
-        const float2 p1 = __bfloat1622float2(__hmul2(h1, wv[1]));
-        const float2 p2 = __bfloat1622float2(__hmul2(h2, wv[2]));
-        const float2 p3 = __bfloat1622float2(__hmul2(xv, wv[3]));
-        float a0 = p0.x, a1 = p0.y;
-        a0 += p1.x; a1 += p1.y;
-        a0 += p2.x; a1 += p2.y;
-        a0 += p3.x; a1 += p3.y;
-        const float y0 = a0 * rcp_approx(1.0f + __expf(-a0));
-        const float y1 = a1 * rcp_approx(1.0f + __expf(-a1));
-        *reinterpret_cast<__nv_bfloat162*>(&sy[j][c]) = __floats2bfloat162_rn(y0, y1);
+        const __nv_bfloat162 q0 = __hmul2(h0, wv[0]), q1 = __hmul2(h1, wv[1]);
+        const __nv_bfloat162 q2 = __hmul2(h2, wv[2]), q3 = __hmul2(xv, wv[3]);
+        unsigned long long a = bf16x2_to_f2(*reinterpret_cast<const uint32_t*>(&q0));
+        a = f2_add(a, bf16x2_to_f2(*reinterpret_cast<const uint32_t*>(&q1)));
+        a = f2_add(a, bf16x2_to_f2(*reinterpret_cast<const uint32_t*>(&q2)));
+        a = f2_add(a, bf16x2_to_f2(*reinterpret_cast<const uint32_t*>(&q3)));
+        const unsigned long long t = f2_mul(a, neg_log2e);
+        const unsigned long long d = f2_add(f2_pack(ex2_ftz(f2_lo(t)), ex2_ftz(f2_hi(t))), one);
+        const unsigned long long y = f2_mul(a, f2_pack(rcp_approx(f2_lo(d)), rcp_approx(f2_hi(d))));
+        *reinterpret_cast<__nv_bfloat162*>(&sy[j][c]) = __floats2bfloat162_rn(f2_lo(y), f2_hi(y));
         h0 = h1;
         h1 = h2;
         h2 = xv;
