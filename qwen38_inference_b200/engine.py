@@ -53,7 +53,9 @@ class Engine:
         return {k: dev[o:o + n] for k, (o, n) in offs.items()}
 
     # ------------------------------------------------------------------ entry
-    def forward(self, flat, slots, prefixes, lens, cache, is_decode, return_all_logits):
+    def forward(self, flat, slots, prefixes, lens, cache, is_decode, return_all_logits, dev_tokens=None):
+        """One forward_step; ``dev_tokens`` (a device integer tensor of the call's T ids) replaces
+        the host ids of ``flat`` when the caller's ids are already on the device."""
         packed, offs, T = build_metadata(slots, prefixes, lens, cache.capacity)
         tokens = np.asarray(flat, dtype=np.int32)
         arr = np.concatenate([tokens, packed])
@@ -69,8 +71,10 @@ class Engine:
         small_prefill = T <= self.GRAPH_MAX_PREFILL_T and self.m.tp is None
         if self.use_graphs and not return_all_logits and (is_decode or small_prefill):
             shape = ("decode", B, T) if is_decode else ("prefill", B, T, tuple(lens), pf_splits)
-            return self._graph_call(shape, arr, offs, T, B, max(lens), cache, is_decode, pf_splits)
+            return self._graph_call(shape, arr, offs, T, B, max(lens), cache, is_decode, pf_splits, dev_tokens)
         dev = self.staging.upload(arr, self.dev)
+        if dev_tokens is not None:
+            dev[:T].copy_(dev_tokens)
         md = self._meta_views(dev[T:], offs)
         md["tokens"] = dev[:T]
         return self._run(md, T, B, max(lens), cache, is_decode, return_all_logits, pf_splits=pf_splits)
@@ -81,7 +85,7 @@ class Engine:
     # more host time than the GPU spends (chunked prefill of one long request, 512 tokens a call)
     GRAPH_MAX_PREFILL_T = 2048
 
-    def _graph_call(self, shape, arr, offs, T, B, max_len, cache, is_decode, pf_splits):
+    def _graph_call(self, shape, arr, offs, T, B, max_len, cache, is_decode, pf_splits, dev_tokens=None):
         """Run through a CUDA graph keyed by the call's launch shape and the addresses of every
         cache buffer. A graph bakes in its pointers and grid sizes, so any call with that shape
         on a cache whose buffers sit at exactly those addresses with the same capacity and slot
@@ -105,11 +109,15 @@ class Engine:
             # through pinned memory, so the host queues the replay while earlier work (the
             # call's KV growth) still runs instead of waiting for it in a pageable copy
             self.staging.upload(arr, self.dev, dst=ent["input"])
+            if dev_tokens is not None:
+                ent["input"][:T].copy_(dev_tokens)
             ent["graph"].replay()
             self.replays += 1
             ops.LAUNCHES[0] += ent["launches"]
             return ent["out"].clone()
         dev_in = self.staging.upload(arr, self.dev)  # kept by the graph of this key
+        if dev_tokens is not None:
+            dev_in[:T].copy_(dev_tokens)
         md = self._meta_views(dev_in[T:], offs)
         md["tokens"] = dev_in[:T]
         out = self._run(md, T, B, max_len, cache, is_decode, False, self.ws, pf_splits=pf_splits)

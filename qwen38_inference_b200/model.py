@@ -415,6 +415,16 @@ class Qwen38:
         active = list(range(len(rows)))
         logits = torch.stack([last_logits[i] for i in active])
         while active:
+            # decode steps that can run before the host must look at a token: every active
+            # request's remaining context (a step past it would raise) and the most tokens any
+            # request still needs
+            room = min(cache.max_context - cache.lengths[s] for s in active)
+            need = (max(max_new_tokens - len(output[s]) for s in active) if max_new_tokens is not None
+                    else math.inf)
+            w = min(self.GEN_WINDOW, room, need)
+            if w > 1:
+                active, logits = self._decode_window(w, need, active, logits, cache, output, eos, max_new_tokens)
+                continue
             tokens = logits.argmax(-1).tolist()
             next_active, next_inputs = [], []
             for slot, token in zip(active, tokens):
@@ -430,6 +440,54 @@ class Qwen38:
             if active:
                 logits = self.forward_step(next_inputs, cache, request_indices=active)
         return output[0] if single else output
+
+    # decode steps queued back to back inside generate between two host reads of the tokens
+    GEN_WINDOW = 8
+
+    def _decode_window(self, w, need, active, logits, cache, output, eos, max_new_tokens):
+        """``w`` greedy steps of every request in ``active`` with the tokens kept on the device
+        (each step's argmax is the next step's input), then one host read of all ``w`` token
+        rows, replayed through REF's per-step bookkeeping (REF:5133-5146): a request stops at
+        EOS or at max_new_tokens and its later tokens are dropped. The cache belongs to this
+        generate call, so the steps a finished request ran past its end change nothing the
+        caller sees; w never exceeds any request's remaining context, so REF's exhaustion
+        error can only arise at a window boundary, where the step-by-step loop raises it.
+        Returns the requests still generating and their logits."""
+        toks = []
+        for j in range(w):
+            t = logits.argmax(-1)
+            toks.append(t)
+            if j + 1 < w or w < need:  # the last step feeds no one when every request is done
+                logits = self._decode_device_tokens(t, cache, active)
+        rows = torch.stack(toks).tolist()  # the window's only device -> host read
+        pos = {s: k for k, s in enumerate(active)}
+        alive = list(active)
+        for j in range(w):
+            nxt = []
+            for s in alive:
+                output[s].append(rows[j][pos[s]])
+                if rows[j][pos[s]] in eos or (max_new_tokens is not None and len(output[s]) >= max_new_tokens):
+                    continue
+                nxt.append(s)
+            alive = nxt
+            if not alive:
+                break
+        if alive and len(alive) < len(active):
+            logits = logits[torch.tensor([pos[s] for s in alive], device=logits.device)]
+        return alive, logits
+
+    def _decode_device_tokens(self, tokens, cache, slots):
+        """forward_step for one token per slot whose ids are already on the device (an argmax
+        over the vocabulary, so always valid): the engine copies them into its input on the
+        device instead of uploading host ids."""
+        prefixes = [cache.lengths[s] for s in slots]
+        lengths = [p + 1 for p in prefixes]
+        self._reserve(cache, max(lengths))
+        n = len(slots)
+        logits = self._engine.forward([0] * n, slots, prefixes, [1] * n, cache, True, False, dev_tokens=tokens)
+        for slot, length in zip(slots, lengths):
+            cache.lengths[slot] = length
+        return logits
 
 
 def forward_step(model, input_ids, kv_cache, **kwargs):

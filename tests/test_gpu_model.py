@@ -167,6 +167,23 @@ def test_generate_matches_oracle(pair):
     assert a[0][0] == b[0][0] and a[1][0] == b[1][0]
 
 
+def test_generate_window_matches_stepwise(pair, monkeypatch):
+    """generate's device-token windows give the step-by-step loop's tokens on the GPU, also
+    when a request stops early (the window keeps decoding it until its end; per-row decode
+    results do not depend on which other requests share the call)."""
+    _, gpu, cfg = pair
+    prompts = [[5, 6, 7, 8, 9], [100, 3], [42] * 70]
+    kw = dict(max_new_tokens=12, eos_token_ids=[cfg.vocab_size - 1])
+    monkeypatch.setattr(type(gpu), "GEN_WINDOW", 1)
+    ref = gpu.generate(prompts, **kw)
+    eos = ref[0][3]  # request 0 stops at its fourth token at the latest
+    ref_eos = gpu.generate(prompts, max_new_tokens=12, eos_token_ids=[eos])
+    monkeypatch.setattr(type(gpu), "GEN_WINDOW", 8)
+    assert gpu.generate(prompts, **kw) == ref
+    got = gpu.generate(prompts, max_new_tokens=12, eos_token_ids=[eos])
+    assert got == ref_eos and len(got[0]) <= 4
+
+
 def test_errors_before_mutation(pair):
     _, gpu, cfg = pair
     c = gpu.new_cache(2, initial_capacity=64)

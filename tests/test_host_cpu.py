@@ -84,11 +84,18 @@ class _StubEngine:
     def __init__(self, vocab):
         self.vocab = vocab
         self.calls = []
+        self.next_token = None  # f(last id of a row) = the argmax of its logits; None: all zero
 
-    def forward(self, flat, slots, prefixes, lens, cache, is_decode, all_logits):
-        self.calls.append(dict(slots=list(slots), prefixes=list(prefixes), lens=list(lens), is_decode=is_decode))
+    def forward(self, flat, slots, prefixes, lens, cache, is_decode, all_logits, dev_tokens=None):
+        self.calls.append(dict(slots=list(slots), prefixes=list(prefixes), lens=list(lens), is_decode=is_decode,
+                               device_tokens=dev_tokens is not None))
         n = sum(lens) if all_logits else len(lens)
-        return torch.zeros(n, self.vocab)
+        out = torch.zeros(n, self.vocab)
+        if self.next_token is not None and not all_logits:
+            ids = dev_tokens.tolist() if dev_tokens is not None else flat
+            for r, last in enumerate(np.cumsum(lens) - 1):
+                out[r, self.next_token(ids[last])] = 1.0
+        return out
 
 
 def _cpu_kv_grow(src_k, src_v, dst_k, dst_v, lengths, S, old_cap, new_cap):
@@ -160,6 +167,43 @@ def test_new_cache_and_growth_policy(host_model):
     assert c.capacity == 1024 or c.capacity == math.ceil(min(1000, max(1000, 1280)) / 64) * 64
     with pytest.raises(ValueError):
         m._reserve(c, 1001)
+
+
+def test_generate_window_matches_stepwise(host_model, monkeypatch):
+    """generate's device-token windows (several decode steps between host reads) produce the
+    step-by-step loop's tokens (window 1 is REF's loop, REF:5133-5146) through EOS inside a
+    window, max_new_tokens and context exhaustion, with a stub whose next token is a fixed
+    function of the last one (+2 mod 64: odd EOS ids are never reached from even ids)."""
+    m = host_model
+    m._engine.next_token = lambda t: (t + 2) % 64
+
+    def run(window, *args, **kw):
+        monkeypatch.setattr(M.Qwen38, "GEN_WINDOW", window)
+        m._engine.calls.clear()
+        try:
+            out = m.generate(*args, **kw)
+        except RuntimeError as e:
+            out = ("RuntimeError", str(e))
+        return out, [c["device_tokens"] for c in m._engine.calls]
+
+    cases = [
+        # request 0 meets EOS (8 = 2 + 6) at its third token, inside the first window
+        (([[2], [10, 4], [20, 20, 20]],), dict(max_new_tokens=11, eos_token_ids=[8])),
+        (([[2], [11]],), dict(max_new_tokens=3, eos_token_ids=[1])),
+        (([[2, 4]],), dict(max_new_tokens=9, eos_token_ids=[1])),
+        # no EOS reachable: runs until the context (1000) is exhausted
+        (([[2] * 990, [4] * 3],), dict(eos_token_ids=[1])),
+        (([[2] * 990],), dict(eos_token_ids=[1], max_new_tokens=10)),
+    ]
+    for args, kw in cases:
+        want, step_calls = run(1, *args, **kw)
+        got, win_calls = run(8, *args, **kw)
+        assert got == want, (args, kw)
+        assert not any(step_calls)
+        assert any(win_calls) or kw.get("max_new_tokens", 2) <= 1
+    assert run(8, [[2], [10, 4], [20, 20, 20]], max_new_tokens=11, eos_token_ids=[8])[0][0] == [4, 6, 8]
+    assert run(8, [[2] * 990], eos_token_ids=[1])[0] == (
+        "RuntimeError", "Request 0 exhausted context without EOS; produced 11 tokens")
 
 
 def test_forward_step_validation_before_mutation(host_model):
