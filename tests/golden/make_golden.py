@@ -2,8 +2,8 @@
 
 Runs reference/qwen38_inference.py's kernels under the Triton CPU interpreter
 (``TRITON_INTERPRET=1``) on small seeded inputs and writes ``tests/golden/*.pt``. This
-needs ``/root/reference`` (this container only); the fixtures it writes are committed and
-the tests read only the fixtures.
+needs a checkout of the reference (``--reference``); the fixtures it writes are committed
+and the tests read only the fixtures.
 
 Two fixes are applied to the stock interpreter so that it follows GPU semantics:
   * it stores bfloat16 as raw uint16 and applies numpy arithmetic to the bit patterns,
@@ -19,7 +19,7 @@ The reference's wrappers refuse CPU tensors in three places (eligibility check o
 decode conv, PDL capability probe, SM-count query); those host checks are bypassed, the
 kernels and their launch code are the reference's.
 
-Usage: python tests/golden/make_golden.py [--reference /root/reference]
+Usage: python tests/golden/make_golden.py --reference <reference checkout>
 """
 from __future__ import annotations
 
@@ -115,7 +115,7 @@ def bf(t):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True, help="directory of the reference checkout")
     args = ap.parse_args()
     _patch_interpreter()
     R = _load_reference(Path(args.reference))
