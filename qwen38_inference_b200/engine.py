@@ -46,8 +46,11 @@ class Engine:
 
     # ------------------------------------------------------------------ helpers
     def _decode_splits(self, capacity):
-        # key splits of decode attention: one per 128 slots of capacity (CTAs of 2 warps)
-        return int(min(128, max(1, (capacity + 127) // 128)))
+        """Key splits of decode attention: one per 512 slots of capacity, at most 128. A CTA of
+        2 warps then streams up to 256 keys per warp, long enough to hide its start-up (27B
+        decode steps at B32/1024, B4/8192 and B64/512 tokens of context measured 0.2-0.7 ms
+        faster than with 128-slot splits; equal at B1/16384)."""
+        return int(min(128, max(1, (capacity + 511) // 512)))
 
     def _meta_views(self, dev, offs):
         return {k: dev[o:o + n] for k, (o, n) in offs.items()}
