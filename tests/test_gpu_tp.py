@@ -25,6 +25,7 @@ import torch
 pytestmark = pytest.mark.gpu
 ROOT = Path(__file__).resolve().parents[1]
 ATOL = RTOL = 0.03
+GEN_PROMPTS = [[5, 6, 7], [9] * 40]
 
 
 def _free_port():
@@ -69,6 +70,7 @@ def _rank_main(rank, world, port, res):
         if rank == 0:
             one = Qwen38(config=cfg, seed=21, device="cuda:0", max_context=8192)
             ref = _run(one, calls)
+            res["gen_one"] = one.generate(GEN_PROMPTS, max_new_tokens=10, eos_token_ids=[cfg.vocab_size - 1])
             del one
         dist.barrier()
         model = Qwen38(config=cfg, seed=21, device=f"cuda:{rank}", max_context=8192, tensor_parallel=True)
@@ -88,6 +90,8 @@ def _rank_main(rank, world, port, res):
                                   float((d <= 1e-3 + 1e-3 * b.abs()).float().mean()), tuple(a.shape), tuple(b.shape)))
                 res[f"stats_{path}"] = stats
                 res[f"logits_{path}"] = [g[:, :64].clone() for g in got]
+        # greedy generation: decode windows with device-side token feedback, collectives inside
+        res[f"gen{rank}"] = model.generate(GEN_PROMPTS, max_new_tokens=10, eos_token_ids=[cfg.vocab_size - 1])
     finally:
         if model is not None:
             model.close()  # graphs (NCCL inside) and peer buffers go before the process group
@@ -115,3 +119,7 @@ def test_two_rank_tensor_parallel_matches_one_gpu():
     assert torch.equal(res["logits_nccl"][0], res["logits_peer"][0])
     # the peer path launches fewer kernels (no NCCL calls or add-norm kernels in decode)
     assert res["launches_peer0"] < res["launches_nccl0"]
+    # both ranks see the same all-gathered logits, so they generate the same tokens; the
+    # first token of each request comes from prefill logits within tolerance of one GPU's
+    assert res["gen0"] == res["gen1"] and [len(x) for x in res["gen0"]] == [10, 10]
+    assert [x[0] for x in res["gen0"]] == [x[0] for x in res["gen_one"]]
