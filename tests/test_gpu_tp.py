@@ -103,7 +103,7 @@ def _rank_main(rank, world, port, res):
 def test_two_rank_tensor_parallel_matches_one_gpu():
     import torch.multiprocessing as mp
     world = 2
-    with mp.Manager() as mgr:
+    with mp.get_context("spawn").Manager() as mgr:  # a fresh process, not a fork of this one
         res = mgr.dict()
         mp.spawn(_rank_main, args=(world, _free_port(), res), nprocs=world, join=True)
         res = dict(res)
