@@ -15,6 +15,7 @@ from __future__ import annotations
 
 import collections
 import dataclasses
+import itertools
 import json
 import math
 import weakref
@@ -83,7 +84,7 @@ def _token_batch(input_ids):
             row = row.tolist()
         if not isinstance(row, (list, tuple)) or not row:
             raise ValueError("Empty requests and padded tensors are not accepted; pass unpadded lists")
-        if any(type(t) is not int for t in row):
+        if set(map(type, row)) != {int}:  # exactly int (no bool, float or numpy scalars)
             raise ValueError("Token IDs must be integers")
         result.append(list(row))
     return result, single
@@ -372,11 +373,14 @@ class Qwen38:
         if len(slots) != len(rows) or len(set(slots)) != len(slots) or any(
                 type(s) is not int or s < 0 or s >= len(cache.lengths) for s in slots):
             raise ValueError("request_indices must identify one distinct cache slot per input sequence")
-        flat = [t for row in rows for t in row]
-        vocab = self.cfg.vocab_size
-        if any(t < 0 or t >= vocab for t in flat):
-            raise ValueError("Token ID outside model vocabulary")
         lens = [len(r) for r in rows]
+        vocab = self.cfg.vocab_size
+        try:  # one C-level pass over the ids (a prefill call holds tens of thousands)
+            flat = np.fromiter(itertools.chain.from_iterable(rows), dtype=np.int64, count=sum(lens))
+        except OverflowError:  # beyond int64, so outside the vocabulary too
+            raise ValueError("Token ID outside model vocabulary") from None
+        if int(flat.min()) < 0 or int(flat.max()) >= vocab:
+            raise ValueError("Token ID outside model vocabulary")
         prefixes = [cache.lengths[s] for s in slots]
         lengths = [p + n for p, n in zip(prefixes, lens)]
         self._reserve(cache, max(lengths))

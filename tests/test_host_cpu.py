@@ -21,7 +21,7 @@ FORMS = [
     [torch.tensor([7, 8]), torch.tensor([9], dtype=torch.int32)],
 ]
 BAD = [[], [[]], [[1], []], torch.zeros(2, 2, 2, dtype=torch.int64), torch.zeros(3), [1.0, 2.0], [[1, 2.5]],
-       "abc", [torch.zeros(2, 2, dtype=torch.int64)], [True, 2]]
+       "abc", [torch.zeros(2, 2, dtype=torch.int64)], [True, 2], [[1, np.int64(3)]], [[4], [5, False]]]
 
 
 @pytest.mark.parametrize("x", FORMS)
@@ -209,7 +209,7 @@ def test_generate_window_matches_stepwise(host_model, monkeypatch):
 def test_forward_step_validation_before_mutation(host_model):
     m = host_model
     c = m.new_cache(2, initial_capacity=64)
-    for bad in ([[1, 2], [64]], [[-1], [2]]):
+    for bad in ([[1, 2], [64]], [[-1], [2]], [[1], [2 ** 70]], [[1], [-2 ** 70]]):
         with pytest.raises(ValueError):
             m.forward_step(bad, c)
     with pytest.raises(ValueError):
