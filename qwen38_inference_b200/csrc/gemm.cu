@@ -148,23 +148,55 @@ QW_DEV void partial_norm_finish(const GemmParams& p) {
   const int m = t - first;
   const int N = p.a_rows;
   const float* ws = reinterpret_cast<const float*>(p.out) + (int64_t)m * p.ldo;
+  // the row's residual and the norm weights do not depend on the partials: their loads go
+  // out first and overlap the partial sums (round-only calls have neither)
+  uint4 res_u[MAXC], w_u[MAXC];
+  const bool norm = !(p.tp_world > 1 && p.tp_round_only);
+#pragma unroll
+  for (int i = 0; i < MAXC; ++i) {
+    const int c = (threadIdx.x + i * NT) * 8;
+    if (norm && c < N) {
+      res_u[i] = *reinterpret_cast<const uint4*>(p.resid + (int64_t)m * N + c);
+      w_u[i] = *reinterpret_cast<const uint4*>(p.norm_w + c);
+    }
+  }
   float v[MAXC][8];
 #pragma unroll
   for (int i = 0; i < MAXC; ++i)
 #pragma unroll
     for (int j = 0; j < 8; ++j) v[i][j] = 0.f;
-  // splits in order; every chunk's loads of one split are independent, so they are in
-  // flight together
-  for (int sp = 0; sp < p.k_splits; ++sp) {
+  // splits in order, two at a time: the loads of both splits for every chunk are in flight
+  // together, and each sum still adds split s before split s + 1
+  auto add4 = [](float* d, const float4& a) {
+    d[0] += a.x; d[1] += a.y; d[2] += a.z; d[3] += a.w;
+  };
+  int sp = 0;
+  for (; sp + 1 < p.k_splits; sp += 2) {
+    const float* s0 = ws + sp * p.part_stride;
+    const float* s1 = s0 + p.part_stride;
+#pragma unroll
+    for (int i = 0; i < MAXC; ++i) {
+      const int c = (threadIdx.x + i * NT) * 8;
+      if (c < N) {
+        const float4 a0 = __ldcg(reinterpret_cast<const float4*>(s0 + c));
+        const float4 b0 = __ldcg(reinterpret_cast<const float4*>(s0 + c + 4));
+        const float4 a1 = __ldcg(reinterpret_cast<const float4*>(s1 + c));
+        const float4 b1 = __ldcg(reinterpret_cast<const float4*>(s1 + c + 4));
+        add4(v[i], a0);
+        add4(v[i] + 4, b0);
+        add4(v[i], a1);
+        add4(v[i] + 4, b1);
+      }
+    }
+  }
+  if (sp < p.k_splits) {
     const float* src = ws + sp * p.part_stride;
 #pragma unroll
     for (int i = 0; i < MAXC; ++i) {
       const int c = (threadIdx.x + i * NT) * 8;
       if (c < N) {
-        const float4 a = __ldcg(reinterpret_cast<const float4*>(src + c));
-        const float4 b = __ldcg(reinterpret_cast<const float4*>(src + c + 4));
-        v[i][0] += a.x; v[i][1] += a.y; v[i][2] += a.z; v[i][3] += a.w;
-        v[i][4] += b.x; v[i][5] += b.y; v[i][6] += b.z; v[i][7] += b.w;
+        add4(v[i], __ldcg(reinterpret_cast<const float4*>(src + c)));
+        add4(v[i] + 4, __ldcg(reinterpret_cast<const float4*>(src + c + 4)));
       }
     }
   }
@@ -247,7 +279,10 @@ QW_DEV void partial_norm_finish(const GemmParams& p) {
     const int c = (threadIdx.x + i * NT) * 8;
     if (c < N) {
       float r[8];
-      load_bf16x8(p.resid + (int64_t)m * N + c, r);
+      unpack_bf16x2(res_u[i].x, r[0], r[1]);
+      unpack_bf16x2(res_u[i].y, r[2], r[3]);
+      unpack_bf16x2(res_u[i].z, r[4], r[5]);
+      unpack_bf16x2(res_u[i].w, r[6], r[7]);
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         v[i][j] = bf16_round(v[i][j]) + r[j];
@@ -268,7 +303,10 @@ QW_DEV void partial_norm_finish(const GemmParams& p) {
     const int c = (threadIdx.x + i * NT) * 8;
     if (c < N) {
       float wf[8], o[8];
-      load_bf16x8(p.norm_w + c, wf);
+      unpack_bf16x2(w_u[i].x, wf[0], wf[1]);
+      unpack_bf16x2(w_u[i].y, wf[2], wf[3]);
+      unpack_bf16x2(w_u[i].z, wf[4], wf[5]);
+      unpack_bf16x2(w_u[i].w, wf[6], wf[7]);
 #pragma unroll
       for (int j = 0; j < 8; ++j) o[j] = v[i][j] * rstd * (1.0f + wf[j]);
       store_bf16x8(p.hidden + (int64_t)m * N + c, o);
