@@ -17,11 +17,15 @@
 //    gating, K K^T and Q K^T (mma.sync), T by a blocked inverse (16 x 16 diagonal blocks by
 //    forward substitution in fp32, off-diagonal blocks on tf32 tensor cores), b e^G K,
 //    W = T (b e^G K), b V and e^{G_C - G} K; the chunk is handed over on an mbarrier;
-//  * state warps 8-15 each own 16 rows (dv) of S in registers (mma accumulator layout for the
-//    whole sequence) and compute their strips of U^T = (bV)^T T^T - S0 W^T,
-//    O^T = scale S0 Q^T diag(e^G) + U^T P^T and S += U^T (e^{G_C-G} K) with S0 and U^T as
-//    register A operands; then the gated RMSNorm y = bf16(o) rstd w silu(z) through a per-warp
-//    staging tile (z in, y out, both 16-byte coalesced).
+//  * state warps 8-15 keep S in tensor memory (one value row dv per TMEM lane, fp32) and run
+//    the state products on tcgen05 with dv as the MMA M dimension (128):
+//      warps 8-11 (one elected thread issues the MMAs): S0 = bf16(S) and S <- e^{G_C} S
+//      (tcgen05.ld / st), U^T = (bV)^T T^T + S0 (-W)^T (A = bV MN-major from shared memory,
+//      then S0 from TMEM), O1^T = S0 Q^T, U^T to bf16 in TMEM, O2^T = U^T P^T and
+//      S += U^T (e^{G_C-G} K) (B MN-major);
+//      warps 12-15: O = bf16(scale e^G O1 + O2) out of TMEM, the gated RMSNorm over the 128
+//      value rows of each token (halving exchange in the warp, then shared memory) and
+//      y = o rstd w silu(z) through a double-buffered z / y staging tile.
 // Q, K, V chunks arrive by TMA (128-byte swizzle) into two chunk buffers; the state warps
 // release a buffer and issue the loads of the chunk two ahead. Every mbarrier wait is bounded
 // (QW_DEV_ERR_TIMEOUT_GDN); after a timeout all waits return at once and both groups run
@@ -43,16 +47,24 @@ constexpr int BUF = B_P + TILE64;     // multiple of 1024 (TMA swizzle atoms)
 constexpr int BLD = 20;               // row stride (floats) of a compact 16 x 16 fp32 block
 constexpr int BLK = 16 * BLD;         // floats per block
 constexpr int S_BLK = 2 * BUF;        // 20 blocks: [0,6) A_ij then T_ij (i > j), [6,10) A_ii, [10,14) T_ii, [14,20) M_ik
-// gating of a chunk (written by the state warps two chunks ahead, three slots):
+// gating of a chunk (written by the state warps two chunks ahead, four slots: the output
+// warps read a chunk's e^G up to two chunks after the MMA warps move on):
 // G * log2(e), beta, e^{G_C - G}, e^G (64 each), e^{G_C}
 constexpr int GB_G2 = 0, GB_BETA = CH, GB_EGL = 2 * CH, GB_EG = 3 * CH, GB_EC = 4 * CH, GB_FLOATS = 4 * CH + 4;
+constexpr int GB_SLOTS = 4;
 constexpr int S_GB = S_BLK + 20 * BLK * 4;
-constexpr int S_SS = S_GB + 3 * GB_FLOATS * 4;  // state: [8][64] partial sums of squares, rstd [64]
-constexpr int S_Z = (S_SS + 9 * CH * 4 + 127) / 128 * 128;  // state: per-warp z / y staging [64][16] bf16
-constexpr int S_U = S_Z + 8 * CH * 32;      // state: per-warp bf16 U^T strip [16][64]
-constexpr int S_BAR = S_U + 8 * 16 * CH * 2;
-constexpr int SMEM = S_BAR + 64 + 1024;     // + slack to align the base to 1024
+constexpr int S_RED = S_GB + GB_SLOTS * GB_FLOATS * 4;      // output warps: [4][64] sums of squares, rstd [64]
+constexpr int S_Z = (S_RED + 5 * CH * 4 + 127) / 128 * 128;  // output warps: two z / y tiles [64 tokens][128] bf16
+constexpr int ZBUF = CH * D * 2;
+constexpr int S_BAR = S_Z + 2 * ZBUF;
+constexpr int SMEM = S_BAR + 128 + 1024;                     // + slack to align the base to 1024
 static_assert(BUF % 1024 == 0 && S_Z % 128 == 0, "layout alignment");
+// tensor memory columns: S fp32, S0 = bf16(S) pairs, U^T fp32, U^T bf16 pairs, O1^T, O2^T
+constexpr uint32_t TMEM_COLS = 512;
+constexpr uint32_t T_S = 0, T_S0 = 128, T_U = 192, T_UB = 256, T_O1 = 320, T_O2 = 384;
+constexpr uint32_t IDESC_N64 = umma_idesc_bf16(128, 64);
+constexpr uint32_t IDESC_U_AMN = umma_idesc_bf16(128, 64) | (1u << 15);  // A (bV) MN-major
+constexpr uint32_t IDESC_S_BMN = umma_idesc_bf16(128, 128) | (1u << 16);  // B (e^{G_C-G} K) MN-major
 
 QW_DEV int blk_lo(int i, int j) { return i * (i - 1) / 2 + j; }  // i > j
 
@@ -110,6 +122,19 @@ QW_DEV void cpa16(uint32_t dst, const void* src, bool pred) {
 constexpr int PREP_REGS = 88, STATE_REGS = 168;
 static_assert(256 * PREP_REGS + 256 * STATE_REGS == 512 * 128, "register split must equal the launch allocation");
 QW_DEV void named_bar(int id) { asm volatile("bar.sync %0, 256;" ::"r"(id) : "memory"); }
+QW_DEV void named_bar_n(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
+// a[0, 2W) -> a[0, W): partner lanes (lane ^ bit) add their halves; lanes with `bit` set keep
+// the upper half
+template <int W>
+QW_DEV void halve(float* a, int lane, int bit) {
+  const bool up = (lane & bit) != 0;
+#pragma unroll
+  for (int i = 0; i < W; ++i) {
+    const float send = up ? a[i] : a[i + W];
+    const float keep = up ? a[i + W] : a[i];
+    a[i] = keep + __shfl_xor_sync(0xffffffffu, send, bit);
+  }
+}
 QW_DEV void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 // mma.sync fragments from swizzled 64-row tiles
@@ -270,7 +295,13 @@ __global__ void __launch_bounds__(512, 1) gdn_prefill_kernel(
   const uint32_t s0 = smem_u32(smem);
   uint64_t* loaded = reinterpret_cast<uint64_t*>(smem + S_BAR);  // [2] chunk tiles landed
   uint64_t* ready = loaded + 2;                                  // [2] chunk prepared
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(ready + 2);
+  uint64_t* bar_u = ready + 2;                                   // U^T products complete
+  uint64_t* bar_o = bar_u + 1;                                   // O1^T and O2^T complete
+  uint64_t* bar_s = bar_o + 1;                                   // state update complete
+  uint64_t* o_free = bar_s + 1;                                  // output warps have read O
+  uint64_t* gate_pub = o_free + 1;                               // [4] gating slot written
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(gate_pub + GB_SLOTS);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gate_pub + GB_SLOTS) + 1;
 
   // value heads vary fastest: the CTAs resident together read whole token rows of q, k, v, z
   // (DRAM page locality) and the value heads of one key head share its q, k tiles in L2
@@ -291,6 +322,11 @@ __global__ void __launch_bounds__(512, 1) gdn_prefill_kernel(
     mbar_init(&loaded[1], 1);
     mbar_init(&ready[0], 256);
     mbar_init(&ready[1], 256);
+    mbar_init(bar_u, 1);
+    mbar_init(bar_o, 1);
+    mbar_init(bar_s, 1);
+    mbar_init(o_free, 128);
+    for (int i = 0; i < GB_SLOTS; ++i) mbar_init(&gate_pub[i], 32);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -316,7 +352,7 @@ __global__ void __launch_bounds__(512, 1) gdn_prefill_kernel(
       const uint32_t sb = s0 + b * BUF;
       const int nc = min(CH, n - c * CH);
       // gating of this chunk (written by the state warps before they issued its loads)
-      const float* gb = gbuf + (c % 3) * GB_FLOATS;
+      const float* gb = gbuf + (c % GB_SLOTS) * GB_FLOATS;
       const float* sG = gb + GB_G2;
       const float* sBeta = gb + GB_BETA;
       const float* sEGl = gb + GB_EGL;
@@ -449,259 +485,268 @@ __global__ void __launch_bounds__(512, 1) gdn_prefill_kernel(
         named_bar(1);
         store_tile_bf16<8>(buf + B_W, w, mt * 16, nh * 64, lane, -1.f);
       }
+      fence_proxy_async_smem();  // the tiles written here are read by tcgen05.mma (async proxy)
       mbar_arrive(&ready[b]);
     }
   } else {
     // =============================================================== state warps
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(STATE_REGS));
-    const int sw = warp - 8, dv0 = sw * 16, stid = tid - 256;
-    float* sSS = reinterpret_cast<float*>(smem + S_SS);  // [8][64]
-    float* sRstd = sSS + 8 * CH;
-    const uint32_t zb = s0 + S_Z + sw * (CH * 32);
-    const uint32_t ub = s0 + S_U + sw * (16 * CH * 2);  // U^T strip, rows dv, 128-byte swizzled
-    float* Sg = state + ((int64_t)slot * HV + hv) * D * D;
-    float sacc[16][4];
-#pragma unroll
-    for (int nt = 0; nt < 16; ++nt) {
-      const int col = nt * 8 + c4 * 2;
-      const float2 lo = *reinterpret_cast<const float2*>(Sg + (int64_t)(dv0 + g4) * D + col);
-      const float2 hi = *reinterpret_cast<const float2*>(Sg + (int64_t)(dv0 + g4 + 8) * D + col);
-      sacc[nt][0] = lo.x;
-      sacc[nt][1] = lo.y;
-      sacc[nt][2] = hi.x;
-      sacc[nt][3] = hi.y;
-    }
-    const float w_lo = bf2f(norm_w[dv0 + g4]), w_hi = bf2f(norm_w[dv0 + g4 + 8]);
-    // staging row t holds dv0..dv0+15 of token t: 32 bytes, 16-byte halves swapped on rows 4-7 mod 8
-    auto z_addr = [&](int t, int half) -> uint32_t { return zb + t * 32 + ((half ^ ((t >> 2) & 1)) << 4); };
-    auto prefetch_z = [&](int c) {
-      const int64_t tz = t_begin + (int64_t)c * CH;
-      const int ncz = min(CH, n - c * CH);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int q = lane + 32 * i, t = q >> 1, half = q & 1;
-        const bool ok = t < ncz;
-        cpa16(z_addr(t, half), z + (tz + (ok ? t : 0)) * ldz + (int64_t)hv * D + dv0 + half * 8, ok);
-      }
-      asm volatile("cp.async.commit_group;" ::: "memory");
-    };
-    if (n_chunks > 0) prefetch_z(0);
-    float rb[2] = {0.f, 0.f}, ra[2] = {0.f, 0.f};  // warp 8: raw gating inputs of chunk c + 2
+    const int sw = warp - 8, stid = tid - 256;
+    const int quarter = warp & 3;                             // TMEM lanes 32 quarter .. + 31
+    const int dv = 32 * quarter + lane;                       // the value row this thread owns
+    const uint32_t lanes = (uint32_t)(32 * quarter) << 16;  // lane field of its TMEM addresses
     if (sw == 0) {
-      // gating of chunks 0 and 1, then their loads (the load mbarrier publishes the gating
-      // to the prep warps, as for every later chunk)
-      for (int c = 0; c < 2 && c < n_chunks; ++c) {
-        load_gating_inputs(rb, ra, ba, ldba, t_begin, n, c, hv, HV, lane);
-        chunk_gating(gbuf + c * GB_FLOATS, rb, ra, min(CH, n - c * CH), a_log, dtb, lane);
-      }
-      __syncwarp();
-      if (lane == 0) {
-        tma_prefetch_desc(&tm_q);
-        tma_prefetch_desc(&tm_k);
-        tma_prefetch_desc(&tm_v);
-        for (int c = 0; c < 2 && c < n_chunks; ++c)
-          issue_chunk_loads(smem + c * BUF, &loaded[c], &tm_q, &tm_k, &tm_v, h, hv, t_begin + c * CH);
-      }
-      load_gating_inputs(rb, ra, ba, ldba, t_begin, n, 2, hv, HV, lane);
+      tmem_alloc(tmem_slot, TMEM_COLS);
+      tmem_relinquish();
     }
-    for (int c = 0; c < n_chunks; ++c) {
-      const int b = c & 1;
-      const uint32_t sb = s0 + b * BUF;
-      const float* gb = gbuf + (c % 3) * GB_FLOATS;
-      const float* sEG = gb + GB_EG;
-      const int nc = min(CH, n - c * CH);
-      const int64_t tc = t_begin + (int64_t)c * CH;
-      if (sw == 0 && c + 2 < n_chunks) {
-        // gating of chunk c + 2 into its slot; published to the prep warps by the release
-        // barrier below and the mbarrier of that chunk's loads
-        chunk_gating(gbuf + ((c + 2) % 3) * GB_FLOATS, rb, ra, min(CH, n - (c + 2) * CH), a_log, dtb, lane);
-        load_gating_inputs(rb, ra, ba, ldba, t_begin, n, c + 3, hv, HV, lane);
-      }
-      mbar_wait(&ready[b], (c >> 1) & 1, abort_flag, err, QW_DEV_ERR_TIMEOUT_GDN);
-      // ---- U^T = (bV)^T T^T + S0 (-W)^T, rounded to bf16 into the warp's strip
+    tc_fence_before();
+    named_bar_n(3, 256);
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    float* Sg = state + ((int64_t)slot * HV + hv) * D * D;
+    if (sw < 4) {
+      // ------------------------------------------------------------- MMA warps 8-11
       {
-        float u[8][4];
+        const float4* src = reinterpret_cast<const float4*>(Sg + (int64_t)dv * D);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) u[i][0] = u[i][1] = u[i][2] = u[i][3] = 0.f;
+        for (int j = 0; j < 4; ++j) {
+          uint32_t r[32];
 #pragma unroll
-        for (int ks = 0; ks < 4; ++ks) {
-          uint32_t a[4];
-          frag_a_t(sb + B_V, dv0, ks * 16, lane, a);
-#pragma unroll
-          for (int np = ks; np < 4; ++np) {  // T[t][s] = 0 for s-blocks after the t-block
-            uint32_t bq[4];
-            frag_b(sb + B_T, np * 16, ks * 16, lane, bq);
-            mma16816(u[2 * np], a, bq[0], bq[1]);
-            mma16816(u[2 * np + 1], a, bq[2], bq[3]);
+          for (int i = 0; i < 8; ++i) {
+            const float4 v = src[8 * j + i];
+            r[4 * i] = __float_as_uint(v.x);
+            r[4 * i + 1] = __float_as_uint(v.y);
+            r[4 * i + 2] = __float_as_uint(v.z);
+            r[4 * i + 3] = __float_as_uint(v.w);
           }
+          tmem_st_32x32b_x32(tmem + lanes + T_S + 32 * j, r);
         }
-#pragma unroll
-        for (int ks = 0; ks < 8; ++ks) {
-          uint32_t a[4];
-          acc_to_a(sacc, ks, a);
-#pragma unroll
-          for (int np = 0; np < 4; ++np) {
-            uint32_t bq[4];
-            frag_b(sb + B_W, np * 16, ks * 16, lane, bq);
-            mma16816(u[2 * np], a, bq[0], bq[1]);
-            mma16816(u[2 * np + 1], a, bq[2], bq[3]);
-          }
-        }
-#pragma unroll
-        for (int ks = 0; ks < 4; ++ks) {
-          uint32_t a[4];
-          acc_to_a(u, ks, a);
-          stsm_x4(ub + swz(lane & 15, 2 * ks + (lane >> 4)), a);
+        tmem_st_wait();
+      }
+      float rb[2] = {0.f, 0.f}, ra[2] = {0.f, 0.f};  // warp 8: raw gating inputs of chunk c + 2
+      if (sw == 0) {
+        // gating of chunks 0 and 1, then their loads (the load mbarrier publishes the gating
+        // to the prep warps, gate_pub to the output warps)
+        for (int c = 0; c < 2 && c < n_chunks; ++c) {
+          load_gating_inputs(rb, ra, ba, ldba, t_begin, n, c, hv, HV, lane);
+          chunk_gating(gbuf + c * GB_FLOATS, rb, ra, min(CH, n - c * CH), a_log, dtb, lane);
+          __syncwarp();
+          mbar_arrive(&gate_pub[c]);
         }
         __syncwarp();
+        if (lane == 0) {
+          tma_prefetch_desc(&tm_q);
+          tma_prefetch_desc(&tm_k);
+          tma_prefetch_desc(&tm_v);
+          for (int c = 0; c < 2 && c < n_chunks; ++c)
+            issue_chunk_loads(smem + c * BUF, &loaded[c], &tm_q, &tm_k, &tm_v, h, hv, t_begin + c * CH);
+        }
+        load_gating_inputs(rb, ra, ba, ldba, t_begin, n, 2, hv, HV, lane);
       }
-      // ---- O^T = scale S0 Q^T diag(e^G) + U^T P^T
-      float o[8][4];
+      for (int c = 0; c < n_chunks; ++c) {
+        const int b = c & 1;
+        const uint32_t sb = s0 + b * BUF;
+        const float* gb = gbuf + (c % GB_SLOTS) * GB_FLOATS;
+        if (sw == 0 && c + 2 < n_chunks) {
+          // gating of chunk c + 2 into the slot of chunk c - 2, which the output warps have
+          // finished with (the MMA warps passed o_free of chunk c - 2 in the last iteration)
+          const int g2 = (c + 2) % GB_SLOTS;
+          chunk_gating(gbuf + g2 * GB_FLOATS, rb, ra, min(CH, n - (c + 2) * CH), a_log, dtb, lane);
+          __syncwarp();
+          mbar_arrive(&gate_pub[g2]);
+          load_gating_inputs(rb, ra, ba, ldba, t_begin, n, c + 3, hv, HV, lane);
+        }
+        // ---- S after chunk c - 1: S0 = bf16(S) for this chunk's products, S <- e^{G_C} S
+        // (e^{G_C} from this chunk's gating, which warp 8 may have written just now)
+        mbar_wait(&gate_pub[c % GB_SLOTS], (c / GB_SLOTS) & 1, abort_flag, err, QW_DEV_ERR_TIMEOUT_GDN);
+        if (c > 0) mbar_wait(bar_s, (c - 1) & 1, abort_flag, err, QW_DEV_ERR_TIMEOUT_GDN);
+        tc_fence_after();
+        {
+          const float eC = gb[GB_EC];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+          for (int j = 0; j < 4; ++j) {
+            uint32_t r[32], pk[16];
+            tmem_ld_32x32b_x32(tmem + lanes + T_S + 32 * j, r);
+            tmem_ld_wait();
 #pragma unroll
-      for (int ks = 0; ks < 8; ++ks) {
-        uint32_t a[4];
-        acc_to_a(sacc, ks, a);
+            for (int i = 0; i < 16; ++i) pk[i] = pack_bf16x2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
 #pragma unroll
-        for (int np = 0; np < 4; ++np) {
-          uint32_t bq[4];
-          frag_b(sb + B_Q, np * 16, ks * 16, lane, bq);
-          mma16816(o[2 * np], a, bq[0], bq[1]);
-          mma16816(o[2 * np + 1], a, bq[2], bq[3]);
+            for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * eC);
+            tmem_st_32x32b_x16(tmem + lanes + T_S0 + 16 * j, pk);
+            tmem_st_32x32b_x32(tmem + lanes + T_S + 32 * j, r);
+          }
+          tmem_st_wait();
+        }
+        tc_fence_before();
+        mbar_wait(&ready[b], (c >> 1) & 1, abort_flag, err, QW_DEV_ERR_TIMEOUT_GDN);
+        named_bar_n(4, 128);
+        if (stid == 0) {
+          tc_fence_after();
+          // U^T = (bV)^T T^T + S0 (-W)^T
+#pragma unroll
+          for (int ks = 0; ks < 4; ++ks)
+            umma_bf16(tmem + T_U, umma_sdesc_mn_sw128(sb + B_V + ks * 2048, TILE / 2),
+                      umma_sdesc_sw128(sb + B_T + ks * 32), IDESC_U_AMN, ks > 0 ? 1u : 0u);
+#pragma unroll
+          for (int ks = 0; ks < 8; ++ks)
+            umma_bf16_ts(tmem + T_U, tmem + T_S0 + ks * 8,
+                         umma_sdesc_sw128(sb + B_W + (ks >> 2) * (TILE / 2) + (ks & 3) * 32), IDESC_N64, 1u);
+          umma_commit(bar_u);
+          // O1^T = S0 Q^T, once the output warps have read the previous chunk's O
+          if (c > 0) mbar_wait(o_free, (c - 1) & 1, abort_flag, err, QW_DEV_ERR_TIMEOUT_GDN);
+          tc_fence_after();
+#pragma unroll
+          for (int ks = 0; ks < 8; ++ks)
+            umma_bf16_ts(tmem + T_O1, tmem + T_S0 + ks * 8,
+                         umma_sdesc_sw128(sb + B_Q + (ks >> 2) * (TILE / 2) + (ks & 3) * 32), IDESC_N64,
+                         ks > 0 ? 1u : 0u);
+        }
+        // ---- U^T rounded to bf16 into TMEM: the A operand of O2^T and of the state update
+        mbar_wait(bar_u, c & 1, abort_flag, err, QW_DEV_ERR_TIMEOUT_GDN);
+        tc_fence_after();
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          uint32_t r[32], pk[16];
+          tmem_ld_32x32b_x32(tmem + lanes + T_U + 32 * j, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 16; ++i) pk[i] = pack_bf16x2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
+          tmem_st_32x32b_x16(tmem + lanes + T_UB + 16 * j, pk);
+        }
+        tmem_st_wait();
+        tc_fence_before();
+        named_bar_n(4, 128);
+        if (stid == 0) {
+          tc_fence_after();
+          // O2^T = U^T P^T, then S += U^T (e^{G_C-G} K)
+#pragma unroll
+          for (int ks = 0; ks < 4; ++ks)
+            umma_bf16_ts(tmem + T_O2, tmem + T_UB + ks * 8, umma_sdesc_sw128(sb + B_P + ks * 32), IDESC_N64,
+                         ks > 0 ? 1u : 0u);
+          umma_commit(bar_o);
+#pragma unroll
+          for (int ks = 0; ks < 4; ++ks)
+            umma_bf16_ts(tmem + T_S, tmem + T_UB + ks * 8, umma_sdesc_mn_sw128(sb + B_K + ks * 2048, TILE / 2),
+                         IDESC_S_BMN, 1u);
+          umma_commit(bar_s);
+          if (c + 2 < n_chunks) {
+            // every product reading buffer b is complete once the state update is: refill it
+            mbar_wait(bar_s, c & 1, abort_flag, err, QW_DEV_ERR_TIMEOUT_GDN);
+            fence_proxy_async_smem();
+            if (!*abort_flag)
+              issue_chunk_loads(smem + b * BUF, &loaded[b], &tm_q, &tm_k, &tm_v, h, hv, t_begin + (c + 2) * CH);
+          }
         }
       }
-#pragma unroll
-      for (int nt = 0; nt < 8; ++nt) {
-        const float2 e2 = *reinterpret_cast<const float2*>(sEG + nt * 8 + 2 * c4);
-        o[nt][0] *= scale * e2.x;
-        o[nt][1] *= scale * e2.y;
-        o[nt][2] *= scale * e2.x;
-        o[nt][3] *= scale * e2.y;
-      }
-#pragma unroll
-      for (int ks = 0; ks < 4; ++ks) {
-        uint32_t a[4];
-        frag_a(ub, 0, ks * 16, lane, a);
-#pragma unroll
-        for (int np = ks; np < 4; ++np) {  // P[t][s] = 0 for s > t
-          uint32_t bq[4];
-          frag_b(sb + B_P, np * 16, ks * 16, lane, bq);
-          mma16816(o[2 * np], a, bq[0], bq[1]);
-          mma16816(o[2 * np + 1], a, bq[2], bq[3]);
-        }
-      }
-      // ---- S <- e^{G_C} S + U^T (e^{G_C-G} K)
+      // ---- final state, in place
+      if (n_chunks > 0) mbar_wait(bar_s, (n_chunks - 1) & 1, abort_flag, err, QW_DEV_ERR_TIMEOUT_GDN);
+      tc_fence_after();
       {
-        const float eC = gb[GB_EC];
+        float4* dst = reinterpret_cast<float4*>(Sg + (int64_t)dv * D);
 #pragma unroll
-        for (int nt = 0; nt < 16; ++nt) {
-          sacc[nt][0] *= eC;
-          sacc[nt][1] *= eC;
-          sacc[nt][2] *= eC;
-          sacc[nt][3] *= eC;
-        }
+        for (int j = 0; j < 4; ++j) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(tmem + lanes + T_S + 32 * j, r);
+          tmem_ld_wait();
 #pragma unroll
-        for (int ks = 0; ks < 4; ++ks) {
-          uint32_t a[4];
-          frag_a(ub, 0, ks * 16, lane, a);
-#pragma unroll
-          for (int np = 0; np < 8; ++np) {
-            uint32_t bq[4];
-            frag_b_t(sb + B_K, np * 16, ks * 16, lane, bq);
-            mma16816(sacc[2 * np], a, bq[0], bq[1]);
-            mma16816(sacc[2 * np + 1], a, bq[2], bq[3]);
-          }
+          for (int i = 0; i < 8; ++i)
+            dst[8 * j + i] = make_float4(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1]),
+                                         __uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3]));
         }
       }
-      named_bar(2);  // every state warp is done with chunk buffer b
-      if (stid == 0 && c + 2 < n_chunks && !*abort_flag) {
-        fence_proxy_async_smem();
-        issue_chunk_loads(smem + b * BUF, &loaded[b], &tm_q, &tm_k, &tm_v, h, hv, t_begin + (c + 2) * CH);
-      }
-      // ---- gated RMSNorm of bf16(o) over the 128 values of each token
-      {
-        float ss[8][2];
-#pragma unroll
-        for (int nt = 0; nt < 8; ++nt) {
-#pragma unroll
-          for (int e = 0; e < 4; ++e) o[nt][e] = bf16_round(o[nt][e]);
-#pragma unroll
-          for (int j = 0; j < 2; ++j) {
-            float v = o[nt][j] * o[nt][j] + o[nt][2 + j] * o[nt][2 + j];
-            v += __shfl_xor_sync(0xffffffffu, v, 4);
-            v += __shfl_xor_sync(0xffffffffu, v, 8);
-            v += __shfl_xor_sync(0xffffffffu, v, 16);
-            ss[nt][j] = v;
-          }
+      tc_fence_before();
+    } else {
+      // ------------------------------------------------------------- output warps 12-15
+      const int otid = tid - 384;
+      float* sRed = reinterpret_cast<float*>(smem + S_RED);  // [4][64] sums of squares
+      float* sRstd = sRed + 4 * CH;
+      const float wdv = bf2f(norm_w[dv]);
+      // z tile of chunk c: row t = token t (256 bytes), filled by 16-byte copies
+      auto prefetch_z = [&](int c) {
+        const int64_t tz = t_begin + (int64_t)c * CH;
+        const int ncz = min(CH, n - c * CH);
+        const uint32_t base = s0 + S_Z + (c & 1) * ZBUF;
+        for (int i = otid; i < CH * 16; i += 128) {
+          const int t = i >> 4, part = i & 15;
+          const bool ok = t < ncz;
+          cpa16(base + t * 256 + part * 16, z + (tz + (ok ? t : 0)) * ldz + (int64_t)hv * D + part * 8, ok);
         }
-        if (g4 == 0) {
+        asm volatile("cp.async.commit_group;" ::: "memory");
+      };
+      if (n_chunks > 0) prefetch_z(0);
+      for (int c = 0; c < n_chunks; ++c) {
+        const int nc = min(CH, n - c * CH);
+        const int64_t tc = t_begin + (int64_t)c * CH;
+        if (c + 1 < n_chunks) prefetch_z(c + 1);  // into the tile chunk c - 1 used
+        const float* gb = gbuf + (c % GB_SLOTS) * GB_FLOATS;
+        mbar_wait(&gate_pub[c % GB_SLOTS], (c / GB_SLOTS) & 1, abort_flag, err, QW_DEV_ERR_TIMEOUT_GDN);
+        mbar_wait(bar_o, c & 1, abort_flag, err, QW_DEV_ERR_TIMEOUT_GDN);
+        tc_fence_after();
+        // ---- o = bf16(scale e^G O1 + O2): this thread's value row for the 64 tokens
+        float o[CH];
 #pragma unroll
-          for (int nt = 0; nt < 8; ++nt) {
-            sSS[sw * CH + nt * 8 + 2 * c4] = ss[nt][0];
-            sSS[sw * CH + nt * 8 + 2 * c4 + 1] = ss[nt][1];
-          }
+        for (int j = 0; j < 2; ++j) {
+          uint32_t r1[32], r2[32];
+          tmem_ld_32x32b_x32(tmem + lanes + T_O1 + 32 * j, r1);
+          tmem_ld_32x32b_x32(tmem + lanes + T_O2 + 32 * j, r2);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            o[32 * j + i] =
+                bf16_round(__uint_as_float(r1[i]) * (scale * gb[GB_EG + 32 * j + i]) + __uint_as_float(r2[i]));
         }
-      }
-      named_bar(2);
-      if (stid < CH) {
-        float tot = 0.f;
+        tc_fence_before();
+        mbar_arrive(o_free);
+        // ---- sum of o^2 over the 128 value rows of each token: halving exchange in the warp
+        // (lane l ends with tokens 2l and 2l + 1), then the four warps through shared memory
+        {
+          float a[CH];
 #pragma unroll
-        for (int w = 0; w < 8; ++w) tot += sSS[w * CH + stid];
-        sRstd[stid] = rsqrtf(tot / (float)D + eps);
-      }
-      named_bar(2);
-      asm volatile("cp.async.wait_group 0;" ::: "memory");  // this chunk's z rows
-      __syncwarp();
-#pragma unroll
-      for (int np = 0; np < 4; ++np) {
-        const int tl = np * 16 + (lane & 7) + ((lane >> 4) << 3), half = (lane >> 3) & 1;
-        uint32_t zr[4], yr[4];
-        ldsm_x4_t(z_addr(tl, half), zr);
-        const float2 ra = *reinterpret_cast<const float2*>(sRstd + np * 16 + 2 * c4);
-        const float2 rb = *reinterpret_cast<const float2*>(sRstd + np * 16 + 8 + 2 * c4);
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int nt = 2 * np + (q >> 1), hi = q & 1;
-          const float2 r = (q >> 1) ? rb : ra;
-          float z0, z1;
-          unpack_bf16x2(zr[q], z0, z1);
-          const float wv = hi ? w_hi : w_lo;
-          const float y0 = o[nt][2 * hi] * r.x * wv * __fdividef(z0, 1.f + __expf(-z0));
-          const float y1 = o[nt][2 * hi + 1] * r.y * wv * __fdividef(z1, 1.f + __expf(-z1));
-          yr[q] = pack_bf16x2(y0, y1);
+          for (int i = 0; i < CH; ++i) a[i] = o[i] * o[i];
+          halve<32>(a, lane, 16);
+          halve<16>(a, lane, 8);
+          halve<8>(a, lane, 4);
+          halve<4>(a, lane, 2);
+          halve<2>(a, lane, 1);
+          *reinterpret_cast<float2*>(sRed + quarter * CH + 2 * lane) = make_float2(a[0], a[1]);
         }
-        stsm_x4_t(z_addr(tl, half), yr);
-      }
-      __syncwarp();
+        named_bar_n(5, 128);
+        if (otid < CH)
+          sRstd[otid] = rsqrtf(((sRed[otid] + sRed[CH + otid]) + (sRed[2 * CH + otid] + sRed[3 * CH + otid])) /
+                                   (float)D + eps);
+        if (c + 1 < n_chunks) asm volatile("cp.async.wait_group 1;" ::: "memory");  // this chunk's z
+        else asm volatile("cp.async.wait_group 0;" ::: "memory");
+        named_bar_n(5, 128);
+        // ---- y = o rstd w silu(z), written over z in the staging tile
+        uint8_t* zt = smem + S_Z + (c & 1) * ZBUF;
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int q = lane + 32 * i, t = q >> 1, half = q & 1;
-        if (t < nc) {
-          uint4 v;
-          asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
-                       : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-                       : "r"(z_addr(t, half)));
-          *reinterpret_cast<uint4*>(y + (tc + t) * ldy + (int64_t)hv * D + dv0 + half * 8) = v;
+        for (int t = 0; t < CH; ++t) {
+          __nv_bfloat16* p = reinterpret_cast<__nv_bfloat16*>(zt + t * 256) + dv;
+          const float zv = bf2f(*p);
+          *p = f2bf(o[t] * sRstd[t] * wdv * __fdividef(zv, 1.f + __expf(-zv)));
         }
+        named_bar_n(5, 128);
+        for (int i = otid; i < CH * 16; i += 128) {
+          const int t = i >> 4, part = i & 15;
+          if (t < nc)
+            *reinterpret_cast<uint4*>(y + (tc + t) * ldy + (int64_t)hv * D + part * 8) =
+                *reinterpret_cast<const uint4*>(zt + t * 256 + part * 16);
+        }
+        named_bar_n(5, 128);  // the tile is refilled by the prefetch of chunk c + 2
       }
-      __syncwarp();
-      if (c + 1 < n_chunks) prefetch_z(c + 1);
-    }
-    // ---- final state, in place
-#pragma unroll
-    for (int nt = 0; nt < 16; ++nt) {
-      const int col = nt * 8 + c4 * 2;
-      *reinterpret_cast<float2*>(Sg + (int64_t)(dv0 + g4) * D + col) = make_float2(sacc[nt][0], sacc[nt][1]);
-      *reinterpret_cast<float2*>(Sg + (int64_t)(dv0 + g4 + 8) * D + col) = make_float2(sacc[nt][2], sacc[nt][3]);
     }
   }
   __syncthreads();
   if (tid == 0 && *abort_flag) {
-    // a wait gave up: leave time for any bulk copy still in flight before the CTA exits
+    // a wait gave up: leave time for any bulk copy or tensor-core product still in flight
     const uint64_t t0 = globaltimer();
     while (globaltimer() - t0 < 200000ull) {
     }
+  }
+  __syncthreads();
+  if (warp == 8) {
+    tc_fence_after();
+    tmem_dealloc(*tmem_slot, TMEM_COLS);
   }
 }
 
