@@ -117,8 +117,8 @@ QW_DEV void cpa16(uint32_t dst, const void* src, bool pred) {
 }
 // Register split between the warp groups: the CTA is launched with 512 x 128 registers
 // (ptxas is held to 128 by the launch bounds); the prep warpgroups give 40 back and the
-// state warpgroups (64 accumulator registers of S each) take 40 more:
-// 256 x 88 + 256 x 168 = 512 x 128.
+// state warpgroups take 40 more (the output warps hold a token row of O, 64 values, and its
+// squares while they reduce them): 256 x 88 + 256 x 168 = 512 x 128.
 constexpr int PREP_REGS = 88, STATE_REGS = 168;
 static_assert(256 * PREP_REGS + 256 * STATE_REGS == 512 * 128, "register split must equal the launch allocation");
 QW_DEV void named_bar(int id) { asm volatile("bar.sync %0, 256;" ::"r"(id) : "memory"); }
