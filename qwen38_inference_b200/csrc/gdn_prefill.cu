@@ -339,6 +339,7 @@ __global__ void __launch_bounds__(512, 1) gdn_prefill_kernel(
     if ((cc >> 4) > (r >> 4))
       *reinterpret_cast<__nv_bfloat16*>(smem + bb * BUF + B_T + swz_elem(r, cc)) = f2bf(0.f);
   }
+  fence_proxy_async_smem();  // T is an operand of the state warps' tensor-core products
   __syncthreads();
 
   if (warp < 8) {
