@@ -632,29 +632,12 @@ def run_op(args):
         def launch():
             ops.attn_prefill(qkv, nq, nkv, d, kc, vc, md["tiles"], md["cu"], md["prefix"], md["kv_base"], out,
                              d ** -0.5)
+    elif args.op == "gdn_decode":
+        launch, work, unit, extra = _gdn_decode_case(cfg, B, g)
+    elif args.op == "gdn_prefill_flashinfer":
+        launch, work, unit, extra = _gdn_prefill_case(cfg, B, L, g, flashinfer=True)
     else:
-        H, HV, dk, dv = cfg.linear_num_key_heads, cfg.linear_num_value_heads, cfg.linear_key_head_dim, \
-            cfg.linear_value_head_dim
-        nrm = torch.nn.functional.normalize
-        q = nrm(torch.randn(T, H, dk, device=dev, generator=g), dim=-1).bfloat16().view(T, H * dk)
-        k = nrm(torch.randn(T, H, dk, device=dev, generator=g), dim=-1).bfloat16().view(T, H * dk)
-        v = torch.randn(T, HV * dv, device=dev, generator=g).bfloat16()
-        ba = torch.randn(T, 2 * HV, device=dev, generator=g).bfloat16()
-        A_log = torch.zeros(HV, device=dev)
-        dt_bias = torch.zeros(HV, device=dev).bfloat16()
-        cu = torch.arange(0, T + 1, L, dtype=torch.int32, device=dev)
-        slots = torch.arange(B, dtype=torch.int32, device=dev)
-        state = torch.zeros(B, HV, dv, dk, device=dev)
-        z = torch.randn(T, HV * dv, device=dev, generator=g).bfloat16()
-        nw = torch.ones(dv, device=dev).bfloat16()
-        y = torch.empty(T, HV * dv, device=dev, dtype=torch.bfloat16)
-        # algorithmic bytes: q, k, v, z, ba read once, y written once, state read + written
-        work = 2.0 * T * (2 * H * dk + 2 * HV * dv + 2 * HV) + 2.0 * T * HV * dv + 2.0 * B * HV * dv * dk * 4
-        unit = "GB/s"
-
-        def launch():
-            ops.gdn_prefill(q, k, v, ba, A_log, dt_bias, cu, slots, B, state, z, nw, y, H, HV, dk, dv, dk ** -0.5,
-                            cfg.rms_norm_eps)
+        launch, work, unit, extra = _gdn_prefill_case(cfg, B, L, g)
     for _ in range(args.warmup):
         launch()
     torch.cuda.synchronize()
@@ -666,8 +649,189 @@ def run_op(args):
     torch.cuda.synchronize()
     ms = statistics.median(ev[2 * i].elapsed_time(ev[2 * i + 1]) for i in range(args.steps))
     rate = work / (ms * 1e-3) / (1e12 if unit == "TFLOP/s" else 1e9)
-    print(json.dumps({"op": args.op, "batch": B, "length": L, "median_ms": round(ms, 4),
-                      "achieved": round(rate, 1), "unit": unit, "work_per_launch": work}), flush=True)
+    line = {"op": args.op, "batch": B, "length": L, "median_ms": round(ms, 4), "achieved": round(rate, 1),
+            "unit": unit, "work_per_launch": work}
+    hbm, tf_burst, _, src = _peaks()
+    line["frac_of_peak"] = round(rate / (hbm if unit == "GB/s" else tf_burst), 4)
+    line["peak_source"] = f"{src} {'hbm_gbs' if unit == 'GB/s' else 'bf16_tflops (burst: kernel timed alone)'}"
+    if "extra" in locals():
+        line.update(extra)
+    print(json.dumps(line), flush=True)
+    return line
+
+
+def _gdn_gating_inputs(T, HV, dev, g):
+    """configs[3] gating: g = -softplus(N(0,1)), beta = sigmoid(N(0,1)). The kernels compute
+    g = -exp(A_log) softplus(a + dt_bias) and beta = sigmoid(b) from the projection's b and a
+    columns (REF:1274-1289), so A_log = 0 and dt_bias = 0 with a, b ~ N(0,1) give exactly
+    those distributions."""
+    import torch
+    ba = torch.randn(T, 2 * HV, device=dev, generator=g).bfloat16()  # [b | a]
+    A_log = torch.zeros(HV, device=dev)
+    dt_bias = torch.zeros(HV, device=dev).bfloat16()
+    return ba, A_log, dt_bias
+
+
+def _gdn_prefill_case(cfg, B, L, g, flashinfer=False):
+    """The chunked delta rule with the fused gating and gated RMSNorm over B requests of L
+    tokens, 27B head geometry, configs[3] inputs: q and k L2-normalised, v ~ N(0,1), the
+    gating above, zero initial state (a fresh prefill). ``flashinfer``: the same recurrence
+    through flashinfer's sm100 chunked kernel (the reference's REF:5084 kernel), given
+    alpha = exp(g) and beta in fp32 like the reference passes them; it computes o only
+    (no gating, no norm), so its algorithmic bytes omit z, y and ba and count o."""
+    import torch
+    from qwen38_inference_b200 import ops
+    dev = "cuda"
+    T = B * L
+    H, HV, dk, dv = cfg.linear_num_key_heads, cfg.linear_num_value_heads, cfg.linear_key_head_dim, \
+        cfg.linear_value_head_dim
+    nrm = torch.nn.functional.normalize
+    q = nrm(torch.randn(T, H, dk, device=dev, generator=g), dim=-1).bfloat16().view(T, H * dk)
+    k = nrm(torch.randn(T, H, dk, device=dev, generator=g), dim=-1).bfloat16().view(T, H * dk)
+    v = torch.randn(T, HV * dv, device=dev, generator=g).bfloat16()
+    ba, A_log, dt_bias = _gdn_gating_inputs(T, HV, dev, g)
+    a = ba[:, HV:].float()
+    gg = -torch.nn.functional.softplus(a)
+    extra = {"gating": "g = -softplus(a), a ~ N(0,1) (A_log = 0, dt_bias = 0); beta = sigmoid(b), b ~ N(0,1)",
+             "g_mean": round(float(gg.mean()), 4), "beta_mean": round(float(torch.sigmoid(ba[:, :HV].float()).mean()), 4)}
+    cu = torch.arange(0, T + 1, L, dtype=torch.int32, device=dev)
+    state = torch.zeros(B, HV, dv, dk, device=dev)
+    if flashinfer:
+        from flashinfer.gdn_kernels import chunk_gated_delta_rule_sm100
+        alpha = torch.exp(gg).contiguous()
+        beta = torch.sigmoid(ba[:, :HV].float()).bfloat16().float().contiguous()
+        o = torch.empty(T, HV, dv, device=dev, dtype=torch.bfloat16)
+        out_state = torch.empty(B, HV, dv, dk, device=dev)
+        q3, k3, v3 = q.view(T, H, dk), k.view(T, H, dk), v.view(T, HV, dv)
+        extra["kernel"] = "flashinfer chunk_gated_delta_rule_sm100 (CuTe DSL), o only"
+        work = 2.0 * T * (2 * H * dk + HV * dv) + 4.0 * T * HV * 2 + 2.0 * T * HV * dv + 2.0 * B * HV * dv * dk * 4
+
+        def launch():
+            chunk_gated_delta_rule_sm100(q3, k3, v3, alpha, beta, o, cu, state, out_state, dk ** -0.5)
+        return launch, work, "GB/s", extra
+    z = torch.randn(T, HV * dv, device=dev, generator=g).bfloat16()
+    nw = torch.ones(dv, device=dev).bfloat16()
+    y = torch.empty(T, HV * dv, device=dev, dtype=torch.bfloat16)
+    slots = torch.arange(B, dtype=torch.int32, device=dev)
+    # algorithmic bytes: q, k, v, z, ba read once, y written once, state read + written
+    work = 2.0 * T * (2 * H * dk + 2 * HV * dv + 2 * HV) + 2.0 * T * HV * dv + 2.0 * B * HV * dv * dk * 4
+    extra["flop_per_launch"] = (8 * dk * dv + 10 * 64 * dv) * T * HV  # SURVEY 8(d): (8d^2 + 10Cd) per token and head
+    extra["kernel"] = "qw gdn_prefill_kernel (chunked delta rule + gating + gated RMSNorm)"
+
+    def launch():
+        ops.gdn_prefill(q, k, v, ba, A_log, dt_bias, cu, slots, B, state, z, nw, y, H, HV, dk, dv, dk ** -0.5,
+                        cfg.rms_norm_eps)
+    return launch, work, "GB/s", extra
+
+
+def _gdn_decode_case(cfg, B, g):
+    """The fused decode step of B requests (conv update, L2 norm of q and k, gating, one
+    recurrent step of the fp32 state, gated RMSNorm), 27B head geometry, configs[3] inputs
+    (projection rows ~ N(0,1), the gating above, a state of a previous prefill ~ N(0, 0.05)).
+    Algorithmic bytes: the state read and written, the conv state read and written, the
+    projection row and ba read, y written (SURVEY 8(d) per-op units)."""
+    import torch
+    from qwen38_inference_b200 import ops
+    dev = "cuda"
+    H, HV, dk, dv = cfg.linear_num_key_heads, cfg.linear_num_value_heads, cfg.linear_key_head_dim, \
+        cfg.linear_value_head_dim
+    C = cfg.conv_dim
+    qkvz = torch.randn(B, cfg.qkvz_dim, device=dev, generator=g).bfloat16()
+    ba, A_log, dt_bias = _gdn_gating_inputs(B, HV, dev, g)
+    conv_w = (torch.randn(C, 4, device=dev, generator=g) * 0.5).bfloat16()
+    conv_state = torch.randn(B, C, 3, device=dev, generator=g).bfloat16()
+    state = torch.randn(B, HV, dv, dk, device=dev, generator=g) * 0.05
+    slots = torch.arange(B, dtype=torch.int32, device=dev)
+    nw = torch.ones(dv, device=dev).bfloat16()
+    y = torch.empty(B, HV * dv, device=dev, dtype=torch.bfloat16)
+    work = 2.0 * B * HV * dv * dk * 4 + 2.0 * B * C * 3 * 2 + 2.0 * B * (cfg.qkvz_dim + 2 * HV) + 2.0 * B * HV * dv
+    extra = {"gating": "g = -softplus(a), a ~ N(0,1) (A_log = 0, dt_bias = 0); beta = sigmoid(b), b ~ N(0,1)",
+             "kernel": "qw gdn_decode_kernel (conv + L2 norm + gating + recurrent step + gated RMSNorm)"}
+
+    def launch():
+        ops.gdn_decode(qkvz, ba, conv_w, conv_state, state, slots, B, A_log, dt_bias, nw, y, H, HV, dk, dv,
+                       cfg.rms_norm_eps)
+    return launch, work, "GB/s", extra
+
+
+def run_gdn_sweep(args):
+    """configs[3]: the gated-delta-rule op sweep, B in {16, 32, 64} x L in {2048, 1024, 512}
+    for the chunked prefill and B in {16, 32, 64} for the single-token decode step; one JSON
+    line per case (each with its fraction of the measured HBM peak)."""
+    lines = []
+    for B in (16, 32, 64):
+        for L in (2048, 1024, 512):
+            args.batch, args.length, args.op = B, L, "gdn_prefill"
+            lines.append(run_op(args))
+    for B in (16, 32, 64):
+        args.batch, args.length, args.op = B, 1, "gdn_decode"
+        lines.append(run_op(args))
+    return lines
+
+
+# the prefill step's projection shapes at B32 x L1024 and their launches per prefill
+# (qkv and o_proj in 16 attention layers, qkvz|ba and out_proj in 48 GDN layers, gate_up
+# and down in all 64, lm_head once on the 32 last rows)
+STEP_GEMMS = [("qkv", 32768, 14336, 5120, 0, 16), ("qkvz_ba", 32768, 16480, 5120, 0, 48),
+              ("o_proj", 32768, 5120, 6144, 0, 16), ("out_proj", 32768, 5120, 6144, 0, 48),
+              ("gate_up", 32768, 34816, 5120, 2, 64), ("down", 32768, 5120, 17408, 0, 64),
+              ("lm_head", 32, 248320, 5120, 1, 1)]
+
+
+def run_gemm_cublas(args):
+    """Comparator (outside the product path and its timed region): each projection shape of
+    the B32 x L1024 prefill through this library's tcgen05 GEMM and through cuBLAS
+    (torch F.linear, bf16 in and out), alternately in the same process at the same clocks,
+    CUDA events, median of ``--steps``. The SwiGLU shape is timed as our fused GEMM against
+    the plain cuBLAS GEMM of the same [T, 2I] product (cuBLAS then still owes the SwiGLU).
+    Totals weight each shape by its launches per prefill."""
+    import torch
+    import torch.nn.functional as F
+    from qwen38_inference_b200 import ops
+    dev = "cuda"
+    g = torch.Generator(device=dev).manual_seed(0)
+    ws = ops.Workspace(dev)
+    rows, ours_tot, cub_tot, flop_tot = [], 0.0, 0.0, 0.0
+    for name, M, N, K, kind, per in STEP_GEMMS:
+        x = torch.randn(M, K, device=dev, generator=g).bfloat16()
+        w = (torch.randn(N, K, device=dev, generator=g) * 0.02).bfloat16()
+        n_out = N // 2 if kind == 2 else N
+        y = torch.empty(M, n_out, device=dev, dtype=torch.float32 if kind == 1 else torch.bfloat16)
+        yc = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+
+        def ours():
+            ops.gemm(x, w, y, out_kind=kind, ws=ws)
+
+        def cub():
+            torch.matmul(x, w.t(), out=yc)
+        for fn in (ours, cub, ours, cub, ours, cub):
+            fn()
+        torch.cuda.synchronize()
+        t = {"ours": [], "cublas": []}
+        for _ in range(args.steps):
+            for key, fn in (("ours", ours), ("cublas", cub)):
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                fn()
+                e1.record()
+                e1.synchronize()
+                t[key].append(e0.elapsed_time(e1))
+        mo, mc = statistics.median(t["ours"]), statistics.median(t["cublas"])
+        flop = 2.0 * M * N * K
+        rows.append({"shape": name, "M": M, "N": N, "K": K, "launches_per_prefill": per, "ours_ms": round(mo, 4),
+                     "cublas_ms": round(mc, 4), "ours_tflops": round(flop / mo / 1e9, 1),
+                     "cublas_tflops": round(flop / mc / 1e9, 1), "ratio_cublas_over_ours": round(mc / mo, 4)})
+        ours_tot += per * mo
+        cub_tot += per * mc
+        flop_tot += per * flop
+        del x, w, y, yc
+    out = {"op": "gemm_cublas", "shapes": rows, "prefill_gemm_ms": {"ours": round(ours_tot, 2),
+                                                                     "cublas": round(cub_tot, 2)},
+           "prefill_gemm_tflops": {"ours": round(flop_tot / ours_tot / 1e9, 1),
+                                   "cublas": round(flop_tot / cub_tot / 1e9, 1)},
+           "ratio_cublas_over_ours": round(cub_tot / ours_tot, 4),
+           "note": "alternating launches; inputs larger than L2 (each A panel >= 335 MB)"}
+    print(json.dumps(out), flush=True)
 
 
 def run_reference(args):
@@ -704,15 +868,21 @@ def main():
     ap.add_argument("--decode-steps", type=int, default=10)
     ap.add_argument("--tp-allreduce", choices=["peer", "nccl"], default="peer",
                     help="long workload, N > 1: decode all-reduce inside the projection kernels (peer) or NCCL")
-    ap.add_argument("--op", choices=["gate_up", "qkvz_proj", "down_proj", "gdn_prefill", "conv_prefill",
+    ap.add_argument("--op", choices=["gate_up", "qkvz_proj", "down_proj", "gdn_prefill", "gdn_decode",
+                                     "gdn_sweep", "gdn_prefill_flashinfer", "gemm_cublas", "conv_prefill",
                                      "attn_prefill", "decode_step"],
                     default=None,
-                    help="time one kernel of the step alone (the case the ncu captures run)")
+                    help="time one kernel of the step alone (the case the ncu captures run); gdn_sweep: the "
+                         "configs[3] sweep; gdn_prefill_flashinfer and gemm_cublas: library comparators")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         print("note: fewer than 3 warm-up steps", file=sys.stderr)
     if args.op == "decode_step":
         run_decode_step(args)
+    elif args.op == "gdn_sweep":
+        run_gdn_sweep(args)
+    elif args.op == "gemm_cublas":
+        run_gemm_cublas(args)
     elif args.op:
         run_op(args)
     elif args.impl == "reference":

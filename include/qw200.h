@@ -41,11 +41,21 @@ typedef struct CUstream_st* qw_stream_t;
 #define QW_DEV_ERR_TIMEOUT_GDN 103 /* a bounded wait of the chunked delta-rule pipeline gave up */
 #define QW_DEV_ERR_TIMEOUT_ATTN 104 /* a bounded wait of the prefill attention pipeline gave up */
 #define QW_DEV_ERR_TIMEOUT_TP 105 /* a peer rank's row did not arrive in the one-shot all-reduce */
+#define QW_DEV_ERR_GEMM_COUNTER 106 /* the add-norm ticket pair of the weight-streaming GEMM did
+                                       not start at zero (an earlier launch gave up a wait, or two
+                                       launches overlapped); the launch skipped its add-norm rows */
 
 /* ---- library ----------------------------------------------------------------------- */
 int qw_version(void);
-/* Synchronizes the device, stores the device error word in *code and clears it. */
+/* Synchronizes the device, stores the device error word in *code and clears it; also
+ * zeroes the add-norm ticket pair of qw_gemm_add_rmsnorm (see there), so calls after a
+ * reported error start clean. */
 int qw_take_device_error(int* code);
+/* Queues a 4-byte copy of the device error word (current device) into host_dst on `stream`
+ * without synchronizing or clearing it: host_dst (pinned host memory) holds the word once
+ * the stream's work up to this call has finished. Lets a caller check for device-side
+ * failures at its own sync points; qw_take_device_error() then reads and clears the word. */
+int qw_peek_device_error_async(int* host_dst, qw_stream_t stream);
 
 /* ---- dense projections (REF:5054,5067,5069,5070,5087,5089,5092,5096: F.linear) ------ *
  * y = x[M,K] . w[N,K]^T with fp32 accumulation on tcgen05 tensor cores.
@@ -74,7 +84,12 @@ int qw_gemm_bf16(const void* x, const void* w, void* y, int64_t M, int64_t N, in
  * leave SMs idle (a 512-token chunk) splits K as well. The split-K partials ([splits, M, N]
  * fp32, workspace of qw_gemm_add_rmsnorm_workspace_bytes) are summed in k order by the
  * norm kernel. When that size is 0 for a large M, the call is a bf16 GEMM into hidden and
- * then qw_add_rmsnorm (REF:5087-5088 / 5092 + 5052: F.linear then gemma_fused_add_rmsnorm) */
+ * then qw_add_rmsnorm (REF:5087-5088 / 5092 + 5052: F.linear then gemma_fused_add_rmsnorm).
+ * When the add-norm runs inside the GEMM (qw_gemm_add_rmsnorm_kernels() == 1), its CTAs
+ * take turns from one ticket pair per device: such calls (and qw_gemm_add_rmsnorm_tp) must
+ * not overlap in time on one device, i.e. issue them on one stream. An overlap, or a pair
+ * left stale by a wait that gave up, is reported as QW_DEV_ERR_GEMM_COUNTER; no row outside
+ * [0, M) is ever touched.                                                                   */
 size_t qw_gemm_add_rmsnorm_workspace_bytes(int64_t M, int64_t N, int64_t K);
 /* Kernels one qw_gemm_add_rmsnorm call of this shape launches: 1 when the add-norm runs
  * inside the weight-streaming GEMM (its last M CTAs to finish each take one row), else 2. */

@@ -17,11 +17,19 @@ SZ = C.c_size_t
 F32 = C.c_float
 
 ERRORS = {1: "QW_ERR_ARG", 2: "QW_ERR_ALIGN", 3: "QW_ERR_UNSUPPORTED", 4: "QW_ERR_WORKSPACE", 5: "QW_ERR_DRIVER"}
+# values of the device error word (include/qw200.h QW_DEV_ERR_*)
+DEVICE_ERRORS = {101: "QW_DEV_ERR_TIMEOUT_GEMM", 102: "QW_DEV_ERR_INDEX", 103: "QW_DEV_ERR_TIMEOUT_GDN",
+                 104: "QW_DEV_ERR_TIMEOUT_ATTN", 105: "QW_DEV_ERR_TIMEOUT_TP", 106: "QW_DEV_ERR_GEMM_COUNTER"}
+
+
+def device_error_name(code: int) -> str:
+    return DEVICE_ERRORS.get(code, f"device error {code}")
 
 # name -> (restype, argtypes); kept in the order of include/qw200.h
 SIGNATURES = {
     "qw_version": (I32, []),
     "qw_take_device_error": (I32, [C.POINTER(I32)]),
+    "qw_peek_device_error_async": (I32, [P, P]),
     "qw_gemm_workspace_bytes": (SZ, [I64, I64, I64, I32]),
     "qw_gemm_bf16": (I32, [P, P, P, I64, I64, I64, I64, I64, I64, I32, P, SZ, P]),
     "qw_gemm_add_rmsnorm_workspace_bytes": (SZ, [I64, I64, I64]),

@@ -72,7 +72,11 @@ struct GemmParams {
   int64_t tp_slot_off;                  // byte offset of this call's slot in every buffer
 };
 
-// Ticket counters of partial_norm_finish, one pair per device (launches on one stream only).
+// Ticket counters of partial_norm_finish, one pair per device. Launches that use them must
+// not overlap in time (calls ordered on one stream): two overlapping launches would draw
+// tickets from the same pair. A launch that sees a ticket beyond its own grid knows the pair
+// was left stale (an earlier launch gave up a wait) and records QW_DEV_ERR_GEMM_COUNTER
+// instead of touching memory; qw_take_device_error() zeroes the pair after its synchronize.
 __device__ int g_norm_counter[2];
 
 static int* norm_counter_ptr() {
@@ -130,7 +134,22 @@ QW_DEV void partial_norm_finish(const GemmParams& p) {
   __syncthreads();
   const int first = (int)gridDim.x - p.norm_rows;
   const int t = s_ticket;
+  if (t < 0 || t >= (int)gridDim.x) {
+    // the pair did not start this launch at zero: no row index derived from it is valid
+    if (threadIdx.x == 0) set_error(p.err, QW_DEV_ERR_GEMM_COUNTER);
+    return;
+  }
   if (t < first) return;
+  // every exit from here on counts this finisher; the last one resets the pair for the next
+  // launch (all CTAs of the grid hold a ticket by then, unless the ticket wait gave up)
+  auto release = [&]() {
+    __syncthreads();
+    if (threadIdx.x == 0 && atomicAdd(p.norm_counter + 1, 1) == p.norm_rows - 1) {
+      p.norm_counter[0] = 0;
+      p.norm_counter[1] = 0;
+      __threadfence();
+    }
+  };
   if (threadIdx.x == 0) {
     int ok = 1;
     const uint64_t t0 = globaltimer();
@@ -144,8 +163,8 @@ QW_DEV void partial_norm_finish(const GemmParams& p) {
     s_ok = ok;
   }
   __syncthreads();
-  if (!s_ok) return;
-  const int m = t - first;
+  if (!s_ok) return;  // the pair stays stale: the next launch reports it (see above)
+  const int m = t - first;  // 0 <= m < norm_rows by the ticket check
   const int N = p.a_rows;
   const float* ws = reinterpret_cast<const float*>(p.out) + (int64_t)m * p.ldo;
   // the row's residual and the norm weights do not depend on the partials: their loads go
@@ -242,7 +261,10 @@ QW_DEV void partial_norm_finish(const GemmParams& p) {
       s_ok = ok;
     }
     __syncthreads();
-    if (!s_ok) return;
+    if (!s_ok) {  // every CTA of this grid holds a ticket: the reset stays exact
+      release();
+      return;
+    }
 #pragma unroll
     for (int i = 0; i < MAXC; ++i) {
       const int c = (threadIdx.x + i * NT) * 8;
@@ -264,12 +286,7 @@ QW_DEV void partial_norm_finish(const GemmParams& p) {
         const int c = (threadIdx.x + i * NT) * 8;
         if (c < N) store_bf16x8(p.hidden + (int64_t)m * N + c, v[i]);
       }
-      __syncthreads();
-      if (threadIdx.x == 0 && atomicAdd(p.norm_counter + 1, 1) == p.norm_rows - 1) {
-        p.norm_counter[0] = 0;
-        p.norm_counter[1] = 0;
-        __threadfence();
-      }
+      release();
       return;
     }
   }
@@ -312,12 +329,7 @@ QW_DEV void partial_norm_finish(const GemmParams& p) {
       store_bf16x8(p.hidden + (int64_t)m * N + c, o);
     }
   }
-  __syncthreads();
-  if (threadIdx.x == 0 && atomicAdd(p.norm_counter + 1, 1) == p.norm_rows - 1) {
-    p.norm_counter[0] = 0;  // every waiter is past its wait: reset for the next launch
-    p.norm_counter[1] = 0;
-    __threadfence();
-  }
+  release();  // every waiter is past its wait
 }
 
 constexpr int BM = 128;  // rows of one MMA (one TMEM accumulator)
@@ -1463,6 +1475,15 @@ extern "C" int qw_add_rmsnorm_f32(const float* x, int64_t n_parts, int64_t part_
 
 extern "C" int qw_version(void) { return 1; }
 
+extern "C" int qw_peek_device_error_async(int* host_dst, qw_stream_t stream) {
+  if (!host_dst) return QW_ERR_ARG;
+  int* word = qw::device_error_ptr();
+  if (!word) return QW_ERR_CUDA_BASE + (int)cudaErrorInvalidSymbol;
+  cudaError_t e = cudaMemcpyAsync(host_dst, word, sizeof(int), cudaMemcpyDeviceToHost,
+                                  reinterpret_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? QW_OK : QW_ERR_CUDA_BASE + (int)e;
+}
+
 extern "C" int qw_take_device_error(int* code) {
   if (!code) return QW_ERR_ARG;
   cudaError_t e = cudaDeviceSynchronize();
@@ -1471,6 +1492,11 @@ extern "C" int qw_take_device_error(int* code) {
   e = cudaMemcpyFromSymbol(&v, qw::g_device_error_word, sizeof(int));
   if (e != cudaSuccess) return QW_ERR_CUDA_BASE + (int)e;
   e = cudaMemcpyToSymbol(qw::g_device_error_word, &zero, sizeof(int));
+  if (e != cudaSuccess) return QW_ERR_CUDA_BASE + (int)e;
+  // nothing runs after the synchronize: a ticket pair left stale by a wait that gave up
+  // starts from zero again
+  const int zeros[2] = {0, 0};
+  e = cudaMemcpyToSymbol(qw::g_norm_counter, zeros, sizeof(zeros));
   if (e != cudaSuccess) return QW_ERR_CUDA_BASE + (int)e;
   *code = v;
   return QW_OK;

@@ -19,7 +19,7 @@ import collections
 import numpy as np
 import torch
 
-from . import ops
+from . import _lib, ops
 from .model import _Staging, build_metadata
 
 BF16 = torch.bfloat16
@@ -43,6 +43,9 @@ class Engine:
         self.graphs = collections.OrderedDict()
         self.use_graphs = True
         self.replays = 0  # calls served by a captured graph
+        self._err_host = torch.zeros(1, dtype=torch.int32, pin_memory=True)
+        self._err_np = self._err_host.numpy()  # host view: read and cleared outside inference mode too
+        self._err_event = None
 
     # ------------------------------------------------------------------ helpers
     def _decode_splits(self, capacity):
@@ -55,10 +58,42 @@ class Engine:
     def _meta_views(self, dev, offs):
         return {k: dev[o:o + n] for k, (o, n) in offs.items()}
 
+    # ------------------------------------------------------------------ device errors
+    def check_device_error(self, block=False):
+        """Raise :class:`QwError` if a kernel of an earlier call recorded a device-side failure
+        (a bounded wait that gave up, an index outside its range). Every call queues a copy of
+        the library's error word into pinned memory after its kernels; this reads it once that
+        copy has landed (at once when ``block``, else only if it already has), and on a nonzero
+        word takes and clears it (``qw_take_device_error``, which also resets the GEMM's ticket
+        counters) before raising."""
+        ev = self._err_event
+        if ev is None or not (block or ev.query()):
+            return
+        if block:
+            ev.synchronize()
+        self._err_event = None
+        if int(self._err_np[0]) != 0:
+            code = _lib.take_device_error()
+            self._err_np[0] = 0
+            raise _lib.QwError(f"device-side failure in an earlier forward_step: {_lib.device_error_name(code)}")
+
+    def _peek_device_error(self):
+        _lib.call("qw_peek_device_error_async", self._err_host.data_ptr(), ops._stream())
+        ev = torch.cuda.Event()
+        ev.record()
+        self._err_event = ev
+
     # ------------------------------------------------------------------ entry
     def forward(self, flat, slots, prefixes, lens, cache, is_decode, return_all_logits, dev_tokens=None):
         """One forward_step; ``dev_tokens`` (a device integer tensor of the call's T ids) replaces
-        the host ids of ``flat`` when the caller's ids are already on the device."""
+        the host ids of ``flat`` when the caller's ids are already on the device. Raises first
+        if an earlier call's kernels recorded a device error that has reached the host."""
+        self.check_device_error()
+        out = self._forward(flat, slots, prefixes, lens, cache, is_decode, return_all_logits, dev_tokens)
+        self._peek_device_error()
+        return out
+
+    def _forward(self, flat, slots, prefixes, lens, cache, is_decode, return_all_logits, dev_tokens=None):
         packed, offs, T = build_metadata(slots, prefixes, lens, cache.capacity)
         tokens = np.asarray(flat, dtype=np.int32)
         arr = np.concatenate([tokens, packed])

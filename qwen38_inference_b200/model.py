@@ -289,6 +289,13 @@ class Qwen38:
         self.tp.enable_peer_buffers(self.cfg.hidden_size, self.device)
         self._engine.graphs.clear()  # graphs captured on the NCCL path
 
+    def check_device_error(self):
+        """Wait for the calls queued so far and raise :class:`QwError` naming the failure if a
+        kernel recorded one (a bounded wait that gave up, an index outside its range).
+        ``forward_step`` also raises at its start for a failure of an earlier call that has
+        already reached the host, and ``generate`` checks at each of its token reads."""
+        self._engine.check_device_error(block=True)
+
     def close(self):
         """Release what outlives a call: captured graphs (they may hold NCCL calls) and the
         peer buffers of tensor parallelism. Collective under tensor parallelism."""
@@ -430,6 +437,7 @@ class Qwen38:
                 active, logits = self._decode_window(w, need, active, logits, cache, output, eos, max_new_tokens)
                 continue
             tokens = logits.argmax(-1).tolist()
+            self._engine.check_device_error(block=True)  # the read above synchronized the stream
             next_active, next_inputs = [], []
             for slot, token in zip(active, tokens):
                 output[slot].append(token)
@@ -464,6 +472,7 @@ class Qwen38:
             if j + 1 < w or w < need:  # the last step feeds no one when every request is done
                 logits = self._decode_device_tokens(t, cache, active)
         rows = torch.stack(toks).tolist()  # the window's only device -> host read
+        self._engine.check_device_error(block=True)
         pos = {s: k for k, s in enumerate(active)}
         alive = list(active)
         for j in range(w):

@@ -97,6 +97,9 @@ class _StubEngine:
                 out[r, self.next_token(ids[last])] = 1.0
         return out
 
+    def check_device_error(self, block=False):
+        self.calls and self.calls[-1].setdefault("checked", True)
+
 
 def _cpu_kv_grow(src_k, src_v, dst_k, dst_v, lengths, S, old_cap, new_cap):
     dst_k.zero_()
