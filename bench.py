@@ -37,6 +37,14 @@ UNIT = "tok/s"
 # The reference GPU path's published number for this exact metric on one B200
 # (results/shapes.csv: 1298.65 ms prefill + 35.26 ms decode at B32/L1024).
 BASELINE_TOK_S = 24589.0
+# results/shapes.csv:22-27, (batch, length) -> (prefill ms, decode ms): the same metric at
+# the other shapes the reference publishes (configs[1] is B16 x L2048)
+PUBLISHED_MS = {(16, 2048): (1292.67, 30.287), (32, 1024): (1298.65, 35.257), (64, 512): (1302.68, 44.580)}
+
+
+def published_tok_s(B, L):
+    p = PUBLISHED_MS.get((B, L))
+    return None if p is None else (B * L + B) / ((p[0] + p[1]) * 1e-3)
 
 
 EPI_NAMES = {0: "bf16", 1: "f32-of-bf16", 2: "SwiGLU"}
@@ -350,9 +358,11 @@ def run_gpu(args):
             "share_of_prefill": round(g_ms / mp, 4) if mp else None,
             "all_gemms": {"achieved": round(all_flops / (all_ms * 1e-3) / 1e12, 1), "launches": len(prof),
                           "share_of_prefill": round(all_ms / mp, 4) if mp else None}}
-    out = {"metric": METRIC, "value": round(tokens / (step_ms * 1e-3), 1), "unit": UNIT, "n_gpus": world,
+    pub = published_tok_s(B, L)
+    metric = METRIC if (B, L) == (32, 1024) else METRIC.replace("B32/L1024", f"B{B}/L{L}")
+    out = {"metric": metric, "value": round(tokens / (step_ms * 1e-3), 1), "unit": UNIT, "n_gpus": world,
            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_ms, 3), "higher_is_better": True,
-           "scaling": "weak", "vs_baseline": round(tokens / (step_ms * 1e-3) / BASELINE_TOK_S, 4),
+           "scaling": "weak", "vs_baseline": round(tokens / (step_ms * 1e-3) / pub, 4) if pub else None,
            "dtype": "bf16", "data": "synthetic (random-init N(0,0.02) 27B weights; uniform token ids, reference case seeds 26/27)",
            "config": {"workload": f"B{B}xL{L} prefill into a fresh cache + B{B} decode at {L} context, 27B hybrid",
                       "model": "Qwen3.8-27B hybrid geometry (48 GDN + 16 gated GQA), random init",
@@ -525,6 +535,208 @@ def run_long(args):
     del cache
     model.close()  # graphs holding NCCL calls and the peer buffers go before the process group
     torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def _dist_setup(args):
+    import torch
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def _max_over_ranks(vals, world):
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor(vals, dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return t.tolist()
+
+
+def run_continuous(args):
+    """configs[2], continuous batching on the 27B model: 32 requests with prompt lengths
+    uniform in [512, 1536] prefilled in one ragged call into a fresh cache, then 64 decode
+    steps; before every 8th step 4 requests (slots 4j..4j+3 at the j-th refill) are reset and
+    refilled with new prompts of uniform random length, in the same call as the other 28
+    requests' decode tokens (a mixed call, which the reference runs as prefill, REF:5027).
+    Exercises cache growth and slot reuse. One step = that whole sequence; ``value`` = tokens
+    consumed / device time (CUDA events per call, summed), max over ranks (each rank its own
+    replica and requests)."""
+    import torch
+    import torch.distributed as dist
+    world, rank, local = _dist_setup(args)
+    from qwen38_inference_b200 import Qwen38, ops
+    from qwen38_inference_b200.config import qwen38_27b
+    cfg = qwen38_27b()
+    B, V = 32, cfg.vocab_size
+    model = Qwen38(config=cfg, seed=0, device=f"cuda:{local}", max_context=8192)
+    g = torch.Generator().manual_seed(26 + 1000 * rank)
+    plan = [("prefill", [torch.randint(V, (int(n),), generator=g).tolist()
+                         for n in torch.randint(512, 1537, (B,), generator=g)], None)]
+    for step in range(64):
+        if step % 8 == 7:
+            j = step // 8
+            slots = list(range(4 * j, 4 * j + 4))
+            rows = [torch.randint(V, (int(torch.randint(512, 1537, (1,), generator=g)),), generator=g).tolist()
+                    if s in slots else [int(torch.randint(V, (1,), generator=g))] for s in range(B)]
+            plan.append(("mixed", rows, slots))
+        else:
+            plan.append(("decode", [[int(t)] for t in torch.randint(V, (B,), generator=g)], None))
+    stream = torch.cuda.current_stream()
+
+    def one_run(rec):
+        cache = model.new_cache(B, initial_capacity=64)
+        evs, tok, wall = [], 0, 0.0
+        h2d = d2h = 0
+        torch.cuda.synchronize()
+        for kind, rows, reset in plan:
+            if reset:
+                cache.reset(reset)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            t0 = time.perf_counter()
+            e0.record(stream)
+            lg = model.forward_step(rows, cache)
+            e1.record(stream)
+            h2d += model._engine.last_h2d_bytes
+            host = lg.cpu()
+            wall += time.perf_counter() - t0
+            d2h += host.numel() * 4
+            evs.append((kind, e0, e1))
+            tok += sum(len(r) for r in rows)
+        torch.cuda.synchronize()
+        if rec is not None:
+            ms = {k: [a.elapsed_time(b) for kk, a, b in evs if kk == k] for k in ("prefill", "decode", "mixed")}
+            rec.append((sum(sum(v) for v in ms.values()), wall * 1e3, ms, tok, h2d, d2h))
+
+    for _ in range(args.warmup):
+        one_run(None)
+    rec = []
+    ops.LAUNCHES[0] = 0
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    with ClockSampler(local) as clk:
+        for _ in range(args.steps):
+            one_run(rec)
+    launches = ops.LAUNCHES[0] // max(1, args.steps)
+    dev_ms = statistics.median(r[0] for r in rec)
+    wall_ms = statistics.median(r[1] for r in rec)
+    dev_ms, wall_ms = _max_over_ranks([dev_ms, wall_ms], world)
+    ms, tok, h2d, d2h = rec[-1][2], rec[-1][3], rec[-1][4], rec[-1][5]
+    out = {"metric": "continuous-batching tok/s (27B hybrid, bf16; B32, prompts U[512,1536], 64 decode steps, "
+                     "4 slots refilled every 8 steps)", "value": round(world * tok / (dev_ms * 1e-3), 1),
+           "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dev_ms, 3),
+           "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+           "data": "synthetic (random-init N(0,0.02) 27B weights; uniform token ids and prompt lengths, seed 26)",
+           "config": {"workload": "configs[2]: ragged B32 prefill, 56 decode calls and 8 mixed refill calls into "
+                                  "one cache", "global_batch": world * B, "seq_len": "512-1536",
+                      "parallelism": f"replicas x{world} (requests sharded)",
+                      "l2": "inputs larger than L2 (54 GB of weights streamed per call)"},
+           "tokens_per_step_per_rank": tok,
+           "median_ms": {"prefill_call": round(ms["prefill"][0], 3), "decode_call": round(statistics.median(ms["decode"]), 3),
+                         "mixed_call": round(statistics.median(ms["mixed"]), 3)},
+           "e2e": {"value": round(world * tok / (wall_ms * 1e-3), 1), "unit": UNIT, "h2d_bytes_per_step": h2d,
+                   "d2h_bytes_per_step": d2h},
+           "gpu_launches": launches, "clocks": clk.summary()}
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_split(args):
+    """configs[4], throughput half: decode of B64 requests at 512 tokens of context with the
+    requests split across the N GPUs of the job (B64/N per replica; strong scaling: the same
+    64 requests whatever N). One step = a prefill of each rank's requests (512 tokens each)
+    into a fresh cache, then ``--decode-steps`` decode calls (the first two set up the decode
+    graph, untimed). ``value`` = 64 / (median decode call, max over ranks) tokens per second;
+    the prefill is reported beside it. No collective on the data path."""
+    import torch
+    import torch.distributed as dist
+    world, rank, local = _dist_setup(args)
+    from qwen38_inference_b200 import Qwen38, ops
+    from qwen38_inference_b200.config import qwen38_27b
+    cfg = qwen38_27b()
+    B_all, L = 64, 512
+    if B_all % world:
+        raise SystemExit("the 64 requests must split evenly over the GPUs")
+    B = B_all // world
+    n_dec = max(3, args.decode_steps)
+    model = Qwen38(config=cfg, seed=0, device=f"cuda:{local}", max_context=8192)
+    g = torch.Generator().manual_seed(26)
+    ids = torch.randint(cfg.vocab_size, (B_all, L), generator=g)
+    prompts = [r.tolist() for r in ids[rank * B:(rank + 1) * B]]
+    g = torch.Generator().manual_seed(27)
+    dec = torch.randint(cfg.vocab_size, (n_dec, B_all), generator=g)[:, rank * B:(rank + 1) * B].tolist()
+    stream = torch.cuda.current_stream()
+
+    rec_io = [0]
+
+    def one_step(rec):
+        cache = model.new_cache(B, initial_capacity=64)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        model.forward_step(prompts, cache).cpu()
+        e1.record(stream)
+        dd, dw = [], []
+        for i, t in enumerate(dec):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            t0 = time.perf_counter()
+            a.record(stream)
+            model.forward_step([[x] for x in t], cache).cpu()
+            b.record(stream)
+            rec_io[0] = model._engine.last_h2d_bytes
+            if i >= 2:
+                dw.append((time.perf_counter() - t0) * 1e3)
+                dd.append((a, b))
+        torch.cuda.synchronize()
+        if rec is not None:
+            rec["p"].append(e0.elapsed_time(e1))
+            rec["d"].append(statistics.median(a.elapsed_time(b) for a, b in dd))
+            rec["d_wall"].append(statistics.median(dw))
+
+    for _ in range(args.warmup):
+        one_step(None)
+    rec = {"p": [], "d": [], "d_wall": []}
+    ops.LAUNCHES[0] = 0
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    with ClockSampler(local) as clk:
+        for _ in range(args.steps):
+            one_step(rec)
+    launches = ops.LAUNCHES[0] // max(1, args.steps)
+    mp, md, mdw = _max_over_ranks([statistics.median(rec["p"]), statistics.median(rec["d"]),
+                                   statistics.median(rec["d_wall"])], world)
+    pub = PUBLISHED_MS[(64, 512)][1]
+    out = {"metric": "decode tok/s at B64/L512 (27B hybrid, bf16), requests split across GPUs",
+           "value": round(B_all / (md * 1e-3), 1), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+           "warmup": args.warmup, "ms_per_step": round(md, 3), "higher_is_better": True, "scaling": "strong",
+           "vs_baseline": round(pub / md, 4) if world == 1 else None, "dtype": "bf16",
+           "data": "synthetic (random-init N(0,0.02) 27B weights; uniform token ids, seeds 26/27)",
+           "config": {"workload": f"configs[4]: B64 x L512 split {B} requests per GPU; prefill, then decode at 512",
+                      "global_batch": B_all, "seq_len": L, "parallelism": f"replicas x{world} (requests split)",
+                      "l2": "inputs larger than L2 (54 GB of weights streamed per call)"},
+           "median_ms": {"prefill_per_rank": round(mp, 3), "decode": round(md, 3)},
+           "reference_published_ms": {"prefill_b64_l512": PUBLISHED_MS[(64, 512)][0], "decode_b64_l512": pub},
+           "e2e": {"value": round(B_all / (mdw * 1e-3), 1), "unit": UNIT, "per": "decode call",
+                   "h2d_bytes_per_step": rec_io[0], "d2h_bytes_per_step": 4 * B * cfg.vocab_size},
+           "gpu_launches": launches, "clocks": clk.summary()}
+    if rank == 0:
+        print(json.dumps(out), flush=True)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -860,9 +1072,11 @@ def main():
     ap.add_argument("--batch", type=int, default=32)
     ap.add_argument("--length", type=int, default=1024)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["step", "long"], default="step",
-                    help="step: the headline B32/L1024 prefill+decode (replicas over N GPUs); long: one long "
-                         "request with head-wise tensor parallelism over N GPUs")
+    ap.add_argument("--workload", choices=["step", "long", "continuous", "split"], default="step",
+                    help="step: the headline B32/L1024 prefill+decode (replicas over N GPUs; --batch 16 "
+                         "--length 2048 is configs[1]); long: one long request with head-wise tensor parallelism "
+                         "over N GPUs; continuous: configs[2] continuous batching; split: configs[4] decode of "
+                         "B64 at L512 with the requests split across the N GPUs")
     ap.add_argument("--long-tokens", type=int, default=131071)
     ap.add_argument("--chunk", type=int, default=512)
     ap.add_argument("--decode-steps", type=int, default=10)
@@ -889,6 +1103,10 @@ def main():
         run_reference(args)
     elif args.workload == "long":
         run_long(args)
+    elif args.workload == "continuous":
+        run_continuous(args)
+    elif args.workload == "split":
+        run_split(args)
     else:
         run_gpu(args)
 

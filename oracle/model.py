@@ -94,8 +94,15 @@ class OracleModel:
     """CPU forward of the hybrid model. ``dtype`` is the storage dtype: bf16 reproduces the
     27B model's rounding points, fp32 is the tiny configuration's arithmetic."""
 
-    def __init__(self, cfg, weights: dict, *, dtype=torch.bfloat16, max_context=None):
+    def __init__(self, cfg, weights: dict, *, dtype=torch.bfloat16, max_context=None, gdn_prefill_form="token"):
+        """``gdn_prefill_form``: "token" runs prefill GDN as the per-token recurrence (the
+        reference's definition, REF:1355-1408 applied per token); "chunked" as the chunked form
+        with bf16 operands of oracle/chunked.py (the arithmetic of the prefill kernel, whose
+        algorithm the reference's flashinfer chunked kernel shares)."""
         from qwen38_inference_b200.config import nested_layers, rope_table  # pure-Python helpers
+        if gdn_prefill_form not in ("token", "chunked"):
+            raise ValueError("gdn_prefill_form must be 'token' or 'chunked'")
+        self.gdn_prefill_form = gdn_prefill_form
         self.cfg = cfg
         self.dtype = dtype
         self.rnd = ops.bf16 if dtype == torch.bfloat16 else ops.ident
@@ -148,7 +155,11 @@ class OracleModel:
 
     # ------------------------------------------------------------------ forward (REF:5004-5099)
     @torch.inference_mode()
-    def forward_step(self, input_ids, kv_cache, *, request_indices=None, return_all_logits=False):
+    def forward_step(self, input_ids, kv_cache, *, request_indices=None, return_all_logits=False, trace=None):
+        """REF:5004-5099. ``trace`` (a list) receives the layer loop's state at every half-layer
+        boundary as (hidden, residual) pairs, storage-dtype values as fp32: entry 2i is layer
+        i's normalized input, entry 2i + 1 the normalized input of its MLP, and the last entry
+        the last down projection's output with the residual before the final norm."""
         c, rnd, eps = self.cfg, self.rnd, self.eps
         rows, _ = token_batch(input_ids)
         cache = kv_cache
@@ -178,6 +189,8 @@ class OracleModel:
                 hidden = ops.gemma_rmsnorm(hidden, w["input_norm"], eps, rnd)
             else:
                 hidden, residual = ops.gemma_add_rmsnorm(hidden, residual, w["input_norm"], eps, rnd)
+            if trace is not None:
+                trace.append((hidden.clone(), residual.clone()))
             if kind == "full_attention":
                 proj = ops.linear(hidden, w["qkv"], rnd)
                 qg, k, v = proj.split([c.q_gate_dim, c.kv_dim, c.kv_dim], dim=-1)
@@ -209,14 +222,23 @@ class OracleModel:
                 rec = cache.recurrent[i]
                 for j, s in enumerate(slots):
                     a0, a1 = md["cu"][j], md["cu"][j + 1]
+                    if self.gdn_prefill_form == "chunked" and not md["is_decode"]:
+                        from .chunked import chunked_gdn
+                        o[a0:a1], rec[s] = chunked_gdn(q[a0:a1], k[a0:a1], v[a0:a1], a[a0:a1], b[a0:a1], w["A_log"],
+                                                       w["dt_bias"], rec[s], dk ** -0.5, HV // H)
+                        continue
                     o[a0:a1], rec[s] = ops.gdn_recurrence(q[a0:a1], k[a0:a1], v[a0:a1], g[a0:a1],
                                                           beta[a0:a1], rec[s], dk ** -0.5, HV // H)
                 o = rnd(o)
                 y = ops.gated_rmsnorm(o.reshape(-1, dv), w["norm"], z.reshape(-1, dv), eps, rnd)
                 hidden = ops.linear(y.reshape(-1, c.gdn_v_dim), w["out"], rnd)
             hidden, residual = ops.gemma_add_rmsnorm(hidden, residual, w["post_norm"], eps, rnd)
+            if trace is not None:
+                trace.append((hidden.clone(), residual.clone()))
             act = ops.silu_mul(ops.linear(hidden, w["gate_up"], rnd), rnd)
             hidden = ops.linear(act, w["down"], rnd)
+        if trace is not None:
+            trace.append((hidden.clone(), residual.clone()))
         hidden, residual = ops.gemma_add_rmsnorm(hidden, residual, self.final_norm, eps, rnd)
         if not return_all_logits:
             hidden = hidden[torch.tensor([e - 1 for e in md["cu"][1:]], dtype=torch.int64)]

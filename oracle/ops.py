@@ -64,8 +64,13 @@ def l2norm(x, eps=1e-6):
 
 # ----------------------------------------------------------------------------- dense
 def linear(x, w, rnd):
-    """``F.linear`` (REF:5054 etc.): fp32 accumulate of storage-dtype operands, rounded."""
-    return rnd(f32(x) @ f32(w).t())
+    """``F.linear`` (REF:5054 etc.): fp32 accumulate of storage-dtype operands, rounded.
+    Weights of more than 2^26 elements (the 27B lm_head) are widened 2^15 rows at a time,
+    so the fp32 copy stays small; each output is the same K-long dot product either way."""
+    if w.numel() <= 1 << 26:
+        return rnd(f32(x) @ f32(w).t())
+    xf = f32(x)
+    return rnd(torch.cat([xf @ f32(w[i:i + 32768]).t() for i in range(0, w.shape[0], 32768)], dim=-1))
 
 
 def silu_mul(gate_up, rnd):

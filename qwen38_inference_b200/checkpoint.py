@@ -53,37 +53,73 @@ def _names(cfg: HybridConfig):
     return out
 
 
+# fused checkpoint tensors accepted in place of a pair of split ones (REF:4944-4953); the
+# fused name is preferred when the index holds it, as in REF
+FUSED = {"in_proj_qkv.weight": "in_proj_qkvz.weight", "in_proj_z.weight": "in_proj_qkvz.weight",
+         "in_proj_b.weight": "in_proj_ba.weight", "in_proj_a.weight": "in_proj_ba.weight"}
+ACCEPTED_DTYPES = (torch.bfloat16, torch.float32, torch.float16)
+
+
+def validate_text_config(c: dict) -> None:
+    """The configuration checks of REF:4872-4882 and 4900-4903 that do not pin the 27B
+    sizes: the activation, the attention output gate, no bias, the swish gate of the GDN
+    norm, unquantized weights, the hybrid layer pattern and the default partial RoPE."""
+    if c.get("attention_bias") or c.get("hidden_act") != "silu" or not c.get("attn_output_gate"):
+        raise ValueError("Unsupported attention/activation configuration")
+    if c.get("output_gate_type", "swish") != "swish" or c.get("quantization_config"):
+        raise ValueError("Only unquantized weights with the swish output gate are supported")
+    n = c.get("num_hidden_layers")
+    interval = c.get("full_attention_interval", 4)
+    if c.get("layer_types") is not None and c["layer_types"] != [
+            "full_attention" if i % interval == interval - 1 else "linear_attention" for i in range(n)]:
+        raise ValueError("Unexpected hybrid attention layout")
+    rp = c.get("rope_parameters", {})
+    if rp.get("rope_type", "default") != "default":
+        raise ValueError("Unsupported rotary embedding configuration")
+
+
 def load_weights(path, cfg: HybridConfig, device, shard=None) -> dict:
-    """``shard(name, tensor) -> tensor`` keeps a tensor-parallel rank's slice of each tensor."""
+    """Read a checkpoint directory of REF's layout into the flat weight dict (REF:4911-4963):
+    every tensor of ``_names(cfg)`` with its shape checked, gate/up, q/k/v and b/a concatenated
+    along dim 0, the GDN input projections from their fused form when the index has it.
+    Raises ValueError, as REF does, for a missing tensor, a wrong shape, a quantized or other
+    unsupported dtype (REF:4922-4923) and any language-model tensor the model does not
+    consume other than the MTP head's (REF:4960-4962). ``shard(name, tensor) -> tensor``
+    keeps a tensor-parallel rank's slice of each tensor."""
     from safetensors import safe_open
     path = Path(path)
     index = json.loads((path / "model.safetensors.index.json").read_text())["weight_map"]
+    loaded = set()
+
+    def read(tname, shape):
+        if tname not in index:
+            raise ValueError(f"Missing weight: {tname}")
+        with safe_open(path / index[tname], framework="pt", device="cpu") as f:
+            t = f.get_tensor(tname)
+        if tuple(t.shape) != tuple(shape):
+            raise ValueError(f"Wrong shape for {tname}: {tuple(t.shape)}, expected {tuple(shape)}")
+        if t.dtype not in ACCEPTED_DTYPES:
+            raise ValueError(f"Quantized/unsupported weight: {tname} ({t.dtype})")
+        loaded.add(tname)
+        return t
+
     flat = {}
     for name, parts in _names(cfg).items():
-        ts = []
-        for tname, shape in parts:
-            alt = None
-            if tname not in index:
-                # fused checkpoint variants accepted by REF:4944-4953
-                if tname.endswith("in_proj_qkv.weight") or tname.endswith("in_proj_z.weight"):
-                    alt = tname.rsplit(".", 2)[0] + ".in_proj_qkvz.weight"
-                elif tname.endswith("in_proj_b.weight") or tname.endswith("in_proj_a.weight"):
-                    alt = tname.rsplit(".", 2)[0] + ".in_proj_ba.weight"
-                if alt is None or alt not in index:
-                    raise ValueError(f"Missing weight: {tname}")
-                with safe_open(path / index[alt], framework="pt", device="cpu") as f:
-                    ts = [f.get_tensor(alt)]
-                break
-            with safe_open(path / index[tname], framework="pt", device="cpu") as f:
-                t = f.get_tensor(tname)
-            if tuple(t.shape) != tuple(shape):
-                raise ValueError(f"Wrong shape for {tname}: {tuple(t.shape)}, expected {shape}")
-            ts.append(t)
-        t = torch.cat(ts) if len(ts) > 1 else ts[0]
+        base = parts[0][0].rsplit(".", 2)[0] + "."
+        fused = FUSED.get(parts[0][0][len(base):]) if len(parts) > 1 else None
+        if fused is not None and base + fused in index:
+            rows = sum(shape[0] for _, shape in parts)
+            t = read(base + fused, (rows,) + tuple(parts[0][1][1:]))
+        else:
+            ts = [read(tname, shape) for tname, shape in parts]
+            t = torch.cat(ts) if len(ts) > 1 else ts[0]
         if name.endswith(".conv"):
             t = t.reshape(t.shape[0], -1)
         t = t.to(device=device, dtype=torch.float32 if name.endswith("A_log") else torch.bfloat16)
         flat[name] = shard(name, t) if shard is not None else t
+    unexpected = [n for n in index if n.startswith(PREFIX) and n not in loaded and ".mtp." not in n]
+    if unexpected:
+        raise ValueError(f"Unconsumed language-model weights: {unexpected[:8]}")
     return flat
 
 

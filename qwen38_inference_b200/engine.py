@@ -177,7 +177,31 @@ class Engine:
         return out
 
     # ------------------------------------------------------------------ the layer loop
-    def _run(self, md, T, B, max_len, cache, is_decode, return_all_logits, ws=None, pf_splits=1):
+    def run_units(self, flat, slots, prefixes, lens, cache, is_decode, units, hidden, resid):
+        """Part of one forward_step's layer loop, eagerly, from a given state: ``units`` =
+        (first, last) half-layer units, unit 2i being layer i's mixer (attention or GDN, its
+        output projection and the post-mixer add-norm) and unit 2i + 1 its MLP (with the next
+        layer's input add-norm, except after the last layer). ``hidden`` (the normalized input
+        of unit ``first``) and ``resid`` (the residual stream), bf16 [T, H] on the device, are
+        updated in place to the state after unit ``last - 1``: the normalized input of the
+        next unit, or after the last layer the down projection's output. The cache is used
+        and written as by forward_step, but lengths are not committed. The parity tests feed
+        single units the oracle's state this way."""
+        packed, offs, T = build_metadata(slots, prefixes, lens, cache.capacity)
+        dev = self.staging.upload(np.concatenate([np.asarray(flat, dtype=np.int32), packed]), self.dev)
+        md = self._meta_views(dev[T:], offs)
+        md["tokens"] = dev[:T]
+        pf_splits = 1
+        if not is_decode:
+            pf_splits = ops.prefill_attn_splits(self.c.num_attention_heads, offs["tiles"][1] // 2,
+                                                max(p + n for p, n in zip(prefixes, lens)))
+        h, r = self._run(md, T, len(slots), max(lens), cache, is_decode, False, pf_splits=pf_splits, units=units,
+                         start=(hidden, resid))
+        hidden.copy_(h)
+        resid.copy_(r)
+
+    def _run(self, md, T, B, max_len, cache, is_decode, return_all_logits, ws=None, pf_splits=1, units=None,
+             start=None):
         m, c, dev = self.m, self.c, self.dev
         tp = m.tp
         ws = self.ws if ws is None else ws
@@ -185,7 +209,11 @@ class Engine:
         eps = m.eps
         resid = torch.empty(T, H, dtype=BF16, device=dev)
         hidden = torch.empty(T, H, dtype=BF16, device=dev)
-        ops.embed_rmsnorm(md["tokens"], m.embedding, m.layers[0]["input_norm"], resid, hidden, eps)
+        if start is None:
+            ops.embed_rmsnorm(md["tokens"], m.embedding, m.layers[0]["input_norm"], resid, hidden, eps)
+        else:
+            hidden.copy_(start[0])
+            resid.copy_(start[1])
         nq, nkv, d = c.num_attention_heads, c.num_key_value_heads, c.head_dim
         Hk, HV, dk, dv = c.linear_num_key_heads, c.linear_num_value_heads, c.linear_key_head_dim, c.linear_value_head_dim
         big = proj_stride(c)
@@ -228,7 +256,9 @@ class Engine:
                 ops.add_rmsnorm(hidden, resid, norm_w, eps)
 
         n_layers = len(m.layers)
-        for i, (kind, w) in enumerate(zip(m.layer_types, m.layers)):
+
+        def mixer(i):
+            kind, w = m.layer_types[i], m.layers[i]
             if kind == "full_attention":
                 qkv = proj[:, :c.qkv_dim]
                 ops.gemm(hidden, w["qkv"], qkv, ws=ws)
@@ -257,6 +287,9 @@ class Engine:
                                     cache.recurrent[i], qkvz[:, c.conv_dim:], w["norm"], y, Hk, HV, dk, dv,
                                     dk ** -0.5, eps)
                 proj_add_norm(y, w["out"], w["post_norm"])
+
+        def mlp(i):
+            w = m.layers[i]
             ops.gemm(hidden, w["gate_up"], act, out_kind=ops.OUT_SWIGLU, ws=ws)
             if i + 1 < n_layers:
                 proj_add_norm(act, w["down"], m.layers[i + 1]["input_norm"])  # the next layer's input norm
@@ -269,6 +302,12 @@ class Engine:
                 ops.round_f32_bf16(part, hidden)
             else:
                 ops.gemm(act, w["down"], hidden, ws=ws)
+
+        lo, hi = (0, 2 * n_layers) if units is None else units
+        for u in range(lo, hi):
+            (mlp if u % 2 else mixer)(u // 2)
+        if units is not None:
+            return hidden, resid
         rows = None if return_all_logits else md["last_rows"]
         R = T if return_all_logits else B
         fin = torch.empty(R, H, dtype=BF16, device=dev)

@@ -212,8 +212,13 @@ def _check_device(device):
 
 
 def load_checkpoint_config(path) -> HybridConfig:
+    """``config.json["text_config"]`` of a checkpoint directory (REF:4861), checked as REF
+    checks it apart from the fixed 27B sizes (checkpoint.validate_text_config)."""
+    from .checkpoint import validate_text_config
     c = json.loads((Path(path) / "config.json").read_text())
-    return HybridConfig.from_text_config(c.get("text_config", c))
+    c = c.get("text_config", c)
+    validate_text_config(c)
+    return HybridConfig.from_text_config(c)
 
 
 class Qwen38:

@@ -237,6 +237,10 @@ def test_conv_prefill(K):
     close(ko, ek, n_ulp=2, max_frac=0.05)
 
 
+# bf16 ulps allowed between the chunked prefill kernel and oracle/chunked.py
+GDN_CHUNK_ULPS = 4.0
+
+
 def _gdn_inputs(g, lens, H=2, HV=6, S=None):
     dk = 128
     T = sum(lens)
@@ -278,18 +282,42 @@ def test_gdn_prefill_chunked(K, lens):
                                                       state[s], dk ** -0.5, HV // H)
     exp_y = O.gated_rmsnorm(O.bf16(exp_o).reshape(-1, dk), norm_w, zbuf[:, HV * dk:].reshape(-1, dk), 1e-6,
                             O.bf16).reshape(T, HV, dk)
-    # the chunk products use bf16 operands (like the reference's chunked kernel), so the
-    # comparison is relative to each head's output scale
     got = y.cpu().float().view(T, HV, dk)
+    got_state = sd.cpu()
+    # 1) against the kernel-rounding restatement of the chunked form (oracle/chunked.py):
+    # the same bf16 / tf32 operands, so what is left is fp32 summation order and the rare
+    # bf16 rounding flip it causes in an operand tile; bounded in bf16 ulps of y (plus 2^-12
+    # of the token's largest |y| for outputs near zero), and the state to 1e-4 of its scale
+    from oracle.chunked import chunked_gdn
+    ch_state = state.clone()
+    ch_o = torch.empty(T, HV, dk)
+    for i, s in enumerate(slots):
+        a0, a1 = cu[i], cu[i + 1]
+        ch_o[a0:a1], ch_state[s] = chunked_gdn(q[a0:a1], k[a0:a1], v[a0:a1], ba[a0:a1, HV:], ba[a0:a1, :HV], A_log, dt,
+                                               state[s], dk ** -0.5, HV // H)
+    ch_y = O.gated_rmsnorm(ch_o.reshape(-1, dk), norm_w, zbuf[:, HV * dk:].reshape(-1, dk), 1e-6,
+                           O.bf16).reshape(T, HV, dk)
+    d = (got - ch_y).abs()
+    row = ch_y.abs().amax(dim=-1, keepdim=True)
+    n_ulp = d / torch.maximum(ulp(got), ulp(ch_y))
+    bad = d > GDN_CHUNK_ULPS * torch.maximum(ulp(got), ulp(ch_y)) + 2.0 ** -12 * row
+    assert not bool(bad.any()), f"{int(bad.sum())} outputs beyond {GDN_CHUNK_ULPS} ulps; max {n_ulp.max().item():.1f} ulps"
+    serr_ch = ((got_state - ch_state).abs().max() / ch_state.abs().max()).item()
+    assert serr_ch < 1e-4, f"state vs the chunked restatement: {serr_ch}"
+    # 2) against the per-token fp32 recurrence (the reference's definition): the bf16
+    # operands of the chunked form move the output by up to ~1e-2 of its scale (the size the
+    # CPU test of oracle/chunked.py measures between the two oracles), hence 3e-2 here
     scale = exp_y.abs().amax(dim=-1, keepdim=True).clamp_min(1e-3)
     err = ((got - exp_y).abs() / scale).max().item()
     assert err < 3e-2, f"relative output error {err}"
-    serr = ((sd.cpu() - exp_state).abs().max() / exp_state.abs().max()).item()
+    serr = ((got_state - exp_state).abs().max() / exp_state.abs().max()).item()
     assert serr < 2e-2, f"relative state error {serr}"
     untouched = [s for s in range(len(lens) + 1) if s not in slots]
     for s in untouched:
-        assert torch.equal(sd.cpu()[s], state[s])
-    print("gdn chunked: max relative output error", round(err, 5), "state", round(serr, 6))
+        assert torch.equal(got_state[s], state[s])
+    print("gdn chunked: vs restatement max", round(n_ulp.max().item(), 2), "ulps,",
+          f"{(d > 0).float().mean().item():.4f} of outputs differ, state {serr_ch:.2e};",
+          "vs token recurrence: output", round(err, 5), "state", round(serr, 6))
 
 
 def test_gdn_decode_fused(K):
