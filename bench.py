@@ -872,6 +872,10 @@ def run_op(args):
     return line
 
 
+class Unavailable(Exception):
+    """A library comparator that cannot run on this box (the reason goes into the JSON line)."""
+
+
 def _gdn_gating_inputs(T, HV, dev, g):
     """configs[3] gating: g = -softplus(N(0,1)), beta = sigmoid(N(0,1)). The kernels compute
     g = -exp(A_log) softplus(a + dt_bias) and beta = sigmoid(b) from the projection's b and a
@@ -909,7 +913,10 @@ def _gdn_prefill_case(cfg, B, L, g, flashinfer=False):
     cu = torch.arange(0, T + 1, L, dtype=torch.int32, device=dev)
     state = torch.zeros(B, HV, dv, dk, device=dev)
     if flashinfer:
-        from flashinfer.gdn_kernels import chunk_gated_delta_rule_sm100
+        try:
+            from flashinfer.gdn_kernels import chunk_gated_delta_rule_sm100
+        except Exception as e:
+            raise Unavailable(f"flashinfer sm100 chunked GDN not importable: {type(e).__name__}: {e}") from None
         alpha = torch.exp(gg).contiguous()
         beta = torch.sigmoid(ba[:, :HV].float()).bfloat16().float().contiguous()
         o = torch.empty(T, HV, dv, device=dev, dtype=torch.bfloat16)
@@ -920,6 +927,13 @@ def _gdn_prefill_case(cfg, B, L, g, flashinfer=False):
 
         def launch():
             chunk_gated_delta_rule_sm100(q3, k3, v3, alpha, beta, o, cu, state, out_state, dk ** -0.5)
+        try:
+            launch()  # the CuTe DSL kernel compiles at its first call
+            torch.cuda.synchronize()
+        except Exception as e:
+            msg = str(e).strip().splitlines()
+            raise Unavailable(f"flashinfer chunk_gated_delta_rule_sm100 failed at its first call: {type(e).__name__}: "
+                              f"{msg[0][:200] if msg else ''}") from None
         return launch, work, "GB/s", extra
     z = torch.randn(T, HV * dv, device=dev, generator=g).bfloat16()
     nw = torch.ones(dv, device=dev).bfloat16()
@@ -1005,6 +1019,8 @@ def run_gemm_cublas(args):
     ws = ops.Workspace(dev)
     rows, ours_tot, cub_tot, flop_tot = [], 0.0, 0.0, 0.0
     for name, M, N, K, kind, per in STEP_GEMMS:
+        if args.gemm_shape and name != args.gemm_shape:
+            continue
         x = torch.randn(M, K, device=dev, generator=g).bfloat16()
         w = (torch.randn(N, K, device=dev, generator=g) * 0.02).bfloat16()
         n_out = N // 2 if kind == 2 else N
@@ -1082,6 +1098,8 @@ def main():
     ap.add_argument("--decode-steps", type=int, default=10)
     ap.add_argument("--tp-allreduce", choices=["peer", "nccl"], default="peer",
                     help="long workload, N > 1: decode all-reduce inside the projection kernels (peer) or NCCL")
+    ap.add_argument("--gemm-shape", default=None, choices=[g[0] for g in STEP_GEMMS],
+                    help="--op gemm_cublas: time only this projection shape")
     ap.add_argument("--op", choices=["gate_up", "qkvz_proj", "down_proj", "gdn_prefill", "gdn_decode",
                                      "gdn_sweep", "gdn_prefill_flashinfer", "gemm_cublas", "conv_prefill",
                                      "attn_prefill", "decode_step"],
@@ -1098,7 +1116,10 @@ def main():
     elif args.op == "gemm_cublas":
         run_gemm_cublas(args)
     elif args.op:
-        run_op(args)
+        try:
+            run_op(args)
+        except Unavailable as e:
+            print(json.dumps({"op": args.op, "unavailable": str(e)}), flush=True)
     elif args.impl == "reference":
         run_reference(args)
     elif args.workload == "long":

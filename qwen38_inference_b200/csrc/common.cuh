@@ -343,7 +343,11 @@ QW_DEV void umma_bf16_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, ui
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
-// arrive on `bar` in every CTA of `mask` once the pair's MMAs issued so far complete
+// arrive on `bar` in every CTA of `mask` once the pair's MMAs issued so far complete.
+// The .multicast::cluster qualifier here only signals the mbarriers of the pair's two CTAs
+// (this GPU's shared memory, same offset in each CTA); it loads nothing. Every TMA load in
+// this library is a per-CTA copy without multicast (tma_load_2d, tma_load_2d_pair), so the
+// same code runs in multi-GPU jobs.
 QW_DEV void umma_commit_pair(uint64_t* bar, uint16_t mask) {
   asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
                    smem_u32(bar)),

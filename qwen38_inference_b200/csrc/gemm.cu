@@ -994,14 +994,17 @@ static int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const GemmP
   return QW_OK;
 }
 
-// CTA-pair GEMM for large M unless QW_GEMM_PAIR=0 selects the single-CTA kernels.
-static bool gemm_use_pairs() {
+// CTA-pair GEMM for large M: 1 (default) for the shapes the dispatch picks it for, 0 (the
+// environment variable QW_GEMM_PAIR=0) for none, 2 (QW_GEMM_PAIR=2) for every large-M shape
+// (tuning knobs).
+static int gemm_pair_mode() {
   static int v = -1;
   if (v < 0) {
     const char* e = getenv("QW_GEMM_PAIR");
-    v = (e && atoi(e) == 0) ? 0 : 1;
+    v = e ? atoi(e) : 1;
+    if (v < 0 || v > 2) v = 1;
   }
-  return v == 1;
+  return v;
 }
 
 struct SkinnyPlan {
@@ -1185,7 +1188,8 @@ extern "C" int qw_gemm_bf16(const void* x, const void* w, void* y, int64_t M, in
     // projections on B200: CTA pairs win for K <= 6144 plain outputs (qkvz, qkv, out_proj,
     // o_proj: 5-11%); the SwiGLU epilogue and K >= 8192 do better on one CTA (the pair's
     // cross-SM accumulator handshake costs more than it saves there).
-    if (M >= 256 && !swiglu && K < 8192 && gemm_use_pairs()) {
+    const int pair_mode = gemm_pair_mode();
+    if (M >= 256 && ((!swiglu && K < 8192 && pair_mode == 1) || pair_mode == 2)) {
       if ((rc = make_tmap(&ta, x, M, K, ldx, BM)) != QW_OK) return rc;
       if ((rc = make_tmap(&tb, w, N, K, ldw, P_BN / 2)) != QW_OK) return rc;
       p.a_rows = (int)M;

@@ -99,6 +99,7 @@ def _calls(vocab):
             ([ids(130), ids(70)], [1, 0]), ([ids(1), ids(1)], [0, 1])]
 
 
+@torch.inference_mode()
 def test_units_teacher_forced(wide):
     cfg, gpu, ref, ref_ch = wide
     B, cap = 2, 256  # no growth: both caches keep one layout
