@@ -742,6 +742,90 @@ def run_split(args):
         dist.destroy_process_group()
 
 
+def run_step_cublas(args):
+    """Comparator (not the product path): the B32 x L1024 prefill of the headline step with
+    every projection done by cuBLAS through torch (plain bf16 GEMMs; the SwiGLU, the logits'
+    fp32 widening, the add-norms and q/k norm + RoPE + KV store then run as separate steps,
+    the last two as this library's kernels), alternated call by call with the product's own
+    prefill on the same model, inputs and box, so both see the same power-capped clocks.
+    Prints both medians (CUDA events) and the clocks seen."""
+    import torch
+    import torch.nn.functional as F
+    from qwen38_inference_b200 import Qwen38, ops
+    from qwen38_inference_b200.config import qwen38_27b
+    cfg = qwen38_27b()
+    B, L = args.batch, args.length
+    model = Qwen38(config=cfg, seed=0, device="cuda:0", max_context=max(8192, 2 * L))
+    prefill, _ = make_inputs(cfg.vocab_size, B, L, 0)
+    own = {k: getattr(ops, k) for k in ("gemm", "gemm_qkv_rope_store", "gemm_add_rmsnorm")}
+
+    def lib_gemm(x, w, out=None, *, out_kind=ops.OUT_BF16, ws=None):
+        y = torch.matmul(x, w.t())
+        if out_kind == ops.OUT_SWIGLU:
+            if fused_silu is not None:
+                r = torch.empty(y.shape[0], y.shape[1] // 2, dtype=y.dtype, device=y.device)
+                fused_silu(r, y)
+            else:
+                g, u = y.chunk(2, dim=-1)
+                r = F.silu(g) * u
+        elif out_kind in (ops.OUT_F32_OF_BF16, ops.OUT_F32):
+            r = y.float()
+        else:
+            r = y
+        if out is None:
+            return r
+        out.copy_(r)
+        return out
+
+    def lib_qkv(x, w, qkv, nq, nkv, d, q_w, k_w, rope, positions, locations, kc, vc, eps, ws):
+        qkv.copy_(torch.matmul(x, w.t()))
+        ops.qk_norm_rope_store(qkv, nq, nkv, d, q_w, k_w, rope, positions, locations, kc, vc, eps)
+        return qkv
+
+    def lib_add_norm(x, w, resid, norm_w, hidden, eps, ws):
+        hidden.copy_(torch.matmul(x, w.t()))
+        ops.add_rmsnorm(hidden, resid, norm_w, eps)
+
+    lib = {"gemm": lib_gemm, "gemm_qkv_rope_store": lib_qkv, "gemm_add_rmsnorm": lib_add_norm}
+    swiglu_kind = "torch bf16 elementwise"
+    try:  # a fused silu-and-mul kernel, as the reference's stack has (sgl_kernel); vllm's if importable
+        import vllm._C  # noqa: F401
+        fused_silu = torch.ops._C.silu_and_mul
+        swiglu_kind = "vllm silu_and_mul (one fused kernel)"
+    except Exception:
+        fused_silu = None
+    stream = torch.cuda.current_stream()
+
+    def one(which):
+        for k, v in (lib if which == "cublas" else own).items():
+            setattr(ops, k, v)
+        cache = model.new_cache(B, initial_capacity=64)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        model.forward_step(prefill, cache)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        for k, v in own.items():
+            setattr(ops, k, v)
+        return e0.elapsed_time(e1)
+
+    for _ in range(args.warmup):
+        one("ours")
+        one("cublas")
+    t = {"ours": [], "cublas": []}
+    with ClockSampler(0) as clk:
+        for _ in range(args.steps):
+            for which in ("ours", "cublas"):
+                t[which].append(one(which))
+    mo, mc = statistics.median(t["ours"]), statistics.median(t["cublas"])
+    print(json.dumps({"op": "step_cublas", "batch": B, "length": L, "prefill_ms": {"ours": round(mo, 2),
+                      "cublas_gemms": round(mc, 2)}, "ratio_cublas_over_ours": round(mc / mo, 4),
+                      "samples": {k: [round(x, 1) for x in v] for k, v in t.items()}, "swiglu": swiglu_kind,
+                      "clocks": clk.summary()}),
+          flush=True)
+
+
 def run_decode_step(args):
     """The B32 decode step at 1024 tokens of context alone, for a launch list: three rounds of
     prefill + decode on fresh caches (which the buffer arena places at the same addresses,
@@ -1101,7 +1185,8 @@ def main():
     ap.add_argument("--gemm-shape", default=None, choices=[g[0] for g in STEP_GEMMS],
                     help="--op gemm_cublas: time only this projection shape")
     ap.add_argument("--op", choices=["gate_up", "qkvz_proj", "down_proj", "gdn_prefill", "gdn_decode",
-                                     "gdn_sweep", "gdn_prefill_flashinfer", "gemm_cublas", "conv_prefill",
+                                     "gdn_sweep", "gdn_prefill_flashinfer", "gemm_cublas", "step_cublas",
+                                     "conv_prefill",
                                      "attn_prefill", "decode_step"],
                     default=None,
                     help="time one kernel of the step alone (the case the ncu captures run); gdn_sweep: the "
@@ -1115,6 +1200,8 @@ def main():
         run_gdn_sweep(args)
     elif args.op == "gemm_cublas":
         run_gemm_cublas(args)
+    elif args.op == "step_cublas":
+        run_step_cublas(args)
     elif args.op:
         try:
             run_op(args)

@@ -133,6 +133,22 @@ int qw_qk_norm_rope_store(void* qkv, int64_t ldq, int64_t T, int64_t nq, int64_t
                           const void* k_w, const float* rope, int64_t rotary_dim, int64_t rope_rows,
                           const int32_t* positions, const int32_t* locations, void* k_cache, void* v_cache,
                           int64_t cache_rows, float eps, qw_stream_t stream);
+/* The attention input projection with q/k norm, RoPE and the KV store in its epilogue:
+ * qkv = bf16(x[M,K] . w[N,K]^T) with N = (2*nq + 2*nkv)*d (REF:5054 F.linear, REF:4940 row
+ * layout), then exactly the arithmetic of qw_qk_norm_rope_store on that output (REF:5055-5058:
+ * REF:83-190 + REF:2656-2687): q (normalized and rotated) and the gate are written to qkv;
+ * k (normalized and rotated) and v go only to their cache rows locations[t] (the k and v
+ * columns of qkv are left unwritten). For d = 256 and rotary_dim = 64 with tiles that fill the
+ * SMs, this is one tcgen05 GEMM whose epilogue does all of it (one 256-column tile = one head
+ * segment); decode (M <= 64) and chunks whose tiles leave SMs idle run the split-K product and
+ * one finishing kernel (partials summed in split order, then the same epilogue). Workspace:
+ * qw_gemm_qkv_workspace_bytes(M, N, K, d, rotary_dim) bytes.                                 */
+size_t qw_gemm_qkv_workspace_bytes(int64_t M, int64_t N, int64_t K, int64_t d, int64_t rotary_dim);
+int qw_gemm_qkv_rope_store(const void* x, const void* w, void* qkv, int64_t M, int64_t N, int64_t K, int64_t ldx,
+                           int64_t ldw, int64_t ldq, int64_t nq, int64_t nkv, int64_t d, const void* q_w,
+                           const void* k_w, const float* rope, int64_t rotary_dim, int64_t rope_rows,
+                           const int32_t* positions, const int32_t* locations, void* k_cache, void* v_cache,
+                           int64_t cache_rows, float eps, void* workspace, size_t ws_bytes, qw_stream_t stream);
 /* Causal varlen attention for prefill/extend; tiles = int32 pairs (request, first query)
  * of 128-query tiles; request i owns query rows cu[i]..cu[i+1] of the T rows of qkv, has
  * prefix[i] cached tokens and its keys start at cache row kv_base[i] of the cache_rows rows

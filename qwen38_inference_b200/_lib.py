@@ -49,6 +49,9 @@ SIGNATURES = {
     "qw_add_rmsnorm_rows": (I32, [P, P, P, I64, I64, I64, P, P, F32, P]),
     "qw_gated_rmsnorm": (I32, [P, I64, P, I64, P, P, I64, I64, I64, I64, F32, P]),
     "qw_qk_norm_rope_store": (I32, [P, I64, I64, I64, I64, I64, P, P, P, I64, I64, P, P, P, P, I64, F32, P]),
+    "qw_gemm_qkv_workspace_bytes": (SZ, [I64, I64, I64, I64, I64]),
+    "qw_gemm_qkv_rope_store": (I32, [P, P, P, I64, I64, I64, I64, I64, I64, I64, I64, I64, P, P, P, I64, I64, P, P, P,
+                                     P, I64, F32, P, SZ, P]),
     "qw_attn_prefill": (I32, [P, I64, I64, I64, I64, P, P, P, I64, P, P, P, P, I64, F32, I64, I64, P]),
     "qw_attn_prefill_split_workspace_bytes": (SZ, [I64, I64, I64, I64]),
     "qw_attn_prefill_split": (I32, [P, I64, I64, I64, I64, P, P, P, I64, P, P, P, P, I64, F32, I64, I64, I64, P, SZ, P]),

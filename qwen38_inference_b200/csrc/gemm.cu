@@ -36,7 +36,10 @@ int* device_error_ptr() {
   return ptrs[dev];
 }
 
-enum Epi : int { EPI_BF16 = 0, EPI_F32 = 1, EPI_SWIGLU = 2, EPI_PARTIAL = 3, EPI_F32RAW = 4, EPI_SWIGLU_SWAP = 5 };
+enum Epi : int {
+  EPI_BF16 = 0, EPI_F32 = 1, EPI_SWIGLU = 2, EPI_PARTIAL = 3, EPI_F32RAW = 4, EPI_SWIGLU_SWAP = 5,
+  EPI_QKV = 6  // the attention projection: q/k Gemma norm + RoPE, k/v into the cache (qkv_tile_row)
+};
 
 // fp32 outputs: EPI_F32 stores float(bf16(acc)) (F.linear().float()), EPI_F32RAW the accumulator itself
 template <int EPI>
@@ -70,7 +73,133 @@ struct GemmParams {
   int tp_round_only;                    // 1: hidden = bf16(sum over ranks), no add-norm
   const unsigned long long* tp_bases;   // device array [tp_world]: every rank's buffer base
   int64_t tp_slot_off;                  // byte offset of this call's slot in every buffer
+  // EPI_QKV: the output tile of 256 columns is one head segment of [q|gate per head, k, v]
+  int qkv_nq, qkv_nkv;
+  const __nv_bfloat16* q_w;
+  const __nv_bfloat16* k_w;
+  const float* rope;          // [rope_rows, 64] fp32: cos of 32 frequencies, then their sin
+  int64_t rope_rows;
+  const int32_t* positions;   // [M]
+  const int32_t* locs;        // [M] cache row of each token
+  __nv_bfloat16* kc;          // [cache_rows, nkv, 256]
+  __nv_bfloat16* vc;
+  int64_t cache_rows;
 };
+
+// The attention projection's epilogue for one token row of a 256-column output tile: tile bt
+// is one head segment of the row [q_0 | gate_0 | ... | q_{nq-1} | gate_{nq-1} | k_0 .. | v_0 ..]
+// (REF:4940), d = 256. x = bf16(acc) as F.linear rounds it; then, as REF:116-184 and
+// REF:2656-2687 do (and qk_norm_rope_store_kernel):
+//   gate: stored in place; v: stored at the token's cache row;
+//   q, k: xn = bf16(x * rsqrt(mean x^2 + eps) * (1 + w)), NeoX RoPE on dims [0, 64) with the
+//   pair (i, i + 32): o1 = xn1 cos - xn2 sin, o2 = xn2 cos + xn1 sin, rounded; q stored in
+//   place, k at the token's cache row.
+// t_row: TMEM address of this thread's row at the tile's first column. Every lane of the
+// warp runs the whole function (tcgen05.ld is warp-collective); a lane whose row is past M
+// (valid = false) reads along and touches no memory.
+QW_DEV void qkv_tile_row(const GemmParams& p, uint32_t t_row, int a_row, int bt, bool valid) {
+  constexpr int D = 256;
+  const int nq = p.qkv_nq, nkv = p.qkv_nkv;
+  __nv_bfloat16* row = reinterpret_cast<__nv_bfloat16*>(p.out) + (int64_t)a_row * p.ldo;
+  const bool is_q = bt < 2 * nq && (bt & 1) == 0;
+  const bool is_gate = bt < 2 * nq && (bt & 1) == 1;
+  const bool is_k = bt >= 2 * nq && bt < 2 * nq + nkv;
+  const int kh = is_k ? bt - 2 * nq : bt - 2 * nq - nkv;  // kv head of a k or v segment
+  __nv_bfloat16* dst = nullptr;
+  if (!valid) {
+  } else if (is_q || is_gate) {
+    dst = row + (int64_t)bt * D;
+  } else {
+    const int64_t loc = p.locs[a_row];
+    if (loc < 0 || loc >= p.cache_rows) {
+      set_error(p.err, QW_DEV_ERR_INDEX);
+      dst = nullptr;
+    } else if (loc != 0) {  // row 0 is reserved and never written (REF:2683)
+      dst = (is_k ? p.kc : p.vc) + (loc * nkv + kh) * D;
+    }
+  }
+  if (is_gate || (!is_q && !is_k)) {
+    // gate or v: the rounded projection as it is
+#pragma unroll 1
+    for (int c = 0; c < D; c += 32) {
+      uint32_t r[32];
+      tmem_ld_32x32b_x32(t_row + c, r);
+      tmem_ld_wait();
+      if (dst) {
+        float f[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(r[j]);
+#pragma unroll
+        for (int j = 0; j < 32; j += 8) store_bf16x8(dst + c + j, f + j);
+      }
+    }
+    return;
+  }
+  // q or k: sum of squares of the rounded row, then the norm and the rotation
+  float ss = 0.f;
+#pragma unroll 1
+  for (int c = 0; c < D; c += 32) {
+    uint32_t r[32];
+    tmem_ld_32x32b_x32(t_row + c, r);
+    tmem_ld_wait();
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const float x = bf16_round(__uint_as_float(r[j]));
+      ss += x * x;
+    }
+  }
+  const float inv = rsqrtf(ss / (float)D + p.eps);
+  const __nv_bfloat16* wt = is_k ? p.k_w : p.q_w;
+  int pos = valid ? p.positions[a_row] : 0;
+  if (pos < 0 || pos >= p.rope_rows) {
+    set_error(p.err, QW_DEV_ERR_INDEX);
+    pos = 0;
+  }
+  const float* cs = p.rope + (int64_t)pos * 64;
+  {
+    uint32_t r1[32], r2[32];
+    tmem_ld_32x32b_x32(t_row, r1);
+    tmem_ld_32x32b_x32(t_row + 32, r2);
+    tmem_ld_wait();
+    float o[64];
+#pragma unroll
+    for (int j = 0; j < 32; j += 8) {
+      float w1[8], w2[8];
+      load_bf16x8(wt + j, w1);
+      load_bf16x8(wt + 32 + j, w2);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float x1 = bf16_round(bf16_round(__uint_as_float(r1[j + e])) * inv * (w1[e] + 1.0f));
+        const float x2 = bf16_round(bf16_round(__uint_as_float(r2[j + e])) * inv * (w2[e] + 1.0f));
+        const float c = cs[j + e], sn = cs[32 + j + e];
+        o[j + e] = x1 * c + (-1.f * x2) * sn;
+        o[32 + j + e] = x2 * c + (1.f * x1) * sn;
+      }
+    }
+    if (dst) {
+#pragma unroll
+      for (int j = 0; j < 64; j += 8) store_bf16x8(dst + j, o + j);
+    }
+  }
+#pragma unroll 1
+  for (int c = 64; c < D; c += 32) {
+    uint32_t r[32];
+    tmem_ld_32x32b_x32(t_row + c, r);
+    tmem_ld_wait();
+    float o[32];
+#pragma unroll
+    for (int j = 0; j < 32; j += 8) {
+      float w[8];
+      load_bf16x8(wt + c + j, w);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) o[j + e] = bf16_round(bf16_round(__uint_as_float(r[j + e])) * inv * (w[e] + 1.0f));
+    }
+    if (dst) {
+#pragma unroll
+      for (int j = 0; j < 32; j += 8) store_bf16x8(dst + c + j, o + j);
+    }
+  }
+}
 
 // Ticket counters of partial_norm_finish, one pair per device. Launches that use them must
 // not overlap in time (calls ordered on one stream): two overlapping launches would draw
@@ -563,10 +692,15 @@ __global__ void __launch_bounds__(gemm_threads<MT>(), 1)
 #pragma unroll
               for (int j = 0; j < 32; j += 8) store_bf16x8(dst + j, f + j);
             } else {
-              for (int j = 0; j < ncols; ++j) dst[j] = f2bf(f[j]);
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (j < ncols) dst[j] = f2bf(f[j]);
             }
           }
         }
+      } else if constexpr (EPI == EPI_QKV) {
+        static_assert(BN == 256 && MT == 1, "the qkv epilogue takes one 256-column head segment per tile");
+        qkv_tile_row(p, t_row, a_row, bt, a_ok);
       } else {
 #pragma unroll 1
         for (int c = 0; c < BN; c += 32) {
@@ -591,7 +725,9 @@ __global__ void __launch_bounds__(gemm_threads<MT>(), 1)
 #pragma unroll
                 for (int j = 0; j < 32; j += 8) store_bf16x8(dst + j, f + j);
               } else {
-                for (int j = 0; j < nb; ++j) dst[j] = f2bf(f[j]);
+#pragma unroll
+                for (int j = 0; j < 32; ++j)
+                  if (j < nb) dst[j] = f2bf(f[j]);
               }
             } else if constexpr (EPI == EPI_F32 || EPI == EPI_F32RAW || EPI == EPI_PARTIAL) {
               // EPI_PARTIAL: this split's fp32 slice of a split-K product, [M, ldo] per split
@@ -605,20 +741,28 @@ __global__ void __launch_bounds__(gemm_threads<MT>(), 1)
                   *reinterpret_cast<float4*>(dst + j) = v4;
                 }
               } else {
-                for (int j = 0; j < nb; ++j) dst[j] = f32_out<EPI>(__uint_as_float(r[j]));
+#pragma unroll
+                for (int j = 0; j < 32; ++j)
+                  if (j < nb) dst[j] = f32_out<EPI>(__uint_as_float(r[j]));
               }
             }
           } else {
             // swap: out[b_row][a_row]; lanes of a warp write 32 consecutive a_rows
             if constexpr (EPI == EPI_BF16) {
               __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.out) + a_row;
-              for (int j = 0; j < nb; ++j) dst[(int64_t)(b0 + j) * p.ldo] = f2bf(__uint_as_float(r[j]));
+#pragma unroll
+              for (int j = 0; j < (BN < 32 ? BN : 32); ++j)
+                if (j < nb) dst[(int64_t)(b0 + j) * p.ldo] = f2bf(__uint_as_float(r[j]));
             } else if constexpr (EPI == EPI_F32 || EPI == EPI_F32RAW) {
               float* dst = reinterpret_cast<float*>(p.out) + a_row;
-              for (int j = 0; j < nb; ++j) dst[(int64_t)(b0 + j) * p.ldo] = f32_out<EPI>(__uint_as_float(r[j]));
+#pragma unroll
+              for (int j = 0; j < (BN < 32 ? BN : 32); ++j)
+                if (j < nb) dst[(int64_t)(b0 + j) * p.ldo] = f32_out<EPI>(__uint_as_float(r[j]));
             } else if constexpr (EPI == EPI_PARTIAL) {
               float* dst = reinterpret_cast<float*>(p.out) + (int64_t)split * p.part_stride + a_row;
-              for (int j = 0; j < nb; ++j) dst[(int64_t)(b0 + j) * p.ldo] = __uint_as_float(r[j]);
+#pragma unroll
+              for (int j = 0; j < (BN < 32 ? BN : 32); ++j)
+                if (j < nb) dst[(int64_t)(b0 + j) * p.ldo] = __uint_as_float(r[j]);
             }
           }
         }
@@ -793,10 +937,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
 #pragma unroll
               for (int j = 0; j < 32; j += 8) store_bf16x8(dst + j, f + j);
             } else {
-              for (int j = 0; j < ncols && j < 32; ++j) dst[j] = f2bf(f[j]);
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (j < ncols) dst[j] = f2bf(f[j]);
             }
           }
         }
+      } else if constexpr (EPI == EPI_QKV) {
+        qkv_tile_row(p, t_row, a_row, bt, a_ok);
       } else {
 #pragma unroll 1
         for (int c = 0; c < P_BN; c += 32) {
@@ -816,7 +964,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
 #pragma unroll
               for (int j = 0; j < 32; j += 8) store_bf16x8(dst + j, f + j);
             } else {
-              for (int j = 0; j < nb; ++j) dst[j] = f2bf(f[j]);
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (j < nb) dst[j] = f2bf(f[j]);
             }
           } else {
             float* dst = reinterpret_cast<float*>(p.out) + (int64_t)a_row * p.ldo + b0;
@@ -827,7 +977,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
                     make_float4(f32_out<EPI>(__uint_as_float(r[j])), f32_out<EPI>(__uint_as_float(r[j + 1])),
                                 f32_out<EPI>(__uint_as_float(r[j + 2])), f32_out<EPI>(__uint_as_float(r[j + 3])));
             } else {
-              for (int j = 0; j < nb; ++j) dst[j] = f32_out<EPI>(__uint_as_float(r[j]));
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (j < nb) dst[j] = f32_out<EPI>(__uint_as_float(r[j]));
             }
           }
         }
@@ -916,6 +1068,91 @@ __global__ void __launch_bounds__(kAddNormMaxThreads) splitk_add_rmsnorm_kernel(
     for (int j = 0; j < 8; ++j) o[j] = v[j] * rstd * (1.0f + wf[j]);
     store_bf16x8(hidden + (int64_t)m * N + c, o);
   }
+}
+
+// The attention projection after a split-K product (decode, or a chunk whose tiles leave SMs
+// idle): one warp per (token, head segment of D columns), lane owning D/32 consecutive
+// columns. x = bf16(sum of the split partials, in split order), then the epilogue of
+// qkv_tile_row for any D and rotary width: gate stored in place, v at the token's cache row,
+// q and k Gemma-normalized and rotated (pairs (i, i + rd/2)), q in place and k at the cache
+// row (REF:116-184, REF:2656-2687).
+template <int D>
+__global__ void qkv_finish_kernel(const float* __restrict__ ws, int splits, int64_t part_stride, int N, int T,
+                                  __nv_bfloat16* __restrict__ qkv, int64_t ldq, int nq, int nkv,
+                                  const __nv_bfloat16* __restrict__ q_w, const __nv_bfloat16* __restrict__ k_w,
+                                  const float* __restrict__ rope, int rd, int64_t rope_rows,
+                                  const int32_t* __restrict__ positions, const int32_t* __restrict__ locs,
+                                  __nv_bfloat16* __restrict__ kc, __nv_bfloat16* __restrict__ vc, int64_t cache_rows,
+                                  float eps, int* err) {
+  constexpr int E = D / 32;
+  const int segs = 2 * nq + 2 * nkv;
+  const int gw = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  if (gw >= T * segs) return;
+  const int t = gw / segs, sg = gw % segs;
+  const int c0 = lane * E;
+  const int64_t col = (int64_t)sg * D + c0;
+  float x[E];
+#pragma unroll
+  for (int j = 0; j < E; ++j) x[j] = 0.f;
+  for (int sp = 0; sp < splits; ++sp) {
+    const float* src = ws + sp * part_stride + (int64_t)t * N + col;
+#pragma unroll
+    for (int j = 0; j < E; ++j) x[j] += __ldcg(src + j);
+  }
+#pragma unroll
+  for (int j = 0; j < E; ++j) x[j] = bf16_round(x[j]);
+  const bool is_q = sg < 2 * nq && (sg & 1) == 0;
+  const bool is_gate = sg < 2 * nq && (sg & 1) == 1;
+  const bool is_k = sg >= 2 * nq && sg < 2 * nq + nkv;
+  const int kh = is_k ? sg - 2 * nq : sg - 2 * nq - nkv;
+  __nv_bfloat16* dst = nullptr;
+  if (is_q || is_gate) {
+    dst = qkv + (int64_t)t * ldq + col;
+  } else {
+    const int64_t loc = locs[t];
+    if (loc < 0 || loc >= cache_rows) {
+      if (lane == 0) set_error(err, QW_DEV_ERR_INDEX);
+      return;
+    }
+    if (loc == 0) return;  // reserved row (REF:2683)
+    dst = (is_k ? kc : vc) + (loc * nkv + kh) * D + c0;
+  }
+  if (is_gate || (!is_q && !is_k)) {
+    for (int j = 0; j < E; j += 2) *reinterpret_cast<uint32_t*>(dst + j) = pack_bf16x2(x[j], x[j + 1]);
+    return;
+  }
+  const __nv_bfloat16* wt = (is_k ? k_w : q_w) + c0;
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < E; ++j) ss += x[j] * x[j];
+  ss = warp_sum(ss);
+  const float inv = rsqrtf(ss / (float)D + eps);
+  float xn[E];
+#pragma unroll
+  for (int j = 0; j < E; ++j) xn[j] = bf16_round(x[j] * inv * (bf2f(wt[j]) + 1.0f));
+  const int half = rd / 2;
+  const int off = half / E;
+  int pos = positions[t];
+  if (pos < 0 || pos >= rope_rows) {
+    if (lane == 0) set_error(err, QW_DEV_ERR_INDEX);
+    pos = 0;
+  }
+  float partner[E], o[E];
+#pragma unroll
+  for (int j = 0; j < E; ++j) partner[j] = __shfl_sync(0xffffffffu, xn[j], (c0 < half) ? lane + off : lane - off);
+  if (c0 < rd) {
+    const int ci = c0 < half ? c0 : c0 - half;
+    const float* cs = rope + (int64_t)pos * rd + ci;
+    const float* sn = cs + half;
+    const float sign = c0 < half ? -1.f : 1.f;
+#pragma unroll
+    for (int j = 0; j < E; ++j) o[j] = xn[j] * cs[j] + sign * partner[j] * sn[j];
+  } else {
+#pragma unroll
+    for (int j = 0; j < E; ++j) o[j] = xn[j];
+  }
+  for (int j = 0; j < E; j += 2) *reinterpret_cast<uint32_t*>(dst + j) = pack_bf16x2(o[j], o[j + 1]);
 }
 
 // ------------------------------------------------------------------ host side
@@ -1457,6 +1694,141 @@ extern "C" int qw_gemm_add_rmsnorm_tp(const void* x, const void* w, int64_t M, i
     case 32: return launch_gemm<32, 8, EPI_PARTIAL>(ta, tb, p, s);
     default: return launch_gemm<64, 8, EPI_PARTIAL>(ta, tb, p, s);
   }
+}
+
+// ------------------------------------------------------------------ attention projection
+// Whether qw_gemm_qkv_rope_store takes a split-K product (decode, a chunk whose tiles leave SMs
+// idle) and its partial count; 0: the whole epilogue runs in the GEMM (one kernel).
+static int qkv_splits(int64_t M, int64_t N, int64_t K, int64_t d, int64_t rd) {
+  if (use_skinny(M)) return plan_skinny(M, N, K).splits;
+  const int s = plan_wide_splits(M, N, K);
+  if (s > 1) return s;
+  return (d == 256 && rd == 64) ? 0 : -1;  // -1: GEMM, then qk_norm_rope_store (other head sizes)
+}
+
+extern "C" size_t qw_gemm_qkv_workspace_bytes(int64_t M, int64_t N, int64_t K, int64_t d, int64_t rotary_dim) {
+  const int s = qkv_splits(M, N, K, d, rotary_dim);
+  return s > 0 ? (size_t)s * (size_t)M * (size_t)N * sizeof(float) : 0;
+}
+
+extern "C" int qw_gemm_qkv_rope_store(const void* x, const void* w, void* qkv, int64_t M, int64_t N, int64_t K,
+                                      int64_t ldx, int64_t ldw, int64_t ldq, int64_t nq, int64_t nkv, int64_t d,
+                                      const void* q_w, const void* k_w, const float* rope, int64_t rotary_dim,
+                                      int64_t rope_rows, const int32_t* positions, const int32_t* locations,
+                                      void* k_cache, void* v_cache, int64_t cache_rows, float eps, void* workspace,
+                                      size_t ws_bytes, qw_stream_t stream) {
+  QW_CHECK_ARG(x && w && qkv && q_w && k_w && rope && positions && locations && k_cache && v_cache, QW_ERR_ARG);
+  QW_CHECK_ARG(M > 0 && K > 0 && ldx >= K && ldw >= K && nq > 0 && nkv > 0 && nq % nkv == 0, QW_ERR_ARG);
+  QW_CHECK_ARG(N == (2 * nq + 2 * nkv) * d && ldq >= N && M < (1 << 30) && N < (1 << 30), QW_ERR_ARG);
+  QW_CHECK_ARG(rotary_dim > 0 && rotary_dim <= d && rotary_dim % 2 == 0 && rope_rows > 0 && cache_rows > 0, QW_ERR_ARG);
+  QW_CHECK_ARG(d == 64 || d == 128 || d == 256, QW_ERR_UNSUPPORTED);
+  QW_CHECK_ARG(((rotary_dim / 2) % (d / 32)) == 0, QW_ERR_UNSUPPORTED);
+  QW_CHECK_ARG(((uintptr_t)x % 16) == 0 && ((uintptr_t)w % 16) == 0 && (ldx % 8) == 0 && (ldw % 8) == 0 &&
+                   ((uintptr_t)qkv % 16) == 0 && (ldq % 8) == 0 && ((uintptr_t)k_cache % 16) == 0 &&
+                   ((uintptr_t)v_cache % 16) == 0 && ((uintptr_t)q_w % 16) == 0 && ((uintptr_t)k_w % 16) == 0,
+               QW_ERR_ALIGN);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const int splits = qkv_splits(M, N, K, d, rotary_dim);
+  if (splits < 0) {
+    int rc = qw_gemm_bf16(x, w, qkv, M, N, K, ldx, ldw, ldq, QW_OUT_BF16, workspace, ws_bytes, stream);
+    if (rc != QW_OK) return rc;
+    return qw_qk_norm_rope_store(qkv, ldq, M, nq, nkv, d, q_w, k_w, rope, rotary_dim, rope_rows, positions, locations,
+                                 k_cache, v_cache, cache_rows, eps, stream);
+  }
+  int rc;
+  if (splits == 0) {
+    // one kernel: 256-column tiles are head segments, the epilogue is qkv_tile_row
+    CUtensorMap ta, tb;
+    GemmParams p{};
+    p.err = device_error_ptr();
+    p.K = (int)K;
+    p.kb_total = (int)((K + BK - 1) / BK);
+    p.a_rows = (int)M;
+    p.b_rows = (int)N;
+    p.b_tiles = (int)(N / 256);
+    p.k_splits = 1;
+    p.kb_per_split = p.kb_total;
+    p.swap = 0;
+    p.out = qkv;
+    p.ldo = ldq;
+    p.vec_ok = 1;
+    p.eps = eps;
+    p.qkv_nq = (int)nq;
+    p.qkv_nkv = (int)nkv;
+    p.q_w = static_cast<const __nv_bfloat16*>(q_w);
+    p.k_w = static_cast<const __nv_bfloat16*>(k_w);
+    p.rope = rope;
+    p.rope_rows = rope_rows;
+    p.positions = positions;
+    p.locs = locations;
+    p.kc = static_cast<__nv_bfloat16*>(k_cache);
+    p.vc = static_cast<__nv_bfloat16*>(v_cache);
+    p.cache_rows = cache_rows;
+    if (M >= 256 && gemm_pair_mode() != 0) {
+      if ((rc = make_tmap(&ta, x, M, K, ldx, BM)) != QW_OK) return rc;
+      if ((rc = make_tmap(&tb, w, N, K, ldw, P_BN / 2)) != QW_OK) return rc;
+      p.a_tiles = (int)((M + 255) / 256);
+      p.group = raster_group(8);
+      return launch_pair<EPI_QKV>(ta, tb, p, s);
+    }
+    if ((rc = make_tmap(&ta, x, M, K, ldx, BM)) != QW_OK) return rc;
+    if ((rc = make_tmap(&tb, w, N, K, ldw, 256)) != QW_OK) return rc;
+    p.a_tiles = (int)((M + BM - 1) / BM);
+    p.group = raster_group(24);
+    return launch_gemm<256, 4, EPI_QKV>(ta, tb, p, s);
+  }
+  const size_t need = (size_t)splits * (size_t)M * (size_t)N * sizeof(float);
+  QW_CHECK_ARG(workspace != nullptr && ws_bytes >= need, QW_ERR_WORKSPACE);
+  QW_CHECK_ARG(((uintptr_t)workspace % 16) == 0, QW_ERR_ALIGN);
+  if (use_skinny(M)) {
+    const SkinnyPlan pl = plan_skinny(M, N, K);
+    CUtensorMap ta, tb;
+    if ((rc = make_tmap(&ta, w, N, K, ldw, BM)) != QW_OK) return rc;
+    if ((rc = make_tmap(&tb, x, M, K, ldx, pl.bn)) != QW_OK) return rc;
+    GemmParams p{};
+    p.err = device_error_ptr();
+    p.K = (int)K;
+    p.kb_total = pl.kb_total;
+    p.group = 1;
+    p.a_rows = (int)N;
+    p.b_rows = (int)M;
+    p.a_tiles = pl.a_tiles;
+    p.b_tiles = 1;
+    p.k_splits = pl.splits;
+    p.kb_per_split = pl.kb_per_split;
+    p.swap = 1;
+    p.out = workspace;
+    p.ldo = N;
+    p.part_stride = (int64_t)M * N;
+    switch (pl.bn) {
+      case 16: rc = launch_gemm<16, 8, EPI_PARTIAL>(ta, tb, p, s); break;
+      case 32: rc = launch_gemm<32, 8, EPI_PARTIAL>(ta, tb, p, s); break;
+      default: rc = launch_gemm<64, 8, EPI_PARTIAL>(ta, tb, p, s); break;
+    }
+  } else {
+    rc = launch_wide_partials(x, w, M, N, K, ldx, ldw, splits, workspace, s);
+  }
+  if (rc != QW_OK) return rc;
+  const int64_t warps = M * (2 * nq + 2 * nkv);
+  const unsigned blocks = (unsigned)((warps + 7) / 8);
+  const float* ws = static_cast<const float*>(workspace);
+  auto* q = static_cast<__nv_bfloat16*>(qkv);
+  const auto* qw_ = static_cast<const __nv_bfloat16*>(q_w);
+  const auto* kw_ = static_cast<const __nv_bfloat16*>(k_w);
+  auto* kc = static_cast<__nv_bfloat16*>(k_cache);
+  auto* vc = static_cast<__nv_bfloat16*>(v_cache);
+  int* err = device_error_ptr();
+  const int nsp = use_skinny(M) ? plan_skinny(M, N, K).splits : splits;
+#define QW_QKV_FINISH(DD)                                                                                            \
+  qkv_finish_kernel<DD><<<blocks, 256, 0, s>>>(ws, nsp, M * N, (int)N, (int)M, q, ldq, (int)nq, (int)nkv, qw_, kw_, \
+                                               rope, (int)rotary_dim, rope_rows, positions, locations, kc, vc,     \
+                                               cache_rows, eps, err)
+  if (d == 256) QW_QKV_FINISH(256);
+  else if (d == 128) QW_QKV_FINISH(128);
+  else QW_QKV_FINISH(64);
+#undef QW_QKV_FINISH
+  QW_LAUNCH_CHECK();
+  return QW_OK;
 }
 
 extern "C" int qw_add_rmsnorm_f32(const float* x, int64_t n_parts, int64_t part_stride, int64_t T, int64_t H,

@@ -1,7 +1,8 @@
 """The layer loop of ``forward_step`` on the sm_100a kernels (REF:5045-5099).
 
 Prefill (any call that is not pure decode, REF:5027) runs per layer:
-  norm -> [attention: qkv GEMM, q/k norm + RoPE + KV store, varlen attention (gated), o GEMM]
+  norm -> [attention: qkv GEMM with q/k norm + RoPE + KV store in its epilogue, varlen
+           attention (gated), o GEMM]
        or [GDN: one qkvz|ba GEMM, conv + split + L2 norm, chunked delta rule (gating
            fused, state in place), gated RMSNorm, out GEMM]
   -> add-norm -> gate_up GEMM with fused SwiGLU -> down GEMM
@@ -261,10 +262,11 @@ class Engine:
             kind, w = m.layer_types[i], m.layers[i]
             if kind == "full_attention":
                 qkv = proj[:, :c.qkv_dim]
-                ops.gemm(hidden, w["qkv"], qkv, ws=ws)
                 kc, vc = cache.kv[i]
-                ops.qk_norm_rope_store(qkv, nq, nkv, d, w["q_norm"], w["k_norm"], m.rope, md["positions"],
-                                       md["locations"], kc, vc, eps)
+                # projection, q/k norm, RoPE and the KV store in one GEMM epilogue (a split-K
+                # product and one finishing kernel for decode and sparse-tile chunks)
+                ops.gemm_qkv_rope_store(hidden, w["qkv"], qkv, nq, nkv, d, w["q_norm"], w["k_norm"], m.rope,
+                                        md["positions"], md["locations"], kc, vc, eps, ws)
                 att = mix[:, :c.attn_out_dim]
                 if is_decode:
                     ops.attn_decode(qkv, B, nq, nkv, d, kc, vc, md["seq_len"], md["kv_base"], cache.capacity, splits,

@@ -201,6 +201,35 @@ def qk_norm_rope_store(qkv, nq, nkv, d, q_w, k_w, rope, positions, locations, kc
               kc.data_ptr(), vc.data_ptr(), kc.shape[0], eps, _stream())
 
 
+def gemm_qkv_rope_store(x, w, qkv, nq, nkv, d, q_w, k_w, rope, positions, locations, kc, vc, eps, ws: Workspace):
+    """The attention input projection fused with q/k norm, RoPE and the KV store:
+    qkv[:, q and gate columns] and the cache rows of k and v, as gemm() into qkv followed by
+    qk_norm_rope_store() (the k and v columns of qkv are not written)."""
+    _req(x, BF16, "x")
+    _req(w, BF16, "w")
+    M, K = x.shape
+    N = w.shape[0]
+    if not (qkv.shape[0] == M and qkv.shape[1] >= N and qkv.stride(1) == 1 and x.stride(1) == 1 and w.stride(1) == 1
+            and kc.is_contiguous() and vc.is_contiguous() and kc.shape == vc.shape):
+        raise ValueError("gemm_qkv_rope_store expects x [M, K], w [N, K], qkv [M, >= N], contiguous K/V caches")
+    rd = rope.shape[1]
+    need = int(_lib.load().qw_gemm_qkv_workspace_bytes(M, N, K, d, rd))
+    buf = ws.get(need) if need else None
+    prof = PROFILE
+    if prof is not None:
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+    _lib.call("qw_gemm_qkv_rope_store", x.data_ptr(), w.data_ptr(), qkv.data_ptr(), M, N, K, x.stride(0), w.stride(0),
+              qkv.stride(0), nq, nkv, d, q_w.data_ptr(), k_w.data_ptr(), rope.data_ptr(), rd, rope.shape[0],
+              positions.data_ptr(), locations.data_ptr(), kc.data_ptr(), vc.data_ptr(), kc.shape[0], eps, _ptr(buf),
+              need, _stream())
+    if prof is not None:
+        e1.record()
+        prof.append((2.0 * M * N * K, e0, e1, (M, N, K, "qkv")))
+    LAUNCHES[0] += 2 if need else 1
+    return qkv
+
+
 def attn_prefill(qkv, nq, nkv, d, kc, vc, tiles, cu, prefix, kv_base, out, scale, splits=1, ws=None):
     """Causal varlen attention over the cache; qkv [T, ldq] rows, kc/vc [cache_rows, nkv, d].
     ``splits > 1`` divides every tile's keys over that many CTAs (long prefixes) and merges

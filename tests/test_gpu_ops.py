@@ -41,6 +41,17 @@ def close(got, exp, n_ulp=2.0, atol=1e-5, max_frac=0.05):
     assert frac <= max_frac, f"{frac:.3f} of elements differ"
 
 
+def close_rows(got, exp, n_ulp, max_frac):
+    """Like close(), in bf16 ulps of max(|element|, RMS of its row along the last dimension):
+    an element that cancellation made small (a rotated pair) is measured at its row's scale."""
+    got, exp = got.float().cpu(), exp.float().cpu()
+    d = (got - exp).abs()
+    rms = exp.pow(2).mean(dim=-1, keepdim=True).sqrt()
+    u = d / ulp(torch.maximum(torch.maximum(got.abs(), exp.abs()), rms))
+    assert not bool((u > n_ulp).any()), f"{int((u > n_ulp).sum())}/{d.numel()} beyond {n_ulp} ulps; max {u.max().item():.2f}"
+    assert (d > 0).float().mean().item() <= max_frac
+
+
 def gen(seed):
     return torch.Generator().manual_seed(seed)
 
@@ -286,8 +297,9 @@ def test_gdn_prefill_chunked(K, lens):
     got_state = sd.cpu()
     # 1) against the kernel-rounding restatement of the chunked form (oracle/chunked.py):
     # the same bf16 / tf32 operands, so what is left is fp32 summation order and the rare
-    # bf16 rounding flip it causes in an operand tile; bounded in bf16 ulps of y (plus 2^-12
-    # of the token's largest |y| for outputs near zero), and the state to 1e-4 of its scale
+    # bf16 rounding flip it causes in an operand tile; bounded in bf16 ulps (of an element, or
+    # of its (token, head) row's RMS where it is smaller); the state to 1e-2 of its largest
+    # entry (one flipped U element moves a row of S by ~2^-8 of that element's share)
     from oracle.chunked import chunked_gdn
     ch_state = state.clone()
     ch_o = torch.empty(T, HV, dk)
@@ -298,12 +310,13 @@ def test_gdn_prefill_chunked(K, lens):
     ch_y = O.gated_rmsnorm(ch_o.reshape(-1, dk), norm_w, zbuf[:, HV * dk:].reshape(-1, dk), 1e-6,
                            O.bf16).reshape(T, HV, dk)
     d = (got - ch_y).abs()
-    row = ch_y.abs().amax(dim=-1, keepdim=True)
-    n_ulp = d / torch.maximum(ulp(got), ulp(ch_y))
-    bad = d > GDN_CHUNK_ULPS * torch.maximum(ulp(got), ulp(ch_y)) + 2.0 ** -12 * row
+    rms = ch_y.pow(2).mean(dim=-1, keepdim=True).sqrt()
+    # bf16 ulps of max(|element|, RMS of its (token, head) row)
+    n_ulp = d / ulp(torch.maximum(torch.maximum(got.abs(), ch_y.abs()), rms))
+    bad = n_ulp > GDN_CHUNK_ULPS
     assert not bool(bad.any()), f"{int(bad.sum())} outputs beyond {GDN_CHUNK_ULPS} ulps; max {n_ulp.max().item():.1f} ulps"
     serr_ch = ((got_state - ch_state).abs().max() / ch_state.abs().max()).item()
-    assert serr_ch < 1e-4, f"state vs the chunked restatement: {serr_ch}"
+    assert serr_ch < 1e-2, f"state vs the chunked restatement: {serr_ch}"
     # 2) against the per-token fp32 recurrence (the reference's definition): the bf16
     # operands of the chunked form move the output by up to ~1e-2 of its scale (the size the
     # CPU test of oracle/chunked.py measures between the two oracles), hence 3e-2 here
@@ -372,5 +385,55 @@ def test_kv_grow(K):
 
 
 def test_no_device_error_after_ops(K):
+    from qwen38_inference_b200 import _lib
+    assert _lib.take_device_error() == 0
+
+
+@pytest.mark.parametrize("M", [2, 37, 130, 300, 512])
+@pytest.mark.parametrize("nq,nkv,d,rd", [(24, 4, 256, 64), (6, 1, 256, 64), (4, 2, 64, 16)])
+def test_gemm_qkv_rope_store_matches_unfused(K, M, nq, nkv, d, rd):
+    """The attention projection with q/k norm, RoPE and the KV store in the GEMM (or its
+    split-K finisher) against the GEMM followed by qk_norm_rope_store (tested against the
+    oracle above), on NaN-poisoned caches: the gate columns and the V rows bit for bit (the
+    same GEMM and rounding), q and the K rows within two bf16 ulps of the larger of the
+    element and its head row's RMS (the sum of squares is reduced in another order in the
+    GEMM epilogue, which can move both normalized elements of a rotated pair by an ulp), no
+    other cache row written. M = 2 and
+    37 take the weight-streaming split-K path, 130 the single-CTA kernel, 300 the CTA pair,
+    512 a split-K chunk; d = 64 runs the GEMM and qk_norm_rope_store."""
+    from qwen38_inference_b200.config import rope_table, HybridConfig
+    g = torch.Generator(device=DEV).manual_seed(M + nq)
+    H = 5120 if nq == 24 else 512
+    N = (2 * nq + 2 * nkv) * d
+    cfg = HybridConfig(hidden_size=64, intermediate_size=64, num_attention_heads=nq, num_key_value_heads=nkv,
+                       head_dim=d, linear_num_key_heads=1, linear_num_value_heads=1, linear_key_head_dim=128,
+                       linear_value_head_dim=128, linear_conv_kernel_dim=4, num_hidden_layers=4, vocab_size=8,
+                       partial_rotary_factor=rd / d)
+    rope = rope_table(cfg, 4096, DEV)
+    x = torch.randn(M, H, device=DEV, generator=g).bfloat16()
+    w = (torch.randn(N, H, device=DEV, generator=g) * 0.02).bfloat16()
+    qw = (torch.randn(d, device=DEV, generator=g) * 0.1).bfloat16()
+    kw = (torch.randn(d, device=DEV, generator=g) * 0.1).bfloat16()
+    rows = 2 * M + 64
+    pos = torch.randint(0, 4096, (M,), device=DEV, generator=g, dtype=torch.int32)
+    loc = (torch.randperm(rows - 64, device=DEV, generator=g)[:M] + 64).to(torch.int32)
+    ld = N + 16  # a row stride wider than the projection, as the engine's shared buffer
+    caches = [torch.full((rows, nkv, d), float("nan"), dtype=torch.bfloat16, device=DEV) for _ in range(4)]
+    ws = K.Workspace(DEV)
+    a = torch.zeros(M, ld, dtype=torch.bfloat16, device=DEV)[:, :N]
+    K.gemm_qkv_rope_store(x, w, a, nq, nkv, d, qw, kw, rope, pos, loc, caches[0], caches[1], 1e-6, ws)
+    b = torch.zeros(M, ld, dtype=torch.bfloat16, device=DEV)[:, :N]
+    K.gemm(x, w, b, ws=ws)
+    K.qk_norm_rope_store(b, nq, nkv, d, qw, kw, rope, pos, loc, caches[2], caches[3], 1e-6)
+    torch.cuda.synchronize()
+    qa, qb = a[:, :2 * nq * d].reshape(M, nq, 2, d), b[:, :2 * nq * d].reshape(M, nq, 2, d)
+    assert torch.equal(qa[:, :, 1], qb[:, :, 1])  # gates
+    close_rows(qa[:, :, 0], qb[:, :, 0], n_ulp=2, max_frac=0.02)
+    li = loc.long()
+    assert torch.equal(caches[1][li], caches[3][li])  # v rows
+    close_rows(caches[0][li], caches[2][li], n_ulp=2, max_frac=0.02)
+    untouched = torch.ones(rows, dtype=torch.bool, device=DEV)
+    untouched[li] = False
+    assert bool(torch.isnan(caches[0][untouched].float()).all()) and bool(torch.isnan(caches[1][untouched].float()).all())
     from qwen38_inference_b200 import _lib
     assert _lib.take_device_error() == 0
