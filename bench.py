@@ -689,15 +689,17 @@ def run_split(args):
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
-        model.forward_step(prompts, cache).cpu()
+        lg = model.forward_step(prompts, cache)
         e1.record(stream)
+        lg.cpu()
         dd, dw = [], []
         for i, t in enumerate(dec):
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             t0 = time.perf_counter()
             a.record(stream)
-            model.forward_step([[x] for x in t], cache).cpu()
+            lg = model.forward_step([[x] for x in t], cache)
             b.record(stream)
+            lg.cpu()  # the device-timed region ends before the copy; the wall time includes it
             rec_io[0] = model._engine.last_h2d_bytes
             if i >= 2:
                 dw.append((time.perf_counter() - t0) * 1e3)
@@ -831,12 +833,18 @@ def run_decode_step(args):
     prefill + decode on fresh caches (which the buffer arena places at the same addresses,
     so the decodes run eagerly, then capture, then replay the decode graph), a fourth
     prefill, and its decode from the graph bracketed by the CUDA profiler API, so that
-    ``ncu --profile-from-start off`` captures exactly that call's kernels."""
+    ``ncu --profile-from-start off`` captures exactly that call's kernels. ``--layers N``
+    builds the 27B geometry with N layers (every layer's kernels keep their 27B shapes; the
+    small-footprint case for counter captures)."""
+    import dataclasses
+
     import torch
     from qwen38_inference_b200 import Qwen38
     from qwen38_inference_b200.config import qwen38_27b
 
     cfg = qwen38_27b()
+    if args.layers:
+        cfg = dataclasses.replace(cfg, num_hidden_layers=args.layers)
     B, L = args.batch, args.length
     model = Qwen38(config=cfg, seed=0, device="cuda:0", max_context=max(8192, 2 * L))
     prefill, decode = make_inputs(cfg.vocab_size, B, L, 0)
@@ -1182,6 +1190,7 @@ def main():
     ap.add_argument("--decode-steps", type=int, default=10)
     ap.add_argument("--tp-allreduce", choices=["peer", "nccl"], default="peer",
                     help="long workload, N > 1: decode all-reduce inside the projection kernels (peer) or NCCL")
+    ap.add_argument("--layers", type=int, default=0, help="--op decode_step: layers of the 27B geometry (0: all 64)")
     ap.add_argument("--gemm-shape", default=None, choices=[g[0] for g in STEP_GEMMS],
                     help="--op gemm_cublas: time only this projection shape")
     ap.add_argument("--op", choices=["gate_up", "qkvz_proj", "down_proj", "gdn_prefill", "gdn_decode",

@@ -1423,10 +1423,17 @@ extern "C" int qw_gemm_bf16(const void* x, const void* w, void* y, int64_t M, in
     constexpr int BN = 256;
     // Kernel choice per shape, from sustained (power-capped) runs of a whole prefill's
     // projections on B200: CTA pairs win for K <= 6144 plain outputs (qkvz, qkv, out_proj,
-    // o_proj: 5-11%); the SwiGLU epilogue and K >= 8192 do better on one CTA (the pair's
-    // cross-SM accumulator handshake costs more than it saves there).
+    // o_proj: 5-11%) and for the SwiGLU gate_up (below); K >= 8192 (the down projection)
+    // does better on one CTA with 256-row tiles (pairs drew 2.6x its DRAM bytes there).
     const int pair_mode = gemm_pair_mode();
-    if (M >= 256 && ((!swiglu && K < 8192 && pair_mode == 1) || pair_mode == 2)) {
+    // The SwiGLU gate_up shape on pairs too (QW_GEMM_PAIR_SWIGLU=0 keeps it on one CTA): in
+    // the power-capped B32 x L1024 step the pair kernel runs it at 1413 against 1340 TFLOP/s
+    // and the step gains 0.8 % (two A/B runs on one box), although the SM clock drops ~4 %.
+    static const int pair_swiglu = [] {
+      const char* e = getenv("QW_GEMM_PAIR_SWIGLU");
+      return e ? atoi(e) : 1;
+    }();
+    if (M >= 256 && ((!swiglu && K < 8192 && pair_mode == 1) || pair_mode == 2 || (swiglu && pair_swiglu == 1))) {
       if ((rc = make_tmap(&ta, x, M, K, ldx, BM)) != QW_OK) return rc;
       if ((rc = make_tmap(&tb, w, N, K, ldw, P_BN / 2)) != QW_OK) return rc;
       p.a_rows = (int)M;

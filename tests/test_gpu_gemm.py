@@ -79,7 +79,8 @@ def test_gemm_f32_logits(ops, M, N, K):
 
 
 @pytest.mark.parametrize("M,I,K", [(300, 384, 512), (128, 1024, 256), (32, 512, 1024), (3, 256, 512),
-                                   (32, 17408, 5120), (7, 200, 256), (64, 2304, 512)])
+                                   (32, 17408, 5120), (7, 200, 256), (64, 2304, 512), (520, 200, 256),
+                                   (2048, 1536, 640)])
 def test_gemm_swiglu(ops, M, I, K):
     """SwiGLU in the epilogue: large M pairs gate and up columns in one B tile; decode
     (M <= 64) pairs 64 gate rows with their 64 up rows in one weight tile when the product
