@@ -191,6 +191,43 @@ QW_DEV void tma_load_2d(void* dst, const CUtensorMap* m, uint64_t* bar, int32_t 
       : "memory");
 }
 
+// TMA store of a box from this CTA's shared memory to global memory (bulk-group completion):
+// rows and columns of the box outside the tensor map's extent are not written.
+QW_DEV void tma_store_2d(const CUtensorMap* m, uint32_t smem_src, int32_t x, int32_t y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(m)),
+               "r"(smem_src), "r"(x), "r"(y)
+               : "memory");
+}
+QW_DEV void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// wait until at most N committed bulk groups of this thread still read their shared source
+template <int N>
+QW_DEV void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+// wait until at most N committed bulk groups of this thread are incomplete
+template <int N>
+QW_DEV void bulk_wait() {
+  asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
+}
+// generic-proxy writes to shared memory made visible to the async proxy (TMA, tcgen05)
+QW_DEV void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// 32 fp32 of one row as bf16 into a 64-column (128-byte) row of a SWIZZLE_128B staging box
+// (16-byte chunk j of row r at chunk j ^ (r % 8)); half = which 32 columns of the 64
+QW_DEV void stage_row_bf16_sw128(uint8_t* box, int r, int half, const float* f) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    uint4 u;
+    u.x = pack_bf16x2(f[8 * j], f[8 * j + 1]);
+    u.y = pack_bf16x2(f[8 * j + 2], f[8 * j + 3]);
+    u.z = pack_bf16x2(f[8 * j + 4], f[8 * j + 5]);
+    u.w = pack_bf16x2(f[8 * j + 6], f[8 * j + 7]);
+    const int chunk = (half * 4 + j) ^ (r & 7);
+    *reinterpret_cast<uint4*>(box + r * 128 + chunk * 16) = u;
+  }
+}
+
 // ------------------------------------------------------------------ tcgen05 (cta_group::1)
 QW_DEV void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)), "r"(ncols)

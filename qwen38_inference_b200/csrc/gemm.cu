@@ -59,6 +59,7 @@ struct GemmParams {
   int64_t part_stride; // EPI_PARTIAL: elements between split slices
   int* err;            // device error word
   int vec_ok;          // output rows 16-byte aligned: vector stores allowed
+  int tma_out;         // CTA-pair bf16 / SwiGLU outputs: 32 x 64 boxes staged in shared memory, TMA stores
   // EPI_PARTIAL (weight streaming) with norm_rows > 0: the residual add-norm of the output
   // rows after the split-K product, by the last norm_rows CTAs to finish (partial_norm_finish)
   int norm_rows;
@@ -477,6 +478,11 @@ struct GemmSmem {
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int BAR_OFFSET = STAGES * STAGE_BYTES;
   static constexpr int TOTAL = BAR_OFFSET + 256 + 1024;  // barriers + alignment slack
+  // TMA-store epilogue (BN = 256 large-M tiles): per epilogue warp NBOX staging boxes of
+  // 32 rows x 64 bf16 columns (4 KB, SWIZZLE_128B), two (used alternately) when they fit
+  static constexpr int STG = BAR_OFFSET + 1024, STG_BOX = 32 * 64 * 2;
+  static constexpr int NBOX = (STG + 4 * MT * 2 * STG_BOX + 1024 <= 232448) ? 2 : 1;
+  static constexpr int TOTAL_TMA_OUT = STG + 4 * MT * NBOX * STG_BOX + 1024;
   // EPI_SWIGLU_SWAP: the up half of a tile handed from its TMEM lanes to the gate lanes,
   // [64 rows][33] fp32 (padded against bank conflicts), after the barriers
   static constexpr int XCH = BAR_OFFSET + 256;
@@ -498,7 +504,7 @@ QW_DEV void decode_unit(const GemmParams& p, int unit, int& at, int& bt, int& sp
 template <int BN, int STAGES, int EPI, int MT>
 __global__ void __launch_bounds__(gemm_threads<MT>(), 1)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                        const GemmParams p) {
+                        const __grid_constant__ CUtensorMap tmC, const GemmParams p) {
   using L = GemmSmem<BN, STAGES, MT>;
   constexpr int NBUF = (2 * MT * BN <= 512) ? 2 : 1;  // TMEM accumulator buffers
   constexpr int ACC = MT * BN;                        // TMEM columns of one buffer
@@ -621,6 +627,8 @@ __global__ void __launch_bounds__(gemm_threads<MT>(), 1)
     const int q = warp & 3;             // TMEM lane quarter this warp may access
     const int msub = (warp - 2) >> 2;   // which 128-row accumulator this warp drains
     const int row_in_tile = msub * BM + q * 32 + lane;
+    uint8_t* stg = smem + L::STG + (warp - 2) * L::NBOX * L::STG_BOX;  // this warp's staging boxes
+    int sbox = 0;
     int tcount = 0;
     for (int u = blockIdx.x; u < units; u += gridDim.x, ++tcount) {
       int at, bt, split;
@@ -632,7 +640,51 @@ __global__ void __launch_bounds__(gemm_threads<MT>(), 1)
       const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + buf * ACC + msub * BN;
       const int a_row = at * (BM * MT) + row_in_tile;
       const bool a_ok = a_row < p.a_rows;
-      if constexpr (EPI == EPI_SWIGLU_SWAP) {
+      if ((EPI == EPI_BF16 || EPI == EPI_SWIGLU) && BN == 256 && p.tma_out) {
+        // 64 output columns at a time: the warp's 32 rows staged as bf16 (row = lane), then one
+        // TMA store of the 32 x 64 box; rows past M and columns past N are not written
+        const int row0 = at * (BM * MT) + msub * BM + q * 32;
+        constexpr int NOUT = EPI == EPI_SWIGLU ? BN / 2 : BN;
+#pragma unroll 1
+        for (int c = 0; c < NOUT; c += 64) {
+          uint8_t* box = stg + (sbox % L::NBOX) * L::STG_BOX;
+          ++sbox;
+          if (lane == 0) {  // the store issued from this box earlier has read it
+            if constexpr (L::NBOX == 2) bulk_wait_read<1>();
+            else bulk_wait_read<0>();
+          }
+          __syncwarp();
+#pragma unroll
+          for (int hf = 0; hf < 2; ++hf) {
+            float f[32];
+            if constexpr (EPI == EPI_SWIGLU) {
+              uint32_t g[32], v[32];
+              tmem_ld_32x32b_x32(t_row + c + 32 * hf, g);
+              tmem_ld_32x32b_x32(t_row + BN / 2 + c + 32 * hf, v);
+              tmem_ld_wait();
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                const float gg = bf16_round(__uint_as_float(g[j]));
+                const float uu = bf16_round(__uint_as_float(v[j]));
+                f[j] = gg / (1.0f + expf(-gg)) * uu;
+              }
+            } else {
+              uint32_t r[32];
+              tmem_ld_32x32b_x32(t_row + c + 32 * hf, r);
+              tmem_ld_wait();
+#pragma unroll
+              for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(r[j]);
+            }
+            stage_row_bf16_sw128(box, lane, hf, f);
+          }
+          fence_async_smem();
+          __syncwarp();
+          if (lane == 0 && bt * NOUT + c < p.b_rows && row0 < p.a_rows) {  // a box wholly past the edge writes nothing
+            tma_store_2d(&tmC, smem_u32(box), bt * NOUT + c, row0);
+            bulk_commit();
+          }
+        }
+      } else if constexpr (EPI == EPI_SWIGLU_SWAP) {
         // weight-streaming SwiGLU: TMEM lanes 0-63 hold gate rows at*64 + lane (warps with
         // q = 0, 1), lanes 64-127 the matching up rows (q = 2, 3). The up warps hand their
         // bf16-rounded values over in shared memory; the gate warps write
@@ -771,6 +823,7 @@ __global__ void __launch_bounds__(gemm_threads<MT>(), 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[buf]);
     }
+    if (lane == 0) bulk_wait<0>();  // every store of this warp complete before the CTA exits
   }
 
   tc_fence_before();
@@ -796,12 +849,17 @@ __global__ void __launch_bounds__(gemm_threads<MT>(), 1)
 constexpr int P_BN = 256, P_STAGES = 6;
 constexpr int P_A_BYTES = BM * BK * 2, P_B_BYTES = (P_BN / 2) * BK * 2, P_STAGE = P_A_BYTES + P_B_BYTES;
 constexpr int P_BAR = P_STAGES * P_STAGE;
-constexpr int P_SMEM = P_BAR + 256 + 1024;
+// output staging of the TMA-store epilogue: per epilogue warp two 32-row x 64-column bf16 boxes
+// (4 KB each, SWIZZLE_128B) used alternately, so a box is rewritten only after the store
+// issued from it two boxes earlier has read it
+constexpr int P_STG = P_BAR + 1024, P_STG_BOX = 32 * 64 * 2;
+constexpr int P_SMEM = P_STG + 4 * 2 * P_STG_BOX + 1024;
+static_assert(P_SMEM <= 232448, "CTA-pair GEMM shared memory above the sm_100 per-block limit");
 
 template <int EPI>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                     const GemmParams p) {
+                     const __grid_constant__ CUtensorMap tmC, const GemmParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + P_BAR);
@@ -903,6 +961,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
     const int q = warp & 3;
     const int row_in_tile = (int)rank * BM + q * 32 + lane;
     const uint32_t tempty_leader0 = mapa_shared(smem_u32(&tempty[0]), 0);
+    uint8_t* stg = smem + P_STG + q * 2 * P_STG_BOX;  // this warp's two staging boxes
+    int sbox = 0;
     int tcount = 0;
     for (int u = pair; u < units; u += npairs, ++tcount) {
       int at, bt, split;
@@ -914,7 +974,48 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
       const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + buf * P_BN;
       const int a_row = at * 256 + row_in_tile;
       const bool a_ok = a_row < p.a_rows;
-      if constexpr (EPI == EPI_SWIGLU) {
+      if ((EPI == EPI_BF16 || EPI == EPI_SWIGLU) && p.tma_out) {
+        // 64 output columns at a time: the warp's 32 rows staged as bf16 (row = lane), then one
+        // TMA store of the 32 x 64 box; rows past M and columns past N are not written
+        const int row0 = at * 256 + (int)rank * BM + q * 32;
+        constexpr int NOUT = EPI == EPI_SWIGLU ? P_BN / 2 : P_BN;
+#pragma unroll 1
+        for (int c = 0; c < NOUT; c += 64) {
+          uint8_t* box = stg + (sbox & 1) * P_STG_BOX;
+          ++sbox;
+          if (lane == 0) bulk_wait_read<1>();  // the store issued from this box two boxes ago
+          __syncwarp();
+#pragma unroll
+          for (int hf = 0; hf < 2; ++hf) {
+            float f[32];
+            if constexpr (EPI == EPI_SWIGLU) {
+              uint32_t g[32], v[32];
+              tmem_ld_32x32b_x32(t_row + c + 32 * hf, g);
+              tmem_ld_32x32b_x32(t_row + P_BN / 2 + c + 32 * hf, v);
+              tmem_ld_wait();
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                const float gg = bf16_round(__uint_as_float(g[j]));
+                const float uu = bf16_round(__uint_as_float(v[j]));
+                f[j] = gg / (1.0f + expf(-gg)) * uu;
+              }
+            } else {
+              uint32_t r[32];
+              tmem_ld_32x32b_x32(t_row + c + 32 * hf, r);
+              tmem_ld_wait();
+#pragma unroll
+              for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(r[j]);
+            }
+            stage_row_bf16_sw128(box, lane, hf, f);
+          }
+          fence_async_smem();
+          __syncwarp();
+          if (lane == 0 && bt * NOUT + c < p.b_rows && row0 < p.a_rows) {  // a box wholly past the edge writes nothing
+            tma_store_2d(&tmC, smem_u32(box), bt * NOUT + c, row0);
+            bulk_commit();
+          }
+        }
+      } else if constexpr (EPI == EPI_SWIGLU) {
         __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.out);
 #pragma unroll 1
         for (int c = 0; c < P_BN / 2; c += 32) {
@@ -988,6 +1089,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(tempty_leader0 + buf * 8);  // the leader's tempty[buf]
     }
+    if (lane == 0) bulk_wait<0>();  // every store of this warp complete before the CTA exits
   }
 
   tc_fence_before();
@@ -1199,9 +1301,12 @@ static int num_sms() {
 }
 
 template <int BN, int STAGES, int EPI, int MT = 1>
-static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, cudaStream_t s) {
+static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, cudaStream_t s,
+                       const CUtensorMap* tc = nullptr) {
+  using L = GemmSmem<BN, STAGES, MT>;
   auto kern = gemm_tcgen05_kernel<BN, STAGES, EPI, MT>;
-  const int smem = GemmSmem<BN, STAGES, MT>::TOTAL + (EPI == EPI_SWIGLU_SWAP ? GemmSmem<BN, STAGES, MT>::XCH_BYTES : 0);
+  constexpr bool tma_epi = (EPI == EPI_BF16 || EPI == EPI_SWIGLU) && BN == 256;
+  const int smem = tma_epi ? L::TOTAL_TMA_OUT : L::TOTAL + (EPI == EPI_SWIGLU_SWAP ? L::XCH_BYTES : 0);
   static bool configured = false;  // one flag per instantiation
   if (!configured) {
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
@@ -1209,13 +1314,16 @@ static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmP
   }
   const int units = p.a_tiles * p.b_tiles * p.k_splits;
   const int grid = units < num_sms() ? units : num_sms();
-  kern<<<grid, gemm_threads<MT>(), smem, s>>>(ta, tb, p);
+  GemmParams pp = p;
+  pp.tma_out = tma_epi && tc != nullptr && !p.swap;
+  kern<<<grid, gemm_threads<MT>(), smem, s>>>(ta, tb, pp.tma_out ? *tc : ta, pp);
   QW_LAUNCH_CHECK();
   return QW_OK;
 }
 
 template <int EPI>
-static int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, cudaStream_t s) {
+static int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, cudaStream_t s,
+                       const CUtensorMap* tc = nullptr) {
   auto kern = gemm_pair_kernel<EPI>;
   static bool configured = false;
   if (!configured) {
@@ -1226,9 +1334,22 @@ static int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const GemmP
   int grid = 2 * units;
   const int max_ctas = (num_sms() / 2) * 2;
   if (grid > max_ctas) grid = max_ctas;
-  kern<<<grid, 192, P_SMEM, s>>>(ta, tb, p);
+  GemmParams pp = p;
+  pp.tma_out = tc != nullptr;
+  kern<<<grid, 192, P_SMEM, s>>>(ta, tb, tc ? *tc : ta, pp);
   QW_LAUNCH_CHECK();
   return QW_OK;
+}
+
+// bf16 outputs of the large-M kernels through shared-memory staging and TMA stores unless the
+// environment variable QW_GEMM_TMA_STORE=0 selects the per-thread global stores (a tuning knob)
+static bool gemm_tma_store() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("QW_GEMM_TMA_STORE");
+    v = (e && atoi(e) == 0) ? 0 : 1;
+  }
+  return v == 1;
 }
 
 // CTA-pair GEMM for large M: 1 (default) for the shapes the dispatch picks it for, 0 (the
@@ -1447,10 +1568,14 @@ extern "C" int qw_gemm_bf16(const void* x, const void* w, void* y, int64_t M, in
       p.b_up_offset = (int)n_out;
       p.out = y;
       p.ldo = ldy;
-      if (swiglu) return launch_pair<EPI_SWIGLU>(ta, tb, p, s);
+      // bf16 outputs leave through TMA stores when their rows are 16-byte aligned
+      CUtensorMap tc;
+      const bool tma_out = (out_kind == QW_OUT_BF16 || swiglu) && p.vec_ok && gemm_tma_store() &&
+                           make_tmap(&tc, y, M, n_out, ldy, 32) == QW_OK;
+      if (swiglu) return launch_pair<EPI_SWIGLU>(ta, tb, p, s, tma_out ? &tc : nullptr);
       if (out_kind == QW_OUT_F32_OF_BF16) return launch_pair<EPI_F32>(ta, tb, p, s);
       if (out_kind == QW_OUT_F32) return launch_pair<EPI_F32RAW>(ta, tb, p, s);
-      return launch_pair<EPI_BF16>(ta, tb, p, s);
+      return launch_pair<EPI_BF16>(ta, tb, p, s, tma_out ? &tc : nullptr);
     }
     // 256-row tiles win when the main loop is long enough to hide their single-buffered
     // epilogue (measured on B200: K = 17408 +14%, N = 16384 +3%; SwiGLU, N = 5120 and
@@ -1469,17 +1594,22 @@ extern "C" int qw_gemm_bf16(const void* x, const void* w, void* y, int64_t M, in
     p.b_up_offset = (int)n_out;
     p.out = y;
     p.ldo = ldy;
+    // bf16 outputs leave through TMA stores when their rows are 16-byte aligned
+    CUtensorMap tc;
+    const bool tma_out = (out_kind == QW_OUT_BF16 || swiglu) && p.vec_ok && gemm_tma_store() &&
+                         make_tmap(&tc, y, M, n_out, ldy, 32) == QW_OK;
+    const CUtensorMap* tcp = tma_out ? &tc : nullptr;
     if (mt == 2) {
       p.group = raster_group(8);
-      if (swiglu) return launch_gemm<BN, 3, EPI_SWIGLU, 2>(ta, tb, p, s);
+      if (swiglu) return launch_gemm<BN, 3, EPI_SWIGLU, 2>(ta, tb, p, s, tcp);
       if (out_kind == QW_OUT_F32_OF_BF16) return launch_gemm<BN, 3, EPI_F32, 2>(ta, tb, p, s);
       if (out_kind == QW_OUT_F32) return launch_gemm<BN, 3, EPI_F32RAW, 2>(ta, tb, p, s);
-      return launch_gemm<BN, 3, EPI_BF16, 2>(ta, tb, p, s);
+      return launch_gemm<BN, 3, EPI_BF16, 2>(ta, tb, p, s, tcp);
     }
-    if (swiglu) return launch_gemm<BN, 4, EPI_SWIGLU>(ta, tb, p, s);
+    if (swiglu) return launch_gemm<BN, 4, EPI_SWIGLU>(ta, tb, p, s, tcp);
     if (out_kind == QW_OUT_F32_OF_BF16) return launch_gemm<BN, 4, EPI_F32>(ta, tb, p, s);
     if (out_kind == QW_OUT_F32) return launch_gemm<BN, 4, EPI_F32RAW>(ta, tb, p, s);
-    return launch_gemm<BN, 4, EPI_BF16>(ta, tb, p, s);
+    return launch_gemm<BN, 4, EPI_BF16>(ta, tb, p, s, tcp);
   }
 
   // Skinny: A = weights [N, K] (streamed once), B = activations [M, K]
