@@ -24,6 +24,8 @@ LIB = PKG / "libqw200.so"
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ARCH + ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr",
                      "-I", str(ROOT / "include")]
+# extra preprocessor definitions for a tuning build, e.g. QW_NVCC_DEFINES="QW_MBAR_SPIN"
+NVCC_FLAGS += ["-D" + d for d in os.environ.get("QW_NVCC_DEFINES", "").split() if d]
 
 
 def nvcc() -> str:
