@@ -121,6 +121,24 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(rows)}
 
 
+class HostReader:
+    """Reads a call's result (the logits) into one page-locked host buffer that is allocated
+    on first use (in the warm-up calls) and reused, so the device-to-host copy of every timed
+    call runs at the rate of pinned memory instead of paying for a fresh pageable array."""
+
+    def __init__(self):
+        self.buf = None
+
+    def __call__(self, t):
+        import torch
+        n = t.numel()
+        if self.buf is None or self.buf.numel() < n or self.buf.dtype != t.dtype:
+            self.buf = torch.empty(n, dtype=t.dtype, pin_memory=True)
+        out = self.buf[:n].view(t.shape)
+        out.copy_(t)
+        return out
+
+
 def make_inputs(V, B, L, rank):
     import torch
     g = torch.Generator().manual_seed(26 + 1000 * rank)
@@ -261,6 +279,7 @@ def run_gpu(args):
     model = Qwen38(config=cfg, seed=0, device=f"cuda:{local}", max_context=max(8192, 2 * L))
     prefill, decode = make_inputs(cfg.vocab_size, B, L, rank)
     stream = torch.cuda.current_stream()
+    read = HostReader()
 
     def barrier():
         torch.cuda.synchronize()
@@ -278,7 +297,7 @@ def run_gpu(args):
         t_issue_p = time.perf_counter()
         ev[1].record(stream)
         h2d = model._engine.last_h2d_bytes
-        host_p = lg.cpu()
+        host_p = read(lg)
         t1 = time.perf_counter()
         t_dec = time.perf_counter()
         ev[2].record(stream)
@@ -286,7 +305,7 @@ def run_gpu(args):
         t_issue_d = time.perf_counter()
         ev[3].record(stream)
         h2d += model._engine.last_h2d_bytes
-        host_d = lg.cpu()
+        host_d = read(lg)
         t2 = time.perf_counter()
         torch.cuda.synchronize()
         if record is not None:
@@ -435,6 +454,7 @@ def run_long(args):
     dec_tokens = torch.randint(cfg.vocab_size, (n_dec,), generator=g).tolist()
     chunks = [prompt[i:i + chunk] for i in range(0, n_tok, chunk)]
     stream = torch.cuda.current_stream()
+    read = HostReader()
 
     def one_step(n_chunks, rec):
         cache = model.new_cache(1, initial_capacity=64)
@@ -448,7 +468,7 @@ def run_long(args):
             lg = model.forward_step([c], cache)
             e1.record(stream)
             h2d += model._engine.last_h2d_bytes
-            host = lg.cpu()
+            host = read(lg)
             pw.append((time.perf_counter() - t0) * 1e3)
             d2h += host.numel() * 4
             pf.append((e0, e1))
@@ -458,7 +478,7 @@ def run_long(args):
             e0.record(stream)
             lg = model.forward_step([[t]], cache)
             e1.record(stream)
-            host = lg.cpu()
+            host = read(lg)
             if i >= 2:  # graph set-up calls are untimed
                 dw.append((time.perf_counter() - t0) * 1e3)
                 dd.append((e0, e1))
@@ -594,6 +614,7 @@ def run_continuous(args):
         else:
             plan.append(("decode", [[int(t)] for t in torch.randint(V, (B,), generator=g)], None))
     stream = torch.cuda.current_stream()
+    read = HostReader()
 
     def one_run(rec):
         cache = model.new_cache(B, initial_capacity=64)
@@ -609,7 +630,7 @@ def run_continuous(args):
             lg = model.forward_step(rows, cache)
             e1.record(stream)
             h2d += model._engine.last_h2d_bytes
-            host = lg.cpu()
+            host = read(lg)
             wall += time.perf_counter() - t0
             d2h += host.numel() * 4
             evs.append((kind, e0, e1))
@@ -681,6 +702,7 @@ def run_split(args):
     g = torch.Generator().manual_seed(27)
     dec = torch.randint(cfg.vocab_size, (n_dec, B_all), generator=g)[:, rank * B:(rank + 1) * B].tolist()
     stream = torch.cuda.current_stream()
+    read = HostReader()
 
     rec_io = [0]
 
@@ -691,7 +713,7 @@ def run_split(args):
         e0.record(stream)
         lg = model.forward_step(prompts, cache)
         e1.record(stream)
-        lg.cpu()
+        read(lg)
         dd, dw = [], []
         for i, t in enumerate(dec):
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -699,7 +721,7 @@ def run_split(args):
             a.record(stream)
             lg = model.forward_step([[x] for x in t], cache)
             b.record(stream)
-            lg.cpu()  # the device-timed region ends before the copy; the wall time includes it
+            read(lg)  # the device-timed region ends before the copy; the wall time includes it
             rec_io[0] = model._engine.last_h2d_bytes
             if i >= 2:
                 dw.append((time.perf_counter() - t0) * 1e3)

@@ -566,6 +566,8 @@ __global__ void __launch_bounds__(64) attn_decode_kernel(
     const __nv_bfloat16* __restrict__ qkv, int64_t ldq, int nq, int nkv, const __nv_bfloat16* __restrict__ kc,
     const __nv_bfloat16* __restrict__ vc, const int32_t* __restrict__ seq_len, const int32_t* __restrict__ kv_base,
     int keys_per_split, float scale_log2, float* __restrict__ part_o, float* __restrict__ part_ml, int splits) {
+  griddep_launch_dependents();  // programmatic dependent launch (launch_k): see common.cuh
+  griddep_wait();
   static_assert(G <= 8 && D % 16 == 0, "the query heads of a group fill one 8-wide n-tile");
   using L_ = DecodeSmem<D>;
   constexpr int KB = L_::KB, TK = L_::TK, NCH = D / 8, MT = D / 16, NW = L_::NW;
@@ -721,6 +723,8 @@ template <int D>
 __global__ void attn_decode_combine_kernel(const float* __restrict__ part_o, const float* __restrict__ part_ml,
                                            int splits, const __nv_bfloat16* __restrict__ qkv, int64_t ldq, int nq,
                                            __nv_bfloat16* __restrict__ out, int64_t ldo) {
+  griddep_launch_dependents();  // programmatic dependent launch (launch_k): see common.cuh
+  griddep_wait();
   const int bh = blockIdx.x;  // b * nq + h
   const int b = bh / nq, h = bh % nq;
   // the loops over splits are unrolled so that their independent loads are in flight together
@@ -824,11 +828,11 @@ static int attn_prefill_launch(const void* qkv, int64_t ldq, int64_t nq, int64_t
   const auto* q = static_cast<const __nv_bfloat16*>(qkv);
   auto* o = static_cast<__nv_bfloat16*>(out);
   if (d == 256)
-    attn_decode_combine_kernel<256><<<(unsigned)(T * nq), 128, 0, s>>>(part_o, part_ml, (int)splits, q, ldq, (int)nq, o, ldo);
+    launch_k(qw_pdl_small(), attn_decode_combine_kernel<256>, dim3((unsigned)(T * nq)), dim3(128), 0, s, part_o, part_ml, (int)splits, q, ldq, (int)nq, o, ldo);
   else if (d == 128)
-    attn_decode_combine_kernel<128><<<(unsigned)(T * nq), 128, 0, s>>>(part_o, part_ml, (int)splits, q, ldq, (int)nq, o, ldo);
+    launch_k(qw_pdl_small(), attn_decode_combine_kernel<128>, dim3((unsigned)(T * nq)), dim3(128), 0, s, part_o, part_ml, (int)splits, q, ldq, (int)nq, o, ldo);
   else
-    attn_decode_combine_kernel<64><<<(unsigned)(T * nq), 64, 0, s>>>(part_o, part_ml, (int)splits, q, ldq, (int)nq, o, ldo);
+    launch_k(qw_pdl_small(), attn_decode_combine_kernel<64>, dim3((unsigned)(T * nq)), dim3(64), 0, s, part_o, part_ml, (int)splits, q, ldq, (int)nq, o, ldo);
   QW_LAUNCH_CHECK();
   return QW_OK;
 }
@@ -891,22 +895,22 @@ extern "C" int qw_attn_decode(const void* qkv, int64_t ldq, int64_t B, int64_t n
   const auto* kc = static_cast<const __nv_bfloat16*>(k_cache);
   const auto* vc = static_cast<const __nv_bfloat16*>(v_cache);
   if (d == 256 && group == 6)
-    attn_decode_kernel<256, 6><<<grid, 32 * DecodeSmem<256>::NW, DecodeSmem<256>::TOTAL, s>>>(q, ldq, (int)nq, (int)nkv, kc, vc, seq_len, kv_base, kps, sl2,
+    launch_k(qw_pdl_small(), attn_decode_kernel<256, 6>, dim3(grid), dim3(32 * DecodeSmem<256>::NW), DecodeSmem<256>::TOTAL, s, q, ldq, (int)nq, (int)nkv, kc, vc, seq_len, kv_base, kps, sl2,
                                                     part_o, part_ml, (int)splits);
   else if (d == 256 && group == 3)  // 8-way tensor parallel: 3 query heads per replicated KV head
-    attn_decode_kernel<256, 3><<<grid, 32 * DecodeSmem<256>::NW, DecodeSmem<256>::TOTAL, s>>>(q, ldq, (int)nq, (int)nkv, kc, vc, seq_len, kv_base, kps, sl2,
+    launch_k(qw_pdl_small(), attn_decode_kernel<256, 3>, dim3(grid), dim3(32 * DecodeSmem<256>::NW), DecodeSmem<256>::TOTAL, s, q, ldq, (int)nq, (int)nkv, kc, vc, seq_len, kv_base, kps, sl2,
                                                     part_o, part_ml, (int)splits);
   else if (d == 64 && group == 2)
-    attn_decode_kernel<64, 2><<<grid, 32 * DecodeSmem<64>::NW, DecodeSmem<64>::TOTAL, s>>>(q, ldq, (int)nq, (int)nkv, kc, vc, seq_len, kv_base, kps, sl2,
+    launch_k(qw_pdl_small(), attn_decode_kernel<64, 2>, dim3(grid), dim3(32 * DecodeSmem<64>::NW), DecodeSmem<64>::TOTAL, s, q, ldq, (int)nq, (int)nkv, kc, vc, seq_len, kv_base, kps, sl2,
                                                    part_o, part_ml, (int)splits);
   else
     return QW_ERR_UNSUPPORTED;
   QW_LAUNCH_CHECK();
   if (d == 256)
-    attn_decode_combine_kernel<256><<<(unsigned)(B * nq), 128, 0, s>>>(part_o, part_ml, (int)splits, q, ldq, (int)nq,
+    launch_k(qw_pdl_small(), attn_decode_combine_kernel<256>, dim3((unsigned)(B * nq)), dim3(128), 0, s, part_o, part_ml, (int)splits, q, ldq, (int)nq,
                                                                        static_cast<__nv_bfloat16*>(out), ldo);
   else
-    attn_decode_combine_kernel<64><<<(unsigned)(B * nq), 64, 0, s>>>(part_o, part_ml, (int)splits, q, ldq, (int)nq,
+    launch_k(qw_pdl_small(), attn_decode_combine_kernel<64>, dim3((unsigned)(B * nq)), dim3(64), 0, s, part_o, part_ml, (int)splits, q, ldq, (int)nq,
                                                                      static_cast<__nv_bfloat16*>(out), ldo);
   QW_LAUNCH_CHECK();
   return QW_OK;

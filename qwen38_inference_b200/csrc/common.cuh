@@ -7,6 +7,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <utility>
+
 #include "../../include/qw200.h"
 
 #define QW_DEV __device__ __forceinline__
@@ -419,7 +421,47 @@ QW_DEV bool elect_one() {
   return pred != 0;
 }
 
+// ------------------------------------------------------------------ programmatic dependent launch
+// A kernel launched with programmatic stream serialization (launch_k with pdl = true) may start
+// while the kernel before it on the stream still runs. It must execute griddep_wait() before
+// it reads anything an earlier kernel wrote and before it writes anything an earlier kernel
+// reads: the wait returns once every earlier grid has completed and its memory is visible.
+// Without the launch attribute the wait returns at once. griddep_launch_dependents() lets the
+// next kernel's CTAs start; a CTA executes it only once it holds everything it allocates
+// (shared memory comes with the launch, tensor memory is allocated before it), so a dependent
+// CTA that became resident can never keep an earlier grid's CTA from running.
+QW_DEV void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+QW_DEV void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 }  // namespace qw
+
+// Launch a kernel; with pdl, with programmatic stream serialization (the kernel calls
+// qw::griddep_wait before touching memory that earlier kernels use). PDL is on unless the
+// environment variable QW_PDL=0 turns it off (a tuning knob).
+bool qw_pdl_enabled();
+// the same for the small kernels of the decode step (norms, attention, merge, GDN step): off
+// unless QW_PDL_SMALL=1 (a tuning knob). Measured on the B32 decode graph (27B, 1024 context,
+// replay after idle): 13.44 ms without PDL, 13.10 ms with the weight-streaming GEMMs alone
+// under PDL, 13.53 ms with every kernel under it. The small kernels still execute
+// griddep_launch_dependents at their start, so the GEMM after one of them starts early.
+bool qw_pdl_small();
+template <typename... KArgs, typename... Args>
+static inline cudaError_t launch_k(bool pdl, void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                                   cudaStream_t s, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  if (pdl && qw_pdl_enabled()) {
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+  }
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
 
 // ------------------------------------------------------------------ host-side argument checks
 #define QW_CHECK_ARG(cond, code) \

@@ -48,6 +48,8 @@ __global__ void __launch_bounds__(256, 2) gdn_decode_kernel(
     const int32_t* __restrict__ slots, int n_slots, const float* __restrict__ A_log,
     const __nv_bfloat16* __restrict__ dt_bias, const __nv_bfloat16* __restrict__ norm_w, __nv_bfloat16* __restrict__ y,
     int64_t ldy, int H, float scale, float eps, int* err) {
+  griddep_launch_dependents();  // programmatic dependent launch (launch_k): see common.cuh
+  griddep_wait();
   constexpr int W = 4;  // conv width
   constexpr int NCH = 2 * DK + RATIO * DV;
   const int HV = H * RATIO;
@@ -214,10 +216,10 @@ extern "C" int qw_gdn_decode(const void* qkvz, int64_t ldx, const void* ba, int6
   auto* yp = static_cast<__nv_bfloat16*>(y);
   int* err = device_error_ptr();
   if (dk == 128 && dv == 128 && ratio == 3)
-    gdn_decode_kernel<128, 128, 3><<<grid, 256, 0, s>>>(x, ldx, bap, ldba, cw, cs, state, slots, (int)n_slots, A_log,
+    launch_k(qw_pdl_small(), gdn_decode_kernel<128, 128, 3>, dim3(grid), dim3(256), 0, s, x, ldx, bap, ldba, cw, cs, state, slots, (int)n_slots, A_log,
                                                         dt, nw, yp, ldy, (int)H, 1.0f / sqrtf((float)dk), eps, err);
   else if (dk == 128 && dv == 128 && ratio == 1)
-    gdn_decode_kernel<128, 128, 1><<<grid, 256, 0, s>>>(x, ldx, bap, ldba, cw, cs, state, slots, (int)n_slots, A_log,
+    launch_k(qw_pdl_small(), gdn_decode_kernel<128, 128, 1>, dim3(grid), dim3(256), 0, s, x, ldx, bap, ldba, cw, cs, state, slots, (int)n_slots, A_log,
                                                         dt, nw, yp, ldy, (int)H, 1.0f / sqrtf((float)dk), eps, err);
   else
     return QW_ERR_UNSUPPORTED;

@@ -545,6 +545,11 @@ __global__ void __launch_bounds__(gemm_threads<MT>(), 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // the tensor memory is held: the next kernel on the stream may start its prologue. Every
+  // thread but the producer waits here for the previous kernels (the epilogue reads residuals
+  // and writes outputs, partials and the add-norm tickets that earlier launches use)
+  griddep_launch_dependents();
+  if (warp != 0) griddep_wait();
 
   if (warp == 0) {
     // ---------------------------------------------------------------- TMA producer
@@ -552,22 +557,43 @@ __global__ void __launch_bounds__(gemm_threads<MT>(), 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
+      auto load_a = [&](uint8_t* sa, int kb, int at, uint64_t* bar) {
+        if constexpr (EPI == EPI_SWIGLU_SWAP) {
+          // 64 gate rows, then the 64 up rows of the same output columns (64-row boxes)
+          tma_load_2d(sa, &tmA, bar, kb * BK, at * 64);
+          tma_load_2d(sa + 64 * BK * 2, &tmA, bar, kb * BK, p.b_up_offset + at * 64);
+        } else {
+          tma_load_2d(sa, &tmA, bar, kb * BK, at * (BM * MT));
+        }
+      };
+      // swap form: A is the weight, which no earlier kernel writes, so the first unit's first
+      // STAGES weight tiles are requested before waiting for the previous kernel (programmatic
+      // dependent launch); the activations B follow the wait
+      int npre = 0;
+      if (p.swap && (int)blockIdx.x < units) {
+        int at, bt, split;
+        decode_unit(p, blockIdx.x, at, bt, split);
+        const int kb0 = split * p.kb_per_split;
+        npre = min(STAGES, min(p.kb_total, kb0 + p.kb_per_split) - kb0);
+        for (int i = 0; i < npre; ++i) {
+          mbar_arrive_expect_tx(&full[i], L::STAGE_BYTES);
+          load_a(smem + i * L::STAGE_BYTES, kb0 + i, at, &full[i]);
+        }
+      }
+      griddep_wait();
+      int it = 0;
       for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
         int at, bt, split;
         decode_unit(p, u, at, bt, split);
         const int kb0 = split * p.kb_per_split;
         const int kb1 = min(p.kb_total, kb0 + p.kb_per_split);
-        for (int kb = kb0; kb < kb1; ++kb) {
-          if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, p.err, QW_DEV_ERR_TIMEOUT_GEMM)) { ok = false; break; }
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
           uint8_t* sa = smem + stage * L::STAGE_BYTES;
           uint8_t* sb = sa + L::A_BYTES;
-          mbar_arrive_expect_tx(&full[stage], L::STAGE_BYTES);
-          if constexpr (EPI == EPI_SWIGLU_SWAP) {
-            // 64 gate rows, then the 64 up rows of the same output columns (64-row boxes)
-            tma_load_2d(sa, &tmA, &full[stage], kb * BK, at * 64);
-            tma_load_2d(sa + 64 * BK * 2, &tmA, &full[stage], kb * BK, p.b_up_offset + at * 64);
-          } else {
-            tma_load_2d(sa, &tmA, &full[stage], kb * BK, at * (BM * MT));
+          if (it >= npre) {
+            if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, p.err, QW_DEV_ERR_TIMEOUT_GEMM)) { ok = false; break; }
+            mbar_arrive_expect_tx(&full[stage], L::STAGE_BYTES);
+            load_a(sa, kb, at, &full[stage]);
           }
           if constexpr (EPI == EPI_SWIGLU) {
             tma_load_2d(sb, &tmB, &full[stage], kb * BK, bt * (BN / 2));
@@ -579,6 +605,7 @@ __global__ void __launch_bounds__(gemm_threads<MT>(), 1)
         }
       }
     }
+    griddep_wait();  // the other lanes (they take part in the add-norm finisher)
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA issuer
     constexpr uint32_t IDESC = umma_idesc_bf16(BM, BN);
@@ -1105,6 +1132,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
 template <int EPI>
 __global__ void splitk_reduce_kernel(const float* __restrict__ ws, void* out, int M, int N_out, int64_t ldo,
                                      int splits, int64_t part_stride, int64_t ldw, int up_offset) {
+  griddep_launch_dependents();  // programmatic dependent launch (launch_k): see common.cuh
+  griddep_wait();
   const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= (int64_t)M * N_out) return;
   const int m = (int)(idx / N_out);
@@ -1131,6 +1160,8 @@ constexpr int kAddNormMaxThreads = 1024;
 __global__ void __launch_bounds__(kAddNormMaxThreads) splitk_add_rmsnorm_kernel(
     const float* __restrict__ ws, int splits, int64_t part_stride, int N, __nv_bfloat16* __restrict__ resid,
     const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ hidden, float eps) {
+  griddep_launch_dependents();  // programmatic dependent launch (launch_k): see common.cuh
+  griddep_wait();
   __shared__ float red[32];
   const int m = blockIdx.x;
   const int c = threadIdx.x * 8;
@@ -1186,6 +1217,8 @@ __global__ void qkv_finish_kernel(const float* __restrict__ ws, int splits, int6
                                   const int32_t* __restrict__ positions, const int32_t* __restrict__ locs,
                                   __nv_bfloat16* __restrict__ kc, __nv_bfloat16* __restrict__ vc, int64_t cache_rows,
                                   float eps, int* err) {
+  griddep_launch_dependents();  // programmatic dependent launch (launch_k): see common.cuh
+  griddep_wait();
   constexpr int E = D / 32;
   const int segs = 2 * nq + 2 * nkv;
   const int gw = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
@@ -1316,7 +1349,9 @@ static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmP
   const int grid = units < num_sms() ? units : num_sms();
   GemmParams pp = p;
   pp.tma_out = tma_epi && tc != nullptr && !p.swap;
-  kern<<<grid, gemm_threads<MT>(), smem, s>>>(ta, tb, pp.tma_out ? *tc : ta, pp);
+  // the weight-streaming (swap) form starts under programmatic dependent launch: its weight
+  // tiles load while the previous kernel finishes
+  launch_k(pp.swap != 0, kern, dim3(grid), dim3(gemm_threads<MT>()), smem, s, ta, tb, pp.tma_out ? *tc : ta, pp);
   QW_LAUNCH_CHECK();
   return QW_OK;
 }
@@ -1340,6 +1375,28 @@ static int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const GemmP
   QW_LAUNCH_CHECK();
   return QW_OK;
 }
+
+}  // namespace qw
+
+bool qw_pdl_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("QW_PDL");
+    v = (e && atoi(e) == 0) ? 0 : 1;
+  }
+  return v == 1;
+}
+
+bool qw_pdl_small() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("QW_PDL_SMALL");
+    v = (e && atoi(e) == 1) ? 1 : 0;
+  }
+  return v == 1;
+}
+
+namespace qw {
 
 // bf16 outputs of the large-M kernels through shared-memory staging and TMA stores unless the
 // environment variable QW_GEMM_TMA_STORE=0 selects the per-thread global stores (a tuning knob)
@@ -1529,9 +1586,9 @@ extern "C" int qw_gemm_bf16(const void* x, const void* w, void* y, int64_t M, in
       const int blocks = (int)((total + threads - 1) / threads);
       const float* wsp = reinterpret_cast<const float*>(workspace);
       if (out_kind == QW_OUT_F32)
-        splitk_reduce_kernel<EPI_F32RAW><<<blocks, threads, 0, s>>>(wsp, y, (int)M, (int)N, ldy, splits, M * N, N, 0);
+        launch_k(qw_pdl_small(), splitk_reduce_kernel<EPI_F32RAW>, dim3(blocks), dim3(threads), 0, s, wsp, y, (int)M, (int)N, ldy, splits, M * N, N, 0);
       else
-        splitk_reduce_kernel<EPI_BF16><<<blocks, threads, 0, s>>>(wsp, y, (int)M, (int)N, ldy, splits, M * N, N, 0);
+        launch_k(qw_pdl_small(), splitk_reduce_kernel<EPI_BF16>, dim3(blocks), dim3(threads), 0, s, wsp, y, (int)M, (int)N, ldy, splits, M * N, N, 0);
       QW_LAUNCH_CHECK();
       return QW_OK;
     }
@@ -1667,13 +1724,13 @@ extern "C" int qw_gemm_bf16(const void* x, const void* w, void* y, int64_t M, in
   const int blocks = (int)((total + threads - 1) / threads);
   const float* ws = reinterpret_cast<const float*>(workspace);
   if (out_kind == QW_OUT_SWIGLU)
-    splitk_reduce_kernel<EPI_SWIGLU><<<blocks, threads, 0, s>>>(ws, y, (int)M, (int)n_out, ldy, pl.splits, p.part_stride, N, (int)n_out);
+    launch_k(qw_pdl_small(), splitk_reduce_kernel<EPI_SWIGLU>, dim3(blocks), dim3(threads), 0, s, ws, y, (int)M, (int)n_out, ldy, pl.splits, p.part_stride, N, (int)n_out);
   else if (out_kind == QW_OUT_F32_OF_BF16)
-    splitk_reduce_kernel<EPI_F32><<<blocks, threads, 0, s>>>(ws, y, (int)M, (int)n_out, ldy, pl.splits, p.part_stride, N, 0);
+    launch_k(qw_pdl_small(), splitk_reduce_kernel<EPI_F32>, dim3(blocks), dim3(threads), 0, s, ws, y, (int)M, (int)n_out, ldy, pl.splits, p.part_stride, N, 0);
   else if (out_kind == QW_OUT_F32)
-    splitk_reduce_kernel<EPI_F32RAW><<<blocks, threads, 0, s>>>(ws, y, (int)M, (int)n_out, ldy, pl.splits, p.part_stride, N, 0);
+    launch_k(qw_pdl_small(), splitk_reduce_kernel<EPI_F32RAW>, dim3(blocks), dim3(threads), 0, s, ws, y, (int)M, (int)n_out, ldy, pl.splits, p.part_stride, N, 0);
   else
-    splitk_reduce_kernel<EPI_BF16><<<blocks, threads, 0, s>>>(ws, y, (int)M, (int)n_out, ldy, pl.splits, p.part_stride, N, 0);
+    launch_k(qw_pdl_small(), splitk_reduce_kernel<EPI_BF16>, dim3(blocks), dim3(threads), 0, s, ws, y, (int)M, (int)n_out, ldy, pl.splits, p.part_stride, N, 0);
   QW_LAUNCH_CHECK();
   return QW_OK;
 }
@@ -1721,7 +1778,7 @@ extern "C" int qw_gemm_add_rmsnorm(const void* x, const void* w, int64_t M, int6
     QW_CHECK_ARG(((uintptr_t)workspace % 16) == 0, QW_ERR_ALIGN);
     if ((rc = launch_wide_partials(x, w, M, N, K, ldx, ldw, splits, workspace, s)) != QW_OK) return rc;
     const int threads = (int)((N / 8 + 31) / 32 * 32);
-    splitk_add_rmsnorm_kernel<<<(unsigned)M, threads, 0, s>>>(
+    launch_k(qw_pdl_small(), splitk_add_rmsnorm_kernel, dim3((unsigned)M), dim3(threads), 0, s, 
         static_cast<const float*>(workspace), splits, M * N, (int)N, static_cast<__nv_bfloat16*>(resid),
         static_cast<const __nv_bfloat16*>(norm_w), static_cast<__nv_bfloat16*>(hidden), eps);
     QW_LAUNCH_CHECK();
@@ -1768,7 +1825,7 @@ extern "C" int qw_gemm_add_rmsnorm(const void* x, const void* w, int64_t M, int6
   }
   if (rc != QW_OK || p.norm_rows > 0) return rc;
   const int threads = (int)((N / 8 + 31) / 32 * 32);
-  splitk_add_rmsnorm_kernel<<<(unsigned)M, threads, 0, s>>>(
+  launch_k(qw_pdl_small(), splitk_add_rmsnorm_kernel, dim3((unsigned)M), dim3(threads), 0, s, 
       static_cast<const float*>(workspace), pl.splits, p.part_stride, (int)N, static_cast<__nv_bfloat16*>(resid),
       static_cast<const __nv_bfloat16*>(norm_w), static_cast<__nv_bfloat16*>(hidden), eps);
   QW_LAUNCH_CHECK();
@@ -1957,7 +2014,7 @@ extern "C" int qw_gemm_qkv_rope_store(const void* x, const void* w, void* qkv, i
   int* err = device_error_ptr();
   const int nsp = use_skinny(M) ? plan_skinny(M, N, K).splits : splits;
 #define QW_QKV_FINISH(DD)                                                                                            \
-  qkv_finish_kernel<DD><<<blocks, 256, 0, s>>>(ws, nsp, M * N, (int)N, (int)M, q, ldq, (int)nq, (int)nkv, qw_, kw_, \
+  launch_k(qw_pdl_small(), qkv_finish_kernel<DD>, dim3(blocks), dim3(256), 0, s, ws, nsp, M * N, (int)N, (int)M, q, ldq, (int)nq, (int)nkv, qw_, kw_, \
                                                rope, (int)rotary_dim, rope_rows, positions, locations, kc, vc,     \
                                                cache_rows, eps, err)
   if (d == 256) QW_QKV_FINISH(256);
@@ -1978,7 +2035,7 @@ extern "C" int qw_add_rmsnorm_f32(const float* x, int64_t n_parts, int64_t part_
                QW_ERR_ALIGN);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const int threads = (int)((H / 8 + 31) / 32 * 32);
-  splitk_add_rmsnorm_kernel<<<(unsigned)T, threads, 0, s>>>(x, (int)n_parts, part_stride, (int)H,
+  launch_k(qw_pdl_small(), splitk_add_rmsnorm_kernel, dim3((unsigned)T), dim3(threads), 0, s, x, (int)n_parts, part_stride, (int)H,
                                                             static_cast<__nv_bfloat16*>(resid),
                                                             static_cast<const __nv_bfloat16*>(norm_w),
                                                             static_cast<__nv_bfloat16*>(hidden), eps);

@@ -43,6 +43,8 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_rows_kernel(
     const __nv_bfloat16* __restrict__ src, int64_t ld_src, const int32_t* __restrict__ rows, int64_t n_table,
     __nv_bfloat16* x, __nv_bfloat16* resid, const __nv_bfloat16* __restrict__ w, __nv_bfloat16* out, int H,
     float eps, int* err) {
+  griddep_launch_dependents();  // programmatic dependent launch (launch_k): see common.cuh
+  griddep_wait();
   __shared__ float red[33];
   const int row = blockIdx.x;
   const int nvec = H / 8;
@@ -96,6 +98,8 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_rows_kernel(
 __global__ void __launch_bounds__(kNormThreads) add_rmsnorm_select_kernel(
     const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ resid, const int32_t* __restrict__ rows,
     int T, const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ out, int H, float eps, int* err) {
+  griddep_launch_dependents();  // programmatic dependent launch (launch_k): see common.cuh
+  griddep_wait();
   __shared__ float red[33];
   int r = rows ? rows[blockIdx.x] : blockIdx.x;
   if (r < 0 || r >= T) {
@@ -174,7 +178,7 @@ extern "C" int qw_embed_rmsnorm(const int32_t* tokens, int64_t T, const void* ta
   auto* s = reinterpret_cast<cudaStream_t>(stream);
   const int vec = (int)((H + 8 * kNormThreads - 1) / (8 * kNormThreads));
 #define QW_EMBED(V)                                                                                               \
-  rmsnorm_rows_kernel<0, V><<<(unsigned)T, kNormThreads, 0, s>>>(                                               \
+  launch_k(qw_pdl_small(), rmsnorm_rows_kernel<0, V>, dim3((unsigned)T), dim3(kNormThreads), 0, s,                                                \
       static_cast<const __nv_bfloat16*>(table), H, tokens, vocab, nullptr, static_cast<__nv_bfloat16*>(resid_out), \
       static_cast<const __nv_bfloat16*>(w), static_cast<__nv_bfloat16*>(hidden_out), (int)H, eps, device_error_ptr())
   if (vec <= 1) QW_EMBED(1);
@@ -192,7 +196,7 @@ extern "C" int qw_add_rmsnorm(void* x, void* resid, const void* w, int64_t T, in
   auto* s = reinterpret_cast<cudaStream_t>(stream);
   const int vec = (int)((H + 8 * kNormThreads - 1) / (8 * kNormThreads));
 #define QW_ADDN(V)                                                                                                \
-  rmsnorm_rows_kernel<1, V><<<(unsigned)T, kNormThreads, 0, s>>>(                                               \
+  launch_k(qw_pdl_small(), rmsnorm_rows_kernel<1, V>, dim3((unsigned)T), dim3(kNormThreads), 0, s,                                                \
       nullptr, 0, nullptr, 0, static_cast<__nv_bfloat16*>(x), static_cast<__nv_bfloat16*>(resid),                \
       static_cast<const __nv_bfloat16*>(w), nullptr, (int)H, eps, nullptr)
   if (vec <= 1) QW_ADDN(1);
@@ -208,7 +212,7 @@ extern "C" int qw_add_rmsnorm_rows(const void* x, const void* resid, const int32
   QW_CHECK_ARG(x && resid && w && out && n_rows > 0 && T > 0, QW_ERR_ARG);
   QW_CHECK_ARG(H % 8 == 0 && H <= kNormThreads * kMaxVec * 8, QW_ERR_UNSUPPORTED);
   auto* s = reinterpret_cast<cudaStream_t>(stream);
-  add_rmsnorm_select_kernel<<<(unsigned)n_rows, kNormThreads, 0, s>>>(
+  launch_k(qw_pdl_small(), add_rmsnorm_select_kernel, dim3((unsigned)n_rows), dim3(kNormThreads), 0, s, 
       static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(resid), rows, (int)T,
       static_cast<const __nv_bfloat16*>(w), static_cast<__nv_bfloat16*>(out), (int)H, eps, device_error_ptr());
   QW_LAUNCH_CHECK();
