@@ -1176,6 +1176,52 @@ def run_gemm_cublas(args):
     print(json.dumps(out), flush=True)
 
 
+def run_gemm_sustained(args):
+    """The four large-M projection shapes of the B32 x L1024 prefill (gate_up with the SwiGLU
+    epilogue, qkvz|ba, down, out_proj), launched back to back as in the step so that the
+    GPU sits at its power cap: 40 warm rounds, then ``--steps`` timed rounds with CUDA events
+    around every launch; medians per shape. The GEMM tuning knobs (QW_GEMM_WIDE,
+    QW_GEMM_GROUP, QW_GEMM_PAIR) apply, so runs with different settings compare the shapes
+    under the same kind of load."""
+    import torch
+    from qwen38_inference_b200 import ops
+    from qwen38_inference_b200.config import qwen38_27b
+    cfg = qwen38_27b()
+    dev = "cuda"
+    T = args.batch * args.length
+    g = torch.Generator(device=dev).manual_seed(0)
+    shapes = [("gate_up", 2 * cfg.intermediate_size, cfg.hidden_size, ops.OUT_SWIGLU),
+              ("qkvz_ba", cfg.qkvz_dim + cfg.ba_dim, cfg.hidden_size, ops.OUT_BF16),
+              ("down", cfg.hidden_size, cfg.intermediate_size, ops.OUT_BF16),
+              ("out_proj", cfg.hidden_size, cfg.gdn_v_dim, ops.OUT_BF16)]
+    bufs = {}
+    for name, N, K, kind in shapes:
+        x = torch.randn(T, K, device=dev, generator=g).bfloat16()
+        w = (torch.randn(N, K, device=dev, generator=g) * 0.02).bfloat16()
+        y = torch.empty(T, N // 2 if kind == ops.OUT_SWIGLU else N, device=dev, dtype=torch.bfloat16)
+        bufs[name] = (x, w, y, kind)
+    ws = ops.Workspace(dev)
+    for _ in range(40):
+        for x, w, y, kind in bufs.values():
+            ops.gemm(x, w, y, out_kind=kind, ws=ws)
+    torch.cuda.synchronize()
+    ev = {n: [] for n in bufs}
+    with ClockSampler(0) as clk:
+        for _ in range(args.steps):
+            for name, (x, w, y, kind) in bufs.items():
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record()
+                ops.gemm(x, w, y, out_kind=kind, ws=ws)
+                b.record()
+                ev[name].append((a, b))
+        torch.cuda.synchronize()
+    out = {"op": "gemm_sustained", "tokens": T,
+           "knobs": {k: os.environ.get(k) for k in ("QW_GEMM_WIDE", "QW_GEMM_GROUP", "QW_GEMM_PAIR")},
+           "median_ms": {n: round(statistics.median(a.elapsed_time(b) for a, b in e), 4) for n, e in ev.items()},
+           "clocks": clk.summary()}
+    print(json.dumps(out), flush=True)
+
+
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -1217,6 +1263,7 @@ def main():
                     help="--op gemm_cublas: time only this projection shape")
     ap.add_argument("--op", choices=["gate_up", "qkvz_proj", "down_proj", "gdn_prefill", "gdn_decode",
                                      "gdn_sweep", "gdn_prefill_flashinfer", "gemm_cublas", "step_cublas",
+                                     "gemm_sustained",
                                      "conv_prefill",
                                      "attn_prefill", "decode_step"],
                     default=None,
@@ -1233,6 +1280,8 @@ def main():
         run_gemm_cublas(args)
     elif args.op == "step_cublas":
         run_step_cublas(args)
+    elif args.op == "gemm_sustained":
+        run_gemm_sustained(args)
     elif args.op:
         try:
             run_op(args)

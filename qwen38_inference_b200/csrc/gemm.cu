@@ -873,23 +873,42 @@ __global__ void __launch_bounds__(gemm_threads<MT>(), 1)
 // barriers; both epilogues release the accumulator on the leader's tmem-empty barrier.
 // SwiGLU: CTA 0 stages the gate rows and CTA 1 the matching up rows, so accumulator columns
 // [0,128) are gate and [128,256) up, exactly as in the single-CTA kernel.
-constexpr int P_BN = 256, P_STAGES = 6;
-constexpr int P_A_BYTES = BM * BK * 2, P_B_BYTES = (P_BN / 2) * BK * 2, P_STAGE = P_A_BYTES + P_B_BYTES;
-constexpr int P_BAR = P_STAGES * P_STAGE;
+// The wide form (NH = 2) computes a 256 x 512 tile per pair as two N-halves that share each
+// staged A tile: two MMAs per k-step into accumulators at TMEM columns [0, 256) and [256, 512),
+// which fill tensor memory, so the accumulator is single-buffered and the epilogue does not
+// overlap the next tile's main loop. Per k-block a CTA stages 16 KB of A and 32 KB of B for
+// twice the products of the 256 x 256 tile: 25 % fewer L2-to-SM bytes per FLOP.
+constexpr int P_BN = 256;
+constexpr int P_A_BYTES = BM * BK * 2, P_B_BOX = (P_BN / 2) * BK * 2;
 // output staging of the TMA-store epilogue: per epilogue warp two 32-row x 64-column bf16 boxes
 // (4 KB each, SWIZZLE_128B) used alternately, so a box is rewritten only after the store
 // issued from it two boxes earlier has read it
-constexpr int P_STG = P_BAR + 1024, P_STG_BOX = 32 * 64 * 2;
-constexpr int P_SMEM = P_STG + 4 * 2 * P_STG_BOX + 1024;
-static_assert(P_SMEM <= 232448, "CTA-pair GEMM shared memory above the sm_100 per-block limit");
+constexpr int P_STG_BOX = 32 * 64 * 2;
+template <int NH>
+struct PairCfg {
+  static constexpr int STAGES = NH == 1 ? 6 : 4;
+  static constexpr int STAGE = P_A_BYTES + NH * P_B_BOX;  // per CTA and k-block
+  static constexpr int BAR = STAGES * STAGE;
+  static constexpr int STG = BAR + 1024;
+  // epilogue warps: four per N-half (one per TMEM lane quarter), so the wide form drains its
+  // two halves in parallel; staging boxes per epilogue warp: two (alternating) or one
+  static constexpr int EW = 4 * NH, THREADS = 64 + 32 * EW, NBOX = NH == 1 ? 2 : 1;
+  static constexpr int SMEM = STG + EW * NBOX * P_STG_BOX + 1024;
+  static constexpr int NBUF = NH == 1 ? 2 : 1;  // accumulator buffers in the 512 TMEM columns
+  static_assert(SMEM <= 232448, "CTA-pair GEMM shared memory above the sm_100 per-block limit");
+};
 
-template <int EPI>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
+template <int EPI, int NH>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(64 + 128 * NH, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ CUtensorMap tmC, const GemmParams p) {
+  using C = PairCfg<NH>;
+  static_assert(NH == 1 || EPI == EPI_BF16 || EPI == EPI_SWIGLU || EPI == EPI_QKV,
+                "the wide form has bf16, SwiGLU and attention-projection epilogues");
+  constexpr int P_STAGES = C::STAGES, NBUF = C::NBUF;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + P_BAR);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::BAR);
   uint64_t* empty = full + P_STAGES;
   uint64_t* tfull = empty + P_STAGES;  // [2]
   uint64_t* tempty = tfull + 2;        // [2], used in the leader
@@ -909,7 +928,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], 8);  // 4 epilogue warps in each CTA
+      mbar_init(&tempty[b], 2 * C::EW);  // every epilogue warp of both CTAs
     }
     *abort_flag = 0;
     fence_barrier_init();
@@ -936,15 +955,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
         decode_unit(p, u, at, bt, split);
         for (int kb = 0; kb < p.kb_total; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, p.err, QW_DEV_ERR_TIMEOUT_GEMM)) { ok = false; break; }
-          uint8_t* sa = smem + stage * P_STAGE;
+          uint8_t* sa = smem + stage * C::STAGE;
           uint8_t* sb = sa + P_A_BYTES;
           const uint32_t bar = mapa_shared(smem_u32(&full[stage]), 0);
-          if (leader) mbar_arrive_expect_tx(&full[stage], 2 * P_STAGE);
+          if (leader) mbar_arrive_expect_tx(&full[stage], 2 * C::STAGE);
           tma_load_2d_pair(sa, &tmA, bar, kb * BK, at * 256 + (int)rank * BM);
-          if constexpr (EPI == EPI_SWIGLU) {
-            tma_load_2d_pair(sb, &tmB, bar, kb * BK, (rank ? p.b_up_offset : 0) + bt * (P_BN / 2));
-          } else {
-            tma_load_2d_pair(sb, &tmB, bar, kb * BK, bt * P_BN + (int)rank * (P_BN / 2));
+#pragma unroll
+          for (int h = 0; h < NH; ++h) {
+            const int btx = bt * NH + h;  // the 256-column block of this N-half
+            if constexpr (EPI == EPI_SWIGLU) {
+              tma_load_2d_pair(sb + h * P_B_BOX, &tmB, bar, kb * BK, (rank ? p.b_up_offset : 0) + btx * (P_BN / 2));
+            } else {
+              tma_load_2d_pair(sb + h * P_B_BOX, &tmB, bar, kb * BK, btx * P_BN + (int)rank * (P_BN / 2));
+            }
           }
           if (++stage == P_STAGES) { stage = 0; phase ^= 1; }
         }
@@ -959,20 +982,23 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
       int tcount = 0;
       bool ok = true;
       for (int u = pair; u < units && ok; u += npairs, ++tcount) {
-        const int buf = tcount & 1;
-        if (!mbar_wait(&tempty[buf], ((tcount >> 1) & 1) ^ 1, abort_flag, p.err, QW_DEV_ERR_TIMEOUT_GEMM)) { ok = false; break; }
+        const int buf = tcount % NBUF;
+        if (!mbar_wait(&tempty[buf], ((tcount / NBUF) & 1) ^ 1, abort_flag, p.err, QW_DEV_ERR_TIMEOUT_GEMM)) { ok = false; break; }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + buf * P_BN;
         for (int kb = 0; kb < p.kb_total; ++kb) {
           if (!mbar_wait(&full[stage], phase, abort_flag, p.err, QW_DEV_ERR_TIMEOUT_GEMM)) { ok = false; break; }
           tc_fence_after();
           if (elect_one()) {
-            const uint32_t sa = smem_u32(smem + stage * P_STAGE);
+            const uint32_t sa = smem_u32(smem + stage * C::STAGE);
             const uint64_t da = umma_sdesc_sw128(sa);
-            const uint64_t db = umma_sdesc_sw128(sa + P_A_BYTES);
 #pragma unroll
             for (int k = 0; k < BK / 16; ++k)
-              umma_bf16_pair(d_tmem, da + (uint64_t)(2 * k), db + (uint64_t)(2 * k), IDESC, (kb > 0 || k > 0) ? 1u : 0u);
+#pragma unroll
+              for (int h = 0; h < NH; ++h)
+                umma_bf16_pair(d_tmem + h * P_BN, da + (uint64_t)(2 * k),
+                               umma_sdesc_sw128(sa + P_A_BYTES + h * P_B_BOX) + (uint64_t)(2 * k), IDESC,
+                               (kb > 0 || k > 0) ? 1u : 0u);
             umma_commit_pair(&empty[stage], 0x3);
           }
           __syncwarp();
@@ -988,130 +1014,136 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
     const int q = warp & 3;
     const int row_in_tile = (int)rank * BM + q * 32 + lane;
     const uint32_t tempty_leader0 = mapa_shared(smem_u32(&tempty[0]), 0);
-    uint8_t* stg = smem + P_STG + q * 2 * P_STG_BOX;  // this warp's two staging boxes
+    const int hw = (warp - 2) >> 2;  // the N-half this warp drains
+    uint8_t* stg = smem + C::STG + (warp - 2) * C::NBOX * P_STG_BOX;  // this warp's staging boxes
     int sbox = 0;
     int tcount = 0;
     for (int u = pair; u < units; u += npairs, ++tcount) {
-      int at, bt, split;
-      decode_unit(p, u, at, bt, split);
-      const int buf = tcount & 1;
+      int at, bt_unit, split;
+      decode_unit(p, u, at, bt_unit, split);
+      const int buf = tcount % NBUF;
       // warp-uniform: the tcgen05.ld below are warp-collective
-      if (!__all_sync(0xffffffffu, mbar_wait(&tfull[buf], (tcount >> 1) & 1, abort_flag, p.err, QW_DEV_ERR_TIMEOUT_GEMM))) break;
+      if (!__all_sync(0xffffffffu, mbar_wait(&tfull[buf], (tcount / NBUF) & 1, abort_flag, p.err, QW_DEV_ERR_TIMEOUT_GEMM))) break;
       tc_fence_after();
-      const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + buf * P_BN;
       const int a_row = at * 256 + row_in_tile;
       const bool a_ok = a_row < p.a_rows;
-      if ((EPI == EPI_BF16 || EPI == EPI_SWIGLU) && p.tma_out) {
-        // 64 output columns at a time: the warp's 32 rows staged as bf16 (row = lane), then one
-        // TMA store of the 32 x 64 box; rows past M and columns past N are not written
-        const int row0 = at * 256 + (int)rank * BM + q * 32;
-        constexpr int NOUT = EPI == EPI_SWIGLU ? P_BN / 2 : P_BN;
+      {
+        // N-half h: accumulator columns (buf + h) * 256, output block bt = bt_unit * NH + h
+        const int h = hw;
+        const int bt = bt_unit * NH + h;
+        const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + (buf + h) * P_BN;
+        if ((EPI == EPI_BF16 || EPI == EPI_SWIGLU) && p.tma_out) {
+          // 64 output columns at a time: the warp's 32 rows staged as bf16 (row = lane), then one
+          // TMA store of the 32 x 64 box; rows past M and columns past N are not written
+          const int row0 = at * 256 + (int)rank * BM + q * 32;
+          constexpr int NOUT = EPI == EPI_SWIGLU ? P_BN / 2 : P_BN;
 #pragma unroll 1
-        for (int c = 0; c < NOUT; c += 64) {
-          uint8_t* box = stg + (sbox & 1) * P_STG_BOX;
-          ++sbox;
-          if (lane == 0) bulk_wait_read<1>();  // the store issued from this box two boxes ago
-          __syncwarp();
+          for (int c = 0; c < NOUT; c += 64) {
+            uint8_t* box = stg + (sbox % C::NBOX) * P_STG_BOX;
+            ++sbox;
+            if (lane == 0) bulk_wait_read<C::NBOX - 1>();  // the store issued earlier from this box
+            __syncwarp();
 #pragma unroll
-          for (int hf = 0; hf < 2; ++hf) {
-            float f[32];
-            if constexpr (EPI == EPI_SWIGLU) {
-              uint32_t g[32], v[32];
-              tmem_ld_32x32b_x32(t_row + c + 32 * hf, g);
-              tmem_ld_32x32b_x32(t_row + P_BN / 2 + c + 32 * hf, v);
-              tmem_ld_wait();
+            for (int hf = 0; hf < 2; ++hf) {
+              float f[32];
+              if constexpr (EPI == EPI_SWIGLU) {
+                uint32_t g[32], v[32];
+                tmem_ld_32x32b_x32(t_row + c + 32 * hf, g);
+                tmem_ld_32x32b_x32(t_row + P_BN / 2 + c + 32 * hf, v);
+                tmem_ld_wait();
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                  const float gg = bf16_round(__uint_as_float(g[j]));
+                  const float uu = bf16_round(__uint_as_float(v[j]));
+                  f[j] = gg / (1.0f + expf(-gg)) * uu;
+                }
+              } else {
+                uint32_t r[32];
+                tmem_ld_32x32b_x32(t_row + c + 32 * hf, r);
+                tmem_ld_wait();
+#pragma unroll
+                for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(r[j]);
+              }
+              stage_row_bf16_sw128(box, lane, hf, f);
+            }
+            fence_async_smem();
+            __syncwarp();
+            if (lane == 0 && bt * NOUT + c < p.b_rows && row0 < p.a_rows) {  // a box wholly past the edge writes nothing
+              tma_store_2d(&tmC, smem_u32(box), bt * NOUT + c, row0);
+              bulk_commit();
+            }
+          }
+        } else if constexpr (EPI == EPI_SWIGLU) {
+          __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.out);
+#pragma unroll 1
+          for (int c = 0; c < P_BN / 2; c += 32) {
+            uint32_t g[32], v[32];
+            tmem_ld_32x32b_x32(t_row + c, g);
+            tmem_ld_32x32b_x32(t_row + P_BN / 2 + c, v);
+            tmem_ld_wait();
+            const int col0 = bt * (P_BN / 2) + c;
+            if (a_ok) {
+              float f[32];
 #pragma unroll
               for (int j = 0; j < 32; ++j) {
                 const float gg = bf16_round(__uint_as_float(g[j]));
                 const float uu = bf16_round(__uint_as_float(v[j]));
                 f[j] = gg / (1.0f + expf(-gg)) * uu;
               }
-            } else {
-              uint32_t r[32];
-              tmem_ld_32x32b_x32(t_row + c + 32 * hf, r);
-              tmem_ld_wait();
+              const int ncols = p.b_rows - col0;
+              __nv_bfloat16* dst = out + (int64_t)a_row * p.ldo + col0;
+              if (ncols >= 32 && p.vec_ok) {
+#pragma unroll
+                for (int j = 0; j < 32; j += 8) store_bf16x8(dst + j, f + j);
+              } else {
+#pragma unroll
+                for (int j = 0; j < 32; ++j)
+                  if (j < ncols) dst[j] = f2bf(f[j]);
+              }
+            }
+          }
+        } else if constexpr (EPI == EPI_QKV) {
+          qkv_tile_row(p, t_row, a_row, bt, a_ok);
+        } else {
+#pragma unroll 1
+          for (int c = 0; c < P_BN; c += 32) {
+            uint32_t r[32];
+            tmem_ld_32x32b_x32(t_row + c, r);
+            tmem_ld_wait();
+            if (!a_ok) continue;
+            const int b0 = bt * P_BN + c;
+            const int nb = min(32, p.b_rows - b0);
+            if (nb <= 0) continue;
+            if constexpr (EPI == EPI_BF16) {
+              __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.out) + (int64_t)a_row * p.ldo + b0;
+              float f[32];
 #pragma unroll
               for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(r[j]);
-            }
-            stage_row_bf16_sw128(box, lane, hf, f);
-          }
-          fence_async_smem();
-          __syncwarp();
-          if (lane == 0 && bt * NOUT + c < p.b_rows && row0 < p.a_rows) {  // a box wholly past the edge writes nothing
-            tma_store_2d(&tmC, smem_u32(box), bt * NOUT + c, row0);
-            bulk_commit();
-          }
-        }
-      } else if constexpr (EPI == EPI_SWIGLU) {
-        __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.out);
-#pragma unroll 1
-        for (int c = 0; c < P_BN / 2; c += 32) {
-          uint32_t g[32], v[32];
-          tmem_ld_32x32b_x32(t_row + c, g);
-          tmem_ld_32x32b_x32(t_row + P_BN / 2 + c, v);
-          tmem_ld_wait();
-          const int col0 = bt * (P_BN / 2) + c;
-          if (a_ok) {
-            float f[32];
+              if (nb == 32 && p.vec_ok) {
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const float gg = bf16_round(__uint_as_float(g[j]));
-              const float uu = bf16_round(__uint_as_float(v[j]));
-              f[j] = gg / (1.0f + expf(-gg)) * uu;
-            }
-            const int ncols = p.b_rows - col0;
-            __nv_bfloat16* dst = out + (int64_t)a_row * p.ldo + col0;
-            if (ncols >= 32 && p.vec_ok) {
+                for (int j = 0; j < 32; j += 8) store_bf16x8(dst + j, f + j);
+              } else {
 #pragma unroll
-              for (int j = 0; j < 32; j += 8) store_bf16x8(dst + j, f + j);
+                for (int j = 0; j < 32; ++j)
+                  if (j < nb) dst[j] = f2bf(f[j]);
+              }
             } else {
+              float* dst = reinterpret_cast<float*>(p.out) + (int64_t)a_row * p.ldo + b0;
+              if (nb == 32 && p.vec_ok) {
 #pragma unroll
-              for (int j = 0; j < 32; ++j)
-                if (j < ncols) dst[j] = f2bf(f[j]);
+                for (int j = 0; j < 32; j += 4)
+                  *reinterpret_cast<float4*>(dst + j) =
+                      make_float4(f32_out<EPI>(__uint_as_float(r[j])), f32_out<EPI>(__uint_as_float(r[j + 1])),
+                                  f32_out<EPI>(__uint_as_float(r[j + 2])), f32_out<EPI>(__uint_as_float(r[j + 3])));
+              } else {
+#pragma unroll
+                for (int j = 0; j < 32; ++j)
+                  if (j < nb) dst[j] = f32_out<EPI>(__uint_as_float(r[j]));
+              }
             }
           }
         }
-      } else if constexpr (EPI == EPI_QKV) {
-        qkv_tile_row(p, t_row, a_row, bt, a_ok);
-      } else {
-#pragma unroll 1
-        for (int c = 0; c < P_BN; c += 32) {
-          uint32_t r[32];
-          tmem_ld_32x32b_x32(t_row + c, r);
-          tmem_ld_wait();
-          if (!a_ok) continue;
-          const int b0 = bt * P_BN + c;
-          const int nb = min(32, p.b_rows - b0);
-          if (nb <= 0) continue;
-          if constexpr (EPI == EPI_BF16) {
-            __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.out) + (int64_t)a_row * p.ldo + b0;
-            float f[32];
-#pragma unroll
-            for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(r[j]);
-            if (nb == 32 && p.vec_ok) {
-#pragma unroll
-              for (int j = 0; j < 32; j += 8) store_bf16x8(dst + j, f + j);
-            } else {
-#pragma unroll
-              for (int j = 0; j < 32; ++j)
-                if (j < nb) dst[j] = f2bf(f[j]);
-            }
-          } else {
-            float* dst = reinterpret_cast<float*>(p.out) + (int64_t)a_row * p.ldo + b0;
-            if (nb == 32 && p.vec_ok) {
-#pragma unroll
-              for (int j = 0; j < 32; j += 4)
-                *reinterpret_cast<float4*>(dst + j) =
-                    make_float4(f32_out<EPI>(__uint_as_float(r[j])), f32_out<EPI>(__uint_as_float(r[j + 1])),
-                                f32_out<EPI>(__uint_as_float(r[j + 2])), f32_out<EPI>(__uint_as_float(r[j + 3])));
-            } else {
-#pragma unroll
-              for (int j = 0; j < 32; ++j)
-                if (j < nb) dst[j] = f32_out<EPI>(__uint_as_float(r[j]));
-            }
-          }
-        }
-      }
+      }  // N-halves
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(tempty_leader0 + buf * 8);  // the leader's tempty[buf]
@@ -1356,10 +1388,11 @@ static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmP
   return QW_OK;
 }
 
-template <int EPI>
+template <int EPI, int NH = 1>
 static int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, cudaStream_t s,
                        const CUtensorMap* tc = nullptr) {
-  auto kern = gemm_pair_kernel<EPI>;
+  auto kern = gemm_pair_kernel<EPI, NH>;
+  constexpr int P_SMEM = PairCfg<NH>::SMEM, P_THREADS = PairCfg<NH>::THREADS;
   static bool configured = false;
   if (!configured) {
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, P_SMEM);
@@ -1371,7 +1404,7 @@ static int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const GemmP
   if (grid > max_ctas) grid = max_ctas;
   GemmParams pp = p;
   pp.tma_out = tc != nullptr;
-  kern<<<grid, 192, P_SMEM, s>>>(ta, tb, tc ? *tc : ta, pp);
+  kern<<<grid, P_THREADS, P_SMEM, s>>>(ta, tb, tc ? *tc : ta, pp);
   QW_LAUNCH_CHECK();
   return QW_OK;
 }
@@ -1407,6 +1440,19 @@ static bool gemm_tma_store() {
     v = (e && atoi(e) == 0) ? 0 : 1;
   }
   return v == 1;
+}
+
+// Wide CTA-pair tiles (256 x 512) for the pair kernel's outputs, bit flags: 1 bf16 outputs,
+// 2 SwiGLU outputs, 4 the attention projection's q/k norm + RoPE + KV store; off unless the
+// environment variable QW_GEMM_WIDE sets them (read at every call; a tuning knob). Measured
+// in the power-capped B32 x L1024 step on B200: the wide tile draws less power per cycle
+// (the SM clock rises 14-20 % with every shape on it) but its epilogue no longer overlaps the
+// next tile's main loop; with the exact SwiGLU epilogue the gate_up loses more than the clock
+// gives back, and the whole step is 3 % slower with QW_GEMM_WIDE=7 (bf16 outputs alone: the
+// same as without).
+static int gemm_wide_mode() {
+  const char* e = getenv("QW_GEMM_WIDE");
+  return e ? atoi(e) : 0;
 }
 
 // CTA-pair GEMM for large M: 1 (default) for the shapes the dispatch picks it for, 0 (the
@@ -1516,6 +1562,13 @@ static int launch_wide_partials(const void* x, const void* w, int64_t M, int64_t
 // A tiles per raster group of the large-M kernels (a group's CTAs sweep the B tiles while
 // its A tiles stay in L2): the per-kernel default unless the environment variable
 // QW_GEMM_GROUP gives one for all of them (a tuning knob).
+// Raster group of the kernels with 256-row tiles (CTA pair, and one CTA with two 128-row
+// accumulators). Measured in the power-capped B32 x L1024 step on B200 (QW_GEMM_GROUP, two
+// rounds each): 8: 23,115 / 22,859 tok/s, 12: 23,820 / 23,704, 16: 24,210 / 24,052,
+// 24: 23,536 / 23,485, 32: 22,655 / 22,640 (SM clock 1207, 1260, 1271-1282, 1245-1260,
+// 1144-1155 MHz: the group sets the DRAM traffic of the step's GEMMs and through it their
+// share of the 1 kW budget).
+constexpr int kGroup256 = 16;
 static int raster_group(int dflt) {
   static int v = -1;
   if (v < 0) {
@@ -1621,7 +1674,7 @@ extern "C" int qw_gemm_bf16(const void* x, const void* w, void* y, int64_t M, in
       p.k_splits = 1;
       p.kb_per_split = p.kb_total;
       p.swap = 0;
-      p.group = raster_group(8);
+      p.group = raster_group(kGroup256);
       p.b_up_offset = (int)n_out;
       p.out = y;
       p.ldo = ldy;
@@ -1629,6 +1682,13 @@ extern "C" int qw_gemm_bf16(const void* x, const void* w, void* y, int64_t M, in
       CUtensorMap tc;
       const bool tma_out = (out_kind == QW_OUT_BF16 || swiglu) && p.vec_ok && gemm_tma_store() &&
                            make_tmap(&tc, y, M, n_out, ldy, 32) == QW_OK;
+      const int wide = gemm_wide_mode();
+      if (((wide & 1) && out_kind == QW_OUT_BF16) || ((wide & 2) && swiglu)) {
+        // 256 x 512 tiles per pair: 256 SwiGLU or 512 plain output columns per unit
+        p.b_tiles = swiglu ? (int)((n_out + P_BN - 1) / P_BN) : (int)((N + 2 * P_BN - 1) / (2 * P_BN));
+        if (swiglu) return launch_pair<EPI_SWIGLU, 2>(ta, tb, p, s, tma_out ? &tc : nullptr);
+        return launch_pair<EPI_BF16, 2>(ta, tb, p, s, tma_out ? &tc : nullptr);
+      }
       if (swiglu) return launch_pair<EPI_SWIGLU>(ta, tb, p, s, tma_out ? &tc : nullptr);
       if (out_kind == QW_OUT_F32_OF_BF16) return launch_pair<EPI_F32>(ta, tb, p, s);
       if (out_kind == QW_OUT_F32) return launch_pair<EPI_F32RAW>(ta, tb, p, s);
@@ -1657,7 +1717,7 @@ extern "C" int qw_gemm_bf16(const void* x, const void* w, void* y, int64_t M, in
                          make_tmap(&tc, y, M, n_out, ldy, 32) == QW_OK;
     const CUtensorMap* tcp = tma_out ? &tc : nullptr;
     if (mt == 2) {
-      p.group = raster_group(8);
+      p.group = raster_group(kGroup256);
       if (swiglu) return launch_gemm<BN, 3, EPI_SWIGLU, 2>(ta, tb, p, s, tcp);
       if (out_kind == QW_OUT_F32_OF_BF16) return launch_gemm<BN, 3, EPI_F32, 2>(ta, tb, p, s);
       if (out_kind == QW_OUT_F32) return launch_gemm<BN, 3, EPI_F32RAW, 2>(ta, tb, p, s);
@@ -1962,7 +2022,11 @@ extern "C" int qw_gemm_qkv_rope_store(const void* x, const void* w, void* qkv, i
       if ((rc = make_tmap(&ta, x, M, K, ldx, BM)) != QW_OK) return rc;
       if ((rc = make_tmap(&tb, w, N, K, ldw, P_BN / 2)) != QW_OK) return rc;
       p.a_tiles = (int)((M + 255) / 256);
-      p.group = raster_group(8);
+      p.group = raster_group(kGroup256);
+      if ((gemm_wide_mode() & 4) && (N / 256) % 2 == 0) {
+        p.b_tiles = (int)(N / 512);  // two head segments per unit
+        return launch_pair<EPI_QKV, 2>(ta, tb, p, s);
+      }
       return launch_pair<EPI_QKV>(ta, tb, p, s);
     }
     if ((rc = make_tmap(&ta, x, M, K, ldx, BM)) != QW_OK) return rc;

@@ -437,3 +437,43 @@ def test_gemm_qkv_rope_store_matches_unfused(K, M, nq, nkv, d, rd):
     assert bool(torch.isnan(caches[0][untouched].float()).all()) and bool(torch.isnan(caches[1][untouched].float()).all())
     from qwen38_inference_b200 import _lib
     assert _lib.take_device_error() == 0
+
+
+@pytest.mark.parametrize("M", [2000, 4096])
+@pytest.mark.parametrize("nq,nkv", [(24, 4), (6, 1)])
+def test_gemm_qkv_rope_store_wide_pair_tile(K, monkeypatch, M, nq, nkv):
+    """The attention projection on the 256 x 512 CTA-pair tile (two head segments per unit,
+    QW_GEMM_WIDE=4) against the 256 x 256 tile (QW_GEMM_WIDE=0): projection, q/k norm and
+    RoPE, gate and the cache rows bit for bit, on NaN-poisoned caches. M = 2000 is a ragged
+    last row tile; (6, 1) at M = 2000 has too few tiles for the pair kernel and takes the
+    split-K product (the same in both modes)."""
+    from qwen38_inference_b200.config import rope_table, HybridConfig
+    d, rd = 256, 64
+    g = torch.Generator(device=DEV).manual_seed(M * 3 + nq)
+    H, N = 5120, (2 * nq + 2 * nkv) * d
+    cfg = HybridConfig(hidden_size=64, intermediate_size=64, num_attention_heads=nq, num_key_value_heads=nkv,
+                       head_dim=d, linear_num_key_heads=1, linear_num_value_heads=1, linear_key_head_dim=128,
+                       linear_value_head_dim=128, linear_conv_kernel_dim=4, num_hidden_layers=4, vocab_size=8,
+                       partial_rotary_factor=rd / d)
+    rope = rope_table(cfg, 4096, DEV)
+    x = torch.randn(M, H, device=DEV, generator=g).bfloat16()
+    w = (torch.randn(N, H, device=DEV, generator=g) * 0.02).bfloat16()
+    qw = (torch.randn(d, device=DEV, generator=g) * 0.1).bfloat16()
+    kw = (torch.randn(d, device=DEV, generator=g) * 0.1).bfloat16()
+    rows = 2 * M + 64
+    pos = torch.randint(0, 4096, (M,), device=DEV, generator=g, dtype=torch.int32)
+    loc = (torch.randperm(rows - 64, device=DEV, generator=g)[:M] + 64).to(torch.int32)
+    ws = K.Workspace(DEV)
+    outs = []
+    for mode in ("0", "4"):
+        monkeypatch.setenv("QW_GEMM_WIDE", mode)
+        a = torch.zeros(M, N, dtype=torch.bfloat16, device=DEV)
+        kc = torch.full((rows, nkv, d), float("nan"), dtype=torch.bfloat16, device=DEV)
+        vc = torch.full((rows, nkv, d), float("nan"), dtype=torch.bfloat16, device=DEV)
+        K.gemm_qkv_rope_store(x, w, a, nq, nkv, d, qw, kw, rope, pos, loc, kc, vc, 1e-6, ws)
+        outs.append((a, kc, vc))
+    torch.cuda.synchronize()
+    for t0, t1 in zip(*outs):
+        assert torch.equal(t0.view(torch.int16), t1.view(torch.int16))
+    from qwen38_inference_b200 import _lib
+    assert _lib.take_device_error() == 0
