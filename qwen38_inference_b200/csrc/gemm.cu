@@ -1455,17 +1455,18 @@ static int gemm_wide_mode() {
   return e ? atoi(e) : 0;
 }
 
-// CTA-pair GEMM for large M: 1 (default) for the shapes the dispatch picks it for, 0 (the
-// environment variable QW_GEMM_PAIR=0) for none, 2 (QW_GEMM_PAIR=2) for every large-M shape
-// (tuning knobs).
+// CTA-pair GEMM for large M: 0 (default) for none, 1 (the environment variable QW_GEMM_PAIR=1,
+// read at every call) for plain outputs with K <= 6144 and the attention projection, 2
+// (QW_GEMM_PAIR=2) for every large-M shape (tuning knobs). In the power-capped B32 x L1024 step on B200, with the raster
+// groups of 16 (256-row tiles) and 24 (128-row tiles), three interleaved rounds each: pairs
+// for the plain shapes and the SwiGLU gate_up 24,381 / 24,360 / 24,473 tok/s, pairs for the
+// plain shapes only 24,835 / 24,859 / 24,716, no pairs 24,996 / 24,964 / 24,855. The pair
+// kernel keeps its tensor pipe busier per cycle, but the single-CTA kernels leave the step a
+// higher clock under the 1 kW cap (1383-1402 against 1282-1308 MHz).
 static int gemm_pair_mode() {
-  static int v = -1;
-  if (v < 0) {
-    const char* e = getenv("QW_GEMM_PAIR");
-    v = e ? atoi(e) : 1;
-    if (v < 0 || v > 2) v = 1;
-  }
-  return v;
+  const char* e = getenv("QW_GEMM_PAIR");
+  const int v = e ? atoi(e) : 0;
+  return (v < 0 || v > 2) ? 0 : v;
 }
 
 struct SkinnyPlan {
@@ -1652,18 +1653,13 @@ extern "C" int qw_gemm_bf16(const void* x, const void* w, void* y, int64_t M, in
     const int per16 = (out_kind == QW_OUT_F32_OF_BF16 || out_kind == QW_OUT_F32) ? 4 : 8;  // elements per 16 B
     p.vec_ok = ((uintptr_t)y % 16) == 0 && (ldy % per16) == 0;
     constexpr int BN = 256;
-    // Kernel choice per shape, from sustained (power-capped) runs of a whole prefill's
-    // projections on B200: CTA pairs win for K <= 6144 plain outputs (qkvz, qkv, out_proj,
-    // o_proj: 5-11%) and for the SwiGLU gate_up (below); K >= 8192 (the down projection)
-    // does better on one CTA with 256-row tiles (pairs drew 2.6x its DRAM bytes there).
+    // Kernel choice per shape (gemm_pair_mode): one CTA per tile by default; with
+    // QW_GEMM_PAIR=1 CTA pairs for K <= 6144 plain outputs (qkvz, qkv, out_proj, o_proj),
+    // with QW_GEMM_PAIR_SWIGLU=1 for the SwiGLU gate_up too (tuning knobs). K >= 8192 (the
+    // down projection) does better on one CTA with 256-row tiles in every setting measured.
     const int pair_mode = gemm_pair_mode();
-    // The SwiGLU gate_up shape on pairs too (QW_GEMM_PAIR_SWIGLU=0 keeps it on one CTA): in
-    // the power-capped B32 x L1024 step the pair kernel runs it at 1413 against 1340 TFLOP/s
-    // and the step gains 0.8 % (two A/B runs on one box), although the SM clock drops ~4 %.
-    static const int pair_swiglu = [] {
-      const char* e = getenv("QW_GEMM_PAIR_SWIGLU");
-      return e ? atoi(e) : 1;
-    }();
+    const char* e_sw = getenv("QW_GEMM_PAIR_SWIGLU");
+    const int pair_swiglu = e_sw ? atoi(e_sw) : 0;
     if (M >= 256 && ((!swiglu && K < 8192 && pair_mode == 1) || pair_mode == 2 || (swiglu && pair_swiglu == 1))) {
       if ((rc = make_tmap(&ta, x, M, K, ldx, BM)) != QW_OK) return rc;
       if ((rc = make_tmap(&tb, w, N, K, ldw, P_BN / 2)) != QW_OK) return rc;

@@ -153,26 +153,30 @@ def test_gemm_add_rmsnorm_matches_unfused(ops, M, N, K):
     assert bool((d <= ulp).all()) and (d > 0).float().mean().item() < 0.01
 
 
-# shapes that take the CTA-pair path (M >= 256, no split over K: K of at most 15 k-blocks, or
-# enough 128 x 256 tiles to fill the SMs twice)
+# shapes with M >= 256 and no split over K (K of at most 15 k-blocks, or enough 128 x 256 tiles
+# to fill the SMs twice): the CTA-pair path when it is selected
 @pytest.mark.parametrize("M,N,K,swiglu", [(512, 1024, 512, False), (300, 1000, 512, False),
                                           (1024, 16480, 320, False), (4096, 5120, 6144, False),
                                           (520, 2 * 200, 256, True), (1024, 2 * 1536, 640, True),
                                           (300, 2 * 2304, 512, True)])
-def test_gemm_wide_pair_tile_equals_pair_tile(ops, monkeypatch, M, N, K, swiglu):
-    """The 256 x 512 CTA-pair tile (QW_GEMM_WIDE=7: every epilogue that has it; read at every
-    call) against the 256 x 256 tile (QW_GEMM_WIDE=0): every output element accumulates the same k-steps in the same order, so
-    the outputs are bit-identical, ragged M and N included (a last N-half wholly past N)."""
+def test_gemm_kernel_variants_agree(ops, monkeypatch, M, N, K, swiglu):
+    """The one-CTA kernels (the default), the CTA-pair kernel (QW_GEMM_PAIR=2 and
+    QW_GEMM_PAIR_SWIGLU=1, read at every call) and its 256 x 512 tile (QW_GEMM_WIDE=7) on the
+    same product: every output element accumulates the same 16-wide k-steps in the same order
+    in each, so the outputs are bit-identical, ragged M and N included (a last N-half wholly
+    past N)."""
     g = torch.Generator(device="cuda").manual_seed(M + N + K)
     x = torch.randn(M, K, device="cuda", generator=g).to(torch.bfloat16)
     w = (torch.randn(N, K, device="cuda", generator=g) * 0.05).to(torch.bfloat16)
     kind = ops.OUT_SWIGLU if swiglu else ops.OUT_BF16
     ws = ops.Workspace("cuda")
-    monkeypatch.setenv("QW_GEMM_WIDE", "0")
-    ref = ops.gemm(x, w, out_kind=kind, ws=ws)
-    monkeypatch.setenv("QW_GEMM_WIDE", "7")
-    got = ops.gemm(x, w, out_kind=kind, ws=ws)
+    outs = []
+    for pair, wide in (("0", "0"), ("2", "0"), ("2", "7")):
+        monkeypatch.setenv("QW_GEMM_PAIR", pair)
+        monkeypatch.setenv("QW_GEMM_PAIR_SWIGLU", "1" if pair != "0" else "0")
+        monkeypatch.setenv("QW_GEMM_WIDE", wide)
+        outs.append(ops.gemm(x, w, out_kind=kind, ws=ws))
     torch.cuda.synchronize()
-    assert torch.equal(got, ref)
+    assert torch.equal(outs[1], outs[0]) and torch.equal(outs[2], outs[0])
     if not swiglu:
-        check_bf16(got, x, w)
+        check_bf16(outs[0], x, w)

@@ -399,8 +399,9 @@ def test_gemm_qkv_rope_store_matches_unfused(K, M, nq, nkv, d, rd):
     element and its head row's RMS (the sum of squares is reduced in another order in the
     GEMM epilogue, which can move both normalized elements of a rotated pair by an ulp), no
     other cache row written. M = 2 and
-    37 take the weight-streaming split-K path, 130 the single-CTA kernel, 300 the CTA pair,
-    512 a split-K chunk; d = 64 runs the GEMM and qk_norm_rope_store."""
+    37 take the weight-streaming split-K path, 130 and 300 the one-CTA kernel or a split-K
+    product where the tiles leave SMs idle, 512 a split-K chunk; d = 64 runs the GEMM and
+    qk_norm_rope_store. The CTA-pair variants are compared with the one-CTA kernel below."""
     from qwen38_inference_b200.config import rope_table, HybridConfig
     g = torch.Generator(device=DEV).manual_seed(M + nq)
     H = 5120 if nq == 24 else 512
@@ -441,12 +442,12 @@ def test_gemm_qkv_rope_store_matches_unfused(K, M, nq, nkv, d, rd):
 
 @pytest.mark.parametrize("M", [2000, 4096])
 @pytest.mark.parametrize("nq,nkv", [(24, 4), (6, 1)])
-def test_gemm_qkv_rope_store_wide_pair_tile(K, monkeypatch, M, nq, nkv):
-    """The attention projection on the 256 x 512 CTA-pair tile (two head segments per unit,
-    QW_GEMM_WIDE=4) against the 256 x 256 tile (QW_GEMM_WIDE=0): projection, q/k norm and
-    RoPE, gate and the cache rows bit for bit, on NaN-poisoned caches. M = 2000 is a ragged
-    last row tile; (6, 1) at M = 2000 has too few tiles for the pair kernel and takes the
-    split-K product (the same in both modes)."""
+def test_gemm_qkv_rope_store_kernel_variants_agree(K, monkeypatch, M, nq, nkv):
+    """The attention projection on the one-CTA kernel (the default), the CTA pair
+    (QW_GEMM_PAIR=1) and its 256 x 512 tile (two head segments per unit, QW_GEMM_WIDE=4):
+    projection, q/k norm and RoPE, gate and the cache rows bit for bit, on NaN-poisoned
+    caches. M = 2000 is a ragged last row tile; (6, 1) at M = 2000 has too few tiles and takes
+    the split-K product in every mode."""
     from qwen38_inference_b200.config import rope_table, HybridConfig
     d, rd = 256, 64
     g = torch.Generator(device=DEV).manual_seed(M * 3 + nq)
@@ -465,7 +466,8 @@ def test_gemm_qkv_rope_store_wide_pair_tile(K, monkeypatch, M, nq, nkv):
     loc = (torch.randperm(rows - 64, device=DEV, generator=g)[:M] + 64).to(torch.int32)
     ws = K.Workspace(DEV)
     outs = []
-    for mode in ("0", "4"):
+    for pair, mode in (("0", "0"), ("1", "0"), ("1", "4")):
+        monkeypatch.setenv("QW_GEMM_PAIR", pair)
         monkeypatch.setenv("QW_GEMM_WIDE", mode)
         a = torch.zeros(M, N, dtype=torch.bfloat16, device=DEV)
         kc = torch.full((rows, nkv, d), float("nan"), dtype=torch.bfloat16, device=DEV)
@@ -473,7 +475,8 @@ def test_gemm_qkv_rope_store_wide_pair_tile(K, monkeypatch, M, nq, nkv):
         K.gemm_qkv_rope_store(x, w, a, nq, nkv, d, qw, kw, rope, pos, loc, kc, vc, 1e-6, ws)
         outs.append((a, kc, vc))
     torch.cuda.synchronize()
-    for t0, t1 in zip(*outs):
-        assert torch.equal(t0.view(torch.int16), t1.view(torch.int16))
+    for other in outs[1:]:
+        for t0, t1 in zip(outs[0], other):
+            assert torch.equal(t0.view(torch.int16), t1.view(torch.int16))
     from qwen38_inference_b200 import _lib
     assert _lib.take_device_error() == 0
