@@ -480,3 +480,68 @@ def test_gemm_qkv_rope_store_kernel_variants_agree(K, monkeypatch, M, nq, nkv):
             assert torch.equal(t0.view(torch.int16), t1.view(torch.int16))
     from qwen38_inference_b200 import _lib
     assert _lib.take_device_error() == 0
+
+
+def _ulps(got, exp, d_head):
+    """|got - exp| in bf16 ulps of max(|element|, RMS of its head's d values): an output that
+    cancellation in sum_s p_s v_s made small is measured at its row's scale."""
+    got, exp = got.float().cpu(), exp.float().cpu()
+    d = (got - exp).abs()
+    rms = exp.view(exp.shape[0], -1, d_head).pow(2).mean(-1, keepdim=True).sqrt().expand(-1, -1, d_head)
+    scale = torch.maximum(torch.maximum(got.abs(), exp.abs()), rms.reshape(exp.shape))
+    return d / ulp(scale), d
+
+
+@pytest.mark.parametrize("nq,nkv,d,case", [(24, 4, 256, "mixed"), (6, 1, 256, "mixed"), (4, 2, 64, "mixed"),
+                                           (24, 4, 256, "long"), (4, 2, 64, "long")])
+def test_attn_prefill_against_kernel_restatement(K, nq, nkv, d, case):
+    """The prefill kernel against the CPU restatement of its own steps (64-key blocks, the
+    running maximum raised only past 8, P rounded to bf16 at that scale;
+    oracle/attention_kernels.py): what is left is the order of the fp32 sums and the
+    hardware 2^x, at most 4 bf16 ulps at the scale of the element's head row and at most 1 %
+    of the elements (measured on B200: at most 3 ulps, 0.05-0.09 % of the elements differ)."""
+    from oracle import attention_kernels as AK
+    from qwen38_inference_b200.model import build_metadata
+    g = gen(4)
+    if case == "mixed":
+        prefixes, lens = [0, 37, 130, 0], [200, 1, 77, 129]
+    else:
+        prefixes, lens = [0, 300], [700, 260]
+    kc, vc, qkv, starts = _attn_case(g, nq, nkv, d, prefixes, lens, cap=1024)
+    if case == "long":
+        pos = torch.arange(kc.shape[0], dtype=torch.float32).view(-1, 1, 1)
+        kc = bf(kc.float() * (1.0 + pos / 256.0))
+    packed, offs, T = build_metadata(list(range(len(lens))), prefixes, lens, 1024)
+    md = {k: torch.from_numpy(packed[o:o + n]).to(DEV) for k, (o, n) in offs.items()}
+    out = torch.empty(T, nq * d, dtype=torch.bfloat16, device=DEV)
+    K.attn_prefill(qkv.to(DEV), nq, nkv, d, kc.to(DEV), vc.to(DEV), md["tiles"], md["cu"], md["prefix"],
+                   md["kv_base"], out, d ** -0.5)
+    exp = AK.attn_prefill(qkv.float(), nq, nkv, d, kc.float(), vc.float(), starts, prefixes, lens, d ** -0.5)
+    u, diff = _ulps(out, exp, d)
+    print(f"prefill {case} nq={nq}: max {u.max().item():.2f} ulp, {(diff > 0).float().mean().item():.4f} differ")
+    assert u.max().item() <= 4.0 and (diff > 0).float().mean().item() <= 0.01
+
+
+@pytest.mark.parametrize("nq,nkv,d", [(24, 4, 256), (4, 2, 64)])
+@pytest.mark.parametrize("splits", [1, 3])
+def test_attn_decode_against_kernel_restatement(K, nq, nkv, d, splits):
+    """The split-KV decode kernel and its merge against the CPU restatement of their steps
+    (16-key steps in two warp halves per split, exact running maximum, bf16 P, fp32 merges;
+    oracle/attention_kernels.py): at most 4 bf16 ulps at the scale of the element's head row
+    and at most 1 % of the elements (measured on B200: at most 2 ulps, 0.08-0.15 %)."""
+    from oracle import attention_kernels as AK
+    g = gen(5)
+    lens = [1] * 5
+    prefixes = [1, 63, 64, 300, 511]
+    kc, vc, qkv, starts = _attn_case(g, nq, nkv, d, prefixes, lens)
+    B = len(lens)
+    seq_len = torch.tensor([p + 1 for p in prefixes], dtype=torch.int32)
+    kv_base = torch.tensor(starts, dtype=torch.int32)
+    out = torch.empty(B, nq * d, dtype=torch.bfloat16, device=DEV)
+    K.attn_decode(qkv.to(DEV), B, nq, nkv, d, kc.to(DEV), vc.to(DEV), seq_len.to(DEV), kv_base.to(DEV), 512, splits,
+                  out, d ** -0.5, K.Workspace(DEV))
+    exp = AK.attn_decode(qkv.float(), nq, nkv, d, kc.float(), vc.float(), starts, [p + 1 for p in prefixes], 512,
+                         splits, d ** -0.5)
+    u, diff = _ulps(out, exp, d)
+    print(f"decode splits={splits} nq={nq}: max {u.max().item():.2f} ulp, {(diff > 0).float().mean().item():.4f} differ")
+    assert u.max().item() <= 4.0 and (diff > 0).float().mean().item() <= 0.01
