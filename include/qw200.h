@@ -226,6 +226,14 @@ int qw_gdn_decode(const void* qkvz, int64_t ldx, const void* ba, int64_t ldba, c
  * row zero. Applied to K and V together (REF:4985-5001 _reserve; solution/cache_growth.py) */
 int qw_kv_grow(const void* src_k, const void* src_v, void* dst_k, void* dst_v, const int32_t* lengths, int64_t S,
                int64_t old_cap, int64_t new_cap, int64_t row_elems, qw_stream_t stream);
+/* The same growth for the (K, V) pools of n_layers attention layers in one launch: src_k,
+ * src_v, dst_k, dst_v are host arrays of n_layers device pointers, n_layers at most
+ * QW_KV_GROW_MAX_LAYERS (REF:4985-5001 applied to every layer, as solution/cache_growth.py
+ * grow_fused does with one kernel)                                                          */
+#define QW_KV_GROW_MAX_LAYERS 32
+int qw_kv_grow_layers(const void* const* src_k, const void* const* src_v, void* const* dst_k, void* const* dst_v,
+                      int64_t n_layers, const int32_t* lengths, int64_t S, int64_t old_cap, int64_t new_cap,
+                      int64_t row_elems, qw_stream_t stream);
 
 /* ---- head-wise tensor parallelism (new: the reference runs one GPU) ------------------ *
  * Peer buffers of the one-shot all-reduce fused into the decode projections

@@ -64,6 +64,7 @@ SIGNATURES = {
                              F32, F32, P]),
     "qw_gdn_decode": (I32, [P, I64, P, I64, P, P, P, P, I64, I64, P, P, P, P, I64, I64, I64, I64, I64, F32, P]),
     "qw_kv_grow": (I32, [P, P, P, P, P, I64, I64, I64, I64, P]),
+    "qw_kv_grow_layers": (I32, [P, P, P, P, I64, P, I64, I64, I64, I64, P]),
 }
 
 

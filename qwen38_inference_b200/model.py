@@ -359,10 +359,9 @@ class Qwen38:
         box = getattr(cache, "_arena_box", None)
         for i, (k_old, v_old) in cache.kv.items():
             shape = (S * capacity + PAGE,) + tuple(k_old.shape[1:])
-            k_new = self._arena.take(shape, self.dtype, False)
-            v_new = self._arena.take(shape, self.dtype, False)
-            ops.kv_grow(k_old, v_old, k_new, v_new, lengths, S, cache.capacity, capacity)
-            new_kv[i] = (k_new, v_new)
+            new_kv[i] = (self._arena.take(shape, self.dtype, False), self._arena.take(shape, self.dtype, False))
+        if new_kv:  # every layer's pools in one launch
+            ops.kv_grow_layers(list(cache.kv.values()), list(new_kv.values()), lengths, S, cache.capacity, capacity)
         old = [t for pair in cache.kv.values() for t in pair]
         cache.kv = new_kv
         cache.capacity = capacity

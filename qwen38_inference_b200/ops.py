@@ -316,3 +316,21 @@ def kv_grow(src_k, src_v, dst_k, dst_v, lengths, S, old_cap, new_cap):
     LAUNCHES[0] += 1
     _lib.call("qw_kv_grow", src_k.data_ptr(), src_v.data_ptr(), dst_k.data_ptr(), dst_v.data_ptr(),
               lengths.data_ptr(), S, old_cap, new_cap, row_elems, _stream())
+
+
+KV_GROW_MAX_LAYERS = 32  # QW_KV_GROW_MAX_LAYERS
+
+
+def kv_grow_layers(src, dst, lengths, S, old_cap, new_cap):
+    """The growth of every layer's (K, V) pools (``src``, ``dst``: lists of (K, V) pairs of
+    equal row size) in one launch per QW_KV_GROW_MAX_LAYERS layers."""
+    import ctypes
+    row_elems = src[0][0][0].numel()
+    for i in range(0, len(src), KV_GROW_MAX_LAYERS):
+        s_part, d_part = src[i:i + KV_GROW_MAX_LAYERS], dst[i:i + KV_GROW_MAX_LAYERS]
+        n = len(s_part)
+        arrs = [(ctypes.c_void_p * n)(*[t.data_ptr() for t in col]) for col in
+                ([k for k, _ in s_part], [v for _, v in s_part], [k for k, _ in d_part], [v for _, v in d_part])]
+        LAUNCHES[0] += 1
+        _lib.call("qw_kv_grow_layers", *[ctypes.addressof(a) for a in arrs], n, lengths.data_ptr(), S, old_cap,
+                  new_cap, row_elems, _stream())

@@ -545,3 +545,23 @@ def test_attn_decode_against_kernel_restatement(K, nq, nkv, d, splits):
     u, diff = _ulps(out, exp, d)
     print(f"decode splits={splits} nq={nq}: max {u.max().item():.2f} ulp, {(diff > 0).float().mean().item():.4f} differ")
     assert u.max().item() <= 4.0 and (diff > 0).float().mean().item() <= 0.01
+
+
+def test_kv_grow_layers(K):
+    """The growth of several layers' pools in one launch equals the one-layer growth of each
+    (two row widths: the 27B's 4 KV heads of 256, and one head of 64, the generic path)."""
+    for nkv, d in ((4, 256), (1, 64)):
+        g = gen(11 + d)
+        S, old, new, n_layers = 3, 64, 192, 3
+        lengths = torch.tensor([10, 0, 64], dtype=torch.int32, device=DEV)
+        src = [tuple(bf(torch.randn(S * old + 64, nkv, d, generator=g)).to(DEV) for _ in range(2))
+               for _ in range(n_layers)]
+        dst = [tuple(torch.full((S * new + 64, nkv, d), 7.0, dtype=torch.bfloat16, device=DEV) for _ in range(2))
+               for _ in range(n_layers)]
+        K.kv_grow_layers(src, dst, lengths, S, old, new)
+        for (sk, sv), (dk, dv) in zip(src, dst):
+            ek, ev = (torch.full_like(dk, 7.0) for _ in range(2))
+            K.kv_grow(sk, sv, ek, ev, lengths, S, old, new)
+            torch.cuda.synchronize()
+            assert torch.equal(dk, ek) and torch.equal(dv, ev)
+            assert torch.equal(dk[64 + 2 * new:64 + 2 * new + 64], sk[64 + 2 * old:64 + 3 * old])

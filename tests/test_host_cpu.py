@@ -120,6 +120,8 @@ def host_model(monkeypatch):
     m._engine = _StubEngine(cfg.vocab_size)
     m._arena = M._BufferArena(m.device)
     monkeypatch.setattr(M.ops, "kv_grow", _cpu_kv_grow)
+    monkeypatch.setattr(M.ops, "kv_grow_layers", lambda src, dst, lengths, S, old_cap, new_cap: [
+        _cpu_kv_grow(sk, sv, dk, dv, lengths, S, old_cap, new_cap) for (sk, sv), (dk, dv) in zip(src, dst)])
     return m
 
 
