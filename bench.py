@@ -1055,7 +1055,7 @@ def _gdn_prefill_case(cfg, B, L, g, flashinfer=False):
     slots = torch.arange(B, dtype=torch.int32, device=dev)
     # algorithmic bytes: q, k, v, z, ba read once, y written once, state read + written
     work = 2.0 * T * (2 * H * dk + 2 * HV * dv + 2 * HV) + 2.0 * T * HV * dv + 2.0 * B * HV * dv * dk * 4
-    extra["flop_per_launch"] = (8 * dk * dv + 10 * 64 * dv) * T * HV  # (8d^2 + 10Cd) per token and head
+    extra["flop_per_launch"] = (8 * dk * dv + 10 * 64 * dv) * T * HV  # (8 d^2 + 10 C d) FLOP per token and value head
     extra["kernel"] = "qw gdn_prefill_kernel (chunked delta rule + gating + gated RMSNorm)"
 
     def launch():
@@ -1069,7 +1069,7 @@ def _gdn_decode_case(cfg, B, g):
     recurrent step of the fp32 state, gated RMSNorm), 27B head geometry, configs[3] inputs
     (projection rows ~ N(0,1), the gating above, a state of a previous prefill ~ N(0, 0.05)).
     Algorithmic bytes: the state read and written, the conv state read and written, the
-    projection row and ba read, y written (SURVEY 8(d) per-op units)."""
+    projection row and ba read, y written."""
     import torch
     from qwen38_inference_b200 import ops
     dev = "cuda"
