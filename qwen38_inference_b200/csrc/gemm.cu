@@ -1568,7 +1568,7 @@ static int launch_wide_partials(const void* x, const void* w, int64_t M, int64_t
 // rounds each): 8: 23,115 / 22,859 tok/s, 12: 23,820 / 23,704, 16: 24,210 / 24,052,
 // 24: 23,536 / 23,485, 32: 22,655 / 22,640 (SM clock 1207, 1260, 1271-1282, 1245-1260,
 // 1144-1155 MHz: the group sets the DRAM traffic of the step's GEMMs and through it their
-// share of the 1 kW budget).
+// share of the 1 kW power limit).
 constexpr int kGroup256 = 16;
 static int raster_group(int dflt) {
   static int v = -1;
