@@ -116,10 +116,14 @@ QW_DEV void cpa16(uint32_t dst, const void* src, bool pred) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(pred ? 16 : 0) : "memory");
 }
 // Register split between the warp groups: the CTA is launched with 512 x 128 registers
-// (ptxas is held to 128 by the launch bounds); the prep warpgroups give 40 back and the
-// state warpgroups take 40 more (the output warps hold a token row of O, 64 values, and its
-// squares while they reduce them): 256 x 88 + 256 x 168 = 512 x 128.
-constexpr int PREP_REGS = 88, STATE_REGS = 168;
+// (ptxas is held to 128 by the launch bounds); the prep warpgroups give 32 back and the
+// state warpgroups take 32 more (the output warps hold a token row of O, 64 values, and its
+// squares while they reduce them): 256 x 96 + 256 x 160 = 512 x 128. At 96 the prep code
+// does not spill (at 88 it did, and a B32 x L1024 launch took 2.7 % longer).
+#ifndef QW_GDN_PREP_REGS
+#define QW_GDN_PREP_REGS 96
+#endif
+constexpr int PREP_REGS = QW_GDN_PREP_REGS, STATE_REGS = 256 - QW_GDN_PREP_REGS;
 static_assert(256 * PREP_REGS + 256 * STATE_REGS == 512 * 128, "register split must equal the launch allocation");
 QW_DEV void named_bar(int id) { asm volatile("bar.sync %0, 256;" ::"r"(id) : "memory"); }
 QW_DEV void named_bar_n(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
@@ -402,32 +406,12 @@ __global__ void __launch_bounds__(512, 1) gdn_prefill_kernel(
         store_tile_bf16<4>(buf + B_P, qk, mt * 16, nh * 32, lane, 1.f);
       }
       named_bar(1);
-      // ---- diagonal blocks of T (warps 0-3) || b e^G K, e^{G_C-G} K, b V (warps 4-7)
-      if (warp < 4) {
-        const int i = warp, j = lane;  // lane j < 16 owns column j of T_ii
-        const float* a = blk + (6 + i) * BLK;
-        float tcol[16];
-#pragma unroll
-        for (int r = 0; r < 16; ++r) {
-          float av[16];
-#pragma unroll
-          for (int kx = 0; kx < r; ++kx) av[kx] = a[r * BLD + kx];
-          float acc[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-          for (int kx = 0; kx < r; ++kx) acc[kx & 3] += av[kx] * tcol[kx];  // tcol[kx] = 0 for kx < j
-          const float sum = (acc[0] + acc[1]) + (acc[2] + acc[3]);
-          tcol[r] = (r == j) ? 1.f : (r > j ? -sum : 0.f);
-        }
-        if (j < 16) {
-          float* td = blk + (10 + i) * BLK;
-#pragma unroll
-          for (int r = 0; r < 16; ++r) {
-            td[r * BLD + j] = tcol[r];
-            *reinterpret_cast<__nv_bfloat16*>(buf + B_T + swz_elem(16 * i + r, 16 * i + j)) = f2bf(tcol[r]);
-          }
-        }
-      } else {
-        for (int e = tid - 128; e < CH * 16; e += 128) {
+      // ---- diagonal blocks of T (warps 0-3) || b e^G K, e^{G_C-G} K, b V (warps 4-7 take rows
+      // 0-47 of the tiles, warps 0-3 rows 48-63 once their inverse is done: the two halves of
+      // the phase then take about the same time)
+      constexpr int SCALE_SPLIT = 48 * 16;  // 16-byte items (row, 8 columns) done by warps 4-7
+      auto scale_items = [&](int e_begin, int e_end, int t) {
+        for (int e = e_begin + t; e < e_end; e += 128) {
           const int r = e >> 4;
           const uint32_t off = swz(r, e & 15);
           float kf[8], vf[8], kb[8], kd[8];
@@ -444,6 +428,40 @@ __global__ void __launch_bounds__(512, 1) gdn_prefill_kernel(
           store_bf16x8(reinterpret_cast<__nv_bfloat16*>(buf + B_K + off), kd);
           store_bf16x8(reinterpret_cast<__nv_bfloat16*>(buf + B_V + off), vf);
         }
+      };
+      if (warp < 4) {
+        const int i = warp, j = lane;  // lane j < 16 owns column j of T_ii
+        const float* a = blk + (6 + i) * BLK;
+        float tcol[16];
+#pragma unroll
+        for (int r = 0; r < 16; ++r) {
+          // row r of A_ii as float4s (rows are 16-byte aligned); acc[e] sums the columns
+          // kx = 4 q + e < r in increasing kx, tcol[kx] = 0 for kx < j
+          float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+          for (int q4 = 0; q4 < 4; ++q4) {
+            if (4 * q4 < r) {
+              const float4 a4 = *reinterpret_cast<const float4*>(a + r * BLD + 4 * q4);
+              if (4 * q4 + 0 < r) acc[0] += a4.x * tcol[4 * q4 + 0];
+              if (4 * q4 + 1 < r) acc[1] += a4.y * tcol[4 * q4 + 1];
+              if (4 * q4 + 2 < r) acc[2] += a4.z * tcol[4 * q4 + 2];
+              if (4 * q4 + 3 < r) acc[3] += a4.w * tcol[4 * q4 + 3];
+            }
+          }
+          const float sum = (acc[0] + acc[1]) + (acc[2] + acc[3]);
+          tcol[r] = (r == j) ? 1.f : (r > j ? -sum : 0.f);
+        }
+        if (j < 16) {
+          float* td = blk + (10 + i) * BLK;
+#pragma unroll
+          for (int r = 0; r < 16; ++r) {
+            td[r * BLD + j] = tcol[r];
+            *reinterpret_cast<__nv_bfloat16*>(buf + B_T + swz_elem(16 * i + r, 16 * i + j)) = f2bf(tcol[r]);
+          }
+        }
+        scale_items(SCALE_SPLIT, CH * 16, tid);
+      } else {
+        scale_items(0, SCALE_SPLIT, tid - 128);
       }
       named_bar(1);
       // ---- M_ik = T_ii A_ik for the six blocks below the diagonal (warps 0-5)
