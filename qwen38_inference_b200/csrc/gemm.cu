@@ -1692,10 +1692,8 @@ extern "C" int qw_gemm_bf16(const void* x, const void* w, void* y, int64_t M, in
     }
     // 256-row tiles win when the main loop is long enough to hide their single-buffered
     // epilogue (measured on B200: K = 17408 +14%, N = 16384 +3%; SwiGLU, N = 5120 and
-    // N = 14336 with K <= 6144 lose 3-5% alone). QW_GEMM_SWIGLU_ROWS=256 (read at every call)
-    // gives the SwiGLU products 256-row tiles too.
-    const char* e_swr = getenv("QW_GEMM_SWIGLU_ROWS");
-    const bool big_tile = swiglu ? (e_swr && atoi(e_swr) == 256) : (K >= 8192 || N >= 16384);
+    // N = 14336 with K <= 6144 lose 3-5%)
+    const bool big_tile = !swiglu && (K >= 8192 || N >= 16384);
     const int mt = (M >= 256 && big_tile && gemm_tile_rows() == 256) ? 2 : 1;
     if ((rc = make_tmap(&ta, x, M, K, ldx, BM * mt)) != QW_OK) return rc;
     if ((rc = make_tmap(&tb, w, N, K, ldw, swiglu ? BN / 2 : BN)) != QW_OK) return rc;
